@@ -1,0 +1,344 @@
+"""Benchmark of the k-quant dequantize-and-multiply path on B200.
+
+Default workload: one Llama-8B decode layer in Q4_K at batch 1 --
+the five projections QKV 4096x6144, o 4096x4096, gate and up 4096x14336, down 14336x4096 --
+as fused dequant-GEMVs.  A step is one pass over the layer.  Weights are synthetic
+(N(0, 0.02), seed 0, quantized by vibeblade_b200.quantize); six distinct copies of the
+layer rotate so every step streams weights that are not in the 126 MB L2.
+
+Metric: Q4_K dequant-GEMV HBM GB/s = algorithmic bytes (K*N*bpw + B*K*4 + B*N*4 per
+GEMV) / device time.  With --gpus N (torchrun), every rank streams its own layer copies
+(independent objects, no collective: weak scaling) and the value is the sum over ranks
+divided by the max over ranks of the timed region.
+
+--impl reference times the reference's own CPU gemv_dequant (oracle/_ref, compiled from
+the reference sources; the C restatement when that library is absent) on the same
+workload with all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Q4_K dequant-GEMV HBM GB/s"
+LAYER_8B = [("qkv", 4096, 6144), ("o", 4096, 4096), ("gate", 4096, 14336), ("up", 4096, 14336),
+            ("down", 14336, 4096)]
+QTYPE = 12  # Q4_K
+BPW = 144 / 256
+
+
+def layer_bytes(batch: int) -> int:
+    return sum(int(K * N * BPW) + batch * K * 4 + batch * N * 4 for _, K, N in LAYER_8B)
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        if self.p is not None:
+            time.sleep(0.25)
+            self.p.terminate()
+            try:
+                self.p.wait(5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+
+    def summary(self) -> dict:
+        self.f.flush()
+        rows = [r.split(",") for r in Path(self.f.name).read_text().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus: int):
+    import torch
+    import torch.distributed as dist
+    if n_gpus > 1 or int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        rank = int(os.environ["RANK"])
+        local = int(os.environ.get("LOCAL_RANK", rank))
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        return rank, dist.get_world_size(), local
+    return 0, 1, 0
+
+
+def cpu_reference_gbs(batch: int, seconds: float, threads: int, steps: int | None = None,
+                      warmup: int = 0):
+    """Time the reference's gemv_dequant over the decode layer on host cores.
+
+    Returns (gb_per_s, kind, cores, sample_description, per_step_seconds)."""
+    import numpy as np
+    from oracle import load_oracle, load_ref
+    from concurrent.futures import ThreadPoolExecutor
+    from vibeblade_b200.quantize import synthetic_weights
+
+    ref = load_ref()
+    kind = "reference" if ref is not None else "port"
+    mats = [(K, N, synthetic_weights(K, N, QTYPE, seed=i).numpy()) for i, (_, K, N) in enumerate(LAYER_8B)]
+    rng = np.random.default_rng(1)
+    xs = {K: rng.normal(0, 1, (batch, K)).astype(np.float32) for _, K, _ in LAYER_8B}
+    pool = ThreadPoolExecutor(threads)
+
+    if ref is not None:
+        def one_layer():
+            for K, N, w in mats:
+                ref.gemv_dequant_sliced(xs[K], w, K, N, QTYPE, threads, pool)
+    else:
+        orc = load_oracle()
+        threads = 1
+
+        def one_layer():
+            for K, N, w in mats:
+                orc.gemv_dequant(xs[K], w, K, N, QTYPE)
+
+    for _ in range(warmup):
+        one_layer()
+    times = []
+    t_end = time.perf_counter() + seconds
+    while (steps is None and (time.perf_counter() < t_end or not times)) or \
+            (steps is not None and len(times) < steps):
+        t0 = time.perf_counter()
+        one_layer()
+        times.append(time.perf_counter() - t0)
+    pool.shutdown()
+    total = sum(times)
+    gbs = layer_bytes(batch) * len(times) / total / 1e9
+    sample = (f"{len(times)} passes over the Llama-8B Q4_K decode layer (5 GEMVs, batch {batch}), "
+              f"{total:.1f} s; gemv_dequant split over K across {threads} threads")
+    return gbs, kind, threads, sample, times
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    gbs, kind, cores, sample, times = cpu_reference_gbs(args.batch, 0.0, threads, steps=args.steps,
+                                                        warmup=args.warmup)
+    ms = 1e3 * sum(times) / len(times)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (N(0,0.02) weights, seed 0, quantized Q4_K; x N(0,1) seed 1)",
+        "config": {"workload": "llama8b_decode_layer_q4k", "batch": args.batch,
+                   "matrices": [f"{n} {k}x{m}" for n, k, m in LAYER_8B]},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_gpu(args) -> None:
+    import torch
+    import torch.distributed as dist
+    import vibeblade_b200 as vb
+    from vibeblade_b200 import _lib
+    from vibeblade_b200.quantize import synthetic_weights
+
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    lib = _lib.load()
+    B = args.batch
+    n_copies = args.copies
+    # weights: n_copies distinct layers (distinct seeds per rank and copy)
+    layers = []
+    for c in range(n_copies):
+        mats = []
+        for i, (name, K, N) in enumerate(LAYER_8B):
+            seed = 1000 * rank + 10 * c + i
+            mats.append((K, N, synthetic_weights(K, N, QTYPE, seed=seed, device=dev)))
+        layers.append(mats)
+    g = torch.Generator(device=dev).manual_seed(1)
+    xs = {K: torch.randn(B, K, generator=g, device=dev) for _, K, _ in LAYER_8B}
+    ys = [torch.empty(B, N, device=dev) for _, _, N in LAYER_8B]
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+
+    def step(s: int):
+        for (K, N, w), y in zip(layers[s % n_copies], ys):
+            rc = lib.vbq_gemv(xs[K].data_ptr(), w.data_ptr(), y.data_ptr(), K, N, QTYPE, B, sp)
+            if rc:
+                _lib.check(rc, lib)
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+
+    # ---- timed region: K steps, events on the launching stream ----
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for s in range(args.steps):
+            step(args.warmup + s)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms_total = e0.elapsed_time(e1)
+    t = torch.tensor([ms_total], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total = float(t.item())
+    total_bytes = layer_bytes(B) * args.steps * world
+    value = total_bytes / (ms_total * 1e-3) / 1e9
+
+    # ---- per-launch kernel time (roofline of the GEMV kernel), events per launch ----
+    evs = []
+    for s in range(args.steps):
+        for (K, N, w), y in zip(layers[s % n_copies], ys):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            lib.vbq_gemv(xs[K].data_ptr(), w.data_ptr(), y.data_ptr(), K, N, QTYPE, B, sp)
+            b.record(stream)
+            evs.append((a, b, K, N))
+    torch.cuda.synchronize()
+    kern_ms = sum(a.elapsed_time(b) for a, b, _, _ in evs)
+    alg = sum(int(K * N * BPW) + B * K * 4 + B * N * 4 for _, _, K, N in evs)
+    achieved = alg / (kern_ms * 1e-3) / 1e9
+    big = [(a.elapsed_time(b), K, N) for a, b, K, N in evs if (K, N) == (4096, 14336)]
+    big_gbs = (int(4096 * 14336 * BPW) + B * (4096 + 14336) * 4) / (statistics.mean(t for t, _, _ in big) * 1e-3) / 1e9
+
+    # ---- end to end through the public API with host buffers ----
+    xh = {K: v.cpu().pin_memory() for K, v in xs.items()}
+    yh = [torch.empty(B, N, pin_memory=True) for _, _, N in LAYER_8B]
+    h2d = sum(v.numel() * 4 for v in xh.values())
+    d2h = sum(v.numel() * 4 for v in yh)
+
+    def e2e_step(s: int):
+        xd = {K: v.to(dev, non_blocking=True) for K, v in xh.items()}
+        for (K, N, w), yo in zip(layers[s % n_copies], yh):
+            yd = vb.gemv_dequant(xd[K], w, None, K, N, QTYPE)
+            yo.copy_(yd, non_blocking=True)
+
+    for s in range(args.warmup):
+        e2e_step(s)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for s in range(args.steps):
+        e2e_step(s)
+    b.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b)
+    t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = layer_bytes(B) * args.steps * world / (float(t.item()) * 1e-3) / 1e9
+
+    pk = peaks()
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_total / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (N(0,0.02) weights, seed 0+, quantized Q4_K; x N(0,1) seed 1)",
+            "config": {"workload": "llama8b_decode_layer_q4k", "batch": B,
+                       "matrices": [f"{n} {k}x{m}" for n, k, m in LAYER_8B],
+                       "layer_copies_rotated": n_copies,
+                       "l2": f"inputs larger than L2: {n_copies} distinct layer copies "
+                             f"({n_copies * layer_bytes(B) / 1e6:.0f} MB) rotate per step",
+                       "parallelism": f"{world} independent GPUs, own layers each (no collective)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+                         "traffic": None, "peak_src": pk["src"],
+                         "kernel": "vbq::gemv_kernel<Q4_K,1,32>",
+                         "gemv_4096x14336_gbs": round(big_gbs, 1)},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "api": "vibeblade_b200.gemv_dequant"},
+            "gpu_launches": args.steps * len(LAYER_8B),
+            "clocks": clk.summary(),
+        }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        if not args.no_cpu_baseline:
+            gbs, kind, cores, sample, _ = cpu_reference_gbs(B, args.cpu_seconds, os.cpu_count() or 1)
+            line["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores,
+                                    "kind": kind, "sample": sample}
+        print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--copies", type=int, default=6)
+    ap.add_argument("--impl", default="vbq", choices=["vbq", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

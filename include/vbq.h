@@ -1,0 +1,94 @@
+/*
+ * vbq.h -- C ABI of the B200 (sm_100a) GGUF k-quant dequantize-and-multiply library.
+ *
+ * The library is the device-side replacement for VibeBlade's quantized matmul path
+ * (kevin046/VibeBlade, cpp/src/dequant.cpp and cpp/include/dequant.h).  Every entry
+ * point takes plain device pointers, sizes and a CUDA stream (as `void*`, NULL = the
+ * legacy default stream), enqueues its work on that stream and returns without
+ * synchronising.  No entry point allocates device memory.
+ *
+ * Matrix convention (the reference's, cpp/include/dequant.h:24-35): a weight matrix
+ * is K rows of N values; each row is a run of quant blocks along N, rows are
+ * vbq_row_bytes(type, N) bytes apart, and gemv computes y[n] = sum_k x[k] * W[k][n].
+ *
+ * Type ids are the reference's ggml_type values (cpp/include/ggml_types.h:11-27).
+ *
+ * Dequantized values are bit-identical to the reference CPU functions
+ * (dequantize_row_q4_K / _q6_K, cpp/src/dequant.cpp:268-301, :359-402), including
+ * their fp16 conversion (cpp/src/fp16_compat.cpp:13-35).  Q8_0 uses the GGUF block
+ * with an fp16 scale, like the reference's CUDA kernel (cpp/src/cuda_kernels.cu:718-735).
+ *
+ * Return value: VBQ_OK (0) or one of the VBQ_ERR_* codes; vbq_last_error() returns
+ * the message of the last failure on the calling thread.
+ */
+#ifndef VBQ_H
+#define VBQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ggml type ids (cpp/include/ggml_types.h:17,21,23) */
+#define VBQ_TYPE_Q8_0 8
+#define VBQ_TYPE_Q4_K 12
+#define VBQ_TYPE_Q6_K 14
+
+/* element types of outputs / activations */
+#define VBQ_DTYPE_F32 0
+#define VBQ_DTYPE_BF16 1
+
+/* status codes */
+#define VBQ_OK 0
+#define VBQ_ERR_TYPE 1        /* unsupported ggml type (reference: "Unsupported dequant type") */
+#define VBQ_ERR_SHAPE 2       /* bad sizes: N not a block multiple, batch out of range, ... */
+#define VBQ_ERR_ALIGN 3       /* a pointer or stride breaks an alignment rule */
+#define VBQ_ERR_NULL 4        /* a required pointer is NULL */
+#define VBQ_ERR_CUDA 5        /* a CUDA runtime call or kernel launch failed */
+#define VBQ_ERR_TIMEOUT 6     /* a bounded device-side wait gave up (see vbq_gemm) */
+#define VBQ_ERR_UNSUPPORTED 7 /* a valid request this build does not implement */
+#define VBQ_ERR_WORKSPACE 8   /* workspace missing or too small */
+
+/* Message of the last failing call on this thread ("" after success). */
+const char* vbq_last_error(void);
+
+/* Library version, as major*10000 + minor*100 + patch. */
+int vbq_version(void);
+
+/* Row stride in bytes of a K x N matrix of `type`: (N / block_values) * block_bytes,
+ * truncating like gemv_dequant (cpp/src/dequant.cpp:749-763).  Host-only helper. */
+int vbq_row_bytes(int32_t type, int64_t n, int64_t* out_bytes);
+
+/*
+ * Dequantize a K x N matrix (K rows of vbq_row_bytes(type, N) bytes) into fp32 or
+ * bf16 [K, N], row-major.  With rows == 1 it is the device form of
+ * `void dequantize_row(const void* row, float* out, int64_t n, ggml_type)`
+ * (cpp/include/dequant.h:11); then n may be ragged (not a block multiple) and only n
+ * values are written.  For rows > 1, n must be a multiple of the block size.
+ * bf16 output rounds the fp32 dequantized value to nearest-even.
+ */
+int vbq_dequantize(const void* w, void* out, int64_t rows, int64_t n, int32_t type,
+                   int32_t out_dtype, void* stream);
+
+/*
+ * Batched fused dequant-GEMV, the device form of
+ * `void gemv_dequant(const float* x, const void* W, float* out, int64_t K, int64_t N,
+ *                    ggml_type, float* scratch)` (cpp/include/dequant.h:27-35) and of
+ * `cuda::gemv_dequant(d_x, d_weights, d_y, K, M, ggml_type, d_scratch, stream)`
+ * (cpp/include/cuda_kernels.h:191-199):
+ *     y[b, n] = sum_k x[b, k] * deq(W)[k, n],  b < batch (1..16).
+ * x is fp32 [batch, K], y fp32 [batch, N], both row-major.  N must be a multiple of
+ * the block size (256 for Q4_K/Q6_K, 32 for Q8_0); W, x and y must be 16-byte aligned.
+ * The reference's scratch argument has no use here: the split over K reduces
+ * through distributed shared memory inside a thread-block cluster, so the call needs
+ * no workspace.  Results are deterministic (fixed reduction order).
+ */
+int vbq_gemv(const float* x, const void* w, float* y, int64_t K, int64_t N, int32_t type,
+             int32_t batch, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VBQ_H */

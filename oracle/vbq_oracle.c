@@ -1,0 +1,279 @@
+/*
+ * vbq_oracle.c -- CPU restatement of VibeBlade's GGUF k-quant dequantize-and-multiply path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the checker for the CUDA product in
+ * vibeblade_b200/csrc; nothing in the product links or calls it.  Only tests/,
+ * __graft_entry__.smoke() and bench.py's CPU-baseline leg load it.
+ *
+ * Parity is pinned: tests/test_oracle.py checks every function here bit-exactly
+ * against the reference's own C++ compiled from its sources (oracle/_ref, built by
+ * oracle/build.py) and against the committed golden vectors in tests/golden/.
+ *
+ * Each function restates the reference algorithm it cites (path within the
+ * kevin046/VibeBlade project).  Compile with -ffp-contract=off so the C compiler
+ * never fuses a multiply and an add that the reference evaluates separately.
+ */
+#include <stdint.h>
+#include <string.h>
+#include <stdlib.h>
+#include <math.h>
+
+/* ggml type ids: cpp/include/ggml_types.h:11-27 */
+enum { VBO_Q8_0 = 8, VBO_Q4_K = 12, VBO_Q6_K = 14 };
+
+/* Block geometry: cpp/include/ggml_types.h:31-71 (block sizes 32/256, byte sizes 34/144/210). */
+int64_t vbo_block_values(int32_t type) {
+    switch (type) {
+        case VBO_Q8_0: return 32;
+        case VBO_Q4_K: return 256;
+        case VBO_Q6_K: return 256;
+        default: return -1;
+    }
+}
+
+int64_t vbo_block_bytes(int32_t type) {
+    switch (type) {
+        case VBO_Q8_0: return 34;
+        case VBO_Q4_K: return 144;
+        case VBO_Q6_K: return 210;
+        default: return -1;
+    }
+}
+
+/* Row stride used by gemv_dequant: (N / block_values) * block_bytes, truncating
+ * (cpp/src/dequant.cpp:749-763). */
+int64_t vbo_row_bytes(int32_t type, int64_t n) {
+    int64_t bv = vbo_block_values(type), bb = vbo_block_bytes(type);
+    if (bv <= 0) return -1;
+    return (n / bv) * bb;
+}
+
+/* fp16 -> fp32 as the reference's f16_to_f32 computes it (cpp/src/fp16_compat.cpp:13-35),
+ * written as bit arithmetic on the fields.  Normal numbers, zeros, inf and NaN payloads
+ * convert exactly.  Subnormals do not: the reference normalises the mantissa starting
+ * from exponent 1 and then adds one more to the bias (`exp + 127 - 15 + 1`), so every
+ * subnormal input comes out twice its IEEE value.  The k-quant dequantizers that call it
+ * (Q4_K d/dmin, Q6_K d) inherit that factor, and parity is defined against them. */
+float vbo_f16_to_f32(uint16_t h) {
+    uint32_t sign = (uint32_t)(h >> 15) << 31;
+    uint32_t e = (h >> 10) & 0x1fu;
+    uint32_t m = h & 0x3ffu;
+    uint32_t bits;
+    if (e == 0x1fu) {
+        bits = sign | 0x7f800000u | (m << 13);
+    } else if (e != 0) {
+        bits = sign | ((e + 112u) << 23) | (m << 13);
+    } else if (m == 0) {
+        bits = sign;
+    } else {
+        /* IEEE value m * 2^-24 has biased fp32 exponent 113 - shift; the reference
+         * produces 114 - shift. */
+        int shift = 0;
+        while ((m & 0x400u) == 0) { m <<= 1; ++shift; }
+        bits = sign | ((uint32_t)(114 - shift) << 23) | ((m & 0x3ffu) << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+/* Exact IEEE fp16 -> fp32 (subnormals included), the conversion the reference's CUDA
+ * kernels (__half2float, cpp/src/cuda_kernels.cu:731) and numpy loader
+ * (np.float16, vibeblade/loader.py:131) use for the Q8_0 scale. */
+float vbo_f16_to_f32_ieee(uint16_t h) {
+    uint32_t sign = (uint32_t)(h >> 15) << 31;
+    uint32_t e = (h >> 10) & 0x1fu;
+    uint32_t m = h & 0x3ffu;
+    uint32_t bits;
+    if (e == 0x1fu) {
+        bits = sign | 0x7f800000u | (m << 13);
+    } else if (e != 0) {
+        bits = sign | ((e + 112u) << 23) | (m << 13);
+    } else if (m == 0) {
+        bits = sign;
+    } else {
+        int shift = 0;
+        while ((m & 0x400u) == 0) { m <<= 1; ++shift; }
+        bits = sign | ((uint32_t)(113 - shift) << 23) | ((m & 0x3ffu) << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+static uint16_t rd16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+/* 6-bit scale/min unpacking of a Q4_K super-block (cpp/src/dequant.cpp:258-266). */
+static void q4k_scale_min(int j, const uint8_t* s, int* sc, int* mn) {
+    if (j < 4) {
+        *sc = s[j] & 63;
+        *mn = s[j + 4] & 63;
+    } else {
+        *sc = (s[j + 4] & 0x0f) | ((s[j - 4] >> 6) << 4);
+        *mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+
+/* Q4_K: 144-byte block = d(f16) @0, dmin(f16) @2, scales[12] @4, qs[128] @16.
+ * Four 64-value groups g: byte qs[32g+l] holds value 64g+l (low nibble, scale pair 2g)
+ * and 64g+32+l (high nibble, pair 2g+1); out = (d*sc)*q - dmin*m
+ * (cpp/src/dequant.cpp:268-301). */
+void vbo_dequantize_row_q4_K(const uint8_t* row, float* out, int64_t n) {
+    int64_t nb = (n + 255) / 256;
+    for (int64_t b = 0; b < nb; ++b) {
+        const uint8_t* blk = row + b * 144;
+        float d = vbo_f16_to_f32(rd16(blk));
+        float dmin = vbo_f16_to_f32(rd16(blk + 2));
+        const uint8_t* sc = blk + 4;
+        const uint8_t* qs = blk + 16;
+        for (int g = 0; g < 4; ++g) {
+            int s0, m0, s1, m1;
+            q4k_scale_min(2 * g, sc, &s0, &m0);
+            q4k_scale_min(2 * g + 1, sc, &s1, &m1);
+            float dl = d * (float)s0, ml = dmin * (float)m0;
+            float dh = d * (float)s1, mh = dmin * (float)m1;
+            for (int l = 0; l < 32; ++l) {
+                int64_t i_lo = b * 256 + 64 * g + l;
+                int64_t i_hi = i_lo + 32;
+                float prod_lo = dl * (float)(qs[32 * g + l] & 0x0f);
+                float prod_hi = dh * (float)(qs[32 * g + l] >> 4);
+                if (i_lo < n) out[i_lo] = prod_lo - ml;
+                if (i_hi < n) out[i_hi] = prod_hi - mh;
+            }
+        }
+    }
+}
+
+/* Q6_K (reference layout, not llama.cpp's): 210-byte block = ql[128] @0, qh[64] @128,
+ * int8 scales[16] @192, d(f16) @208.  Value i: low 4 bits = nibble (i&1) of ql[i>>1],
+ * high 2 bits = field (i&3) of qh[i>>2] (LSB first), q = that - 32,
+ * out = (d*scale[i>>4])*q (cpp/src/dequant.cpp:359-402; the 4-way ql index branch at
+ * :379-394 reduces to i>>1). */
+void vbo_dequantize_row_q6_K(const uint8_t* row, float* out, int64_t n) {
+    int64_t nb = (n + 255) / 256;
+    for (int64_t b = 0; b < nb; ++b) {
+        const uint8_t* blk = row + b * 210;
+        float d = vbo_f16_to_f32(rd16(blk + 208));
+        const uint8_t* ql = blk;
+        const uint8_t* qh = blk + 128;
+        const int8_t* sc = (const int8_t*)(blk + 192);
+        int64_t rem = n - b * 256;
+        if (rem > 256) rem = 256;
+        for (int64_t i = 0; i < rem; ++i) {
+            int lo = (ql[i >> 1] >> (4 * (i & 1))) & 0x0f;
+            int hi = (qh[i >> 2] >> (2 * (i & 3))) & 0x03;
+            int q = (lo | (hi << 4)) - 32;
+            float ds = d * (float)sc[i >> 4];
+            out[b * 256 + i] = ds * (float)q;
+        }
+    }
+}
+
+/* Q8_0 with the GGUF block: fp16 d @0, int8 qs[32] @2, 34-byte stride; out = qs[i]*d.
+ * Follows the reference's CUDA kernel (cpp/src/cuda_kernels.cu:718-735) and Python
+ * loader (vibeblade/loader.py:129-133).  The C++ CPU dequantize_row_q8_0
+ * (cpp/src/dequant.cpp:99-112) reads a 4-byte float scale instead; that variant is
+ * restated below as vbo_dequantize_row_q8_0_f32scale to document the defect. */
+void vbo_dequantize_row_q8_0(const uint8_t* row, float* out, int64_t n) {
+    int64_t nb = (n + 31) / 32;
+    for (int64_t b = 0; b < nb; ++b) {
+        const uint8_t* blk = row + b * 34;
+        float d = vbo_f16_to_f32_ieee(rd16(blk));
+        const int8_t* qs = (const int8_t*)(blk + 2);
+        int64_t rem = n - b * 32;
+        if (rem > 32) rem = 32;
+        for (int64_t i = 0; i < rem; ++i) out[b * 32 + i] = (float)qs[i] * d;
+    }
+}
+
+/* The C++ CPU reading of a Q8_0 block (cpp/src/dequant.cpp:99-112): float32 d from
+ * bytes 0-3, quants from byte 4 on, stride 34 (overlaps the next block by 2 bytes). */
+void vbo_dequantize_row_q8_0_f32scale(const uint8_t* row, float* out, int64_t n) {
+    int64_t nb = (n + 31) / 32;
+    for (int64_t b = 0; b < nb; ++b) {
+        const uint8_t* blk = row + b * 34;
+        float d;
+        memcpy(&d, blk, 4);
+        const int8_t* qs = (const int8_t*)(blk + 4);
+        int64_t rem = n - b * 32;
+        if (rem > 32) rem = 32;
+        for (int64_t i = 0; i < rem; ++i) out[b * 32 + i] = (float)qs[i] * d;
+    }
+}
+
+/* Dispatcher (cpp/src/dequant.cpp:407-425).  Returns 0, or -1 for an unsupported type
+ * where the reference throws "Unsupported dequant type". */
+int vbo_dequantize_row(const void* row, float* out, int64_t n, int32_t type) {
+    switch (type) {
+        case VBO_Q4_K: vbo_dequantize_row_q4_K((const uint8_t*)row, out, n); return 0;
+        case VBO_Q6_K: vbo_dequantize_row_q6_K((const uint8_t*)row, out, n); return 0;
+        case VBO_Q8_0: vbo_dequantize_row_q8_0((const uint8_t*)row, out, n); return 0;
+        default: return -1;
+    }
+}
+
+/* Dequantize `rows` rows of a K x N matrix (stride vbo_row_bytes). */
+int vbo_dequantize_matrix(const void* w, float* out, int64_t rows, int64_t n, int32_t type) {
+    int64_t rb = vbo_row_bytes(type, n);
+    if (rb < 0) return -1;
+    for (int64_t r = 0; r < rows; ++r)
+        if (vbo_dequantize_row((const uint8_t*)w + r * rb, out + r * n, n, type)) return -1;
+    return 0;
+}
+
+/* gemv_dequant (cpp/src/dequant.cpp:739-780): out[n] = sum_k x[k] * deq(W[k])[n],
+ * W = K rows of N values (blocks along N), accumulated in fp32 sequentially in k:
+ * zero out, then per row dequantize into scratch and out[n] += x[k]*scratch[n]. */
+int vbo_gemv_dequant(const float* x, const void* w, float* out, int64_t K, int64_t N,
+                     int32_t type, float* scratch) {
+    int64_t rb = vbo_row_bytes(type, N);
+    if (rb < 0) return -1;
+    for (int64_t n = 0; n < N; ++n) out[n] = 0.0f;
+    for (int64_t k = 0; k < K; ++k) {
+        if (vbo_dequantize_row((const uint8_t*)w + k * rb, scratch, N, type)) return -1;
+        float xk = x[k];
+        for (int64_t n = 0; n < N; ++n) {
+            float p = xk * scratch[n];
+            out[n] = out[n] + p;
+        }
+    }
+    return 0;
+}
+
+/* Batched form: B independent gemv_dequant calls, x [B,K] -> out [B,N], which is how
+ * the reference engine handles several tokens (one call per token,
+ * cpp/src/fast_model.cpp:645-660). */
+int vbo_gemv_dequant_batch(const float* x, const void* w, float* out, int64_t K, int64_t N,
+                           int32_t type, int64_t batch) {
+    float* scratch = (float*)malloc((size_t)N * sizeof(float));
+    if (!scratch) return -2;
+    int rc = 0;
+    for (int64_t b = 0; b < batch && rc == 0; ++b)
+        rc = vbo_gemv_dequant(x + b * K, w, out + b * N, K, N, type, scratch);
+    free(scratch);
+    return rc;
+}
+
+/* Wide-accumulator reference GEMM for checking the bf16 tensor-core path:
+ * C[m,n] = sum_k A[m,k] * deq(W)[k,n] in double, A given as fp32 (the bf16 values
+ * widened).  The reference has no batched GEMM; it loops gemv_dequant per token
+ * (cpp/src/fast_model.cpp:645-660), so this is the exact sum that loop approximates. */
+int vbo_gemm_f64(const float* a, const void* w, double* c, int64_t M, int64_t K, int64_t N,
+                 int32_t type) {
+    int64_t rb = vbo_row_bytes(type, N);
+    if (rb < 0) return -1;
+    float* row = (float*)malloc((size_t)N * sizeof(float));
+    if (!row) return -2;
+    for (int64_t i = 0; i < M * N; ++i) c[i] = 0.0;
+    for (int64_t k = 0; k < K; ++k) {
+        if (vbo_dequantize_row((const uint8_t*)w + k * rb, row, N, type)) { free(row); return -1; }
+        for (int64_t m = 0; m < M; ++m) {
+            double am = (double)a[m * K + k];
+            if (am == 0.0) continue;
+            double* cr = c + m * N;
+            for (int64_t n = 0; n < N; ++n) cr[n] += am * (double)row[n];
+        }
+    }
+    free(row);
+    return 0;
+}

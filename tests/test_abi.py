@@ -1,0 +1,77 @@
+"""The C-ABI library: builds for sm_100a, loads, and exports every function include/*.h
+declares.  Only host-side argument checks run here (no GPU in this container)."""
+from __future__ import annotations
+
+import ctypes as C
+import re
+import subprocess
+
+import pytest
+
+from conftest import ROOT
+
+
+def declared_functions() -> set[str]:
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        for m in re.finditer(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b(vbq_\w+)\s*\(", text, re.M):
+            names.add(m.group(1))
+    return names
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from vibeblade_b200 import _lib
+    return _lib.load()
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert {"vbq_dequantize", "vbq_gemv", "vbq_last_error", "vbq_row_bytes"} <= names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    from vibeblade_b200 import _lib
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    missing = declared_functions() - exported
+    assert not missing, f"declared but not exported: {sorted(missing)}"
+    for name in declared_functions():
+        getattr(lib, name)  # resolvable through the dynamic loader
+
+
+def test_row_bytes(lib):
+    v = C.c_int64()
+    assert lib.vbq_row_bytes(12, 4096, C.byref(v)) == 0 and v.value == 16 * 144
+    assert lib.vbq_row_bytes(14, 4096, C.byref(v)) == 0 and v.value == 16 * 210
+    assert lib.vbq_row_bytes(8, 4096, C.byref(v)) == 0 and v.value == 128 * 34
+    assert lib.vbq_row_bytes(3, 4096, C.byref(v)) == 1
+    assert b"Unsupported dequant type: 3" in lib.vbq_last_error()
+
+
+def test_argument_errors_need_no_gpu(lib):
+    from vibeblade_b200 import _lib
+    # unsupported type: reference message (cpp/src/dequant.cpp:764)
+    assert lib.vbq_gemv(None, None, None, 16, 256, 2, 1, None) == _lib.VBQ_ERR_TYPE
+    assert lib.vbq_last_error() == b"gemv_dequant: unsupported type 2"
+    assert lib.vbq_gemv(None, None, None, 16, 256, 12, 17, None) == _lib.VBQ_ERR_SHAPE
+    assert lib.vbq_gemv(None, None, None, 16, 300, 12, 1, None) == _lib.VBQ_ERR_SHAPE
+    assert lib.vbq_gemv(None, None, None, 16, 256, 12, 1, None) == _lib.VBQ_ERR_NULL
+    assert lib.vbq_gemv(16, 16, 8, 16, 256, 12, 1, None) == _lib.VBQ_ERR_ALIGN
+    assert lib.vbq_dequantize(None, None, 2, 100, 12, 0, None) == _lib.VBQ_ERR_SHAPE
+    assert lib.vbq_dequantize(None, None, 1, 256, 13, 0, None) == _lib.VBQ_ERR_TYPE
+    assert lib.vbq_dequantize(None, None, 1, 256, 12, 5, None) == _lib.VBQ_ERR_SHAPE
+    assert lib.vbq_dequantize(0, 0, 0, 256, 12, 0, None) == _lib.VBQ_OK  # empty: no work
+
+
+def test_python_face_rejects_host_tensors():
+    import torch
+    import vibeblade_b200 as vb
+    x = torch.zeros(4096)
+    w = torch.zeros(4096 * 144 * 16, dtype=torch.uint8)
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
+        vb.gemv_dequant(x, w, None, 4096, 4096, "Q4_K")
+    with pytest.raises(RuntimeError, match="Unsupported dequant type"):
+        vb.gemv_dequant(x, w, None, 4096, 4096, 13)

@@ -1,0 +1,117 @@
+"""Device fused dequant-GEMV vs the reference's gemv_dequant.
+
+Tolerance: max-norm relative error <= 1e-3 (fp32 outputs), the bound the north star states.
+Small cases compare against the golden vectors and the oracle (the reference's own
+sequential fp32 accumulation); BASELINE-size cases compare against an fp64 product of
+the bit-exact device dequantization and check size-independent properties (linearity
+in x, batch-row independence, determinism)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import vibeblade_b200 as vb
+from conftest import load_golden, max_rel
+from vibeblade_b200 import formats as F
+from vibeblade_b200.quantize import quantize, synthetic_weights
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+TYPES = [F.GGML_TYPE_Q4_K, F.GGML_TYPE_Q6_K, F.GGML_TYPE_Q8_0]
+
+
+@pytest.mark.parametrize("name", ["q4_k", "q6_k", "q8_0"])
+def test_gemv_golden(cuda, name):
+    g = load_golden(name)
+    K, N, t = int(g["K"]), int(g["N"]), int(g["type"])
+    fin = np.isfinite(g["gemv_f64"]).all(axis=0)
+    x = torch.from_numpy(g["x"]).to(cuda)
+    w = torch.from_numpy(g["w"]).to(cuda)
+    y = vb.gemv_dequant(x, w, None, K, N, t).cpu().numpy()
+    ref = g["gemv"] if "gemv" in g else g["gemv_f64"]
+    assert fin.all()
+    assert max_rel(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("qtype", TYPES)
+@pytest.mark.parametrize("batch", [1, 2, 3, 4, 5, 8, 11, 16])
+def test_gemv_vs_oracle_small(cuda, oracle, qtype, batch):
+    K, N = 300, 1024
+    rng = np.random.default_rng(batch * 31 + qtype)
+    w = quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), qtype).numpy()
+    x = rng.normal(0, 1, (batch, K)).astype(np.float32)
+    ref = oracle.gemv_dequant(x, w, K, N, qtype)
+    y = vb.gemv_dequant(torch.from_numpy(x).to(cuda), torch.from_numpy(w).to(cuda), None, K, N,
+                        qtype).cpu().numpy()
+    assert y.shape == (batch, N)
+    assert max_rel(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("qtype", TYPES)
+@pytest.mark.parametrize("K", [1, 63, 64, 65, 1000])
+def test_gemv_ragged_k(cuda, oracle, qtype, K):
+    N = 512
+    rng = np.random.default_rng(K + qtype)
+    w = quantize(rng.normal(0, 0.5, (K, N)).astype(np.float32), qtype).numpy()
+    x = rng.normal(0, 1, (1, K)).astype(np.float32)
+    ref = oracle.gemv_dequant(x, w, K, N, qtype)
+    y = vb.gemv_dequant(torch.from_numpy(x).to(cuda), torch.from_numpy(w).to(cuda), None, K, N,
+                        qtype).cpu().numpy()
+    assert max_rel(y, ref) <= TOL
+
+
+def test_gemv_1d_x_and_out_buffer(cuda, oracle):
+    K, N, t = 256, 768, F.GGML_TYPE_Q4_K
+    rng = np.random.default_rng(3)
+    w = quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), t).numpy()
+    x = rng.normal(0, 1, K).astype(np.float32)
+    out = torch.full((N,), float("nan"), device=cuda)
+    res = vb.gemv_dequant(torch.from_numpy(x).to(cuda), torch.from_numpy(w).to(cuda), out, K, N, t,
+                          scratch=None)
+    assert res.data_ptr() == out.data_ptr()
+    assert max_rel(out.cpu().numpy(), oracle.gemv_dequant(x, w, K, N, t)[0]) <= TOL
+
+
+def test_gemv_zero_k_gives_zeros(cuda):
+    w = torch.zeros(0, dtype=torch.uint8, device=cuda)
+    x = torch.zeros(0, device=cuda)
+    y = vb.gemv_dequant(x, w, torch.full((256,), 7.0, device=cuda), 0, 256, "Q4_K")
+    assert torch.count_nonzero(y) == 0
+
+
+# (K, N) of the BASELINE decode layer (config 2) plus the 70B-shape Q8_0 rows (config 5)
+FULL = [(F.GGML_TYPE_Q4_K, 4096, 14336), (F.GGML_TYPE_Q4_K, 14336, 4096),
+        (F.GGML_TYPE_Q4_K, 4096, 6144), (F.GGML_TYPE_Q6_K, 4096, 14336),
+        (F.GGML_TYPE_Q8_0, 8192, 10240), (F.GGML_TYPE_Q8_0, 28672, 8192)]
+
+
+@pytest.mark.parametrize("qtype,K,N", FULL)
+@pytest.mark.parametrize("batch", [1, 4, 16])
+def test_gemv_full_size_vs_fp64(cuda, qtype, K, N, batch):
+    w = synthetic_weights(K, N, qtype, seed=0, device=cuda)
+    g = torch.Generator(device=cuda).manual_seed(1)
+    x = torch.randn(batch, K, generator=g, device=cuda)
+    y = vb.gemv_dequant(x, w, None, K, N, qtype)
+    deq = vb.dequantize(w, K, N, qtype)  # bit-exact with the reference (tested above)
+    ref = x.double() @ deq.double()
+    err = ((y.double() - ref).abs().max() / ref.abs().max()).item()
+    assert err <= TOL
+    # determinism: fixed reduction order -> bitwise repeatable
+    y2 = vb.gemv_dequant(x, w, None, K, N, qtype)
+    assert torch.equal(y, y2)
+
+
+@pytest.mark.parametrize("qtype", TYPES)
+def test_gemv_linearity_and_row_independence(cuda, qtype):
+    K, N = 4096, 4096
+    w = synthetic_weights(K, N, qtype, seed=2, device=cuda)
+    g = torch.Generator(device=cuda).manual_seed(4)
+    x = torch.randn(4, K, generator=g, device=cuda)
+    y = vb.gemv_dequant(x, w, None, K, N, qtype)
+    y_sum = vb.gemv_dequant((x[0] + x[1]).contiguous(), w, None, K, N, qtype)
+    assert ((y_sum - (y[0] + y[1])).abs().max() / y_sum.abs().max()).item() <= TOL
+    # each batch row is an independent GEMV: batch 4 row 2 == batch 1 on that row
+    y_one = vb.gemv_dequant(x[2].contiguous(), w, None, K, N, qtype)
+    assert ((y_one - y[2]).abs().max() / y_one.abs().max()).item() <= 1e-5

@@ -1,0 +1,17 @@
+"""vibeblade_b200 -- B200-native (sm_100a) GGUF k-quant dequantize-and-multiply.
+
+Drop-in device implementation of VibeBlade's quantized matmul path
+(kevin046/VibeBlade cpp/src/dequant.cpp, cpp/include/dequant.h): Q4_K, Q6_K and Q8_0
+weights in the reference's K x N block layout, dequantized and multiplied by
+hand-written CUDA kernels in ``libvbq.so`` behind the C ABI in ``include/vbq.h``.
+"""
+from . import formats
+from .formats import GGML_TYPE_Q4_K, GGML_TYPE_Q6_K, GGML_TYPE_Q8_0, row_bytes, tensor_nbytes
+from .dequant import dequantize, dequantize_row, gemv_dequant, gemv_dequant_mt
+from ._lib import VbqError
+
+__all__ = [
+    "formats", "GGML_TYPE_Q4_K", "GGML_TYPE_Q6_K", "GGML_TYPE_Q8_0", "row_bytes",
+    "tensor_nbytes", "dequantize", "dequantize_row", "gemv_dequant", "gemv_dequant_mt",
+    "VbqError",
+]

@@ -1,0 +1,100 @@
+// vbq_common.cuh -- shared device helpers for the sm_100a k-quant kernels.
+//
+// Block formats (kevin046/VibeBlade cpp/include/ggml_types.h:109-141):
+//   Q4_K 144 B: fp16 d @0, fp16 dmin @2, 12 B packed 6-bit scales/mins @4, 128 B nibbles @16
+//   Q6_K 210 B: ql[128] @0, qh[64] @128, int8 scales[16] @192, fp16 d @208
+//   Q8_0  34 B: fp16 d @0, int8 qs[32] @2 (GGUF block)
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace vbq {
+
+constexpr int kQ8_0 = 8;
+constexpr int kQ4_K = 12;
+constexpr int kQ6_K = 14;
+
+template <int QT> struct Fmt;
+template <> struct Fmt<kQ4_K> { static constexpr int kValues = 256, kBytes = 144; };
+template <> struct Fmt<kQ6_K> { static constexpr int kValues = 256, kBytes = 210; };
+template <> struct Fmt<kQ8_0> { static constexpr int kValues = 32, kBytes = 34; };
+
+// Bytes holding one 256-value column tile of a row: one Q4_K / Q6_K block, or eight
+// Q8_0 blocks.
+template <int QT> struct Tile {
+  static constexpr int kBytes = Fmt<QT>::kBytes * (256 / Fmt<QT>::kValues);
+};
+
+// fp16 -> fp32 with the reference's rounding (cpp/src/fp16_compat.cpp:13-35): exact
+// for normals, zeros, inf; fp16 subnormals come out at twice their IEEE value, which
+// the reference's k-quant dequantizers inherit.  Used for Q4_K d/dmin and Q6_K d.
+__device__ __forceinline__ float f16_ref(uint32_t h) {
+  float f = __half2float(__ushort_as_half((unsigned short)(h & 0xffffu)));
+  return ((h & 0x7c00u) == 0u) ? f * 2.0f : f;
+}
+
+// Exact IEEE fp16 -> fp32 (the Q8_0 scale; cpp/src/cuda_kernels.cu:731).
+__device__ __forceinline__ float f16_ieee(uint32_t h) {
+  return __half2float(__ushort_as_half((unsigned short)(h & 0xffffu)));
+}
+
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xffu; }
+
+// Q4_K sub-block scale and min (get_scale_min_k4, cpp/src/dequant.cpp:258-266).
+// s0/s1/s2 are scale bytes 0-3, 4-7, 8-11 as little-endian words.
+__device__ __forceinline__ void q4k_scale_min(int j, uint32_t s0, uint32_t s1, uint32_t s2,
+                                              int& sc, int& mn) {
+  if (j < 4) {
+    sc = (int)(byte_of(s0, j) & 63u);
+    mn = (int)(byte_of(s1, j) & 63u);
+  } else {
+    const int i = j - 4;
+    sc = (int)((byte_of(s2, i) & 0xfu) | ((byte_of(s0, i) >> 6) << 4));
+    mn = (int)((byte_of(s2, i) >> 4) | ((byte_of(s1, i) >> 6) << 4));
+  }
+}
+
+// Read 4 bytes at a 2-byte-aligned shared/global address as one little-endian word.
+// Only aligned words that hold at least one of the 4 bytes are touched, so the read
+// never leaves the pages the data lives on.
+__device__ __forceinline__ uint32_t ld_u32_a2(const uint8_t* p) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uint32_t* q = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+  const uint32_t sh = (uint32_t)(a & 3u) * 8u;
+  const uint32_t lo = q[0];
+  return sh ? __funnelshift_r(lo, q[1], sh) : lo;
+}
+
+__device__ __forceinline__ uint32_t ld_u16(const uint8_t* p) {
+  return (uint32_t)*reinterpret_cast<const uint16_t*>(p);
+}
+
+// Packed fp32x2 FMA (sm_100a): (a.x*b.x+c.x, a.y*b.y+c.y) in one instruction.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(r)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)),
+        "l"(*reinterpret_cast<uint64_t*>(&c)));
+  return *reinterpret_cast<float2*>(&r);
+}
+
+// cp.async (Ampere-style asynchronous global->shared copies), used by the GEMV
+// pipeline: no mbarrier, so no wait on the device can outlive its group.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+}  // namespace vbq

@@ -1,0 +1,154 @@
+// vbq_dequant.cu -- k-quant block dequantization to fp32 / bf16 (sm_100a).
+//
+// Device form of the reference's dequantize_row_q4_K / _q6_K (cpp/src/dequant.cpp:268-301,
+// :359-402) and of the GGUF Q8_0 block (cpp/src/cuda_kernels.cu:718-735).  Values are
+// bit-identical to the reference: every product and difference the reference rounds
+// separately is rounded separately here (__fmul_rn / __fsub_rn stop the compiler from
+// contracting them into an FMA).
+//
+// Work unit: 256 consecutive values of one row (one Q4_K/Q6_K block, eight Q8_0 blocks),
+// one warp per unit, 8 values per lane, so each warp writes 1 KB (fp32) or 512 B (bf16)
+// of contiguous output.  The kernel is HBM-bound on its writes.
+#include "vbq_common.cuh"
+#include "vbq_internal.h"
+
+namespace vbq {
+
+template <int QT>
+__device__ __forceinline__ void decode8(const uint8_t* __restrict__ tile, int lane, float v[8]);
+
+// Q4_K: lane covers values 8*lane..8*lane+7 -> sub-block s = lane/4, nibble half s&1,
+// qs bytes 32*(s/2) + 8*(lane%4) .. +7.
+template <>
+__device__ __forceinline__ void decode8<kQ4_K>(const uint8_t* __restrict__ blk, int lane,
+                                               float v[8]) {
+  const float d = f16_ref(ld_u16(blk));
+  const float dmin = f16_ref(ld_u16(blk + 2));
+  const uint32_t s0 = ld_u32_a2(blk + 4), s1 = ld_u32_a2(blk + 8), s2 = ld_u32_a2(blk + 12);
+  const int s = lane >> 2;
+  int sc, mn;
+  q4k_scale_min(s, s0, s1, s2, sc, mn);
+  const float dl = __fmul_rn(d, (float)sc);
+  const float ml = __fmul_rn(dmin, (float)mn);
+  const uint8_t* q = blk + 16 + 32 * (s >> 1) + 8 * (lane & 3);
+  const uint32_t w0 = ld_u32_a2(q), w1 = ld_u32_a2(q + 4);
+  const int hs = (s & 1) * 4;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t w = i < 4 ? w0 : w1;
+    const uint32_t nib = (w >> (8 * (i & 3) + hs)) & 0xfu;
+    v[i] = __fsub_rn(__fmul_rn(dl, (float)nib), ml);
+  }
+}
+
+// Q6_K (reference layout): value i -> ql nibble i&1 of byte i>>1, qh field i&3 of byte
+// i>>2, int8 scale i>>4, out = (d*scale)*(q-32).  Lane: ql bytes 4*lane..+3, qh bytes
+// 2*lane..+1, scale 192 + lane/2.
+template <>
+__device__ __forceinline__ void decode8<kQ6_K>(const uint8_t* __restrict__ blk, int lane,
+                                               float v[8]) {
+  const float d = f16_ref(ld_u16(blk + 208));
+  const int sc = (int)(int8_t)blk[192 + (lane >> 1)];
+  const float ds = __fmul_rn(d, (float)sc);
+  const uint32_t ql = ld_u32_a2(blk + 4 * lane);
+  const uint32_t qh = ld_u16(blk + 128 + 2 * lane);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int lo = (int)((ql >> (4 * i)) & 0xfu);
+    const int hi = (int)((qh >> (2 * i)) & 0x3u);
+    v[i] = __fmul_rn(ds, (float)((lo | (hi << 4)) - 32));
+  }
+}
+
+// Q8_0 (GGUF block, fp16 d): the 256-value unit spans blocks lane/4, values 8*(lane%4)..
+template <>
+__device__ __forceinline__ void decode8<kQ8_0>(const uint8_t* __restrict__ unit, int lane,
+                                               float v[8]) {
+  const uint8_t* blk = unit + 34 * (lane >> 2);
+  const float d = f16_ieee(ld_u16(blk));
+  const uint8_t* q = blk + 2 + 8 * (lane & 3);
+  const uint32_t w0 = ld_u32_a2(q), w1 = ld_u32_a2(q + 4);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t w = i < 4 ? w0 : w1;
+    const int qv = (int)(int8_t)(uint8_t)(w >> (8 * (i & 3)));
+    v[i] = __fmul_rn((float)qv, d);
+  }
+}
+
+template <int QT, typename OutT>
+__global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict__ w,
+                                                      OutT* __restrict__ out, int64_t rows,
+                                                      int64_t n, int64_t row_bytes,
+                                                      bool vec_ok) {
+  const int lane = threadIdx.x & 31;
+  const int64_t units_per_row = (n + 255) / 256;
+  const int64_t total = rows * units_per_row;
+  const int64_t warp0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  constexpr int kUnitBytes = Tile<QT>::kBytes;
+  for (int64_t u = warp0; u < total; u += nwarps) {
+    const int64_t r = u / units_per_row;
+    const int64_t j = u - r * units_per_row;
+    const int64_t v0 = j * 256 + 8 * lane;  // first value of this lane within the row
+    if (v0 >= n) continue;                  // ragged tail of a single row
+    const uint8_t* unit = w + r * row_bytes + j * kUnitBytes;
+    float v[8];
+    decode8<QT>(unit, lane, v);
+    OutT* o = out + r * n + v0;
+    if (vec_ok && v0 + 8 <= n) {
+      if constexpr (sizeof(OutT) == 4) {
+        float4* o4 = reinterpret_cast<float4*>(o);
+        o4[0] = make_float4(v[0], v[1], v[2], v[3]);
+        o4[1] = make_float4(v[4], v[5], v[6], v[7]);
+      } else {
+        __nv_bfloat162 p[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) p[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        *reinterpret_cast<uint4*>(o) = *reinterpret_cast<uint4*>(p);
+      }
+    } else {
+      const int lim = (int)((n - v0) < 8 ? (n - v0) : 8);
+      for (int i = 0; i < lim; ++i) {
+        if constexpr (sizeof(OutT) == 4) o[i] = v[i];
+        else o[i] = __float2bfloat16_rn(v[i]);
+      }
+    }
+  }
+}
+
+template <int QT, typename OutT>
+static cudaError_t launch_dequant_t(const void* w, void* out, int64_t rows, int64_t n,
+                                    int64_t row_bytes, cudaStream_t st) {
+  const int64_t units = rows * ((n + 255) / 256);
+  const int warps_per_cta = 8;
+  int64_t ctas = (units + warps_per_cta - 1) / warps_per_cta;
+  const int64_t cap = 148LL * 16;  // grid-stride beyond 16 CTAs per SM
+  if (ctas > cap) ctas = cap;
+  if (ctas < 1) ctas = 1;
+  const bool vec_ok = ((reinterpret_cast<uintptr_t>(out) & 15u) == 0) &&
+                      (n % (sizeof(OutT) == 4 ? 4 : 8) == 0);
+  dequant_kernel<QT, OutT><<<(unsigned)ctas, 256, 0, st>>>(
+      static_cast<const uint8_t*>(w), static_cast<OutT*>(out), rows, n, row_bytes, vec_ok);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dequant(int qtype, const void* w, void* out, int64_t rows, int64_t n,
+                           int64_t row_bytes, int out_dtype, cudaStream_t st) {
+  const bool bf = out_dtype == 1;
+  switch (qtype) {
+    case kQ4_K:
+      return bf ? launch_dequant_t<kQ4_K, __nv_bfloat16>(w, out, rows, n, row_bytes, st)
+                : launch_dequant_t<kQ4_K, float>(w, out, rows, n, row_bytes, st);
+    case kQ6_K:
+      return bf ? launch_dequant_t<kQ6_K, __nv_bfloat16>(w, out, rows, n, row_bytes, st)
+                : launch_dequant_t<kQ6_K, float>(w, out, rows, n, row_bytes, st);
+    case kQ8_0:
+      return bf ? launch_dequant_t<kQ8_0, __nv_bfloat16>(w, out, rows, n, row_bytes, st)
+                : launch_dequant_t<kQ8_0, float>(w, out, rows, n, row_bytes, st);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace vbq

@@ -1,0 +1,114 @@
+"""Python face of the device k-quant path, mirroring the reference's operator API.
+
+Names, argument order and error text follow ``cpp/include/dequant.h:11-48``
+(``dequantize_row``, ``gemv_dequant``, ``gemv_dequant_mt``) with torch CUDA tensors in
+place of raw pointers, so call sites such as ``forward_layer``'s
+``gemv_dequant(x, W, out, K, N, type, scratch)`` (cpp/src/fast_model.cpp:655-657) swap over
+unchanged.  All work runs in libvbq.so (sm_100a) on the current torch stream; there is no
+CPU fallback.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from . import formats as F
+
+
+def _stream_ptr(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _require_cuda(name: str, *ts: torch.Tensor) -> None:
+    for t in ts:
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            raise RuntimeError(f"{name}: tensors must be CUDA tensors (the k-quant path runs on "
+                               "the GPU only)")
+        if not t.is_contiguous():
+            raise RuntimeError(f"{name}: tensors must be contiguous")
+
+
+def _weights_u8(w: torch.Tensor) -> torch.Tensor:
+    return w if w.dtype == torch.uint8 else w.view(torch.uint8)
+
+
+def row_bytes(qtype, n: int) -> int:
+    """Bytes per row of a K x N matrix (cpp/src/dequant.cpp:749-763)."""
+    return F.row_bytes(qtype, n)
+
+
+def dequantize(weights: torch.Tensor, K: int, N: int, wtype, dtype=torch.float32,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """Dequantize a K x N quantized matrix to fp32 (bit-exact with the reference's
+    dequantize_row, row by row) or bf16 (that value rounded to nearest-even)."""
+    t = F.parse_type(wtype)
+    _require_cuda("dequantize", weights)
+    if dtype not in (torch.float32, torch.bfloat16):
+        raise RuntimeError("dequantize: dtype must be torch.float32 or torch.bfloat16")
+    w = _weights_u8(weights)
+    need = F.row_bytes(t, N) * K if K > 1 else F.tensor_nbytes(t, N)
+    if w.numel() < need:
+        raise RuntimeError(f"dequantize: weights hold {w.numel()} bytes, need {need}")
+    if out is None:
+        out = torch.empty((K, N), dtype=dtype, device=w.device)
+    else:
+        _require_cuda("dequantize", out)
+        if out.dtype != dtype or out.numel() < K * N:
+            raise RuntimeError("dequantize: out has the wrong dtype or size")
+    lib = _lib.load()
+    od = _lib.DTYPE_F32 if dtype == torch.float32 else _lib.DTYPE_BF16
+    _lib.check(lib.vbq_dequantize(w.data_ptr(), out.data_ptr(), K, N, t, od, _stream_ptr(w)), lib)
+    return out
+
+
+def dequantize_row(row: torch.Tensor, out: torch.Tensor | None, n_values: int, type) -> torch.Tensor:
+    """``void dequantize_row(const void* row, float* out, int64_t n, ggml_type)``
+    (cpp/include/dequant.h:11): n_values may be ragged; returns ``out`` (allocated when
+    None) holding n_values fp32 values."""
+    res = dequantize(row, 1, n_values, type, torch.float32,
+                     None if out is None else out.view(1, -1))
+    return res.view(-1)[:n_values]
+
+
+def gemv_dequant(x: torch.Tensor, weights: torch.Tensor, out: torch.Tensor | None, K: int,
+                 N: int, wtype, scratch: torch.Tensor | None = None) -> torch.Tensor:
+    """``gemv_dequant(x, W, out, K, N, wtype, scratch)`` (cpp/include/dequant.h:27-35):
+    out[n] = sum_k x[k] * deq(W)[k, n].
+
+    ``x`` may also be a batch [B, K] with B <= 16 (the reference engine makes B calls,
+    cpp/src/fast_model.cpp:645-660); ``out`` is then [B, N].  ``scratch`` is accepted
+    for signature parity and unused: the device kernel needs no workspace."""
+    t = F.parse_type(wtype)
+    _require_cuda("gemv_dequant", x, weights)
+    if x.dtype != torch.float32:
+        raise RuntimeError("gemv_dequant: x must be float32")
+    if K > 0:
+        if x.numel() % K != 0:
+            raise RuntimeError(f"gemv_dequant: x has {x.numel()} values, not a multiple of K={K}")
+        batch = x.numel() // K
+    else:
+        batch = x.shape[0] if x.dim() > 1 else 1
+    if not 1 <= batch <= 16:
+        raise RuntimeError(f"gemv_dequant: batch must be in 1..16, got {batch}")
+    w = _weights_u8(weights)
+    need = F.row_bytes(t, N) * K
+    if w.numel() < need:
+        raise RuntimeError(f"gemv_dequant: weights hold {w.numel()} bytes, need {need}")
+    if out is None:
+        out = torch.empty((batch, N) if x.dim() > 1 else (N,), dtype=torch.float32, device=x.device)
+    else:
+        _require_cuda("gemv_dequant", out)
+        if out.dtype != torch.float32 or out.numel() != batch * N:
+            raise RuntimeError("gemv_dequant: out must be float32 with batch*N values")
+    lib = _lib.load()
+    _lib.check(lib.vbq_gemv(x.data_ptr(), w.data_ptr(), out.data_ptr(), K, N, t, batch,
+                            _stream_ptr(x)), lib)
+    return out
+
+
+def gemv_dequant_mt(x: torch.Tensor, weights: torch.Tensor, out: torch.Tensor | None, K: int,
+                    N: int, wtype, n_threads: int = 0,
+                    scratch: torch.Tensor | None = None) -> torch.Tensor:
+    """``gemv_dequant_mt`` (cpp/include/dequant.h:39-48).  The reference ignores
+    n_threads; here the whole GPU runs the call, so it is ignored as well."""
+    return gemv_dequant(x, weights, out, K, N, wtype, scratch)
