@@ -51,7 +51,7 @@ def peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks and throttle reasons sampled every 20 ms during the timed region."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -65,7 +65,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                       "--format=csv,noheader,nounits", "-lms", "20"],
                                       stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
@@ -208,10 +208,14 @@ def run_gpu(args) -> None:
     ys = [torch.empty(B, N, device=dev) for _, _, N in LAYER_8B]
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
+    need = max(vb.gemv_scratch_bytes(K, N, QTYPE, B) for _, K, N in LAYER_8B)
+    scratch = torch.zeros(max(need, 16), dtype=torch.uint8, device=dev)
+    sptr, sbytes = scratch.data_ptr(), scratch.numel()
 
     def step(s: int):
         for (K, N, w), y in zip(layers[s % n_copies], ys):
-            rc = lib.vbq_gemv(xs[K].data_ptr(), w.data_ptr(), y.data_ptr(), K, N, QTYPE, B, sp)
+            rc = lib.vbq_gemv(xs[K].data_ptr(), w.data_ptr(), y.data_ptr(), K, N, QTYPE, B,
+                              sptr, sbytes, sp)
             if rc:
                 _lib.check(rc, lib)
 
@@ -240,21 +244,34 @@ def run_gpu(args) -> None:
     total_bytes = layer_bytes(B) * args.steps * world
     value = total_bytes / (ms_total * 1e-3) / 1e9
 
-    # ---- per-launch kernel time (roofline of the GEMV kernel), events per launch ----
-    evs = []
-    for s in range(args.steps):
-        for (K, N, w), y in zip(layers[s % n_copies], ys):
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            lib.vbq_gemv(xs[K].data_ptr(), w.data_ptr(), y.data_ptr(), K, N, QTYPE, B, sp)
-            b.record(stream)
-            evs.append((a, b, K, N))
+    # ---- roofline of the GEMV kernel ----
+    # Every launch in the timed region is the GEMV kernel, queued back to back with
+    # programmatic dependent launch, so the average launch duration is the timed region
+    # divided by the launches and `achieved` equals `value`.  (Per-launch events would
+    # serialise the launches and hide the overlap.)  The dominant shape, gate/up
+    # 4096x14336 (48% of kernel time in the ncu launch list), is also timed on its own.
+    achieved = value / world
+    big_mats = [w for layer in layers for (K, N, w) in layer if (K, N) == (4096, 14336)]
+    big_y = torch.empty(B, 14336, device=dev)
+    nbig = max(1, args.steps)
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(3):
+        lib.vbq_gemv(xs[4096].data_ptr(), big_mats[i % len(big_mats)].data_ptr(), big_y.data_ptr(),
+                     4096, 14336, QTYPE, B, sptr, sbytes, sp)
+    e2.record(stream)
+    for i in range(nbig):
+        lib.vbq_gemv(xs[4096].data_ptr(), big_mats[i % len(big_mats)].data_ptr(), big_y.data_ptr(),
+                     4096, 14336, QTYPE, B, sptr, sbytes, sp)
+    e3.record(stream)
     torch.cuda.synchronize()
-    kern_ms = sum(a.elapsed_time(b) for a, b, _, _ in evs)
-    alg = sum(int(K * N * BPW) + B * K * 4 + B * N * 4 for _, _, K, N in evs)
-    achieved = alg / (kern_ms * 1e-3) / 1e9
-    big = [(a.elapsed_time(b), K, N) for a, b, K, N in evs if (K, N) == (4096, 14336)]
-    big_gbs = (int(4096 * 14336 * BPW) + B * (4096 + 14336) * 4) / (statistics.mean(t for t, _, _ in big) * 1e-3) / 1e9
+    big_bytes = int(4096 * 14336 * BPW) + B * (4096 + 14336) * 4
+    big_gbs = big_bytes * nbig / (e2.elapsed_time(e3) * 1e-3) / 1e9
+    traffic = None
+    tp = ROOT / "profiles" / "gemv_q4k_4096x14336_b1.txt"
+    if tp.exists():  # dram bytes per launch from the committed ncu capture of this shape
+        for line in tp.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                traffic = int(line.split(":")[1].strip())
 
     # ---- end to end through the public API with host buffers ----
     xh = {K: v.cpu().pin_memory() for K, v in xs.items()}
@@ -302,9 +319,11 @@ def run_gpu(args) -> None:
                        "parallelism": f"{world} independent GPUs, own layers each (no collective)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
                          "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
-                         "traffic": None, "peak_src": pk["src"],
-                         "kernel": "vbq::gemv_kernel<Q4_K,1,32>",
-                         "gemv_4096x14336_gbs": round(big_gbs, 1)},
+                         "traffic": traffic, "traffic_launch": "gate/up 4096x14336 (ncu)",
+                         "peak_src": pk["src"] + " (MEASURED_PEAKS.json hbm_gbs)",
+                         "kernel": f"vbq::gemv_kernel<Q4_K,B={B}>",
+                         "gemv_4096x14336_gbs": round(big_gbs, 1),
+                         "gemv_4096x14336_frac": round(big_gbs / pk["hbm_gbs"], 4)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "vibeblade_b200.gemv_dequant"},
             "gpu_launches": args.steps * len(LAYER_8B),
@@ -324,7 +343,7 @@ def run_gpu(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--copies", type=int, default=6)

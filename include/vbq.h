@@ -73,6 +73,13 @@ int vbq_dequantize(const void* w, void* out, int64_t rows, int64_t n, int32_t ty
                    int32_t out_dtype, void* stream);
 
 /*
+ * Scratch bytes vbq_gemv needs for this shape on the current device (0 when the call
+ * needs none).  The reference's gemv_dequant also takes caller-owned scratch
+ * (cpp/include/dequant.h:34); here it holds the split-K partial sums.
+ */
+int vbq_gemv_scratch_bytes(int64_t K, int64_t N, int32_t type, int32_t batch, size_t* bytes);
+
+/*
  * Batched fused dequant-GEMV, the device form of
  * `void gemv_dequant(const float* x, const void* W, float* out, int64_t K, int64_t N,
  *                    ggml_type, float* scratch)` (cpp/include/dequant.h:27-35) and of
@@ -80,13 +87,25 @@ int vbq_dequantize(const void* w, void* out, int64_t rows, int64_t n, int32_t ty
  * (cpp/include/cuda_kernels.h:191-199):
  *     y[b, n] = sum_k x[b, k] * deq(W)[k, n],  b < batch (1..16).
  * x is fp32 [batch, K], y fp32 [batch, N], both row-major.  N must be a multiple of
- * the block size (256 for Q4_K/Q6_K, 32 for Q8_0); W, x and y must be 16-byte aligned.
- * The reference's scratch argument has no use here: the split over K reduces
- * through distributed shared memory inside a thread-block cluster, so the call needs
- * no workspace.  Results are deterministic (fixed reduction order).
+ * the block size (256 for Q4_K/Q6_K, 32 for Q8_0; this build needs 256 for all);
+ * W and y must be 16-byte aligned, x 4-byte aligned.
+ * scratch: caller-owned device memory of at least vbq_gemv_scratch_bytes(); it must be
+ * zero-filled before its first use, every call leaves it zero-filled again, and two
+ * calls that may run at the same time must not share it.  NULL is allowed when the
+ * size is 0.  Results are deterministic (the split-K partials are added in a fixed
+ * order).
  */
 int vbq_gemv(const float* x, const void* w, float* y, int64_t K, int64_t N, int32_t type,
-             int32_t batch, void* stream);
+             int32_t batch, void* scratch, size_t scratch_bytes, void* stream);
+
+/*
+ * Device-side status of the library's kernels on the current device: bit 0 set means a
+ * bounded wait inside a kernel gave up (VBQ_ERR_TIMEOUT is returned then), which leaves
+ * that call's outputs undefined and its scratch in need of re-zeroing.  Reads
+ * synchronously; `clear` resets the bits.  The reference has no counterpart (its CUDA
+ * path throws on the host, cpp/src/cuda_kernels.cu:24-40).
+ */
+int vbq_device_status(int32_t* status, int32_t clear);
 
 #ifdef __cplusplus
 }

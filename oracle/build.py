@@ -23,7 +23,7 @@ ORACLE_SRC = HERE / "vbq_oracle.c"
 ORACLE_SO = HERE / "liboracle.so"
 REF_DIR = HERE / "_ref"
 REF_SO = REF_DIR / "libvbref.so"
-DEFAULT_REF = "/root/reference"  # mounted read-only in the build container only
+DEFAULT_REF = "/root/reference"  # the read-only mount of the build container
 
 
 def _ref_root() -> Path:

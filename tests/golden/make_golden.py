@@ -1,6 +1,6 @@
 """Generate the golden vectors in tests/golden/*.npz from the reference itself.
 
-Run in a checkout that has the reference mounted (``$VB_REF``, default /root/reference):
+Run where the reference checkout is mounted (``$VB_REF`` names it; build.py holds the default):
 
     python tests/golden/make_golden.py
 

@@ -54,16 +54,28 @@ def test_row_bytes(lib):
 def test_argument_errors_need_no_gpu(lib):
     from vibeblade_b200 import _lib
     # unsupported type: reference message (cpp/src/dequant.cpp:764)
-    assert lib.vbq_gemv(None, None, None, 16, 256, 2, 1, None) == _lib.VBQ_ERR_TYPE
+    assert lib.vbq_gemv(None, None, None, 16, 256, 2, 1, None, 0, None) == _lib.VBQ_ERR_TYPE
     assert lib.vbq_last_error() == b"gemv_dequant: unsupported type 2"
-    assert lib.vbq_gemv(None, None, None, 16, 256, 12, 17, None) == _lib.VBQ_ERR_SHAPE
-    assert lib.vbq_gemv(None, None, None, 16, 300, 12, 1, None) == _lib.VBQ_ERR_SHAPE
-    assert lib.vbq_gemv(None, None, None, 16, 256, 12, 1, None) == _lib.VBQ_ERR_NULL
-    assert lib.vbq_gemv(16, 16, 8, 16, 256, 12, 1, None) == _lib.VBQ_ERR_ALIGN
+    assert lib.vbq_gemv(None, None, None, 16, 256, 12, 17, None, 0, None) == _lib.VBQ_ERR_SHAPE
+    assert lib.vbq_gemv(None, None, None, 16, 300, 12, 1, None, 0, None) == _lib.VBQ_ERR_SHAPE
+    assert lib.vbq_gemv(None, None, None, 16, 256, 12, 1, None, 0, None) == _lib.VBQ_ERR_NULL
+    assert lib.vbq_gemv(16, 16, 8, 16, 256, 12, 1, None, 0, None) == _lib.VBQ_ERR_ALIGN
     assert lib.vbq_dequantize(None, None, 2, 100, 12, 0, None) == _lib.VBQ_ERR_SHAPE
     assert lib.vbq_dequantize(None, None, 1, 256, 13, 0, None) == _lib.VBQ_ERR_TYPE
     assert lib.vbq_dequantize(None, None, 1, 256, 12, 5, None) == _lib.VBQ_ERR_SHAPE
     assert lib.vbq_dequantize(0, 0, 0, 256, 12, 0, None) == _lib.VBQ_OK  # empty: no work
+
+
+def test_scratch_size_query(lib):
+    """Split-K scratch: counters + splits * batch * N partials; none when K is tiny."""
+    v = C.c_size_t()
+    assert lib.vbq_gemv_scratch_bytes(4096, 14336, 12, 1, C.byref(v)) == 0
+    assert v.value > 14336 * 4
+    big = v.value
+    assert lib.vbq_gemv_scratch_bytes(4096, 14336, 12, 16, C.byref(v)) == 0
+    assert v.value > big
+    assert lib.vbq_gemv_scratch_bytes(16, 256, 12, 1, C.byref(v)) == 0 and v.value == 0
+    assert lib.vbq_gemv_scratch_bytes(4096, 14336, 9, 1, C.byref(v)) == 1
 
 
 def test_python_face_rejects_host_tensors():

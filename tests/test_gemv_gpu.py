@@ -114,4 +114,5 @@ def test_gemv_linearity_and_row_independence(cuda, qtype):
     assert ((y_sum - (y[0] + y[1])).abs().max() / y_sum.abs().max()).item() <= TOL
     # each batch row is an independent GEMV: batch 4 row 2 == batch 1 on that row
     y_one = vb.gemv_dequant(x[2].contiguous(), w, None, K, N, qtype)
-    assert ((y_one - y[2]).abs().max() / y_one.abs().max()).item() <= 1e-5
+    # different kernel instantiations (batch 1 vs 4) add in different orders
+    assert ((y_one - y[2]).abs().max() / y_one.abs().max()).item() <= 1e-4

@@ -32,8 +32,11 @@ SIGNATURES = {
     "vbq_row_bytes": (C.c_int, [C.c_int32, C.c_int64, C.POINTER(C.c_int64)]),
     "vbq_dequantize": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int32,
                                  C.c_int32, C.c_void_p]),
+    "vbq_gemv_scratch_bytes": (C.c_int, [C.c_int64, C.c_int64, C.c_int32, C.c_int32,
+                                         C.POINTER(C.c_size_t)]),
     "vbq_gemv": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int32,
-                           C.c_int32, C.c_void_p]),
+                           C.c_int32, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "vbq_device_status": (C.c_int, [C.POINTER(C.c_int32), C.c_int32]),
 }
 
 _lock = threading.Lock()

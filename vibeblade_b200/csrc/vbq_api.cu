@@ -77,8 +77,7 @@ int vbq_dequantize(const void* w, void* out, int64_t rows, int64_t n, int32_t ty
   return ok();
 }
 
-int vbq_gemv(const float* x, const void* w, float* y, int64_t K, int64_t N, int32_t type,
-             int32_t batch, void* stream) {
+static int gemv_checks(int32_t type, int64_t K, int64_t N, int32_t batch) {
   if (!supported(type)) return fail(VBQ_ERR_TYPE, "gemv_dequant: unsupported type " + std::to_string(type));
   if (K < 0 || N < 0) return fail(VBQ_ERR_SHAPE, "vbq_gemv: negative size");
   if (batch < 1 || batch > 16)
@@ -87,22 +86,54 @@ int vbq_gemv(const float* x, const void* w, float* y, int64_t K, int64_t N, int3
   if (N % bv != 0)
     return fail(VBQ_ERR_SHAPE, "vbq_gemv: N = " + std::to_string(N) +
                                    " is not a multiple of the block size " + std::to_string(bv));
+  return VBQ_OK;
+}
+
+int vbq_gemv_scratch_bytes(int64_t K, int64_t N, int32_t type, int32_t batch, size_t* bytes) {
+  if (int rc = gemv_checks(type, K, N, batch)) return rc;
+  if (!bytes) return fail(VBQ_ERR_NULL, "vbq_gemv_scratch_bytes: bytes is NULL");
+  *bytes = (K == 0 || N == 0 || N % 256 != 0) ? 0 : vbq::plan_gemv(K, N, batch).scratch_bytes;
+  return ok();
+}
+
+int vbq_gemv(const float* x, const void* w, float* y, int64_t K, int64_t N, int32_t type,
+             int32_t batch, void* scratch, size_t scratch_bytes, void* stream) {
+  if (int rc = gemv_checks(type, K, N, batch)) return rc;
   if (N == 0) return ok();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (K == 0) {  // empty sum: the reference zeroes out and adds nothing (dequant.cpp:767)
+    if (!y) return fail(VBQ_ERR_NULL, "vbq_gemv: NULL pointer");
+    cudaError_t e = cudaMemsetAsync(y, 0, (size_t)batch * (size_t)N * sizeof(float), st);
+    if (e != cudaSuccess) return cuda_fail(e, "vbq_gemv memset");
+    return ok();
+  }
   if (!x || !w || !y) return fail(VBQ_ERR_NULL, "vbq_gemv: NULL pointer");
   if (!aligned(x, 4) || !aligned(y, 16) || !aligned(w, 16))
     return fail(VBQ_ERR_ALIGN, "vbq_gemv: w and y must be 16-byte aligned, x 4-byte aligned");
   if (N % 256 != 0)
     return fail(VBQ_ERR_UNSUPPORTED,
                 "vbq_gemv: N must be a multiple of 256 (Q8_0 rows of a partial 256-value tile are not implemented)");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (K == 0) {
-    cudaError_t e = cudaMemsetAsync(y, 0, (size_t)batch * (size_t)N * sizeof(float), st);
-    if (e != cudaSuccess) return cuda_fail(e, "vbq_gemv memset");
-    return ok();
+  const vbq::GemvPlan plan = vbq::plan_gemv(K, N, batch);
+  if (plan.scratch_bytes > 0) {
+    if (!scratch || scratch_bytes < plan.scratch_bytes)
+      return fail(VBQ_ERR_WORKSPACE, "vbq_gemv: scratch needs " + std::to_string(plan.scratch_bytes) +
+                                          " bytes (vbq_gemv_scratch_bytes), got " +
+                                          std::to_string(scratch_bytes));
+    if (!aligned(scratch, 16)) return fail(VBQ_ERR_ALIGN, "vbq_gemv: scratch must be 16-byte aligned");
   }
-  const int64_t rb = (N / bv) * block_bytes(type);
-  cudaError_t e = vbq::launch_gemv(type, x, w, y, K, N, rb, batch, st);
+  const int64_t rb = (N / block_values(type)) * block_bytes(type);
+  cudaError_t e = vbq::launch_gemv(type, x, w, y, K, N, rb, batch, plan, scratch, st);
   if (e != cudaSuccess) return cuda_fail(e, "vbq_gemv launch");
+  return ok();
+}
+
+int vbq_device_status(int32_t* status, int32_t clear) {
+  if (!status) return fail(VBQ_ERR_NULL, "vbq_device_status: status is NULL");
+  unsigned g = 0;
+  cudaError_t e = vbq::gemv_status(&g, clear != 0);
+  if (e != cudaSuccess) return cuda_fail(e, "vbq_device_status");
+  *status = (int32_t)g;
+  if (g & 1u) return fail(VBQ_ERR_TIMEOUT, "a bounded device-side wait gave up (a copy never completed)");
   return ok();
 }
 

@@ -56,6 +56,30 @@ __device__ __forceinline__ void q4k_scale_min(int j, uint32_t s0, uint32_t s1, u
   }
 }
 
+// Branch-free form of q4k_scale_min for a sub-block index fixed per thread: the
+// selector/shift/mask recipe is computed once (Q4kScaleRecipe(j)) and applied per row.
+struct Q4kScaleRecipe {
+  bool hi;        // j >= 4
+  int pa, ma;     // low part: (A >> pa) & ma, A = hi ? s2 : s0 (scale) / s2 : s1 (min)
+  int pb;         // high 2 bits: (s0 >> pb) & 0x30 (scale) / (s1 >> pb) & 0x30 (min)
+  int mb;         // 0x30 when hi, else 0
+  __device__ __forceinline__ explicit Q4kScaleRecipe(int j) {
+    hi = j >= 4;
+    const int i = hi ? j - 4 : j;
+    pa = 8 * i;
+    ma = hi ? 0x0f : 0x3f;
+    pb = 8 * i + 2;  // bits 8i+6..8i+7 shifted down to 4..5
+    mb = hi ? 0x30 : 0;
+  }
+  __device__ __forceinline__ void apply(uint32_t s0, uint32_t s1, uint32_t s2, int& sc,
+                                        int& mn) const {
+    const uint32_t As = hi ? s2 : s0;
+    const uint32_t Am = hi ? (s2 >> 4) : s1;
+    sc = (int)(((As >> pa) & (uint32_t)ma) | ((s0 >> pb) & (uint32_t)mb));
+    mn = (int)(((Am >> pa) & (uint32_t)ma) | ((s1 >> pb) & (uint32_t)mb));
+  }
+};
+
 // Read 4 bytes at a 2-byte-aligned shared/global address as one little-endian word.
 // Only aligned words that hold at least one of the 4 bytes are touched, so the read
 // never leaves the pages the data lives on.
@@ -69,16 +93,6 @@ __device__ __forceinline__ uint32_t ld_u32_a2(const uint8_t* p) {
 
 __device__ __forceinline__ uint32_t ld_u16(const uint8_t* p) {
   return (uint32_t)*reinterpret_cast<const uint16_t*>(p);
-}
-
-// Packed fp32x2 FMA (sm_100a): (a.x*b.x+c.x, a.y*b.y+c.y) in one instruction.
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;"
-      : "=l"(r)
-      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)),
-        "l"(*reinterpret_cast<uint64_t*>(&c)));
-  return *reinterpret_cast<float2*>(&r);
 }
 
 // cp.async (Ampere-style asynchronous global->shared copies), used by the GEMV
@@ -96,5 +110,67 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
 }
+
+// ---- mbarrier + bulk-copy (TMA, non-tensor) helpers --------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_inval(uint32_t bar) {
+  asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// Arrive on `bar` once every cp.async this thread issued before has landed (the arrival
+// was counted in the barrier's init count).
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+// Bulk global -> shared copy (16-byte aligned addresses, size a multiple of 16) that
+// reports its bytes to `bar`.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Wait for the phase of `bar` with the given parity, giving up after `budget` SM clock
+// cycles (returns false then).  Every device-side wait in this library is bounded.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
+                                                  long long budget) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > budget) return false;
+  }
+  return true;
+}
+
+// ~2 s at the B200's 1.965 GHz boost clock.
+constexpr long long kWaitBudgetCycles = 4000000000LL;
+
+// Status bits a kernel raises in its file's device status word.
+constexpr unsigned kStatusTimeout = 1u;
 
 }  // namespace vbq

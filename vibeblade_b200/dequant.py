@@ -32,6 +32,29 @@ def _weights_u8(w: torch.Tensor) -> torch.Tensor:
     return w if w.dtype == torch.uint8 else w.view(torch.uint8)
 
 
+# Zero-filled split-K scratch per (device, stream).  Calls on one stream run in order,
+# and every call leaves the buffer zero-filled again, so one buffer per stream is safe.
+_SCRATCH: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def gemv_scratch_bytes(K: int, N: int, wtype, batch: int = 1) -> int:
+    """Bytes of scratch ``gemv_dequant`` needs for this shape on the current device."""
+    import ctypes as C
+    lib = _lib.load()
+    v = C.c_size_t()
+    _lib.check(lib.vbq_gemv_scratch_bytes(K, N, F.parse_type(wtype), batch, C.byref(v)), lib)
+    return int(v.value)
+
+
+def _stream_scratch(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream)
+    buf = _SCRATCH.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _SCRATCH[key] = buf
+    return buf
+
+
 def row_bytes(qtype, n: int) -> int:
     """Bytes per row of a K x N matrix (cpp/src/dequant.cpp:749-763)."""
     return F.row_bytes(qtype, n)
@@ -76,8 +99,11 @@ def gemv_dequant(x: torch.Tensor, weights: torch.Tensor, out: torch.Tensor | Non
     out[n] = sum_k x[k] * deq(W)[k, n].
 
     ``x`` may also be a batch [B, K] with B <= 16 (the reference engine makes B calls,
-    cpp/src/fast_model.cpp:645-660); ``out`` is then [B, N].  ``scratch`` is accepted
-    for signature parity and unused: the device kernel needs no workspace."""
+    cpp/src/fast_model.cpp:645-660); ``out`` is then [B, N].  ``scratch`` is the
+    caller-owned split-K buffer, as in the reference: a CUDA tensor of at least
+    ``gemv_scratch_bytes(K, N, wtype, B)`` bytes, zero-filled before its first use (each
+    call leaves it zero-filled).  When None, a per-stream buffer owned by this module is
+    used."""
     t = F.parse_type(wtype)
     _require_cuda("gemv_dequant", x, weights)
     if x.dtype != torch.float32:
@@ -101,8 +127,17 @@ def gemv_dequant(x: torch.Tensor, weights: torch.Tensor, out: torch.Tensor | Non
         if out.dtype != torch.float32 or out.numel() != batch * N:
             raise RuntimeError("gemv_dequant: out must be float32 with batch*N values")
     lib = _lib.load()
+    sp = _stream_ptr(x)
+    need = gemv_scratch_bytes(K, N, t, batch) if K > 0 else 0
+    if scratch is None:
+        scr = _stream_scratch(x.device, sp, need) if need else None
+    else:
+        _require_cuda("gemv_dequant", scratch)
+        scr = scratch
+    scr_ptr = scr.data_ptr() if scr is not None else None
+    scr_bytes = scr.numel() * scr.element_size() if scr is not None else 0
     _lib.check(lib.vbq_gemv(x.data_ptr(), w.data_ptr(), out.data_ptr(), K, N, t, batch,
-                            _stream_ptr(x)), lib)
+                            scr_ptr, scr_bytes, sp), lib)
     return out
 
 
