@@ -99,6 +99,25 @@ int vbq_gemv(const float* x, const void* w, float* y, int64_t K, int64_t N, int3
              int32_t batch, void* scratch, size_t scratch_bytes, void* stream);
 
 /*
+ * vbq_gemv with library-owned scratch, for callers that cannot allocate device memory --
+ * for example an engine that reserves all of HBM for its own pools at start-up and allows
+ * no later cudaMalloc (which may also synchronise the device), or a plugin that only gets
+ * the host application's buffers.  This entry point has no counterpart in the reference.
+ *
+ * Same arguments and results as vbq_gemv, without the scratch pair.  The split-K scratch
+ * is a fixed 8 MiB array in the library's device memory (present on every GPU that loads
+ * the library until the process exits); shapes whose scratch would exceed it return
+ * VBQ_ERR_WORKSPACE.  The call allocates nothing.  Its first call on a device looks up
+ * the array's device address once (cudaGetSymbolAddress, with that device current); make
+ * that first call before any stream capture.  Every call on a device shares the array
+ * and the array keeps the previous call's contents (the call zeroes the part that must
+ * start at zero), so calls that may overlap on the GPU -- different streams, or graphs
+ * replayed concurrently -- race and must be serialised by the caller.
+ */
+int vbq_gemv_static_scratch(const float* x, const void* w, float* y, int64_t K, int64_t N,
+                            int32_t type, int32_t batch, void* stream);
+
+/*
  * Device-side status of the library's kernels on the current device: bit 0 set means a
  * bounded wait inside a kernel gave up (VBQ_ERR_TIMEOUT is returned then), which leaves
  * that call's outputs undefined and its scratch in need of re-zeroing.  Reads

@@ -7,6 +7,7 @@
 //     (cpp/src/cuda_kernels.cu:24-40), but returned as a status instead of thrown.
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "vbq.h"
@@ -138,3 +139,81 @@ int vbq_device_status(int32_t* status, int32_t clear) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------
+// GEMV with library-owned scratch, for callers that cannot allocate device memory.
+//
+// Some hosts of this library own every byte of device memory: a serving engine that
+// reserves the whole HBM at start-up for its weight and KV-cache pools and forbids later
+// cudaMalloc calls (which can also synchronise the device and stall its other streams),
+// or a plugin that only ever receives the host application's buffers.  Such callers have
+// nowhere to put vbq_gemv's split-K scratch.  This entry point uses a fixed array in the
+// library's own device memory instead; it exists on every GPU that loads the library,
+// from load until process exit.
+// ---------------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kStaticScratchBytes = 8u << 20;  // 8 MiB per device
+static __device__ __align__(256) unsigned char g_gemv_static_scratch[kStaticScratchBytes];
+
+std::mutex g_static_mu;
+void* g_static_ptr[64] = {nullptr};  // device address of the array, per device ordinal
+
+// Device address of the array on the current device.  Host code must not pass
+// g_gemv_static_scratch itself to a kernel: on the host it names a stand-in, not device
+// memory.  The address is looked up once per device, with that device current.
+int static_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "vbq_gemv_static_scratch: cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(VBQ_ERR_UNSUPPORTED, "vbq_gemv_static_scratch: device ordinal >= 64");
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_gemv_static_scratch);
+    if (e != cudaSuccess || !p)
+      return cuda_fail(e != cudaSuccess ? e : cudaErrorInvalidSymbol,
+                       "vbq_gemv_static_scratch: cudaGetSymbolAddress");
+    g_static_ptr[dev] = p;
+  }
+  *out = g_static_ptr[dev];
+  return VBQ_OK;
+}
+
+}  // namespace
+
+extern "C" int vbq_gemv_static_scratch(const float* x, const void* w, float* y, int64_t K,
+                                       int64_t N, int32_t type, int32_t batch, void* stream) {
+  if (int rc = gemv_checks(type, K, N, batch)) return rc;
+  if (N == 0) return ok();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (K == 0) {
+    if (!y) return fail(VBQ_ERR_NULL, "vbq_gemv_static_scratch: NULL pointer");
+    cudaError_t e = cudaMemsetAsync(y, 0, (size_t)batch * (size_t)N * sizeof(float), st);
+    if (e != cudaSuccess) return cuda_fail(e, "vbq_gemv_static_scratch memset");
+    return ok();
+  }
+  if (!x || !w || !y) return fail(VBQ_ERR_NULL, "vbq_gemv_static_scratch: NULL pointer");
+  if (!aligned(x, 4) || !aligned(y, 16) || !aligned(w, 16))
+    return fail(VBQ_ERR_ALIGN, "vbq_gemv_static_scratch: w and y must be 16-byte aligned, x 4-byte aligned");
+  if (N % 256 != 0)
+    return fail(VBQ_ERR_UNSUPPORTED, "vbq_gemv_static_scratch: N must be a multiple of 256");
+  const vbq::GemvPlan plan = vbq::plan_gemv(K, N, batch);
+  if (plan.scratch_bytes > kStaticScratchBytes)
+    return fail(VBQ_ERR_WORKSPACE,
+                "vbq_gemv_static_scratch: this shape needs " + std::to_string(plan.scratch_bytes) +
+                    " bytes of scratch, above the library's fixed " +
+                    std::to_string(kStaticScratchBytes) +
+                    "; use vbq_gemv with caller scratch (or a smaller batch / N)");
+  void* scratch = nullptr;
+  if (plan.scratch_bytes > 0) {
+    if (int rc = static_scratch(&scratch)) return rc;
+    // the array keeps the previous call's contents; the tile counters must start at zero
+    cudaError_t e = cudaMemsetAsync(scratch, 0, (size_t)plan.counter_bytes, st);
+    if (e != cudaSuccess) return cuda_fail(e, "vbq_gemv_static_scratch counter reset");
+  }
+  const int64_t rb = (N / block_values(type)) * block_bytes(type);
+  cudaError_t e = vbq::launch_gemv(type, x, w, y, K, N, rb, batch, plan, scratch, st);
+  if (e != cudaSuccess) return cuda_fail(e, "vbq_gemv_static_scratch launch");
+  return ok();
+}
