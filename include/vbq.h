@@ -99,6 +99,21 @@ int vbq_gemv(const float* x, const void* w, float* y, int64_t K, int64_t N, int3
              int32_t batch, void* scratch, size_t scratch_bytes, void* stream);
 
 /*
+ * Quantized-weight GEMM on the tcgen05 tensor cores (prefill):
+ *     C[m, n] = sum_k A[m, k] * deq(W)[k, n]
+ * A is bf16 [M, K] row-major, C fp32 (VBQ_DTYPE_F32) or bf16 (VBQ_DTYPE_BF16) [M, N]
+ * row-major, W the K x N block layout above.  Weight tiles are dequantized to bf16 in
+ * shared memory (values rounded to nearest-even from the reference's fp32 values) and
+ * multiplied with fp32 accumulation in tensor memory.  The reference has no batched GEMM;
+ * its engine makes one gemv_dequant call per token (cpp/src/fast_model.cpp:645-660),
+ * which this replaces.  Requirements: N % 256 == 0, K % 8 == 0, weight rows a multiple of
+ * 16 bytes (Q6_K: N % 2048 == 0), A, W, C 16-byte aligned.  No workspace.  A device-side
+ * wait that gives up is reported by vbq_device_status (outputs then undefined).
+ */
+int vbq_gemm(const void* a, const void* w, void* c, int64_t M, int64_t K, int64_t N,
+             int32_t type, int32_t c_dtype, void* stream);
+
+/*
  * vbq_gemv with library-owned scratch, for callers that cannot allocate device memory --
  * for example an engine that reserves all of HBM for its own pools at start-up and allows
  * no later cudaMalloc (which may also synchronise the device), or a plugin that only gets

@@ -8,11 +8,12 @@ hand-written CUDA kernels in ``libvbq.so`` behind the C ABI in ``include/vbq.h``
 from . import formats
 from .formats import GGML_TYPE_Q4_K, GGML_TYPE_Q6_K, GGML_TYPE_Q8_0, row_bytes, tensor_nbytes
 from .dequant import dequantize, dequantize_row, gemv_dequant, gemv_dequant_mt, gemv_scratch_bytes
+from .gemm import gemm_dequant, device_status
 from ._lib import VbqError
 
 __all__ = [
     "formats", "GGML_TYPE_Q4_K", "GGML_TYPE_Q6_K", "GGML_TYPE_Q8_0", "row_bytes",
     "tensor_nbytes", "dequantize", "dequantize_row", "gemv_dequant", "gemv_dequant_mt",
-    "gemv_scratch_bytes",
+    "gemv_scratch_bytes", "gemm_dequant", "device_status",
     "VbqError",
 ]

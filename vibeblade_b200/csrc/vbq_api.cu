@@ -128,11 +128,42 @@ int vbq_gemv(const float* x, const void* w, float* y, int64_t K, int64_t N, int3
   return ok();
 }
 
+int vbq_gemm(const void* a, const void* w, void* c, int64_t M, int64_t K, int64_t N, int32_t type,
+             int32_t c_dtype, void* stream) {
+  if (!supported(type)) return fail(VBQ_ERR_TYPE, "gemm_dequant: unsupported type " + std::to_string(type));
+  if (c_dtype != VBQ_DTYPE_F32 && c_dtype != VBQ_DTYPE_BF16)
+    return fail(VBQ_ERR_SHAPE, "vbq_gemm: c_dtype must be VBQ_DTYPE_F32 or VBQ_DTYPE_BF16");
+  if (M < 0 || K < 0 || N < 0) return fail(VBQ_ERR_SHAPE, "vbq_gemm: negative size");
+  if (N % 256 != 0) return fail(VBQ_ERR_SHAPE, "vbq_gemm: N must be a multiple of 256");
+  if (M == 0 || N == 0) return ok();
+  if (K == 0) {
+    if (!c) return fail(VBQ_ERR_NULL, "vbq_gemm: NULL pointer");
+    cudaError_t e = cudaMemsetAsync(c, 0, (size_t)M * N * (c_dtype == VBQ_DTYPE_F32 ? 4 : 2),
+                                    static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "vbq_gemm memset");
+    return ok();
+  }
+  if (!a || !w || !c) return fail(VBQ_ERR_NULL, "vbq_gemm: NULL pointer");
+  if (K % 8 != 0) return fail(VBQ_ERR_SHAPE, "vbq_gemm: K must be a multiple of 8 (16-byte rows of A)");
+  if (M > (int64_t)INT32_MAX || K > (int64_t)INT32_MAX || N > (int64_t)INT32_MAX)
+    return fail(VBQ_ERR_SHAPE, "vbq_gemm: sizes above 2^31 are not supported");
+  const int64_t rb = (N / block_values(type)) * block_bytes(type);
+  if (rb % 16 != 0)
+    return fail(VBQ_ERR_UNSUPPORTED, "vbq_gemm: weight rows must be a multiple of 16 bytes (Q6_K: N % 2048 == 0)");
+  if (!aligned(a, 16) || !aligned(w, 16) || !aligned(c, 16))
+    return fail(VBQ_ERR_ALIGN, "vbq_gemm: a, w and c must be 16-byte aligned");
+  cudaError_t e = vbq::launch_gemm(type, a, w, c, M, K, N, rb, c_dtype, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "vbq_gemm launch");
+  return ok();
+}
+
 int vbq_device_status(int32_t* status, int32_t clear) {
   if (!status) return fail(VBQ_ERR_NULL, "vbq_device_status: status is NULL");
-  unsigned g = 0;
+  unsigned g = 0, g2 = 0;
   cudaError_t e = vbq::gemv_status(&g, clear != 0);
+  if (e == cudaSuccess) e = vbq::gemm_status(&g2, clear != 0);
   if (e != cudaSuccess) return cuda_fail(e, "vbq_device_status");
+  g |= g2;
   *status = (int32_t)g;
   if (g & 1u) return fail(VBQ_ERR_TIMEOUT, "a bounded device-side wait gave up (a copy never completed)");
   return ok();

@@ -24,6 +24,11 @@ cudaError_t launch_gemv(int qtype, const float* x, const void* w, float* y, int6
                         int64_t N, int64_t row_bytes, int batch, const GemvPlan& plan,
                         void* scratch, cudaStream_t st);
 
+// tcgen05 dequant-GEMM: a bf16 [M,K], W K x N blocks, c fp32 (c_dtype 0) / bf16 (1) [M,N].
+cudaError_t launch_gemm(int qtype, const void* a, const void* w, void* c, int64_t M, int64_t K,
+                        int64_t N, int64_t row_bytes, int c_dtype, cudaStream_t st);
+cudaError_t gemm_status(unsigned* out, bool clear);
+
 // Sticky device status bits of the GEMV kernels (kStatusTimeout = 1); synchronous.
 cudaError_t gemv_status(unsigned* out, bool clear);
 

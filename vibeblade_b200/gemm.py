@@ -1,0 +1,53 @@
+"""Quantized-weight GEMM (prefill) on the tcgen05 tensor cores.
+
+The reference runs prefill as one ``gemv_dequant`` per token
+(cpp/src/fast_model.cpp:645-660); ``gemm_dequant`` computes all tokens at once:
+out[m, n] = sum_k a[m, k] * deq(W)[k, n], with a in bf16 and fp32 accumulation.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from . import formats as F
+from .dequant import _require_cuda, _stream_ptr, _weights_u8
+
+
+def gemm_dequant(a: torch.Tensor, weights: torch.Tensor, out: torch.Tensor | None, M: int,
+                 K: int, N: int, wtype, out_dtype=torch.float32) -> torch.Tensor:
+    """a: bf16 [M, K] CUDA tensor; weights: the K x N block bytes; returns [M, N] in
+    out_dtype (torch.float32 or torch.bfloat16)."""
+    t = F.parse_type(wtype)
+    _require_cuda("gemm_dequant", a, weights)
+    if a.dtype != torch.bfloat16:
+        raise RuntimeError("gemm_dequant: a must be bfloat16")
+    if a.numel() != M * K:
+        raise RuntimeError(f"gemm_dequant: a has {a.numel()} values, expected M*K = {M * K}")
+    if out_dtype not in (torch.float32, torch.bfloat16):
+        raise RuntimeError("gemm_dequant: out_dtype must be torch.float32 or torch.bfloat16")
+    w = _weights_u8(weights)
+    need = F.row_bytes(t, N) * K
+    if w.numel() < need:
+        raise RuntimeError(f"gemm_dequant: weights hold {w.numel()} bytes, need {need}")
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    else:
+        _require_cuda("gemm_dequant", out)
+        if out.dtype != out_dtype or out.numel() != M * N:
+            raise RuntimeError("gemm_dequant: out has the wrong dtype or size")
+    lib = _lib.load()
+    cd = _lib.DTYPE_F32 if out_dtype == torch.float32 else _lib.DTYPE_BF16
+    _lib.check(lib.vbq_gemm(a.data_ptr(), w.data_ptr(), out.data_ptr(), M, K, N, t, cd,
+                            _stream_ptr(a)), lib)
+    return out
+
+
+def device_status(clear: bool = True) -> int:
+    """Device-side status bits (1 = a bounded wait inside a kernel gave up)."""
+    import ctypes as C
+    lib = _lib.load()
+    v = C.c_int32()
+    rc = lib.vbq_device_status(C.byref(v), 1 if clear else 0)
+    if rc not in (_lib.VBQ_OK, _lib.VBQ_ERR_TIMEOUT):
+        _lib.check(rc, lib)
+    return int(v.value)
