@@ -49,7 +49,8 @@ template <int QT> struct Smem {
   static constexpr int kStageBytes = 2 * kABoxBytes + Raw<QT>::kSlot;
   static constexpr int kLoadOff = 0;
   static constexpr int kBOff = kLoadStages * kStageBytes;
-  static constexpr int kBarOff = kBOff + kBStages * kBBytes;
+  static constexpr int kTblOff = kBOff + kBStages * kBBytes;  // per-warp scale tables
+  static constexpr int kBarOff = kTblOff + 8 * 768;
   // barriers: full_load[3], empty_load[3], full_b[2], empty_b[2], acc_full, + tmem ptr, abort
   static constexpr int kTotal = kBarOff + 128;
   static constexpr int kAlloc = kTotal + 1024;  // slack for 1024-byte alignment
@@ -119,75 +120,196 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&p);
 }
 
-// ---- dequantization: one thread = one K row-octet x one 8-column group ---------------
-// prep() reads a row's bytes for the thread's 8 columns (shared memory, broadcast-friendly:
-// all lanes of a warp read the same row); value(i) gives column i of that row in fp32,
-// bit-identical to the reference's dequantizers (one rounding per product/difference).
-// Small integers become floats exactly via the 2^23 + v bit pattern.
-__device__ __forceinline__ float small_to_f(uint32_t v) {
-  return __uint_as_float(0x4b000000u | v) - 8388608.0f;
+// ---- dequantization: one thread = 8 K rows x 8 consecutive columns ---------------------
+// Warp w (w = 2..9) owns K rows 8(w-2)..8(w-2)+7 of every stage, lane l the columns
+// 8l..8l+7 of the tile.  Every weight value is produced as the reference's fp32 value
+// (one rounding per product and per difference, cpp/src/dequant.cpp:268-301, :359-402 and
+// the Q8_0 block of cpp/src/cuda_kernels.cu:718-735), then rounded once to bf16.
+//
+// A small integer q becomes the float (magic + q) with one byte permute: the magic's
+// exponent makes its mantissa LSB worth exactly 1, so a packed fp32x2 add or fma removes
+// it without rounding.  Q4_K folds that into the product: fma(2^23 + q, dl, -2^23 dl) is
+// dl*q rounded once (2^23 dl is exact).  The result equals the reference's value up to
+// the sign of an exact zero, for every finite block scale.
+//
+// Two K rows of one column form one packed bf16x2 word; the four words of a column make
+// the 16-byte chunk the MMA reads.
+constexpr float kTwo23 = 8388608.0f;     // 2^23
+constexpr float kOneHalf23 = 12582912.0f; // 1.5 * 2^23: magic 0x4b4000xx = 1.5*2^23 + xx
+constexpr uint32_t kMagic23 = 0x4b000000u, kMagic15 = 0x4b400000u;
+
+// byte i of w as the low byte of magic k (k's bytes 0 and 1 are zero)
+// result bytes: [byte I of w, k.byte0, k.byte2, k.byte3]; k.byte0 is zero for both magics
+template <int I>
+__device__ __forceinline__ float magic_byte(uint32_t w, uint32_t k) {
+  return __uint_as_float(__byte_perm(w, k, 0x7640u | (uint32_t)I));
 }
+template <int QT> struct Producer;
 
-template <int QT> struct Deq;
-
-template <> struct Deq<kQ4_K> {
-  float dl, ml;
-  uint32_t q0, q1, hs;
-  __device__ __forceinline__ void prep(const uint8_t* __restrict__ rp, int ng,
-                                       const Q4kScaleRecipe& rec) {
-    const uint4 h = *reinterpret_cast<const uint4*>(rp);
-    int sc, mn;
-    rec.apply(h.y, h.z, h.w, sc, mn);
-    const float d = f16_ref(h.x & 0xffffu), dmin = f16_ref(h.x >> 16);
-    dl = __fmul_rn(d, (float)sc);
-    ml = __fmul_rn(dmin, (float)mn);
-    const int g = ng >> 3;
-    const uint2 q = *reinterpret_cast<const uint2*>(rp + 16 + 32 * g + 8 * (ng & 3));
-    q0 = q.x;
-    q1 = q.y;
-    hs = ((ng >> 2) & 1) * 4;  // high nibbles for odd sub-blocks
+// Q4_K: all 256 columns of the tile are one block; lane l's columns lie in sub-block
+// l >> 2 (low nibbles for even sub-blocks, high for odd).  The (dl, ml) pair of each of
+// the warp's 8 rows x 8 sub-blocks is computed once per stage into a per-warp table.
+template <> struct Producer<kQ4_K> {
+  static constexpr int kPitch = 144;
+  static constexpr int kTableBytes = 768;  // float4 [4 row pairs][8 sub-blocks] + float2 [4][8]
+  __device__ __forceinline__ static void table(const uint8_t* rows, int lane, uint8_t* tbl) {
+    const int sb = lane & 7, p = lane >> 3;
+    const Q4kScaleRecipe rec(sb);
+    float dl[2], ml[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint4 hd = *reinterpret_cast<const uint4*>(rows + (2 * p + h) * kPitch);
+      int sc, mn;
+      rec.apply(hd.y, hd.z, hd.w, sc, mn);
+      dl[h] = __fmul_rn(f16_ref(hd.x & 0xffffu), (float)sc);
+      ml[h] = __fmul_rn(f16_ref(hd.x >> 16), (float)mn);
+    }
+    reinterpret_cast<float4*>(tbl)[p * 8 + sb] =
+        make_float4(dl[0], dl[1], __fmul_rn(-kTwo23, dl[0]), __fmul_rn(-kTwo23, dl[1]));
+    reinterpret_cast<float2*>(tbl + 512)[p * 8 + sb] = make_float2(-ml[0], -ml[1]);
   }
-  __device__ __forceinline__ float value(int i) const {
-    const uint32_t w = i < 4 ? q0 : q1;
-    const uint32_t nib = (w >> (8 * (i & 3) + hs)) & 0xfu;
-    return __fsub_rn(__fmul_rn(dl, small_to_f(nib)), ml);
+  float2 dl[4], c[4], nm[4];
+  uint32_t w[8][2];
+  template <bool>
+  __device__ __forceinline__ void load(const uint8_t* rows, int lane, const uint8_t* tbl) {
+    const int sb = lane >> 2;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const float4 a = reinterpret_cast<const float4*>(tbl)[p * 8 + sb];
+      dl[p] = make_float2(a.x, a.y);
+      c[p] = make_float2(a.z, a.w);
+      nm[p] = reinterpret_cast<const float2*>(tbl + 512)[p * 8 + sb];
+    }
+    const int off = 16 + 32 * (lane >> 3) + 8 * (lane & 3);
+    const uint32_t hs = (uint32_t)((lane >> 2) & 1) * 4u;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const uint2 q = *reinterpret_cast<const uint2*>(rows + r * kPitch + off);
+      w[r][0] = (q.x >> hs) & 0x0f0f0f0fu;
+      w[r][1] = (q.y >> hs) & 0x0f0f0f0fu;
+    }
+  }
+  template <int I>
+  __device__ __forceinline__ uint32_t pair(int p) const {
+    const float2 m = make_float2(magic_byte<I & 3>(w[2 * p][I >> 2], kMagic23),
+                                 magic_byte<I & 3>(w[2 * p + 1][I >> 2], kMagic23));
+    const float2 v = __fadd2_rn(__ffma2_rn(m, dl[p], c[p]), nm[p]);
+    return pack_bf16x2(v.x, v.y);
   }
 };
 
-template <> struct Deq<kQ6_K> {
-  float ds;
-  uint32_t ql, qh;
-  __device__ __forceinline__ void prep(const uint8_t* __restrict__ bp, int ng,
-                                       const Q4kScaleRecipe&) {
-    const float d = f16_ref(ld_u16(bp + 208));
-    const int sc = (int)(int8_t)bp[192 + (ng >> 1)];
-    ds = __fmul_rn(d, (float)sc);
-    ql = ld_u32_a2(bp + 4 * ng);
-    qh = ld_u16(bp + 128 + 2 * ng);
+// Q6_K (reference layout): lane l's 8 values take ql bytes 4l..4l+3 and qh bytes 2l, 2l+1
+// and share scale l >> 1.  The 6-bit codes are assembled byte-wise: even columns in one
+// word, odd columns in another.
+template <> struct Producer<kQ6_K> {
+  static constexpr int kPitch = 224;
+  static constexpr int kTableBytes = 512;  // float2 [4 row pairs][16 scales]
+  __device__ __forceinline__ static void table(const uint8_t* rows, int lane, uint8_t* tbl) {
+    const int s = lane & 15;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int p = (lane >> 4) + 2 * j;
+      float ds[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint8_t* row = rows + (2 * p + h) * kPitch;
+        ds[h] = __fmul_rn(f16_ref(ld_u16(row + 208)), (float)(int8_t)row[192 + s]);
+      }
+      reinterpret_cast<float2*>(tbl)[p * 16 + s] = make_float2(ds[0], ds[1]);
+    }
   }
-  __device__ __forceinline__ float value(int i) const {
-    const uint32_t u = ((ql >> (4 * i)) & 0xfu) | (((qh >> (2 * i)) & 0x3u) << 4);
-    return __fmul_rn(ds, small_to_f(u) - 32.0f);
+  float2 ds[4];
+  uint32_t ue[8], uo[8];
+  template <bool kMisaligned>  // the block starts 2 mod 4 within the staged row
+  __device__ __forceinline__ void load(const uint8_t* rows, int lane, const uint8_t* tbl) {
+#pragma unroll
+    for (int p = 0; p < 4; ++p) ds[p] = reinterpret_cast<const float2*>(tbl)[p * 16 + (lane >> 1)];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const uint8_t* row = rows + r * kPitch;
+      uint32_t q;
+      if constexpr (kMisaligned) {
+        const uint32_t* a = reinterpret_cast<const uint32_t*>(row + 4 * lane - 2);
+        q = __byte_perm(a[0], a[1], 0x5432u);
+      } else {
+        q = *reinterpret_cast<const uint32_t*>(row + 4 * lane);
+      }
+      // qh bytes h0 (fields of columns 0-3), h1 (4-7) as [h0, h0, h1, h1]
+      const uint32_t hh = __byte_perm(ld_u16(row + 128 + 2 * lane), 0u, 0x1100u);
+      // high bits of column 2j: field 2j -> bits 4-5 of byte j; column 2j+1: field 2j+1
+      ue[r] = (q & 0x0f0f0f0fu) | ((hh << 4) & 0x00300030u) | (hh & 0x30003000u);
+      uo[r] = ((q >> 4) & 0x0f0f0f0fu) | ((hh << 2) & 0x00300030u) | ((hh >> 2) & 0x30003000u);
+    }
+  }
+  template <int I>
+  __device__ __forceinline__ uint32_t pair(int p) const {
+    const uint32_t* u = (I & 1) ? uo : ue;
+    const float2 m = make_float2(magic_byte<(I >> 1)>(u[2 * p], kMagic15),
+                                 magic_byte<(I >> 1)>(u[2 * p + 1], kMagic15));
+    const float2 q = __fadd2_rn(m, make_float2(-(kOneHalf23 + 32.0f), -(kOneHalf23 + 32.0f)));
+    const float2 v = __fmul2_rn(ds[p], q);
+    return pack_bf16x2(v.x, v.y);
   }
 };
 
-template <> struct Deq<kQ8_0> {
-  float d;
-  uint32_t w0, w1;
-  __device__ __forceinline__ void prep(const uint8_t* __restrict__ rp, int ng,
-                                       const Q4kScaleRecipe&) {
-    const uint8_t* bp = rp + 34 * (ng >> 2);
-    d = f16_ieee(ld_u16(bp));
-    const uint8_t* q = bp + 2 + 8 * (ng & 3);
-    w0 = ld_u32_a2(q);
-    w1 = ld_u32_a2(q + 4);
+// Q8_0 (GGUF 34-byte block, fp16 scale): the tile's 256 columns are 8 blocks; lane l's
+// 8 values are bytes 8(l & 3)..+7 of block l >> 2, 2 bytes off a 4-byte boundary for
+// even blocks.
+template <> struct Producer<kQ8_0> {
+  static constexpr int kPitch = 272;
+  static constexpr int kTableBytes = 0;
+  __device__ __forceinline__ static void table(const uint8_t*, int, uint8_t*) {}
+  float2 d[4];
+  uint32_t w[8][2];
+  template <bool>
+  __device__ __forceinline__ void load(const uint8_t* rows, int lane, const uint8_t*) {
+    const int boff = 34 * (lane >> 2);
+    const int a = boff + 2 + 8 * (lane & 3);
+    const int base = a & ~3;
+    const uint32_t sel = (a & 2) ? 0x5432u : 0x3210u;
+    float dr[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const uint8_t* row = rows + r * kPitch;
+      const uint32_t* x = reinterpret_cast<const uint32_t*>(row + base);
+      const uint32_t x0 = x[0], x1 = x[1], x2 = x[2];
+      w[r][0] = __byte_perm(x0, x1, sel) ^ 0x80808080u;  // q + 128 as unsigned bytes
+      w[r][1] = __byte_perm(x1, x2, sel) ^ 0x80808080u;
+      dr[r] = f16_ieee(ld_u16(row + boff));
+    }
+#pragma unroll
+    for (int p = 0; p < 4; ++p) d[p] = make_float2(dr[2 * p], dr[2 * p + 1]);
   }
-  __device__ __forceinline__ float value(int i) const {
-    const uint32_t w = i < 4 ? w0 : w1;
-    const uint32_t b = ((w >> (8 * (i & 3))) & 0xffu) ^ 0x80u;  // q + 128
-    return __fmul_rn(small_to_f(b) - 128.0f, d);
+  template <int I>
+  __device__ __forceinline__ uint32_t pair(int p) const {
+    const float2 m = make_float2(magic_byte<I & 3>(w[2 * p][I >> 2], kMagic15),
+                                 magic_byte<I & 3>(w[2 * p + 1][I >> 2], kMagic15));
+    const float2 q = __fadd2_rn(m, make_float2(-(kOneHalf23 + 128.0f), -(kOneHalf23 + 128.0f)));
+    const float2 v = __fmul2_rn(q, d[p]);
+    return pack_bf16x2(v.x, v.y);
   }
 };
+
+// Value I of lane l (column 8l + I of the tile) goes to B row 8l + ((I + l) & 7): the 8
+// lanes of each 16-byte store phase then hit 8 different swizzle chunks.  The epilogue
+// undoes this rotation inside each group of 8 accumulator columns.
+template <int QT, int I>
+__device__ __forceinline__ void store_column(const Producer<QT>& pr, uint8_t* bt, const uint32_t (&off)[8]) {
+  const uint4 chunk = make_uint4(pr.template pair<I>(0), pr.template pair<I>(1),
+                                 pr.template pair<I>(2), pr.template pair<I>(3));
+  *reinterpret_cast<uint4*>(bt + off[I]) = chunk;
+}
+template <int QT>
+__device__ __forceinline__ void store_all(const Producer<QT>& pr, uint8_t* bt, const uint32_t (&off)[8]) {
+  store_column<QT, 0>(pr, bt, off);
+  store_column<QT, 1>(pr, bt, off);
+  store_column<QT, 2>(pr, bt, off);
+  store_column<QT, 3>(pr, bt, off);
+  store_column<QT, 4>(pr, bt, off);
+  store_column<QT, 5>(pr, bt, off);
+  store_column<QT, 6>(pr, bt, off);
+  store_column<QT, 7>(pr, bt, off);
+}
 
 struct Bars {
   uint64_t full_load[kLoadStages], empty_load[kLoadStages];
@@ -204,7 +326,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   using L = Smem<QT>;
   using R = Raw<QT>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned (128-byte swizzle atoms); derived from the array so that the
+  // compiler keeps shared-memory addressing
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   Bars& bars = *reinterpret_cast<Bars*>(smem + L::kBarOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -304,42 +428,41 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     }
   } else {
     // ------------------------------ dequant warps ------------------------------
+    using P = Producer<QT>;
     const int kc = warp - 2;  // this warp's 8 K rows of each stage
-    const int ng = lane;      // 8-column group: columns 8*ng .. 8*ng+7
-    const Q4kScaleRecipe rec(2 * (ng >> 3) + ((ng >> 2) & 1));  // Q4_K sub-block of the group
+    uint8_t* tbl = smem + L::kTblOff + kc * 768;
+    uint32_t off[8];          // B-tile byte offset of value i's 16-byte chunk
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int rot = (i + lane) & 7;
+      off[i] = (uint32_t)((8 * lane + rot) * 128 + ((kc ^ rot) << 4));
+    }
+    const bool mis = (raw_off & 2) != 0;
     for (int it = 0; it < nk; ++it) {
       if (*abort_flag) break;
       const int s = it % kLoadStages, t = it % kBStages;
-      if (!mbar_wait_bounded(smem_u32(&bars.full_load[s]), (it / kLoadStages) & 1, kWaitBudgetCycles) ||
-          !mbar_wait_bounded(smem_u32(&bars.empty_b[t]), ((it / kBStages) & 1) ^ 1, kWaitBudgetCycles)) {
+      if (!mbar_wait_bounded(smem_u32(&bars.full_load[s]), (it / kLoadStages) & 1, kWaitBudgetCycles)) {
         give_up();
         break;
       }
-      const uint8_t* raw = raw_stage(s);
-      Deq<QT> rows[8];
-#pragma unroll
-      for (int r = 0; r < 8; ++r) rows[r].prep(raw + (8 * kc + r) * R::kPitch + raw_off, ng, rec);
-      // K-major, 128-byte swizzled B tile: column n's values of rows 8kc..8kc+7 form the
-      // 16-byte chunk (kc ^ (n & 7)) of smem row n.  Lane l writes its columns in the order
-      // i = (jj + l) & 7, so the 8 lanes of each store phase hit 8 different chunks.
-      uint8_t* bt = b_stage(t);
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
-        const int i = (jj + lane) & 7;
-        float v[8];
-#pragma unroll
-        for (int r = 0; r < 8; ++r) v[r] = rows[r].value(i);
-        const uint4 chunk = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
-                                       pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
-        const int n = 8 * ng + i;
-        *reinterpret_cast<uint4*>(bt + n * 128 + ((kc ^ (n & 7)) << 4)) = chunk;
+      const uint8_t* rows = raw_stage(s) + 8 * kc * P::kPitch + raw_off;
+      if constexpr (P::kTableBytes > 0) {
+        P::table(rows, lane, tbl);
+        __syncwarp();
       }
+      P pr;
+      if (mis) pr.template load<true>(rows, lane, tbl);
+      else pr.template load<false>(rows, lane, tbl);
+      __syncwarp();  // every lane holds its raw bytes and scales in registers
+      if (lane == 0) mbar_arrive(smem_u32(&bars.empty_load[s]));
+      if (!mbar_wait_bounded(smem_u32(&bars.empty_b[t]), ((it / kBStages) & 1) ^ 1, kWaitBudgetCycles)) {
+        give_up();
+        break;
+      }
+      store_all<QT>(pr, b_stage(t), off);
       fence_proxy_async_smem();  // make the generic stores visible to the tensor core
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(smem_u32(&bars.full_b[t]));
-        mbar_arrive(smem_u32(&bars.empty_load[s]));
-      }
+      if (lane == 0) mbar_arrive(smem_u32(&bars.full_b[t]));
     }
 
     // ------------------------------ epilogue ------------------------------
@@ -353,26 +476,35 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       const int half = (warp - 2) >> 2;         // accumulator 0 (warps 2-5) or 1 (warps 6-9)
       const int row = m0 + half * 128 + quarter * 32 + lane;
       const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * 256);
+      // accumulator column 8L + p holds tile column 8L + ((p - L) & 7) (the producer's
+      // rotation); with 64 columns per step, L & 7 is 4h + g for group g of half h
 #pragma unroll 1
-      for (int cb = 0; cb < BN; cb += 32) {
-        uint32_t r[32];
-        tmem_ld32(tbase + cb, r);
-        if (row < M) {
-          const int64_t off = (int64_t)row * N + (int64_t)n_tile * BN + cb;
-          if constexpr (BF16_OUT) {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(c) + off);
+      for (int cb = 0; cb < BN; cb += 64) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-              dst[q] = make_uint4(pack_bf16x2(__uint_as_float(r[8 * q]), __uint_as_float(r[8 * q + 1])),
-                                  pack_bf16x2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3])),
-                                  pack_bf16x2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5])),
-                                  pack_bf16x2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7])));
-          } else {
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(c) + off);
+        for (int h = 0; h < 2; ++h) {
+          uint32_t r[32], o[32];
+          tmem_ld32(tbase + cb + 32 * h, r);
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-              dst[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                                   __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+          for (int g = 0; g < 4; ++g)
+#pragma unroll
+            for (int q = 0; q < 8; ++q) o[8 * g + q] = r[8 * g + ((q + 4 * h + g) & 7)];
+          if (row < M) {
+            const int64_t off = (int64_t)row * N + (int64_t)n_tile * BN + cb + 32 * h;
+            if constexpr (BF16_OUT) {
+              uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(c) + off);
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                dst[q] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * q]), __uint_as_float(o[8 * q + 1])),
+                                    pack_bf16x2(__uint_as_float(o[8 * q + 2]), __uint_as_float(o[8 * q + 3])),
+                                    pack_bf16x2(__uint_as_float(o[8 * q + 4]), __uint_as_float(o[8 * q + 5])),
+                                    pack_bf16x2(__uint_as_float(o[8 * q + 6]), __uint_as_float(o[8 * q + 7])));
+            } else {
+              float4* dst = reinterpret_cast<float4*>(static_cast<float*>(c) + off);
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                dst[q] = make_float4(__uint_as_float(o[4 * q]), __uint_as_float(o[4 * q + 1]),
+                                     __uint_as_float(o[4 * q + 2]), __uint_as_float(o[4 * q + 3]));
+            }
           }
         }
       }
