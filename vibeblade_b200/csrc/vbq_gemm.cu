@@ -6,17 +6,25 @@
 // cpp/src/dequant.cpp:739-771), C fp32 or bf16 [M, N].  The reference has no batched GEMM:
 // its engine runs one gemv_dequant per token (cpp/src/fast_model.cpp:645-660).
 //
-// One CTA computes a 256 x 256 tile of C with tcgen05 MMAs accumulating in tensor memory
-// (two 128 x 256 fp32 accumulators = all 512 TMEM columns).  Per 64-deep K step:
-//   * warp 0 (one lane) TMA-loads the two 128 x 64 A boxes (128-byte swizzle) and the raw
-//     quant bytes of the 64 W rows of the tile's 256 columns into a 3-deep ring;
-//   * warps 2-9 dequantize the raw bytes to bf16 straight into the K-major, 128-byte
-//     swizzled B tile the MMA reads (2-deep ring), warp w handling K rows 8(w-2)..+7;
-//   * warp 1 (one lane) issues 2 x 4 tcgen05.mma (M=128, N=256, K=16) and commits them to
-//     the barriers that free the A and B stages.
-// After the last K step the dequant warps read the accumulators out of tensor memory
+// A CTA pair (a 2-CTA cluster; rank 0 is the leader) computes a 512 x 256 tile of C with
+// cta_group::2 tcgen05 MMAs: M = 256 spread over the pair (128 rows per CTA), N = 256,
+// K = 16, fp32 accumulators in tensor memory.  Each CTA holds two 128 x 256 accumulators
+// (pair rows 128r.. and 256 + 128r.., all 512 TMEM columns).  Each CTA dequantizes only
+// its 128-column half of the weight tile; the pair MMA reads both halves, so every bf16
+// weight is written to shared memory once and read once per pair.  Per 64-deep K step:
+//   * warp 0 (one lane) TMA-loads the CTA's two 128 x 64 A boxes (128-byte swizzle); the
+//     bytes are reported to the leader's barrier (3-deep ring, freed by the MMAs);
+//   * warp 10 (one lane) TMA-loads the raw quant bytes of the 64 W rows into a 4-deep
+//     ring that the dequant warps free as soon as the bytes are in registers;
+//   * warps 2-9 dequantize the raw bytes to bf16 into the K-major, 128-byte swizzled B
+//     half-tile (3-deep ring): warps 2-5 take the even K steps, warps 6-9 the odd ones,
+//     each warp 16 K rows x 128 columns; they arrive on the leader's B barrier;
+//   * the leader's warp 1 (one lane) issues 2 x 4 MMAs and commits them to barriers in
+//     both CTAs.
+// After the last K step warps 2-9 of each CTA read its accumulators out of tensor memory
 // (tcgen05.ld) and store C.  Every mbarrier wait is bounded; a wait that gives up records
-// kStatusTimeout in the device status word and the CTA drains and exits.
+// kStatusTimeout in the device status word, raises the abort flag of both CTAs, and the
+// pair drains and exits.  No TMA load here uses cluster multicast.
 #include <cuda.h>
 
 #include <cstdlib>
@@ -31,11 +39,15 @@ __device__ unsigned g_gemm_status = 0;
 
 namespace gemm {
 
-constexpr int BM = 256, BN = 256, BK = 64;
-constexpr int kThreads = 320;            // 10 warps
-constexpr int kLoadStages = 3, kBStages = 2;
-constexpr int kABoxBytes = 128 * BK * 2;  // one 128 x 64 bf16 box
-constexpr int kBBytes = BN * BK * 2;      // 256 x 64 bf16 B tile
+constexpr int BMP = 512, BN = 256, BK = 64;  // pair tile rows, tile columns, K step
+constexpr int kHalfN = BN / 2;               // columns dequantized per CTA
+constexpr int kDeqWarps = 8;                 // two groups of 4, alternating K steps
+constexpr int kThreads = 32 * (3 + kDeqWarps);  // + A TMA, MMA, raw TMA warps
+constexpr int kRawWarp = 2 + kDeqWarps;
+constexpr int kAStages = 3, kRStages = 4, kBStages = 3;
+constexpr int kABoxBytes = 128 * BK * 2;      // one 128 x 64 bf16 box
+constexpr int kBBytes = kHalfN * BK * 2;      // 128 x 64 bf16 B half-tile
+constexpr int kTableBytes = 768;              // per dequant warp
 constexpr int kTmemCols = 512;
 
 template <int QT> struct Raw {
@@ -45,18 +57,27 @@ template <int QT> struct Raw {
   static constexpr int kSlot = (kBytes + 1023) / 1024 * 1024;
 };
 
-template <int QT> struct Smem {
-  static constexpr int kStageBytes = 2 * kABoxBytes + Raw<QT>::kSlot;
-  static constexpr int kLoadOff = 0;
-  static constexpr int kBOff = kLoadStages * kStageBytes;
-  static constexpr int kTblOff = kBOff + kBStages * kBBytes;  // per-warp scale tables
-  static constexpr int kBarOff = kTblOff + 8 * 768;
-  // barriers: full_load[3], empty_load[3], full_b[2], empty_b[2], acc_full, + tmem ptr, abort
-  static constexpr int kTotal = kBarOff + 128;
-  static constexpr int kAlloc = kTotal + 1024;  // slack for 1024-byte alignment
+struct Bars {
+  uint64_t full_a[kAStages], empty_a[kAStages];
+  uint64_t full_raw[kRStages], empty_raw[kRStages];
+  uint64_t full_b[kBStages], empty_b[kBStages];
+  uint64_t acc_full;
+  uint32_t tmem_base;
+  int abort;
 };
 
-// ---- tcgen05 / TMA primitives (inline PTX, sm_100a) ----------------------------------
+template <int QT> struct Smem {
+  static constexpr int kAOff = 0;
+  static constexpr int kRawOff = kAOff + kAStages * 2 * kABoxBytes;
+  static constexpr int kBOff = kRawOff + kRStages * Raw<QT>::kSlot;
+  static constexpr int kTblOff = kBOff + kBStages * kBBytes;
+  static constexpr int kBarOff = kTblOff + kDeqWarps * kTableBytes;
+  static constexpr int kTotal = kBarOff + (int)((sizeof(Bars) + 127) / 128 * 128);
+  static constexpr int kAlloc = kTotal + 1024;  // slack for 1024-byte alignment
+  static_assert(kAlloc <= 232448, "shared memory per CTA");
+};
+
+// ---- tcgen05 / TMA / cluster primitives (inline PTX, sm_100a) ------------------------
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
   // K-major operand, 128-byte swizzle: rows of 128 B, 8-row atoms 1024 B apart (SBO),
   // LBO unused (1), descriptor version 1, layout type 2 (SWIZZLE_128B).
@@ -68,10 +89,56 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
   d |= (uint64_t)2 << 61;
   return d;
 }
-// kind::f16 instruction descriptor: D fp32, A and B bf16, both K-major, N = 256, M = 128.
+// kind::f16 instruction descriptor: D fp32, A and B bf16, both K-major, N = 256, M = 256
+// (the pair's M; each CTA's tensor core produces 128 of the rows).
 constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                            ((uint32_t)(128 >> 4) << 24);
+                            ((uint32_t)(256 >> 4) << 24);
 
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+// Whole-cluster barrier (every thread of both CTAs).  Only reached after bounded waits.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+// try_wait with cluster-scope acquire, for barriers that threads of the peer CTA arrive on
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "n"(kTryWaitSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_bounded_cluster(uint32_t bar, uint32_t parity,
+                                                          long long budget) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait_cluster(bar, parity)) {
+    if (clock64() - t0 > budget) return false;
+  }
+  return true;
+}
+
+// TMA tile load into this CTA's shared memory, bytes reported to `bar` in this CTA
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
                                             uint32_t bar) {
   asm volatile(
@@ -79,17 +146,29 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
       : "memory");
 }
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                          uint32_t accumulate) {
+// TMA tile load into this CTA's shared memory, bytes reported to a barrier of the CTA
+// pair (`bar` is a shared::cluster address); no multicast
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void umma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                               uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
       : "memory");
 }
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-               ::"r"(bar) : "memory");
+// arrive on the barrier at `bar`'s offset in both CTAs once the issued MMAs are done
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+      ::"r"(bar), "h"((uint16_t)3)
+      : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -121,10 +200,11 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 }
 
 // ---- dequantization: one thread = 8 K rows x 8 consecutive columns ---------------------
-// Warp w (w = 2..9) owns K rows 8(w-2)..8(w-2)+7 of every stage, lane l the columns
-// 8l..8l+7 of the tile.  Every weight value is produced as the reference's fp32 value
-// (one rounding per product and per difference, cpp/src/dequant.cpp:268-301, :359-402 and
-// the Q8_0 block of cpp/src/cuda_kernels.cu:718-735), then rounded once to bf16.
+// In CTA r, dequant warp q (0..3 within its group) owns K rows 16q..16q+15 of a stage;
+// lane l takes the 8 rows 16q + 8(l >> 4) .. +7 and the tile columns 128r + 8(l & 15) ..
+// +7.  Every weight value is produced as the reference's fp32 value (one rounding per
+// product and per difference, cpp/src/dequant.cpp:268-301, :359-402 and the Q8_0 block of
+// cpp/src/cuda_kernels.cu:718-735), then rounded once to bf16.
 //
 // A small integer q becomes the float (magic + q) with one byte permute: the magic's
 // exponent makes its mantissa LSB worth exactly 1, so a packed fp32x2 add or fma removes
@@ -134,54 +214,70 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 //
 // Two K rows of one column form one packed bf16x2 word; the four words of a column make
 // the 16-byte chunk the MMA reads.
-constexpr float kTwo23 = 8388608.0f;     // 2^23
+constexpr float kTwo23 = 8388608.0f;      // 2^23
 constexpr float kOneHalf23 = 12582912.0f; // 1.5 * 2^23: magic 0x4b4000xx = 1.5*2^23 + xx
 constexpr uint32_t kMagic23 = 0x4b000000u, kMagic15 = 0x4b400000u;
 
-// byte i of w as the low byte of magic k (k's bytes 0 and 1 are zero)
 // result bytes: [byte I of w, k.byte0, k.byte2, k.byte3]; k.byte0 is zero for both magics
 template <int I>
 __device__ __forceinline__ float magic_byte(uint32_t w, uint32_t k) {
   return __uint_as_float(__byte_perm(w, k, 0x7640u | (uint32_t)I));
 }
+
+// Where a thread's rows and columns are.  Scale tables are indexed by the warp's row pair
+// p = 4*oct + pp, stored at slot 2*pp + oct so that the two octets of a warp read
+// adjacent entries.
+struct Lane {
+  int lc;    // column group: tile columns 128*rank + 8*lc .. +7
+  int oct;   // row octet of the warp's 16 rows
+  int rank;  // CTA rank in the pair: which half of the tile's columns
+};
+__device__ __forceinline__ int pair_slot(int p) { return 2 * (p & 3) + (p >> 2); }
+
 template <int QT> struct Producer;
 
-// Q4_K: all 256 columns of the tile are one block; lane l's columns lie in sub-block
-// l >> 2 (low nibbles for even sub-blocks, high for odd).  The (dl, ml) pair of each of
-// the warp's 8 rows x 8 sub-blocks is computed once per stage into a per-warp table.
+// Q4_K: the tile's 256 columns are one block; this CTA's half covers sub-blocks
+// 4r .. 4r+3, lane l's columns lie in sub-block 4r + (lc >> 2).  The (dl, ml) pair of each
+// of the warp's 16 rows x 4 sub-blocks is computed once per stage into a per-warp table.
 template <> struct Producer<kQ4_K> {
   static constexpr int kPitch = 144;
-  static constexpr int kTableBytes = 768;  // float4 [4 row pairs][8 sub-blocks] + float2 [4][8]
-  __device__ __forceinline__ static void table(const uint8_t* rows, int lane, uint8_t* tbl) {
-    const int sb = lane & 7, p = lane >> 3;
-    const Q4kScaleRecipe rec(sb);
+  // table: float4 (dl_r, dl_r+1, -2^23 dl_r, -2^23 dl_r+1) [8 row pairs][4 sub-blocks],
+  // then float2 (-ml_r, -ml_r+1) [8][4]
+  __device__ __forceinline__ static void table(const uint8_t* wrows, int lane, int rank,
+                                               uint8_t* tbl) {
+    const int sbl = lane & 3, p = lane >> 2;
+    const Q4kScaleRecipe rec(4 * rank + sbl);
     float dl[2], ml[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const uint4 hd = *reinterpret_cast<const uint4*>(rows + (2 * p + h) * kPitch);
+      const uint4 hd = *reinterpret_cast<const uint4*>(wrows + (2 * p + h) * kPitch);
       int sc, mn;
       rec.apply(hd.y, hd.z, hd.w, sc, mn);
       dl[h] = __fmul_rn(f16_ref(hd.x & 0xffffu), (float)sc);
       ml[h] = __fmul_rn(f16_ref(hd.x >> 16), (float)mn);
     }
-    reinterpret_cast<float4*>(tbl)[p * 8 + sb] =
+    const int e = pair_slot(p) * 4 + sbl;
+    reinterpret_cast<float4*>(tbl)[e] =
         make_float4(dl[0], dl[1], __fmul_rn(-kTwo23, dl[0]), __fmul_rn(-kTwo23, dl[1]));
-    reinterpret_cast<float2*>(tbl + 512)[p * 8 + sb] = make_float2(-ml[0], -ml[1]);
+    reinterpret_cast<float2*>(tbl + 512)[e] = make_float2(-ml[0], -ml[1]);
   }
   float2 dl[4], c[4], nm[4];
   uint32_t w[8][2];
   template <bool>
-  __device__ __forceinline__ void load(const uint8_t* rows, int lane, const uint8_t* tbl) {
-    const int sb = lane >> 2;
+  __device__ __forceinline__ void load(const uint8_t* rows, const Lane& ln, const uint8_t* tbl) {
+    const int sbl = ln.lc >> 2;
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const float4 a = reinterpret_cast<const float4*>(tbl)[p * 8 + sb];
-      dl[p] = make_float2(a.x, a.y);
-      c[p] = make_float2(a.z, a.w);
-      nm[p] = reinterpret_cast<const float2*>(tbl + 512)[p * 8 + sb];
+    for (int pp = 0; pp < 4; ++pp) {
+      const int e = (2 * pp + ln.oct) * 4 + sbl;
+      const float4 a = reinterpret_cast<const float4*>(tbl)[e];
+      dl[pp] = make_float2(a.x, a.y);
+      c[pp] = make_float2(a.z, a.w);
+      nm[pp] = reinterpret_cast<const float2*>(tbl + 512)[e];
     }
-    const int off = 16 + 32 * (lane >> 3) + 8 * (lane & 3);
-    const uint32_t hs = (uint32_t)((lane >> 2) & 1) * 4u;
+    // column 128r + 8lc + i: 64-value group g = 2r + (lc >> 3), low nibbles when the
+    // column's offset in the group is below 32
+    const int off = 16 + 32 * (2 * ln.rank + (ln.lc >> 3)) + 8 * (ln.lc & 3);
+    const uint32_t hs = (uint32_t)((ln.lc >> 2) & 1) * 4u;
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
       const uint2 q = *reinterpret_cast<const uint2*>(rows + r * kPitch + off);
@@ -198,44 +294,47 @@ template <> struct Producer<kQ4_K> {
   }
 };
 
-// Q6_K (reference layout): lane l's 8 values take ql bytes 4l..4l+3 and qh bytes 2l, 2l+1
-// and share scale l >> 1.  The 6-bit codes are assembled byte-wise: even columns in one
-// word, odd columns in another.
+// Q6_K (reference layout): column 128r + 8lc + i takes ql bytes 64r + 4lc .. +3, qh bytes
+// 32r + 2lc, +1 and scale 8r + (lc >> 1).  The 6-bit codes are assembled byte-wise: even
+// columns in one word, odd columns in another.
 template <> struct Producer<kQ6_K> {
   static constexpr int kPitch = 224;
-  static constexpr int kTableBytes = 512;  // float2 [4 row pairs][16 scales]
-  __device__ __forceinline__ static void table(const uint8_t* rows, int lane, uint8_t* tbl) {
-    const int s = lane & 15;
+  // table: float2 (d*sc_r, d*sc_r+1) [8 row pairs][8 scales]
+  __device__ __forceinline__ static void table(const uint8_t* wrows, int lane, int rank,
+                                               uint8_t* tbl) {
+    const int sl = lane & 7;
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      const int p = (lane >> 4) + 2 * j;
+      const int p = (lane >> 3) + 4 * j;
       float ds[2];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const uint8_t* row = rows + (2 * p + h) * kPitch;
-        ds[h] = __fmul_rn(f16_ref(ld_u16(row + 208)), (float)(int8_t)row[192 + s]);
+        const uint8_t* row = wrows + (2 * p + h) * kPitch;
+        ds[h] = __fmul_rn(f16_ref(ld_u16(row + 208)), (float)(int8_t)row[192 + 8 * rank + sl]);
       }
-      reinterpret_cast<float2*>(tbl)[p * 16 + s] = make_float2(ds[0], ds[1]);
+      reinterpret_cast<float2*>(tbl)[pair_slot(p) * 8 + sl] = make_float2(ds[0], ds[1]);
     }
   }
   float2 ds[4];
   uint32_t ue[8], uo[8];
   template <bool kMisaligned>  // the block starts 2 mod 4 within the staged row
-  __device__ __forceinline__ void load(const uint8_t* rows, int lane, const uint8_t* tbl) {
+  __device__ __forceinline__ void load(const uint8_t* rows, const Lane& ln, const uint8_t* tbl) {
 #pragma unroll
-    for (int p = 0; p < 4; ++p) ds[p] = reinterpret_cast<const float2*>(tbl)[p * 16 + (lane >> 1)];
+    for (int pp = 0; pp < 4; ++pp)
+      ds[pp] = reinterpret_cast<const float2*>(tbl)[(2 * pp + ln.oct) * 8 + (ln.lc >> 1)];
+    const int qlo = 64 * ln.rank + 4 * ln.lc, qho = 128 + 32 * ln.rank + 2 * ln.lc;
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
       const uint8_t* row = rows + r * kPitch;
       uint32_t q;
       if constexpr (kMisaligned) {
-        const uint32_t* a = reinterpret_cast<const uint32_t*>(row + 4 * lane - 2);
+        const uint32_t* a = reinterpret_cast<const uint32_t*>(row + qlo - 2);
         q = __byte_perm(a[0], a[1], 0x5432u);
       } else {
-        q = *reinterpret_cast<const uint32_t*>(row + 4 * lane);
+        q = *reinterpret_cast<const uint32_t*>(row + qlo);
       }
       // qh bytes h0 (fields of columns 0-3), h1 (4-7) as [h0, h0, h1, h1]
-      const uint32_t hh = __byte_perm(ld_u16(row + 128 + 2 * lane), 0u, 0x1100u);
+      const uint32_t hh = __byte_perm(ld_u16(row + qho), 0u, 0x1100u);
       // high bits of column 2j: field 2j -> bits 4-5 of byte j; column 2j+1: field 2j+1
       ue[r] = (q & 0x0f0f0f0fu) | ((hh << 4) & 0x00300030u) | (hh & 0x30003000u);
       uo[r] = ((q >> 4) & 0x0f0f0f0fu) | ((hh << 2) & 0x00300030u) | ((hh >> 2) & 0x30003000u);
@@ -252,19 +351,18 @@ template <> struct Producer<kQ6_K> {
   }
 };
 
-// Q8_0 (GGUF 34-byte block, fp16 scale): the tile's 256 columns are 8 blocks; lane l's
-// 8 values are bytes 8(l & 3)..+7 of block l >> 2, 2 bytes off a 4-byte boundary for
-// even blocks.
+// Q8_0 (GGUF 34-byte block, fp16 scale): the tile's 256 columns are 8 blocks; column
+// 128r + 8lc + i is byte 8(lc & 3) + i of block 4r + (lc >> 2), 2 bytes off a 4-byte
+// boundary for even blocks.
 template <> struct Producer<kQ8_0> {
   static constexpr int kPitch = 272;
-  static constexpr int kTableBytes = 0;
-  __device__ __forceinline__ static void table(const uint8_t*, int, uint8_t*) {}
+  __device__ __forceinline__ static void table(const uint8_t*, int, int, uint8_t*) {}
   float2 d[4];
   uint32_t w[8][2];
   template <bool>
-  __device__ __forceinline__ void load(const uint8_t* rows, int lane, const uint8_t*) {
-    const int boff = 34 * (lane >> 2);
-    const int a = boff + 2 + 8 * (lane & 3);
+  __device__ __forceinline__ void load(const uint8_t* rows, const Lane& ln, const uint8_t*) {
+    const int boff = 34 * (4 * ln.rank + (ln.lc >> 2));
+    const int a = boff + 2 + 8 * (ln.lc & 3);
     const int base = a & ~3;
     const uint32_t sel = (a & 2) ? 0x5432u : 0x3210u;
     float dr[8];
@@ -290,9 +388,9 @@ template <> struct Producer<kQ8_0> {
   }
 };
 
-// Value I of lane l (column 8l + I of the tile) goes to B row 8l + ((I + l) & 7): the 8
-// lanes of each 16-byte store phase then hit 8 different swizzle chunks.  The epilogue
-// undoes this rotation inside each group of 8 accumulator columns.
+// Value I of column group lc goes to B row 8lc + ((I + lc) & 7): the 8 lanes of each
+// 16-byte store phase then hit 8 different swizzle chunks.  The epilogue undoes this
+// rotation inside each group of 8 accumulator columns.
 template <int QT, int I>
 __device__ __forceinline__ void store_column(const Producer<QT>& pr, uint8_t* bt, const uint32_t (&off)[8]) {
   const uint4 chunk = make_uint4(pr.template pair<I>(0), pr.template pair<I>(1),
@@ -311,61 +409,62 @@ __device__ __forceinline__ void store_all(const Producer<QT>& pr, uint8_t* bt, c
   store_column<QT, 7>(pr, bt, off);
 }
 
-struct Bars {
-  uint64_t full_load[kLoadStages], empty_load[kLoadStages];
-  uint64_t full_b[kBStages], empty_b[kBStages];
-  uint64_t acc_full;
-  uint32_t tmem_base;
-  int abort;
-};
-
 template <int QT, bool BF16_OUT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
-            const uint8_t* __restrict__ w, void* __restrict__ c, int M, int K, int N, int64_t RB) {
+            void* __restrict__ c, int M, int K, int N) {
   using L = Smem<QT>;
   using R = Raw<QT>;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned (128-byte swizzle atoms); derived from the array so that the
-  // compiler keeps shared-memory addressing
+  // compiler keeps shared-memory addressing.  Both CTAs get the same offsets, which the
+  // pair MMA relies on.
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   Bars& bars = *reinterpret_cast<Bars*>(smem + L::kBarOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_tile = blockIdx.x, m_tile = blockIdx.y;
-  const int m0 = m_tile * BM;
+  const uint32_t rank = cluster_rank();
+  const int n_tile = blockIdx.x >> 1;
+  const int m0 = blockIdx.y * BMP;
   const int nk = (K + BK - 1) / BK;
+  const bool two_acc = m0 + 256 < M;  // pair rows 256..511 hold data
 
-  auto a_box = [&](int s, int h) { return smem + L::kLoadOff + s * L::kStageBytes + h * kABoxBytes; };
-  auto raw_stage = [&](int s) { return smem + L::kLoadOff + s * L::kStageBytes + 2 * kABoxBytes; };
+  auto a_box = [&](int s, int h) { return smem + L::kAOff + (2 * s + h) * kABoxBytes; };
+  auto raw_stage = [&](int q) { return smem + L::kRawOff + q * R::kSlot; };
   auto b_stage = [&](int t) { return smem + L::kBOff + t * kBBytes; };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kLoadStages; ++s) {
-      mbar_init(smem_u32(&bars.full_load[s]), 1);
-      mbar_init(smem_u32(&bars.empty_load[s]), 1 + 8);  // MMA commit + 8 dequant warps
+    for (int s = 0; s < kAStages; ++s) {
+      mbar_init(smem_u32(&bars.full_a[s]), 1);   // leader: its expect_tx arrival
+      mbar_init(smem_u32(&bars.empty_a[s]), 1);  // MMA commit
+    }
+    for (int q = 0; q < kRStages; ++q) {
+      mbar_init(smem_u32(&bars.full_raw[q]), 1);
+      mbar_init(smem_u32(&bars.empty_raw[q]), 4);  // the 4 warps of one group
     }
     for (int t = 0; t < kBStages; ++t) {
-      mbar_init(smem_u32(&bars.full_b[t]), 8);
-      mbar_init(smem_u32(&bars.empty_b[t]), 1);
+      mbar_init(smem_u32(&bars.full_b[t]), 8);   // leader: 4 warps x 2 CTAs
+      mbar_init(smem_u32(&bars.empty_b[t]), 1);  // MMA commit
     }
     mbar_init(smem_u32(&bars.acc_full), 1);
     bars.abort = 0;
     mbar_fence_init();
   }
-  if (warp == 1) {  // whole warp: allocate the 512 accumulator columns
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+  if (warp == 1) {  // whole warp, both CTAs: the 512 accumulator columns of the pair
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
                  ::"r"(smem_u32(&bars.tmem_base)), "r"(kTmemCols) : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers are initialised before any remote arrival
   tc_fence_after();
   const uint32_t tmem = bars.tmem_base;
   volatile int* abort_flag = &bars.abort;
+  const uint32_t peer_abort = mapa(smem_u32(&bars.abort), rank ^ 1u);
 
   auto give_up = [&]() {
     *abort_flag = 1;
+    st_cluster_u32(peer_abort, 1u);
     atomicOr(&g_gemm_status, kStatusTimeout);
   };
 
@@ -375,36 +474,45 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   tile_x &= ~15;
 
   if (warp == 0) {
-    // ------------------------------ TMA producer ------------------------------
+    // --------------------------- A producer (both CTAs) ---------------------------
     if (lane == 0) {
-      const uint32_t bytes = 2 * kABoxBytes + R::kBytes;
-      int it = 0;
-      for (; it < nk && !*abort_flag; ++it) {
-        const int s = it % kLoadStages;
-        const uint32_t parity = ((it / kLoadStages) & 1) ^ 1;
-        if (!mbar_wait_bounded(smem_u32(&bars.empty_load[s]), parity, kWaitBudgetCycles)) {
+      for (int it = 0; it < nk && !*abort_flag; ++it) {
+        const int s = it % kAStages;
+        if (!mbar_wait_bounded(smem_u32(&bars.empty_a[s]), ((it / kAStages) & 1) ^ 1, kWaitBudgetCycles)) {
           give_up();
           break;
         }
-        const uint32_t fb = smem_u32(&bars.full_load[s]);
-        mbar_arrive_expect_tx(fb, bytes);
-        tma_load_2d(smem_u32(a_box(s, 0)), &tmap_a, it * BK, m0, fb);
-        tma_load_2d(smem_u32(a_box(s, 1)), &tmap_a, it * BK, m0 + 128, fb);
-        tma_load_2d(smem_u32(raw_stage(s)), &tmap_w, tile_x / 2, it * BK, fb);
+        if (rank == 0) mbar_arrive_expect_tx(smem_u32(&bars.full_a[s]), 4 * kABoxBytes);
+        const uint32_t fa = mapa(smem_u32(&bars.full_a[s]), 0u);
+        tma_load_2d_pair(smem_u32(a_box(s, 0)), &tmap_a, it * BK, m0 + 128 * (int)rank, fa);
+        tma_load_2d_pair(smem_u32(a_box(s, 1)), &tmap_a, it * BK, m0 + 256 + 128 * (int)rank, fa);
       }
-      // drain: every issued stage must land before the CTA may exit
-      for (int j = (it > kLoadStages ? it - kLoadStages : 0); j < it; ++j)
-        mbar_wait_bounded(smem_u32(&bars.full_load[j % kLoadStages]), (j / kLoadStages) & 1,
-                          kWaitBudgetCycles);
     }
-  } else if (warp == 1) {
-    // ------------------------------ MMA issuer ------------------------------
+  } else if (warp == kRawWarp) {
+    // --------------------------- raw weight producer ---------------------------
     if (lane == 0) {
       int it = 0;
       for (; it < nk && !*abort_flag; ++it) {
-        const int s = it % kLoadStages, t = it % kBStages;
-        if (!mbar_wait_bounded(smem_u32(&bars.full_load[s]), (it / kLoadStages) & 1, kWaitBudgetCycles) ||
-            !mbar_wait_bounded(smem_u32(&bars.full_b[t]), (it / kBStages) & 1, kWaitBudgetCycles)) {
+        const int q = it % kRStages;
+        if (!mbar_wait_bounded(smem_u32(&bars.empty_raw[q]), ((it / kRStages) & 1) ^ 1, kWaitBudgetCycles)) {
+          give_up();
+          break;
+        }
+        const uint32_t fb = smem_u32(&bars.full_raw[q]);
+        mbar_arrive_expect_tx(fb, R::kBytes);
+        tma_load_2d(smem_u32(raw_stage(q)), &tmap_w, tile_x / 2, it * BK, fb);
+      }
+      // drain: every issued raw stage must land before the CTA may exit
+      for (int j = (it > kRStages ? it - kRStages : 0); j < it; ++j)
+        mbar_wait_bounded(smem_u32(&bars.full_raw[j % kRStages]), (j / kRStages) & 1, kWaitBudgetCycles);
+    }
+  } else if (warp == 1) {
+    // --------------------------- MMA issuer (leader) ---------------------------
+    if (rank == 0 && lane == 0) {
+      for (int it = 0; it < nk && !*abort_flag; ++it) {
+        const int s = it % kAStages, t = it % kBStages;
+        if (!mbar_wait_bounded(smem_u32(&bars.full_a[s]), (it / kAStages) & 1, kWaitBudgetCycles) ||
+            !mbar_wait_bounded_cluster(smem_u32(&bars.full_b[t]), (it / kBStages) & 1, kWaitBudgetCycles)) {
           give_up();
           break;
         }
@@ -416,45 +524,53 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         for (int kk = 0; kk < BK / 16; ++kk) {
           const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
           // +32 bytes per 16-element K step inside the 128-byte swizzle atom (+2 encoded)
-          umma_bf16(tmem, a0 + 2 * kk, b + 2 * kk, acc);
-          umma_bf16(tmem + 256, a1 + 2 * kk, b + 2 * kk, acc);
+          umma_bf16_pair(tmem, a0 + 2 * kk, b + 2 * kk, acc);
+          if (two_acc) umma_bf16_pair(tmem + 256, a1 + 2 * kk, b + 2 * kk, acc);
         }
-        umma_commit(smem_u32(&bars.empty_load[s]));
-        umma_commit(smem_u32(&bars.empty_b[t]));
+        umma_commit_pair(smem_u32(&bars.empty_a[s]));
+        umma_commit_pair(smem_u32(&bars.empty_b[t]));
       }
-      umma_commit(smem_u32(&bars.acc_full));  // arrives once every MMA issued so far is done
-      // tensor memory is freed below only after the MMAs writing it have finished
+      umma_commit_pair(smem_u32(&bars.acc_full));  // arrives once every MMA issued is done
+      // tensor memory is freed only after the MMAs writing it have finished
       if (!mbar_wait_bounded(smem_u32(&bars.acc_full), 0, kWaitBudgetCycles)) give_up();
     }
   } else {
     // ------------------------------ dequant warps ------------------------------
     using P = Producer<QT>;
-    const int kc = warp - 2;  // this warp's 8 K rows of each stage
-    uint8_t* tbl = smem + L::kTblOff + kc * 768;
-    uint32_t off[8];          // B-tile byte offset of value i's 16-byte chunk
+    const int dw = warp - 2;
+    const int grp = dw >> 2;  // group g dequantizes the K steps it = g, g + 2, ...
+    const int wq = dw & 3;    // this warp's 16 K rows of each step: 16 wq .. +15
+    const Lane ln{lane & 15, lane >> 4, (int)rank};
+    uint8_t* tbl = smem + L::kTblOff + dw * kTableBytes;
+    uint32_t off[8];  // B half-tile byte offset of value i's 16-byte chunk
+    {
+      const int kc = 2 * wq + ln.oct;  // 8-row K chunk within the step
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int rot = (i + lane) & 7;
-      off[i] = (uint32_t)((8 * lane + rot) * 128 + ((kc ^ rot) << 4));
+      for (int i = 0; i < 8; ++i) {
+        const int rot = (i + ln.lc) & 7;
+        off[i] = (uint32_t)((8 * ln.lc + rot) * 128 + ((kc ^ rot) << 4));
+      }
     }
     const bool mis = (raw_off & 2) != 0;
-    for (int it = 0; it < nk; ++it) {
+    const uint32_t full_b0 = mapa(smem_u32(&bars.full_b[0]), 0u);
+    for (int it = grp; it < nk; it += 2) {
       if (*abort_flag) break;
-      const int s = it % kLoadStages, t = it % kBStages;
-      if (!mbar_wait_bounded(smem_u32(&bars.full_load[s]), (it / kLoadStages) & 1, kWaitBudgetCycles)) {
+      const int q = it % kRStages, t = it % kBStages;
+      if (!mbar_wait_bounded(smem_u32(&bars.full_raw[q]), (it / kRStages) & 1, kWaitBudgetCycles)) {
         give_up();
         break;
       }
-      const uint8_t* rows = raw_stage(s) + 8 * kc * P::kPitch + raw_off;
-      if constexpr (P::kTableBytes > 0) {
-        P::table(rows, lane, tbl);
+      const uint8_t* wrows = raw_stage(q) + 16 * wq * P::kPitch + raw_off;
+      if constexpr (QT != kQ8_0) {
+        P::table(wrows, lane, (int)rank, tbl);
         __syncwarp();
       }
       P pr;
-      if (mis) pr.template load<true>(rows, lane, tbl);
-      else pr.template load<false>(rows, lane, tbl);
+      const uint8_t* rows = wrows + 8 * ln.oct * P::kPitch;
+      if (mis) pr.template load<true>(rows, ln, tbl);
+      else pr.template load<false>(rows, ln, tbl);
       __syncwarp();  // every lane holds its raw bytes and scales in registers
-      if (lane == 0) mbar_arrive(smem_u32(&bars.empty_load[s]));
+      if (lane == 0) mbar_arrive(smem_u32(&bars.empty_raw[q]));
       if (!mbar_wait_bounded(smem_u32(&bars.empty_b[t]), ((it / kBStages) & 1) ^ 1, kWaitBudgetCycles)) {
         give_up();
         break;
@@ -462,48 +578,53 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       store_all<QT>(pr, b_stage(t), off);
       fence_proxy_async_smem();  // make the generic stores visible to the tensor core
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&bars.full_b[t]));
+      if (lane == 0) mbar_arrive_cluster(full_b0 + 8u * (uint32_t)t);
     }
 
     // ------------------------------ epilogue ------------------------------
     const bool ok = !*abort_flag &&
                     mbar_wait_bounded(smem_u32(&bars.acc_full), 0, kWaitBudgetCycles);
     if (!ok) {
-      if (lane == 0) give_up();
+      if (lane == 0 && !*abort_flag) give_up();
     } else {
       tc_fence_after();
-      const int quarter = warp & 3;             // TMEM lanes 32*quarter .. +31
-      const int half = (warp - 2) >> 2;         // accumulator 0 (warps 2-5) or 1 (warps 6-9)
-      const int row = m0 + half * 128 + quarter * 32 + lane;
+      // 8 warps = 4 TMEM lane quarters x 2 accumulators; a warp may only read the lane
+      // quarter warp % 4
+      const int quarter = warp & 3;
+      const int half = dw >> 2;  // accumulator 0 (pair rows 128r..) or 1 (256 + 128r..)
+      const int row = m0 + half * 256 + (int)rank * 128 + quarter * 32 + lane;
       const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * 256);
-      // accumulator column 8L + p holds tile column 8L + ((p - L) & 7) (the producer's
-      // rotation); with 64 columns per step, L & 7 is 4h + g for group g of half h
+      if (half == 0 || two_acc) {
+        // accumulator column 8L + p holds tile column 8L + ((p - L) & 7) (the producer's
+        // rotation, L & 7 = lc & 7); with 64 columns per step L & 7 is 4h + g for group g
+        // of half-step h
 #pragma unroll 1
-      for (int cb = 0; cb < BN; cb += 64) {
+        for (int cb = 0; cb < BN; cb += 64) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint32_t r[32], o[32];
-          tmem_ld32(tbase + cb + 32 * h, r);
+          for (int h = 0; h < 2; ++h) {
+            uint32_t r[32], o[32];
+            tmem_ld32(tbase + cb + 32 * h, r);
 #pragma unroll
-          for (int g = 0; g < 4; ++g)
+            for (int g = 0; g < 4; ++g)
 #pragma unroll
-            for (int q = 0; q < 8; ++q) o[8 * g + q] = r[8 * g + ((q + 4 * h + g) & 7)];
-          if (row < M) {
-            const int64_t off = (int64_t)row * N + (int64_t)n_tile * BN + cb + 32 * h;
-            if constexpr (BF16_OUT) {
-              uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(c) + off);
+              for (int qq = 0; qq < 8; ++qq) o[8 * g + qq] = r[8 * g + ((qq + 4 * h + g) & 7)];
+            if (row < M) {
+              const int64_t off64 = (int64_t)row * N + (int64_t)n_tile * BN + cb + 32 * h;
+              if constexpr (BF16_OUT) {
+                uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(c) + off64);
 #pragma unroll
-              for (int q = 0; q < 4; ++q)
-                dst[q] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * q]), __uint_as_float(o[8 * q + 1])),
-                                    pack_bf16x2(__uint_as_float(o[8 * q + 2]), __uint_as_float(o[8 * q + 3])),
-                                    pack_bf16x2(__uint_as_float(o[8 * q + 4]), __uint_as_float(o[8 * q + 5])),
-                                    pack_bf16x2(__uint_as_float(o[8 * q + 6]), __uint_as_float(o[8 * q + 7])));
-            } else {
-              float4* dst = reinterpret_cast<float4*>(static_cast<float*>(c) + off);
+                for (int x = 0; x < 4; ++x)
+                  dst[x] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * x]), __uint_as_float(o[8 * x + 1])),
+                                      pack_bf16x2(__uint_as_float(o[8 * x + 2]), __uint_as_float(o[8 * x + 3])),
+                                      pack_bf16x2(__uint_as_float(o[8 * x + 4]), __uint_as_float(o[8 * x + 5])),
+                                      pack_bf16x2(__uint_as_float(o[8 * x + 6]), __uint_as_float(o[8 * x + 7])));
+              } else {
+                float4* dst = reinterpret_cast<float4*>(static_cast<float*>(c) + off64);
 #pragma unroll
-              for (int q = 0; q < 8; ++q)
-                dst[q] = make_float4(__uint_as_float(o[4 * q]), __uint_as_float(o[4 * q + 1]),
-                                     __uint_as_float(o[4 * q + 2]), __uint_as_float(o[4 * q + 3]));
+                for (int x = 0; x < 8; ++x)
+                  dst[x] = make_float4(__uint_as_float(o[4 * x]), __uint_as_float(o[4 * x + 1]),
+                                       __uint_as_float(o[4 * x + 2]), __uint_as_float(o[4 * x + 3]));
+              }
             }
           }
         }
@@ -511,11 +632,19 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     }
   }
 
+  __syncwarp();
   tc_fence_before();
-  __syncthreads();
+  // warp-uniform decision: the cluster barrier below must be reached convergently
+  if (__shfl_sync(0xffffffffu, *abort_flag, 0)) {
+    // A load this CTA issued reports to the leader's barrier, which may never complete
+    // after an abort; give such loads time to land before the shared memory is released.
+    for (int i = 0; i < 64; ++i) __nanosleep(1000);
+  }
+  __syncwarp();
+  cluster_sync_all();  // neither CTA frees TMEM or exits while the pair's MMAs may run
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
                  : "memory");
   }
 }
@@ -582,9 +711,9 @@ static cudaError_t launch_gemm_t(const void* a, const void* w, void* c, int64_t 
     if (e != cudaSuccess) return e;
     if (dev < 32) configured |= (1u << dev);
   }
-  const dim3 grid((unsigned)(N / BN), (unsigned)((M + BM - 1) / BM), 1);
-  kern<<<grid, kThreads, L::kAlloc, st>>>(ma, mw, static_cast<const uint8_t*>(w), c, (int)M, (int)K,
-                                          (int)N, RB);
+  // two CTAs (one cluster) per 512 x 256 tile of C
+  const dim3 grid((unsigned)(2 * (N / BN)), (unsigned)((M + BMP - 1) / BMP), 1);
+  kern<<<grid, kThreads, L::kAlloc, st>>>(ma, mw, c, (int)M, (int)K, (int)N);
   return cudaGetLastError();
 }
 
