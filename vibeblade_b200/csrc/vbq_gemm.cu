@@ -14,14 +14,14 @@
 // weight is written to shared memory once and read once per pair.  Per 64-deep K step:
 //   * warp 0 (one lane) TMA-loads the CTA's two 128 x 64 A boxes (128-byte swizzle); the
 //     bytes are reported to the leader's barrier (3-deep ring, freed by the MMAs);
-//   * warp 10 (one lane) TMA-loads the raw quant bytes of the 64 W rows into a 4-deep
+//   * warp 18 (one lane) TMA-loads the raw quant bytes of the 64 W rows into a 4-deep
 //     ring that the dequant warps free as soon as the bytes are in registers;
-//   * warps 2-9 dequantize the raw bytes to bf16 into the K-major, 128-byte swizzled B
-//     half-tile (3-deep ring): warps 2-5 take the even K steps, warps 6-9 the odd ones,
-//     each warp 16 K rows x 128 columns; they arrive on the leader's B barrier;
+//   * warps 2-17 dequantize the raw bytes to bf16 into the K-major, 128-byte swizzled B
+//     half-tile (3-deep ring): warps 2-9 take the even K steps, warps 10-17 the odd ones,
+//     each warp 8 K rows x 128 columns; they arrive on the leader's B barrier;
 //   * the leader's warp 1 (one lane) issues 2 x 4 MMAs and commits them to barriers in
 //     both CTAs.
-// After the last K step warps 2-9 of each CTA read its accumulators out of tensor memory
+// After the last K step warps 2-17 of each CTA read its accumulators out of tensor memory
 // (tcgen05.ld) and store C.  Every mbarrier wait is bounded; a wait that gives up records
 // kStatusTimeout in the device status word, raises the abort flag of both CTAs, and the
 // pair drains and exits.  No TMA load here uses cluster multicast.
@@ -41,13 +41,13 @@ namespace gemm {
 
 constexpr int BMP = 512, BN = 256, BK = 64;  // pair tile rows, tile columns, K step
 constexpr int kHalfN = BN / 2;               // columns dequantized per CTA
-constexpr int kDeqWarps = 8;                 // two groups of 4, alternating K steps
+constexpr int kDeqWarps = 16;                // two groups of 8, alternating K steps
 constexpr int kThreads = 32 * (3 + kDeqWarps);  // + A TMA, MMA, raw TMA warps
 constexpr int kRawWarp = 2 + kDeqWarps;
 constexpr int kAStages = 3, kRStages = 4, kBStages = 3;
 constexpr int kABoxBytes = 128 * BK * 2;      // one 128 x 64 bf16 box
 constexpr int kBBytes = kHalfN * BK * 2;      // 128 x 64 bf16 B half-tile
-constexpr int kTableBytes = 768;              // per dequant warp
+constexpr int kTableBytes = 384;              // per dequant warp
 constexpr int kTmemCols = 512;
 
 template <int QT> struct Raw {
@@ -200,9 +200,8 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 }
 
 // ---- dequantization: one thread = 8 K rows x 8 consecutive columns ---------------------
-// In CTA r, dequant warp q (0..3 within its group) owns K rows 16q..16q+15 of a stage;
-// lane l takes the 8 rows 16q + 8(l >> 4) .. +7 and the tile columns 128r + 8(l & 15) ..
-// +7.  Every weight value is produced as the reference's fp32 value (one rounding per
+// In CTA r, dequant warp q (0..7 within its group) owns K rows 8q..8q+7 of a stage and
+// the CTA's 128 tile columns; each lane 4 rows x 8 columns.  Every weight value is produced as the reference's fp32 value (one rounding per
 // product and per difference, cpp/src/dequant.cpp:268-301, :359-402 and the Q8_0 block of
 // cpp/src/cuda_kernels.cu:718-735), then rounded once to bf16.
 //
@@ -212,8 +211,8 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 // dl*q rounded once (2^23 dl is exact).  The result equals the reference's value up to
 // the sign of an exact zero, for every finite block scale.
 //
-// Two K rows of one column form one packed bf16x2 word; the four words of a column make
-// the 16-byte chunk the MMA reads.
+// Two K rows of one column form one packed bf16x2 word; a lane's two words for a column
+// are half of the 16-byte chunk (8 K rows) the MMA reads.
 constexpr float kTwo23 = 8388608.0f;      // 2^23
 constexpr float kOneHalf23 = 12582912.0f; // 1.5 * 2^23: magic 0x4b4000xx = 1.5*2^23 + xx
 constexpr uint32_t kMagic23 = 0x4b000000u, kMagic15 = 0x4b400000u;
@@ -224,27 +223,31 @@ __device__ __forceinline__ float magic_byte(uint32_t w, uint32_t k) {
   return __uint_as_float(__byte_perm(w, k, 0x7640u | (uint32_t)I));
 }
 
-// Where a thread's rows and columns are.  Scale tables are indexed by the warp's row pair
-// p = 4*oct + pp, stored at slot 2*pp + oct so that the two octets of a warp read
-// adjacent entries.
+// Where a thread's rows and columns are: lane l takes column group lc = l >> 1 (tile
+// columns 128*rank + 8*lc .. +7) and row quad rq = l & 1 (rows 4rq .. 4rq+3 of its warp's
+// 8 rows).  Adjacent lanes differ in rq, so each half-warp's 8-byte stores cover 8
+// column groups x both row quads: 16 distinct 8-byte slots, no bank conflict.  Scale
+// tables are indexed by the warp's row pair p = 2*rq + pp, stored at slot 2*pp + rq so
+// that one load instruction reads adjacent entries.
 struct Lane {
-  int lc;    // column group: tile columns 128*rank + 8*lc .. +7
-  int oct;   // row octet of the warp's 16 rows
+  int lc;    // column group
+  int rq;    // row quad
   int rank;  // CTA rank in the pair: which half of the tile's columns
 };
-__device__ __forceinline__ int pair_slot(int p) { return 2 * (p & 3) + (p >> 2); }
+__device__ __forceinline__ int pair_slot(int p) { return 2 * (p & 1) + (p >> 1); }
 
 template <int QT> struct Producer;
 
 // Q4_K: the tile's 256 columns are one block; this CTA's half covers sub-blocks
 // 4r .. 4r+3, lane l's columns lie in sub-block 4r + (lc >> 2).  The (dl, ml) pair of each
-// of the warp's 16 rows x 4 sub-blocks is computed once per stage into a per-warp table.
+// of the warp's 8 rows x 4 sub-blocks is computed once per stage into a per-warp table.
 template <> struct Producer<kQ4_K> {
   static constexpr int kPitch = 144;
-  // table: float4 (dl_r, dl_r+1, -2^23 dl_r, -2^23 dl_r+1) [8 row pairs][4 sub-blocks],
-  // then float2 (-ml_r, -ml_r+1) [8][4]
+  // table: float4 (dl_r, dl_r+1, -2^23 dl_r, -2^23 dl_r+1) [4 row pairs][4 sub-blocks],
+  // then float2 (-ml_r, -ml_r+1) [4][4] at byte 256
   __device__ __forceinline__ static void table(const uint8_t* wrows, int lane, int rank,
                                                uint8_t* tbl) {
+    if (lane >= 16) return;
     const int sbl = lane & 3, p = lane >> 2;
     const Q4kScaleRecipe rec(4 * rank + sbl);
     float dl[2], ml[2];
@@ -259,27 +262,27 @@ template <> struct Producer<kQ4_K> {
     const int e = pair_slot(p) * 4 + sbl;
     reinterpret_cast<float4*>(tbl)[e] =
         make_float4(dl[0], dl[1], __fmul_rn(-kTwo23, dl[0]), __fmul_rn(-kTwo23, dl[1]));
-    reinterpret_cast<float2*>(tbl + 512)[e] = make_float2(-ml[0], -ml[1]);
+    reinterpret_cast<float2*>(tbl + 256)[e] = make_float2(-ml[0], -ml[1]);
   }
-  float2 dl[4], c[4], nm[4];
-  uint32_t w[8][2];
+  float2 dl[2], c[2], nm[2];
+  uint32_t w[4][2];
   template <bool>
   __device__ __forceinline__ void load(const uint8_t* rows, const Lane& ln, const uint8_t* tbl) {
     const int sbl = ln.lc >> 2;
 #pragma unroll
-    for (int pp = 0; pp < 4; ++pp) {
-      const int e = (2 * pp + ln.oct) * 4 + sbl;
+    for (int pp = 0; pp < 2; ++pp) {
+      const int e = (2 * pp + ln.rq) * 4 + sbl;
       const float4 a = reinterpret_cast<const float4*>(tbl)[e];
       dl[pp] = make_float2(a.x, a.y);
       c[pp] = make_float2(a.z, a.w);
-      nm[pp] = reinterpret_cast<const float2*>(tbl + 512)[e];
+      nm[pp] = reinterpret_cast<const float2*>(tbl + 256)[e];
     }
     // column 128r + 8lc + i: 64-value group g = 2r + (lc >> 3), low nibbles when the
     // column's offset in the group is below 32
     const int off = 16 + 32 * (2 * ln.rank + (ln.lc >> 3)) + 8 * (ln.lc & 3);
     const uint32_t hs = (uint32_t)((ln.lc >> 2) & 1) * 4u;
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
+    for (int r = 0; r < 4; ++r) {
       const uint2 q = *reinterpret_cast<const uint2*>(rows + r * kPitch + off);
       w[r][0] = (q.x >> hs) & 0x0f0f0f0fu;
       w[r][1] = (q.y >> hs) & 0x0f0f0f0fu;
@@ -299,32 +302,28 @@ template <> struct Producer<kQ4_K> {
 // columns in one word, odd columns in another.
 template <> struct Producer<kQ6_K> {
   static constexpr int kPitch = 224;
-  // table: float2 (d*sc_r, d*sc_r+1) [8 row pairs][8 scales]
+  // table: float2 (d*sc_r, d*sc_r+1) [4 row pairs][8 scales]
   __device__ __forceinline__ static void table(const uint8_t* wrows, int lane, int rank,
                                                uint8_t* tbl) {
-    const int sl = lane & 7;
+    const int sl = lane & 7, p = lane >> 3;
+    float ds[2];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int p = (lane >> 3) + 4 * j;
-      float ds[2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint8_t* row = wrows + (2 * p + h) * kPitch;
-        ds[h] = __fmul_rn(f16_ref(ld_u16(row + 208)), (float)(int8_t)row[192 + 8 * rank + sl]);
-      }
-      reinterpret_cast<float2*>(tbl)[pair_slot(p) * 8 + sl] = make_float2(ds[0], ds[1]);
+    for (int h = 0; h < 2; ++h) {
+      const uint8_t* row = wrows + (2 * p + h) * kPitch;
+      ds[h] = __fmul_rn(f16_ref(ld_u16(row + 208)), (float)(int8_t)row[192 + 8 * rank + sl]);
     }
+    reinterpret_cast<float2*>(tbl)[pair_slot(p) * 8 + sl] = make_float2(ds[0], ds[1]);
   }
-  float2 ds[4];
-  uint32_t ue[8], uo[8];
+  float2 ds[2];
+  uint32_t ue[4], uo[4];
   template <bool kMisaligned>  // the block starts 2 mod 4 within the staged row
   __device__ __forceinline__ void load(const uint8_t* rows, const Lane& ln, const uint8_t* tbl) {
 #pragma unroll
-    for (int pp = 0; pp < 4; ++pp)
-      ds[pp] = reinterpret_cast<const float2*>(tbl)[(2 * pp + ln.oct) * 8 + (ln.lc >> 1)];
+    for (int pp = 0; pp < 2; ++pp)
+      ds[pp] = reinterpret_cast<const float2*>(tbl)[(2 * pp + ln.rq) * 8 + (ln.lc >> 1)];
     const int qlo = 64 * ln.rank + 4 * ln.lc, qho = 128 + 32 * ln.rank + 2 * ln.lc;
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
+    for (int r = 0; r < 4; ++r) {
       const uint8_t* row = rows + r * kPitch;
       uint32_t q;
       if constexpr (kMisaligned) {
@@ -357,17 +356,17 @@ template <> struct Producer<kQ6_K> {
 template <> struct Producer<kQ8_0> {
   static constexpr int kPitch = 272;
   __device__ __forceinline__ static void table(const uint8_t*, int, int, uint8_t*) {}
-  float2 d[4];
-  uint32_t w[8][2];
+  float2 d[2];
+  uint32_t w[4][2];
   template <bool>
   __device__ __forceinline__ void load(const uint8_t* rows, const Lane& ln, const uint8_t*) {
     const int boff = 34 * (4 * ln.rank + (ln.lc >> 2));
     const int a = boff + 2 + 8 * (ln.lc & 3);
     const int base = a & ~3;
     const uint32_t sel = (a & 2) ? 0x5432u : 0x3210u;
-    float dr[8];
+    float dr[4];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
+    for (int r = 0; r < 4; ++r) {
       const uint8_t* row = rows + r * kPitch;
       const uint32_t* x = reinterpret_cast<const uint32_t*>(row + base);
       const uint32_t x0 = x[0], x1 = x[1], x2 = x[2];
@@ -376,7 +375,7 @@ template <> struct Producer<kQ8_0> {
       dr[r] = f16_ieee(ld_u16(row + boff));
     }
 #pragma unroll
-    for (int p = 0; p < 4; ++p) d[p] = make_float2(dr[2 * p], dr[2 * p + 1]);
+    for (int p = 0; p < 2; ++p) d[p] = make_float2(dr[2 * p], dr[2 * p + 1]);
   }
   template <int I>
   __device__ __forceinline__ uint32_t pair(int p) const {
@@ -388,14 +387,12 @@ template <> struct Producer<kQ8_0> {
   }
 };
 
-// Value I of column group lc goes to B row 8lc + ((I + lc) & 7): the 8 lanes of each
-// 16-byte store phase then hit 8 different swizzle chunks.  The epilogue undoes this
-// rotation inside each group of 8 accumulator columns.
+// Value I of column group lc goes to B row 8lc + ((I + lc) & 7), in the 8-byte half of
+// its 16-byte chunk that holds the lane's row quad.  The epilogue undoes the rotation
+// inside each group of 8 accumulator columns.
 template <int QT, int I>
 __device__ __forceinline__ void store_column(const Producer<QT>& pr, uint8_t* bt, const uint32_t (&off)[8]) {
-  const uint4 chunk = make_uint4(pr.template pair<I>(0), pr.template pair<I>(1),
-                                 pr.template pair<I>(2), pr.template pair<I>(3));
-  *reinterpret_cast<uint4*>(bt + off[I]) = chunk;
+  *reinterpret_cast<uint2*>(bt + off[I]) = make_uint2(pr.template pair<I>(0), pr.template pair<I>(1));
 }
 template <int QT>
 __device__ __forceinline__ void store_all(const Producer<QT>& pr, uint8_t* bt, const uint32_t (&off)[8]) {
@@ -440,10 +437,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     }
     for (int q = 0; q < kRStages; ++q) {
       mbar_init(smem_u32(&bars.full_raw[q]), 1);
-      mbar_init(smem_u32(&bars.empty_raw[q]), 4);  // the 4 warps of one group
+      mbar_init(smem_u32(&bars.empty_raw[q]), kDeqWarps / 2);  // the warps of one group
     }
     for (int t = 0; t < kBStages; ++t) {
-      mbar_init(smem_u32(&bars.full_b[t]), 8);   // leader: 4 warps x 2 CTAs
+      mbar_init(smem_u32(&bars.full_b[t]), kDeqWarps);  // leader: one group x 2 CTAs
       mbar_init(smem_u32(&bars.empty_b[t]), 1);  // MMA commit
     }
     mbar_init(smem_u32(&bars.acc_full), 1);
@@ -538,18 +535,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     // ------------------------------ dequant warps ------------------------------
     using P = Producer<QT>;
     const int dw = warp - 2;
-    const int grp = dw >> 2;  // group g dequantizes the K steps it = g, g + 2, ...
-    const int wq = dw & 3;    // this warp's 16 K rows of each step: 16 wq .. +15
-    const Lane ln{lane & 15, lane >> 4, (int)rank};
+    const int grp = dw >> 3;  // group g dequantizes the K steps it = g, g + 2, ...
+    const int wq = dw & 7;    // this warp's 8 K rows of each step: 8 wq .. +7
+    const Lane ln{lane >> 1, lane & 1, (int)rank};
     uint8_t* tbl = smem + L::kTblOff + dw * kTableBytes;
-    uint32_t off[8];  // B half-tile byte offset of value i's 16-byte chunk
-    {
-      const int kc = 2 * wq + ln.oct;  // 8-row K chunk within the step
+    uint32_t off[8];  // B half-tile byte offset of value i's 8-byte half-chunk
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int rot = (i + ln.lc) & 7;
-        off[i] = (uint32_t)((8 * ln.lc + rot) * 128 + ((kc ^ rot) << 4));
-      }
+    for (int i = 0; i < 8; ++i) {
+      const int rot = (i + ln.lc) & 7;  // wq is the 8-row K chunk within the step
+      off[i] = (uint32_t)((8 * ln.lc + rot) * 128 + ((wq ^ rot) << 4) + 8 * ln.rq);
     }
     const bool mis = (raw_off & 2) != 0;
     const uint32_t full_b0 = mapa(smem_u32(&bars.full_b[0]), 0u);
@@ -560,13 +554,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         give_up();
         break;
       }
-      const uint8_t* wrows = raw_stage(q) + 16 * wq * P::kPitch + raw_off;
+      const uint8_t* wrows = raw_stage(q) + 8 * wq * P::kPitch + raw_off;
       if constexpr (QT != kQ8_0) {
         P::table(wrows, lane, (int)rank, tbl);
         __syncwarp();
       }
       P pr;
-      const uint8_t* rows = wrows + 8 * ln.oct * P::kPitch;
+      const uint8_t* rows = wrows + 4 * ln.rq * P::kPitch;
       if (mis) pr.template load<true>(rows, ln, tbl);
       else pr.template load<false>(rows, ln, tbl);
       __syncwarp();  // every lane holds its raw bytes and scales in registers
@@ -578,7 +572,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       store_all<QT>(pr, b_stage(t), off);
       fence_proxy_async_smem();  // make the generic stores visible to the tensor core
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(full_b0 + 8u * (uint32_t)t);
+      if (lane == 0) {
+        if (rank == 0) mbar_arrive(smem_u32(&bars.full_b[t]));
+        else mbar_arrive_cluster(full_b0 + 8u * (uint32_t)t);
+      }
     }
 
     // ------------------------------ epilogue ------------------------------
@@ -588,10 +585,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       if (lane == 0 && !*abort_flag) give_up();
     } else {
       tc_fence_after();
-      // 8 warps = 4 TMEM lane quarters x 2 accumulators; a warp may only read the lane
-      // quarter warp % 4
+      // 16 warps = 4 TMEM lane quarters x 2 accumulators x 2 column halves; a warp may
+      // only read the lane quarter warp % 4
       const int quarter = warp & 3;
-      const int half = dw >> 2;  // accumulator 0 (pair rows 128r..) or 1 (256 + 128r..)
+      const int half = (dw >> 2) & 1;  // accumulator 0 (pair rows 128r..) or 1 (256 + 128r..)
+      const int col0 = (dw >> 3) * (BN / 2);
       const int row = m0 + half * 256 + (int)rank * 128 + quarter * 32 + lane;
       const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * 256);
       if (half == 0 || two_acc) {
@@ -599,7 +597,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         // rotation, L & 7 = lc & 7); with 64 columns per step L & 7 is 4h + g for group g
         // of half-step h
 #pragma unroll 1
-        for (int cb = 0; cb < BN; cb += 64) {
+        for (int cb = col0; cb < col0 + BN / 2; cb += 64) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             uint32_t r[32], o[32];
