@@ -133,6 +133,54 @@ int vbq_gemv_static_scratch(const float* x, const void* w, float* y, int64_t K, 
                             int32_t type, int32_t batch, void* stream);
 
 /*
+ * Grouped quantized-weight GEMM over weight slabs (the MoE expert GEMM; the reference's
+ * slab loop is cpp/src/fast_model.cpp:844-903, vibeblade/moe.py:458-470).  The rows of A
+ * (bf16 [rows, K]) and C ([rows, N], c_dtype as vbq_gemm) are split into n_seg
+ * consecutive segments by seg (DEVICE int32 [n_seg + 1], nondecreasing, seg[n_seg] <=
+ * rows); segment s is multiplied by the K x N slab at w + s * slab_bytes.  slab_bytes is
+ * the per-expert stride, normally tensor_nbytes(type, K, N) = K * row_bytes, a multiple
+ * of 16 (the reference's own stride, ggml_type_size per element at :852-854, is not
+ * used).  Rows outside every segment are left untouched.  Same shape rules as vbq_gemm.
+ * The segments are read on the device, so the call never synchronises.
+ */
+int vbq_gemm_grouped(const void* a, const void* w, int64_t slab_bytes, void* c, int64_t rows,
+                     int64_t K, int64_t N, int32_t type, int32_t c_dtype, const int32_t* seg,
+                     int32_t n_seg, void* stream);
+
+/*
+ * MoE routing (vibeblade/moe.py:170-206, ExpertRouter.route after its matmul; C++:
+ * softmax + top_k_select, cpp/src/fast_model.cpp:534-549, :861-872): for each of T tokens,
+ * softmax over the E logits (fp32 [T, E], clipped to +-50), the topk largest
+ * probabilities in descending order (ties to the lower expert index; the reference leaves
+ * the order of equal values unspecified), renormalised to sum 1.  idx int32 [T, topk],
+ * weight fp32 [T, topk], all device memory.  topk <= 8.
+ */
+int vbq_moe_route(const float* logits, int64_t T, int32_t E, int32_t topk, int32_t* idx,
+                  float* weight, void* stream);
+
+/* Workspace bytes vbq_moe_ffn needs for these sizes. */
+int vbq_moe_workspace_bytes(int64_t T, int64_t H, int64_t I, int32_t E, int32_t topk,
+                            size_t* bytes);
+
+/*
+ * MoE SwiGLU FFN (vibeblade/moe.py:407-505 moe_ffn_silu without a shared expert):
+ *     out[t] = sum over the token's topk experts e of
+ *              weight[t, e] * down_e( silu(gate_e x[t]) * up_e x[t] )
+ * x fp32 [T, H], logits fp32 [T, E] (router output), out fp32 [T, H].  w_gate / w_up hold
+ * E slabs of H x I weights, w_down E slabs of I x H, each in the block layout above and
+ * packed back to back (slab stride = tensor_nbytes).  The gate and up projections are
+ * clipped to +-65504 (NaN to 0) before SwiGLU and the output is sanitised the same way,
+ * as the reference does.  Activations enter the tensor cores as bf16 (x, and the SwiGLU
+ * product), accumulation is fp32.  workspace: device memory of vbq_moe_workspace_bytes(),
+ * 256-byte aligned; it needs no initialisation.  Shape rules: I and H multiples of 256
+ * (and of 2048 for Q6_K), E <= 4096, topk <= 8.
+ */
+int vbq_moe_ffn(const float* x, const float* logits, const void* w_gate, const void* w_up,
+                const void* w_down, float* out, int64_t T, int64_t H, int64_t I, int32_t E,
+                int32_t topk, int32_t type_gate, int32_t type_up, int32_t type_down,
+                void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Device-side status of the library's kernels on the current device: bit 0 set means a
  * bounded wait inside a kernel gave up (VBQ_ERR_TIMEOUT is returned then), which leaves
  * that call's outputs undefined and its scratch in need of re-zeroing.  Reads

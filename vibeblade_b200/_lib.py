@@ -41,6 +41,17 @@ SIGNATURES = {
                            C.c_int32, C.c_int32, C.c_void_p]),
     "vbq_gemv_static_scratch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64,
                                           C.c_int64, C.c_int32, C.c_int32, C.c_void_p]),
+    "vbq_gemm_grouped": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
+                                   C.c_int64, C.c_int64, C.c_int32, C.c_int32, C.c_void_p,
+                                   C.c_int32, C.c_void_p]),
+    "vbq_moe_route": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_void_p,
+                                C.c_void_p, C.c_void_p]),
+    "vbq_moe_workspace_bytes": (C.c_int, [C.c_int64, C.c_int64, C.c_int64, C.c_int32,
+                                          C.c_int32, C.POINTER(C.c_size_t)]),
+    "vbq_moe_ffn": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                              C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int32, C.c_int32,
+                              C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_size_t,
+                              C.c_void_p]),
 }
 
 _lock = threading.Lock()

@@ -248,3 +248,146 @@ extern "C" int vbq_gemv_static_scratch(const float* x, const void* w, float* y, 
   if (e != cudaSuccess) return cuda_fail(e, "vbq_gemv_static_scratch launch");
   return ok();
 }
+
+// ---------------------------------------------------------------------------------
+// Grouped GEMM over weight slabs, and the MoE FFN built on it.
+// ---------------------------------------------------------------------------------
+namespace {
+
+// Shape rules of the tcgen05 GEMM for one K x N weight slab; *rb gets the row bytes.
+int gemm_shape_checks(const char* who, int32_t type, int64_t K, int64_t N, int64_t* rb) {
+  const std::string w(who);
+  if (!supported(type)) return fail(VBQ_ERR_TYPE, w + ": unsupported type " + std::to_string(type));
+  if (K <= 0 || N <= 0) return fail(VBQ_ERR_SHAPE, w + ": K and N must be positive");
+  if (N % 256 != 0) return fail(VBQ_ERR_SHAPE, w + ": N must be a multiple of 256");
+  if (K % 8 != 0) return fail(VBQ_ERR_SHAPE, w + ": K must be a multiple of 8 (16-byte rows of A)");
+  if (K > (int64_t)INT32_MAX || N > (int64_t)INT32_MAX)
+    return fail(VBQ_ERR_SHAPE, w + ": sizes above 2^31 are not supported");
+  *rb = (N / block_values(type)) * block_bytes(type);
+  if (*rb % 16 != 0)
+    return fail(VBQ_ERR_UNSUPPORTED, w + ": weight rows must be a multiple of 16 bytes (Q6_K: N % 2048 == 0)");
+  return VBQ_OK;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// Workspace of vbq_moe_ffn, in order: routing (idx, weight), segments, entry rows, row
+// tokens, gathered activations (bf16), gate and up projections (bf16; SwiGLU overwrites
+// gate), down projection (fp32).
+struct MoeLayout {
+  size_t idx, weight, seg, pos, tok, a, g, u, y, total;
+};
+MoeLayout moe_layout(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k) {
+  MoeLayout l{};
+  const size_t R = (size_t)T * (size_t)k;
+  size_t o = 0;
+  l.idx = o;    o += align256(R * 4);
+  l.weight = o; o += align256(R * 4);
+  l.seg = o;    o += align256((size_t)(E + 1) * 4);
+  l.pos = o;    o += align256(R * 4);
+  l.tok = o;    o += align256(R * 4);
+  l.a = o;      o += align256(R * (size_t)H * 2);
+  l.g = o;      o += align256(R * (size_t)I * 2);
+  l.u = o;      o += align256(R * (size_t)I * 2);
+  l.y = o;      o += align256(R * (size_t)H * 4);
+  l.total = o;
+  return l;
+}
+
+}  // namespace
+
+extern "C" {
+
+int vbq_gemm_grouped(const void* a, const void* w, int64_t slab_bytes, void* c, int64_t rows,
+                     int64_t K, int64_t N, int32_t type, int32_t c_dtype, const int32_t* seg,
+                     int32_t n_seg, void* stream) {
+  int64_t rb = 0;
+  const int rc = gemm_shape_checks("vbq_gemm_grouped", type, K, N, &rb);
+  if (rc != VBQ_OK) return rc;
+  if (c_dtype != VBQ_DTYPE_F32 && c_dtype != VBQ_DTYPE_BF16)
+    return fail(VBQ_ERR_SHAPE, "vbq_gemm_grouped: c_dtype must be VBQ_DTYPE_F32 or VBQ_DTYPE_BF16");
+  if (rows < 0 || n_seg < 0) return fail(VBQ_ERR_SHAPE, "vbq_gemm_grouped: negative size");
+  if (rows > (int64_t)INT32_MAX) return fail(VBQ_ERR_SHAPE, "vbq_gemm_grouped: rows above 2^31");
+  if (rows == 0 || n_seg == 0) return ok();
+  if (!a || !w || !c || !seg) return fail(VBQ_ERR_NULL, "vbq_gemm_grouped: NULL pointer");
+  if (slab_bytes < K * rb || slab_bytes % 16 != 0)
+    return fail(VBQ_ERR_SHAPE, "vbq_gemm_grouped: slab_bytes must be >= K * row_bytes and a multiple of 16");
+  if (!aligned(a, 16) || !aligned(w, 16) || !aligned(c, 16))
+    return fail(VBQ_ERR_ALIGN, "vbq_gemm_grouped: a, w and c must be 16-byte aligned");
+  cudaError_t e = vbq::launch_gemm_grouped(type, a, w, c, rows, K, N, rb, c_dtype, slab_bytes, seg,
+                                           n_seg, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "vbq_gemm_grouped launch");
+  return ok();
+}
+
+int vbq_moe_route(const float* logits, int64_t T, int32_t E, int32_t topk, int32_t* idx,
+                  float* weight, void* stream) {
+  if (T < 0 || E <= 0 || topk < 1 || topk > 8 || topk > E || T > (int64_t)INT32_MAX)
+    return fail(VBQ_ERR_SHAPE, "vbq_moe_route: need T >= 0, 1 <= topk <= min(8, E)");
+  if (T == 0) return ok();
+  if (!logits || !idx || !weight) return fail(VBQ_ERR_NULL, "vbq_moe_route: NULL pointer");
+  cudaError_t e = vbq::launch_moe_route(logits, (int)T, E, topk, idx, weight,
+                                        static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "vbq_moe_route launch");
+  return ok();
+}
+
+int vbq_moe_workspace_bytes(int64_t T, int64_t H, int64_t I, int32_t E, int32_t topk,
+                            size_t* bytes) {
+  if (!bytes) return fail(VBQ_ERR_NULL, "vbq_moe_workspace_bytes: bytes is NULL");
+  if (T < 0 || H <= 0 || I <= 0 || E <= 0 || topk < 1 || topk > 8 || topk > E)
+    return fail(VBQ_ERR_SHAPE, "vbq_moe_workspace_bytes: bad sizes");
+  *bytes = moe_layout(T, H, I, E, topk).total;
+  return ok();
+}
+
+int vbq_moe_ffn(const float* x, const float* logits, const void* w_gate, const void* w_up,
+                const void* w_down, float* out, int64_t T, int64_t H, int64_t I, int32_t E,
+                int32_t topk, int32_t type_gate, int32_t type_up, int32_t type_down,
+                void* workspace, size_t workspace_bytes, void* stream) {
+  int64_t rb_g = 0, rb_u = 0, rb_d = 0;
+  int rc = gemm_shape_checks("vbq_moe_ffn (gate)", type_gate, H, I, &rb_g);
+  if (rc == VBQ_OK) rc = gemm_shape_checks("vbq_moe_ffn (up)", type_up, H, I, &rb_u);
+  if (rc == VBQ_OK) rc = gemm_shape_checks("vbq_moe_ffn (down)", type_down, I, H, &rb_d);
+  if (rc != VBQ_OK) return rc;
+  if (T < 0 || E <= 0 || E > 4096 || topk < 1 || topk > 8 || topk > E ||
+      T * topk > (int64_t)INT32_MAX)
+    return fail(VBQ_ERR_SHAPE, "vbq_moe_ffn: need T >= 0, 1 <= E <= 4096, 1 <= topk <= min(8, E)");
+  if (T == 0) return ok();
+  if (!x || !logits || !w_gate || !w_up || !w_down || !out || !workspace)
+    return fail(VBQ_ERR_NULL, "vbq_moe_ffn: NULL pointer");
+  const MoeLayout l = moe_layout(T, H, I, E, topk);
+  if (workspace_bytes < l.total)
+    return fail(VBQ_ERR_WORKSPACE, "vbq_moe_ffn: workspace needs " + std::to_string(l.total) + " bytes");
+  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(w_gate, 16) || !aligned(w_up, 16) ||
+      !aligned(w_down, 16) || !aligned(workspace, 256))
+    return fail(VBQ_ERR_ALIGN, "vbq_moe_ffn: x, out, weights 16-byte and workspace 256-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int32_t* idx = reinterpret_cast<int32_t*>(ws + l.idx);
+  float* wt = reinterpret_cast<float*>(ws + l.weight);
+  int32_t* seg = reinterpret_cast<int32_t*>(ws + l.seg);
+  int32_t* pos = reinterpret_cast<int32_t*>(ws + l.pos);
+  int32_t* tok = reinterpret_cast<int32_t*>(ws + l.tok);
+  const int64_t R = T * topk;
+  cudaError_t e = vbq::launch_moe_route(logits, (int)T, E, topk, idx, wt, st);
+  if (e == cudaSuccess) e = vbq::launch_moe_sort(idx, (int)T, E, topk, seg, pos, tok, st);
+  if (e == cudaSuccess) e = vbq::launch_moe_gather(x, tok, (int)R, (int)H, ws + l.a, st);
+  if (e == cudaSuccess)
+    e = vbq::launch_gemm_grouped(type_gate, ws + l.a, w_gate, ws + l.g, R, H, I, rb_g, VBQ_DTYPE_BF16,
+                                 H * rb_g, seg, E, st);
+  if (e == cudaSuccess)
+    e = vbq::launch_gemm_grouped(type_up, ws + l.a, w_up, ws + l.u, R, H, I, rb_u, VBQ_DTYPE_BF16,
+                                 H * rb_u, seg, E, st);
+  if (e == cudaSuccess) e = vbq::launch_swiglu(ws + l.g, ws + l.u, ws + l.g, R * I, st);
+  if (e == cudaSuccess)
+    e = vbq::launch_gemm_grouped(type_down, ws + l.g, w_down, ws + l.y, R, I, H, rb_d, VBQ_DTYPE_F32,
+                                 I * rb_d, seg, E, st);
+  if (e == cudaSuccess)
+    e = vbq::launch_moe_combine(reinterpret_cast<const float*>(ws + l.y), pos, wt, (int)T, topk,
+                                (int)H, out, st);
+  if (e != cudaSuccess) return cuda_fail(e, "vbq_moe_ffn launch");
+  return ok();
+}
+
+}  // extern "C"

@@ -146,6 +146,13 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
       : "memory");
 }
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
 // TMA tile load into this CTA's shared memory, bytes reported to a barrier of the CTA
 // pair (`bar` is a shared::cluster address); no multicast
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y,
@@ -406,10 +413,14 @@ __device__ __forceinline__ void store_all(const Producer<QT>& pr, uint8_t* bt, c
   store_column<QT, 7>(pr, bt, off);
 }
 
-template <int QT, bool BF16_OUT>
+// GROUPED: the rows of A and C are split into n_seg consecutive segments (seg[s] ..
+// seg[s+1], device memory), segment s multiplied by weight slab s (the third coordinate of
+// tmap_w).  Work item blockIdx.y walks the segments' 512-row tiles; items past the last
+// tile exit at once (both CTAs of a pair share blockIdx.y).
+template <int QT, bool BF16_OUT, bool GROUPED>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
-            void* __restrict__ c, int M, int K, int N) {
+            void* __restrict__ c, int M, int K, int N, const int* __restrict__ seg, int n_seg) {
   using L = Smem<QT>;
   using R = Raw<QT>;
   extern __shared__ uint8_t smem_raw[];
@@ -422,9 +433,26 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
   const int n_tile = blockIdx.x >> 1;
-  const int m0 = blockIdx.y * BMP;
+  int m0 = blockIdx.y * BMP, row_end = M, slab = 0;
+  if constexpr (GROUPED) {
+    int w = (int)blockIdx.y;
+    bool found = false;
+    for (int sidx = 0; sidx < n_seg && !found; ++sidx) {
+      const int a = seg[sidx], b = seg[sidx + 1];
+      const int tiles = b > a ? (b - a + BMP - 1) / BMP : 0;
+      if (w < tiles) {
+        m0 = a + w * BMP;
+        row_end = b;
+        slab = sidx;
+        found = true;
+      } else {
+        w -= tiles;
+      }
+    }
+    if (!found) return;  // before any barrier: the whole pair leaves together
+  }
   const int nk = (K + BK - 1) / BK;
-  const bool two_acc = m0 + 256 < M;  // pair rows 256..511 hold data
+  const bool two_acc = m0 + 256 < row_end;  // pair rows 256..511 hold data
 
   auto a_box = [&](int s, int h) { return smem + L::kAOff + (2 * s + h) * kABoxBytes; };
   auto raw_stage = [&](int q) { return smem + L::kRawOff + q * R::kSlot; };
@@ -497,7 +525,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         }
         const uint32_t fb = smem_u32(&bars.full_raw[q]);
         mbar_arrive_expect_tx(fb, R::kBytes);
-        tma_load_2d(smem_u32(raw_stage(q)), &tmap_w, tile_x / 2, it * BK, fb);
+        if constexpr (GROUPED) tma_load_3d(smem_u32(raw_stage(q)), &tmap_w, tile_x / 2, it * BK, slab, fb);
+        else tma_load_2d(smem_u32(raw_stage(q)), &tmap_w, tile_x / 2, it * BK, fb);
       }
       // drain: every issued raw stage must land before the CTA may exit
       for (int j = (it > kRStages ? it - kRStages : 0); j < it; ++j)
@@ -606,7 +635,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
             for (int g = 0; g < 4; ++g)
 #pragma unroll
               for (int qq = 0; qq < 8; ++qq) o[8 * g + qq] = r[8 * g + ((qq + 4 * h + g) & 7)];
-            if (row < M) {
+            if (row < row_end) {
               const int64_t off64 = (int64_t)row * N + (int64_t)n_tile * BN + cb + 32 * h;
               if constexpr (BF16_OUT) {
                 uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(c) + off64);
@@ -670,17 +699,21 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-template <int QT, bool BF16_OUT>
-static cudaError_t launch_gemm_t(const void* a, const void* w, void* c, int64_t M, int64_t K,
-                                 int64_t N, int64_t RB, cudaStream_t st) {
+// Plain GEMM: slab_bytes == 0, seg == nullptr, rows = M.  Grouped: `n_seg` slabs of
+// `slab_bytes` each starting at w, rows of A / C split by seg[0..n_seg] (device), `rows`
+// the total row count (seg[n_seg] at most).
+template <int QT, bool BF16_OUT, bool GROUPED>
+static cudaError_t launch_gemm_t(const void* a, const void* w, void* c, int64_t rows, int64_t K,
+                                 int64_t N, int64_t RB, int64_t slab_bytes, const int* seg,
+                                 int n_seg, cudaStream_t st) {
   using namespace gemm;
   using L = Smem<QT>;
   using R = Raw<QT>;
   auto enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
   CUtensorMap ma, mw;
-  {  // A: [M][K] bf16, boxes of 128 rows x 64 K, 128-byte swizzle
-    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+  {  // A: [rows][K] bf16, boxes of 128 rows x 64 K, 128-byte swizzle
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)K * 2};
     cuuint32_t box[2] = {BK, 128};
     cuuint32_t es[2] = {1, 1};
@@ -689,17 +722,17 @@ static cudaError_t launch_gemm_t(const void* a, const void* w, void* c, int64_t 
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
-  {  // W: [K][RB] bytes as uint16, boxes of 64 rows x one tile's (aligned) bytes
-    cuuint64_t dims[2] = {(cuuint64_t)(RB / 2), (cuuint64_t)K};
-    cuuint64_t strides[1] = {(cuuint64_t)RB};
-    cuuint32_t box[2] = {(cuuint32_t)(R::kPitch / 2), BK};
-    cuuint32_t es[2] = {1, 1};
-    if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(w), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+  {  // W: [slab][K][RB] bytes as uint16, boxes of 64 rows x one tile's (aligned) bytes
+    cuuint64_t dims[3] = {(cuuint64_t)(RB / 2), (cuuint64_t)K, (cuuint64_t)(GROUPED ? n_seg : 1)};
+    cuuint64_t strides[2] = {(cuuint64_t)RB, (cuuint64_t)(GROUPED ? slab_bytes : RB * K)};
+    cuuint32_t box[3] = {(cuuint32_t)(R::kPitch / 2), BK, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT16, GROUPED ? 3 : 2, const_cast<void*>(w), dims, strides,
+            box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
-  auto kern = gemm_kernel<QT, BF16_OUT>;
+  auto kern = gemm_kernel<QT, BF16_OUT, GROUPED>;
   static unsigned configured = 0;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -709,24 +742,44 @@ static cudaError_t launch_gemm_t(const void* a, const void* w, void* c, int64_t 
     if (e != cudaSuccess) return e;
     if (dev < 32) configured |= (1u << dev);
   }
-  // two CTAs (one cluster) per 512 x 256 tile of C
-  const dim3 grid((unsigned)(2 * (N / BN)), (unsigned)((M + BMP - 1) / BMP), 1);
-  kern<<<grid, kThreads, L::kAlloc, st>>>(ma, mw, c, (int)M, (int)K, (int)N);
+  // two CTAs (one cluster) per 512 x 256 tile of C; grouped: an upper bound on the
+  // segments' tile count (each segment adds at most one partial tile)
+  const int64_t items = GROUPED ? (rows + BMP - 1) / BMP + n_seg : (rows + BMP - 1) / BMP;
+  const dim3 grid((unsigned)(2 * (N / BN)), (unsigned)items, 1);
+  kern<<<grid, kThreads, L::kAlloc, st>>>(ma, mw, c, (int)rows, (int)K, (int)N, seg, n_seg);
   return cudaGetLastError();
+}
+
+template <bool GROUPED>
+static cudaError_t dispatch_gemm(int qtype, const void* a, const void* w, void* c, int64_t rows,
+                                 int64_t K, int64_t N, int64_t row_bytes, int c_dtype,
+                                 int64_t slab_bytes, const int* seg, int n_seg, cudaStream_t st) {
+  const bool bf = c_dtype == 1;
+#define VBQ_GEMM_CASE(QT)                                                                       \
+  case QT:                                                                                      \
+    return bf ? launch_gemm_t<QT, true, GROUPED>(a, w, c, rows, K, N, row_bytes, slab_bytes, seg, \
+                                                 n_seg, st)                                     \
+              : launch_gemm_t<QT, false, GROUPED>(a, w, c, rows, K, N, row_bytes, slab_bytes,    \
+                                                  seg, n_seg, st);
+  switch (qtype) {
+    VBQ_GEMM_CASE(kQ4_K)
+    VBQ_GEMM_CASE(kQ6_K)
+    VBQ_GEMM_CASE(kQ8_0)
+    default: return cudaErrorInvalidValue;
+  }
+#undef VBQ_GEMM_CASE
 }
 
 cudaError_t launch_gemm(int qtype, const void* a, const void* w, void* c, int64_t M, int64_t K,
                         int64_t N, int64_t row_bytes, int c_dtype, cudaStream_t st) {
-  const bool bf = c_dtype == 1;
-  switch (qtype) {
-    case kQ4_K: return bf ? launch_gemm_t<kQ4_K, true>(a, w, c, M, K, N, row_bytes, st)
-                          : launch_gemm_t<kQ4_K, false>(a, w, c, M, K, N, row_bytes, st);
-    case kQ6_K: return bf ? launch_gemm_t<kQ6_K, true>(a, w, c, M, K, N, row_bytes, st)
-                          : launch_gemm_t<kQ6_K, false>(a, w, c, M, K, N, row_bytes, st);
-    case kQ8_0: return bf ? launch_gemm_t<kQ8_0, true>(a, w, c, M, K, N, row_bytes, st)
-                          : launch_gemm_t<kQ8_0, false>(a, w, c, M, K, N, row_bytes, st);
-    default: return cudaErrorInvalidValue;
-  }
+  return dispatch_gemm<false>(qtype, a, w, c, M, K, N, row_bytes, c_dtype, 0, nullptr, 0, st);
+}
+
+cudaError_t launch_gemm_grouped(int qtype, const void* a, const void* w, void* c, int64_t rows,
+                                int64_t K, int64_t N, int64_t row_bytes, int c_dtype,
+                                int64_t slab_bytes, const int* seg, int n_seg, cudaStream_t st) {
+  return dispatch_gemm<true>(qtype, a, w, c, rows, K, N, row_bytes, c_dtype, slab_bytes, seg,
+                             n_seg, st);
 }
 
 cudaError_t gemm_status(unsigned* out, bool clear) {

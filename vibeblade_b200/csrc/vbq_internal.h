@@ -27,7 +27,29 @@ cudaError_t launch_gemv(int qtype, const float* x, const void* w, float* y, int6
 // tcgen05 dequant-GEMM: a bf16 [M,K], W K x N blocks, c fp32 (c_dtype 0) / bf16 (1) [M,N].
 cudaError_t launch_gemm(int qtype, const void* a, const void* w, void* c, int64_t M, int64_t K,
                         int64_t N, int64_t row_bytes, int c_dtype, cudaStream_t st);
+// Grouped form: rows of A / C split by the device array seg[0..n_seg] into segments,
+// segment s multiplied by the K x N slab at w + s * slab_bytes.
+cudaError_t launch_gemm_grouped(int qtype, const void* a, const void* w, void* c, int64_t rows,
+                                int64_t K, int64_t N, int64_t row_bytes, int c_dtype,
+                                int64_t slab_bytes, const int* seg, int n_seg, cudaStream_t st);
 cudaError_t gemm_status(unsigned* out, bool clear);
+
+// MoE pieces (vbq_moe.cu).  Routing of T tokens over E experts from fp32 logits [T, E]:
+// softmax (logits clipped to +-50), top-k (ties to the lower index), renormalised.
+cudaError_t launch_moe_route(const float* logits, int T, int E, int topk, int32_t* idx,
+                             float* weight, cudaStream_t st);
+// Stable counting sort of the T*topk (token, slot) entries by expert: seg[E + 1] segment
+// offsets, pos[T*topk] the sorted row of each entry, tok[T*topk] the token of each row.
+cudaError_t launch_moe_sort(const int32_t* idx, int T, int E, int topk, int32_t* seg,
+                            int32_t* pos, int32_t* tok, cudaStream_t st);
+// a_perm[row] = bf16(x[tok[row]]), x fp32 [T, H]
+cudaError_t launch_moe_gather(const float* x, const int32_t* tok, int rows, int H, void* a_perm,
+                              cudaStream_t st);
+// h = bf16(silu(g) * u) over n bf16 values, with the reference's clipping (in place in g ok)
+cudaError_t launch_swiglu(const void* g, const void* u, void* h, int64_t n, cudaStream_t st);
+// out[t] = sum_slot weight[t, slot] * y[pos[t * topk + slot]], fp32 [T, H], sanitised
+cudaError_t launch_moe_combine(const float* y, const int32_t* pos, const float* weight, int T,
+                               int topk, int H, float* out, cudaStream_t st);
 
 // Sticky device status bits of the GEMV kernels (kStatusTimeout = 1); synchronous.
 cudaError_t gemv_status(unsigned* out, bool clear);

@@ -1,0 +1,224 @@
+// vbq_moe.cu -- the mixture-of-experts FFN around the grouped dequant-GEMM.
+//
+// Reference semantics: vibeblade/moe.py:170-206 (ExpertRouter.route: softmax over the
+// clipped logits, top-k, renormalised weights) and :407-505 (moe_ffn_silu: per selected
+// expert down(silu(gate x) * (up x)) with the projections clipped to +-65504, weighted sum
+// over the k slots, output sanitised).  The C++ engine's per-token loop
+// (cpp/src/fast_model.cpp:534-571, :844-903) computes the same thing one token and one
+// expert at a time; its slab stride (ggml_type_size per element, :852-854) is not used
+// here: slab e starts at e * tensor_nbytes(type, K, N).
+//
+// Device pipeline (all on the caller's stream): route -> stable sort of the (token, slot)
+// entries by expert into row segments -> gather the rows of x as bf16 -> grouped GEMMs
+// gate and up (bf16 out) -> SwiGLU -> grouped GEMM down (fp32) -> weighted combine.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "vbq_internal.h"
+
+namespace vbq {
+namespace {
+
+constexpr int kMaxTopK = 8;
+
+// One thread per token.  Probabilities are recomputed on each selection pass with the same
+// arithmetic, so the comparisons are consistent; ties go to the lower expert index.
+__global__ void route_kernel(const float* __restrict__ logits, int T, int E, int topk,
+                             int32_t* __restrict__ idx, float* __restrict__ weight) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  const float* l = logits + (int64_t)t * E;
+  float mx = -INFINITY;
+  for (int e = 0; e < E; ++e) mx = fmaxf(mx, fminf(fmaxf(l[e], -50.0f), 50.0f));
+  float sum = 0.0f;
+  for (int e = 0; e < E; ++e) sum += expf(fminf(fmaxf(l[e], -50.0f), 50.0f) - mx);
+  int chosen[kMaxTopK];
+  float w[kMaxTopK];
+  float wsum = 0.0f;
+  for (int k = 0; k < topk; ++k) {
+    int best = -1;
+    float bp = -1.0f;
+    for (int e = 0; e < E; ++e) {
+      bool taken = false;
+      for (int j = 0; j < k; ++j) taken |= (chosen[j] == e);
+      if (taken) continue;
+      const float p = expf(fminf(fmaxf(l[e], -50.0f), 50.0f) - mx) / sum;
+      if (p > bp) {
+        bp = p;
+        best = e;
+      }
+    }
+    chosen[k] = best;
+    w[k] = bp;
+    wsum += bp;
+  }
+  const float div = wsum < 1e-12f ? 1.0f : wsum;
+  for (int k = 0; k < topk; ++k) {
+    idx[(int64_t)t * topk + k] = chosen[k];
+    weight[(int64_t)t * topk + k] = w[k] / div;
+  }
+}
+
+// Single CTA.  Counts per expert, exclusive scan into seg, then one warp assigns rows to
+// the entries in entry order (stable), 32 entries at a time.
+__global__ void sort_kernel(const int32_t* __restrict__ idx, int n, int E, int32_t* __restrict__ seg,
+                            int32_t* __restrict__ pos, int32_t* __restrict__ tok, int topk) {
+  extern __shared__ int32_t sh[];  // cnt[E], next[E]
+  int32_t* cnt = sh;
+  int32_t* next = sh + E;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const int e = idx[j];
+    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int e = 0; e < E; ++e) {
+      seg[e] = run;
+      next[e] = run;
+      run += cnt[e];
+    }
+    seg[E] = run;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const unsigned lane = threadIdx.x;
+    for (int base = 0; base < n; base += 32) {
+      const int j = base + (int)lane;
+      const int e = (j < n) ? idx[j] : -1;
+      const bool valid = e >= 0 && e < E;
+      const unsigned same = __match_any_sync(0xffffffffu, valid ? e : -1);
+      const int rank = __popc(same & ((1u << lane) - 1u));
+      const int row = valid ? next[e] + rank : -1;
+      __syncwarp();
+      if (valid && rank == 0) next[e] += __popc(same);
+      __syncwarp();
+      if (j < n) {
+        pos[j] = row;
+        if (valid) tok[row] = j / topk;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&p);
+}
+
+// a_perm[row, :] = bf16(x[tok[row], :]); one CTA per row, 8 values per thread step
+__global__ void gather_kernel(const float* __restrict__ x, const int32_t* __restrict__ tok, int H,
+                              uint4* __restrict__ a_perm) {
+  const int row = blockIdx.x;
+  const float4* src = reinterpret_cast<const float4*>(x + (int64_t)tok[row] * H);
+  uint4* dst = a_perm + (int64_t)row * (H / 8);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) {
+    const float4 a = src[2 * i], b = src[2 * i + 1];
+    dst[i] = make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y),
+                        pack_bf16(b.z, b.w));
+  }
+}
+
+// nan -> 0, +-inf -> +-65504, then clip to +-65504 (vibeblade/moe.py:472-473)
+__device__ __forceinline__ float sanitize(float v) {
+  if (v != v) return 0.0f;
+  return fminf(fmaxf(v, -65504.0f), 65504.0f);
+}
+// x * sigmoid(x) with the stable two-sided form of vibeblade/moe.py:36-50
+__device__ __forceinline__ float silu_ref(float x) {
+  float s;
+  if (x >= 0.0f) {
+    s = 1.0f / (1.0f + expf(-x));
+  } else {
+    const float e = expf(x);
+    s = e / (1.0f + e);
+  }
+  if (s != s) s = 0.0f;
+  return x * s;
+}
+
+__global__ void swiglu_kernel(const uint4* __restrict__ g, const uint4* __restrict__ u,
+                              uint4* __restrict__ h, int64_t n8) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 gv = g[i], uv = u[i];
+    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const __nv_bfloat162 g2 = *reinterpret_cast<const __nv_bfloat162*>(&gw[q]);
+      const __nv_bfloat162 u2 = *reinterpret_cast<const __nv_bfloat162*>(&uw[q]);
+      const float2 gf = __bfloat1622float2(g2), uf = __bfloat1622float2(u2);
+      o[q] = pack_bf16(silu_ref(sanitize(gf.x)) * sanitize(uf.x),
+                       silu_ref(sanitize(gf.y)) * sanitize(uf.y));
+    }
+    h[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// out[t, d] = sanitize(((0 + w0 y0) + w1 y1) + ...), each product and sum rounded once,
+// in slot order as the reference's accumulation loop (vibeblade/moe.py:466-475)
+__global__ void combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ pos,
+                               const float* __restrict__ weight, int topk, int H,
+                               float* __restrict__ out) {
+  const int t = blockIdx.x;
+  for (int d = threadIdx.x; d < H; d += blockDim.x) {
+    float acc = 0.0f;
+    for (int k = 0; k < topk; ++k) {
+      const int r = pos[(int64_t)t * topk + k];
+      const float v = r >= 0 ? y[(int64_t)r * H + d] : 0.0f;
+      acc = __fadd_rn(acc, __fmul_rn(weight[(int64_t)t * topk + k], v));
+    }
+    out[(int64_t)t * H + d] = sanitize(acc);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_moe_route(const float* logits, int T, int E, int topk, int32_t* idx,
+                             float* weight, cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  if (topk < 1 || topk > kMaxTopK || topk > E) return cudaErrorInvalidValue;
+  route_kernel<<<(T + 127) / 128, 128, 0, st>>>(logits, T, E, topk, idx, weight);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_moe_sort(const int32_t* idx, int T, int E, int topk, int32_t* seg,
+                            int32_t* pos, int32_t* tok, cudaStream_t st) {
+  const size_t shm = (size_t)2 * E * sizeof(int32_t);
+  if (shm > 48 * 1024) return cudaErrorInvalidValue;
+  sort_kernel<<<1, 1024, shm, st>>>(idx, T * topk, E, seg, pos, tok, topk);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_moe_gather(const float* x, const int32_t* tok, int rows, int H, void* a_perm,
+                              cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  gather_kernel<<<rows, 128, 0, st>>>(x, tok, H, static_cast<uint4*>(a_perm));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu(const void* g, const void* u, void* h, int64_t n, cudaStream_t st) {
+  const int64_t n8 = n / 8;
+  if (n8 <= 0) return cudaSuccess;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (n8 + 255) / 256;
+  const int blocks = (int)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
+  swiglu_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint4*>(g), static_cast<const uint4*>(u),
+                                        static_cast<uint4*>(h), n8);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_moe_combine(const float* y, const int32_t* pos, const float* weight, int T,
+                               int topk, int H, float* out, cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  combine_kernel<<<T, 256, 0, st>>>(y, pos, weight, topk, H, out);
+  return cudaGetLastError();
+}
+
+}  // namespace vbq
