@@ -113,6 +113,107 @@ def dist_setup(n_gpus: int):
     return 0, 1, 0
 
 
+def _time_steps(step, steps: int, warmup: int, stream, world: int):
+    """Device time of `steps` calls of step() after `warmup`, max over ranks (ms)."""
+    import torch
+    import torch.distributed as dist
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        step(warmup + i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1)], device=torch.device("cuda", torch.cuda.current_device()),
+                     dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def bench_prefill(dev, steps: int) -> dict:
+    """the 8B layer's five matrices in Q6_K times bf16 activations of
+    M = 2048 tokens (tcgen05 GEMM, bf16 out).  Whole layer per step."""
+    import torch
+    import vibeblade_b200 as vb
+    from vibeblade_b200.quantize import synthetic_weights
+    M = 2048
+    mats = [(K, N, synthetic_weights(K, N, 14, seed=200 + i, device=dev)) for i, (_, K, N) in enumerate(LAYER_8B)]
+    g = torch.Generator(device=dev).manual_seed(2)
+    acts = {K: torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16) for _, K, _ in LAYER_8B}
+    outs = [torch.empty(M, N, device=dev, dtype=torch.bfloat16) for _, _, N in LAYER_8B]
+
+    def step(_):
+        for (K, N, w), o in zip(mats, outs):
+            vb.gemm_dequant(acts[K], w, o, M, K, N, 14, out_dtype=torch.bfloat16)
+
+    ms = _time_steps(step, steps, 3, torch.cuda.current_stream(dev), 1)
+    flops = sum(2 * M * K * N for _, K, N in LAYER_8B)
+    tf = flops * steps / (ms * 1e-3) / 1e12
+    return {"metric": "Q6_K prefill GEMM TFLOP/s (8B layer, M=2048, bf16 out)", "value": round(tf, 1),
+            "unit": "TFLOP/s", "ms_per_layer": round(ms / steps, 4), "steps": steps,
+            "frac_of_bf16_peak": round(tf / peaks()["bf16_tflops"], 4),
+            "kernel": "vbq::gemm::gemm_kernel (2-SM tcgen05, cta_group::2)"}
+
+
+def bench_moe(dev, steps: int) -> dict:
+    """MoE FFN, 8 experts top-2, hidden 4096, intermediate 14336, Q4_K,
+    4096 tokens routed by N(0,1) logits (seed 3)."""
+    import torch
+    import vibeblade_b200 as vb
+    from vibeblade_b200.quantize import synthetic_weights
+    T, H, I, E, k = 4096, 4096, 14336, 8, 2
+    wg = torch.cat([synthetic_weights(H, I, 12, seed=10 + e, device=dev).reshape(-1) for e in range(E)])
+    wu = torch.cat([synthetic_weights(H, I, 12, seed=20 + e, device=dev).reshape(-1) for e in range(E)])
+    wd = torch.cat([synthetic_weights(I, H, 12, seed=30 + e, device=dev).reshape(-1) for e in range(E)])
+    g = torch.Generator(device=dev).manual_seed(3)
+    x = torch.randn(T, H, generator=g, device=dev)
+    lg = torch.randn(T, E, generator=g, device=dev)
+    out = torch.empty(T, H, device=dev)
+
+    def step(_):
+        vb.moe_ffn(x, lg, wg, wu, wd, I, 12, topk=k, out=out)
+
+    ms = _time_steps(step, steps, 3, torch.cuda.current_stream(dev), 1)
+    tf = 2 * T * k * 3 * H * I * steps / (ms * 1e-3) / 1e12
+    return {"metric": "MoE FFN TFLOP/s (8 experts top-2, 4096 tokens, Q4_K)", "value": round(tf, 1),
+            "unit": "TFLOP/s", "ms_per_step": round(ms / steps, 3), "steps": steps,
+            "frac_of_bf16_peak": round(tf / peaks()["bf16_tflops"], 4)}
+
+
+def bench_tp(dev, rank: int, world: int, steps: int) -> dict:
+    """70B FFN (hidden 8192, intermediate 28672, Q8_0) split over the
+    `world` GPUs (gate / up column split, down row split, NCCL all-reduce of the fp32
+    output); prefill M = 2048 (whole-job TFLOP/s) and decode batch 1 (latency)."""
+    import torch
+    from vibeblade_b200 import tp
+    from vibeblade_b200.quantize import synthetic_weights
+    H, I, M = 8192, 28672, 2048
+    wg = synthetic_weights(H, I, 8, seed=51, device=dev)
+    wu = synthetic_weights(H, I, 8, seed=52, device=dev)
+    wd = synthetic_weights(I, H, 8, seed=53, device=dev)
+    ffn = tp.TPFFN(wg, wu, wd, H, I, 8, rank, world, dev)
+    del wg, wu, wd
+    torch.cuda.empty_cache()
+    g = torch.Generator(device=dev).manual_seed(2)
+    x = torch.randn(M, H, generator=g, device=dev).to(torch.bfloat16)
+    xd = torch.randn(1, H, generator=g, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ms = _time_steps(lambda _: ffn.prefill(x), steps, 3, stream, world)
+    tf = 2 * M * 3 * H * I * steps / (ms * 1e-3) / 1e12
+    dms = _time_steps(lambda _: ffn.decode(xd), 5 * steps, 5, stream, world)
+    return {"metric": "70B FFN prefill TFLOP/s (Q8_0, M=2048, TP over the job's GPUs)",
+            "value": round(tf, 1), "unit": "TFLOP/s", "tp": world, "scaling": "strong",
+            "ms_per_step": round(ms / steps, 4), "steps": steps,
+            "decode_b1_us_per_ffn": round(1e3 * dms / (5 * steps), 1),
+            "collective": "torch.distributed all_reduce (NCCL) of the fp32 [M, 8192] partial sums"}
+
+
 def cpu_reference_gbs(batch: int, seconds: float, threads: int, steps: int | None = None,
                       warmup: int = 0):
     """Time the reference's gemv_dequant over the decode layer on host cores.
@@ -302,6 +403,14 @@ def run_gpu(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_value = layer_bytes(B) * args.steps * world / (float(t.item()) * 1e-3) / 1e9
 
+    # ---- configs 3-5: prefill GEMM, MoE (one GPU) and the tensor-parallel 70B FFN ----
+    extras = {}
+    if not args.no_extras:
+        if world == 1:
+            extras["prefill"] = bench_prefill(dev, args.extras_steps)
+            extras["moe"] = bench_moe(dev, args.extras_steps)
+        extras["tp_ffn"] = bench_tp(dev, rank, world, args.extras_steps)
+
     pk = peaks()
     line = None
     if rank == 0:
@@ -329,6 +438,7 @@ def run_gpu(args) -> None:
             "gpu_launches": args.steps * len(LAYER_8B),
             "clocks": clk.summary(),
         }
+        line.update(extras)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -350,6 +460,9 @@ def main() -> None:
     ap.add_argument("--impl", default="vbq", choices=["vbq", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the prefill GEMM, MoE and tensor-parallel FFN measurements")
+    ap.add_argument("--extras-steps", type=int, default=10)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -181,6 +181,15 @@ int vbq_moe_ffn(const float* x, const float* logits, const void* w_gate, const v
                 void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * SwiGLU of the FFN (cpp/src/fast_model.cpp:946-953, vibeblade/moe.py:36-50, :472-474):
+ *     h[i] = silu(g[i]) * u[i],  silu(x) = x * sigmoid(x),
+ * with g and u first sanitised as the reference's MoE path does (NaN -> 0, clip to
+ * +-65504).  n values of dtype VBQ_DTYPE_F32 or VBQ_DTYPE_BF16 (computed in fp32, bf16
+ * output rounded to nearest-even); n % 8 == 0; h may alias g.
+ */
+int vbq_swiglu(const void* g, const void* u, void* h, int64_t n, int32_t dtype, void* stream);
+
+/*
  * Device-side status of the library's kernels on the current device: bit 0 set means a
  * bounded wait inside a kernel gave up (VBQ_ERR_TIMEOUT is returned then), which leaves
  * that call's outputs undefined and its scratch in need of re-zeroing.  Reads

@@ -1,0 +1,104 @@
+"""Tensor-parallel host logic on CPU: shard byte layout and split rules, and a
+world-size-2 gloo run of the Megatron FFN decomposition (column-split gate / up,
+row-split down, one all-reduce) with the oracle's dequantization standing in for the
+device kernels."""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import max_rel
+from vibeblade_b200 import formats as F
+from vibeblade_b200 import tp
+from vibeblade_b200.quantize import quantize
+
+TYPES = [F.GGML_TYPE_Q4_K, F.GGML_TYPE_Q6_K, F.GGML_TYPE_Q8_0]
+
+
+def _w(K, N, qt, seed):
+    return quantize(np.random.default_rng(seed).normal(0, 0.02, (K, N)).astype(np.float32), qt)
+
+
+@pytest.mark.parametrize("qt", TYPES)
+@pytest.mark.parametrize("world", [2, 4])
+def test_column_shard_is_column_slice(oracle, qt, world):
+    K, N = 16, 4096 * world // 2 if qt == F.GGML_TYPE_Q6_K else 512 * world
+    w = _w(K, N, qt, 1)
+    full = oracle.dequantize(w.numpy(), K, N, qt)
+    n = N // world
+    for r in range(world):
+        s = tp.shard(w, K, N, qt, "column", r, world)
+        assert s.shape == (K, F.row_bytes(qt, n))
+        np.testing.assert_array_equal(oracle.dequantize(s.numpy(), K, n, qt), full[:, r * n:(r + 1) * n])
+
+
+@pytest.mark.parametrize("qt", TYPES)
+def test_row_shard_is_row_slice(oracle, qt):
+    K, N, world = 64, 2048, 4
+    w = _w(K, N, qt, 2)
+    full = oracle.dequantize(w.numpy(), K, N, qt)
+    k = K // world
+    for r in range(world):
+        s = tp.shard(w, K, N, qt, "row", r, world)
+        np.testing.assert_array_equal(oracle.dequantize(s.numpy(), k, N, qt), full[r * k:(r + 1) * k])
+
+
+def test_split_rules():
+    # 70B shapes (hidden 8192, intermediate 28672, Q8_0) split at 1, 2, 4, 8
+    for world in (1, 2, 4, 8):
+        tp.check_split("column", 8192, 28672, F.GGML_TYPE_Q8_0, world)
+        tp.check_split("row", 28672, 8192, F.GGML_TYPE_Q8_0, world)
+        tp.check_split("column", 8192, 8192, F.GGML_TYPE_Q8_0, world)
+    tp.check_split("column", 8192, 1024, F.GGML_TYPE_Q8_0, 4)
+    with pytest.raises(ValueError):  # 8 KV heads x 128 over 8 ranks: 128 columns each
+        tp.check_split("column", 8192, 1024, F.GGML_TYPE_Q8_0, 8)
+    with pytest.raises(ValueError):
+        tp.check_split("row", 100, 256, F.GGML_TYPE_Q4_K, 8)
+    with pytest.raises(ValueError):  # Q6_K shard rows must stay 16-byte multiples
+        tp.check_split("column", 64, 2048, F.GGML_TYPE_Q6_K, 2)
+
+
+def _silu(x):
+    return x / (1.0 + np.exp(-x))
+
+
+def _ffn_rank(rank, world, port, H, I, qt, res):
+    import torch.distributed as dist
+    from oracle import load_oracle
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        orc = load_oracle()
+        wg, wu, wd = _w(H, I, qt, 10), _w(H, I, qt, 11), _w(I, H, qt, 12)
+        x = np.random.default_rng(5).normal(0, 1, (3, H))
+        il = I // world
+        g = x @ orc.dequantize(tp.shard(wg, H, I, qt, "column", rank, world).numpy(), H, il, qt)
+        u = x @ orc.dequantize(tp.shard(wu, H, I, qt, "column", rank, world).numpy(), H, il, qt)
+        part = (_silu(g) * u) @ orc.dequantize(tp.shard(wd, I, H, qt, "row", rank, world).numpy(), il, H, qt)
+        y = torch.from_numpy(part)
+        dist.all_reduce(y)
+        full = (_silu(x @ orc.dequantize(wg.numpy(), H, I, qt)) * (x @ orc.dequantize(wu.numpy(), H, I, qt))) \
+            @ orc.dequantize(wd.numpy(), I, H, qt)
+        res[rank] = max_rel(y.numpy(), full)
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("qt", [F.GGML_TYPE_Q8_0, F.GGML_TYPE_Q4_K])
+def test_tp_ffn_gloo_world2(qt):
+    import torch.multiprocessing as mp
+    H, I, world = 256, 1024, 2
+    res = mp.get_context("spawn").Manager().dict()
+    mp.spawn(_ffn_rank, args=(world, _free_port(), H, I, qt, res), nprocs=world, join=True)
+    assert len(res) == world
+    assert max(res.values()) <= 1e-9  # fp64 sums: only the split of the sum differs

@@ -48,6 +48,8 @@ SIGNATURES = {
                                 C.c_void_p, C.c_void_p]),
     "vbq_moe_workspace_bytes": (C.c_int, [C.c_int64, C.c_int64, C.c_int64, C.c_int32,
                                           C.c_int32, C.POINTER(C.c_size_t)]),
+    "vbq_swiglu": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32,
+                             C.c_void_p]),
     "vbq_moe_ffn": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                               C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int32, C.c_int32,
                               C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_size_t,

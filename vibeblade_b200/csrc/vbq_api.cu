@@ -391,3 +391,22 @@ int vbq_moe_ffn(const float* x, const float* logits, const void* w_gate, const v
 }
 
 }  // extern "C"
+
+extern "C" int vbq_swiglu(const void* g, const void* u, void* h, int64_t n, int32_t dtype,
+                          void* stream) {
+  if (dtype != VBQ_DTYPE_F32 && dtype != VBQ_DTYPE_BF16)
+    return fail(VBQ_ERR_SHAPE, "vbq_swiglu: dtype must be VBQ_DTYPE_F32 or VBQ_DTYPE_BF16");
+  if (n < 0) return fail(VBQ_ERR_SHAPE, "vbq_swiglu: negative size");
+  if (n == 0) return ok();
+  if (!g || !u || !h) return fail(VBQ_ERR_NULL, "vbq_swiglu: NULL pointer");
+  if (n % 8 != 0) return fail(VBQ_ERR_SHAPE, "vbq_swiglu: n must be a multiple of 8");
+  if (!aligned(g, 16) || !aligned(u, 16) || !aligned(h, 16))
+    return fail(VBQ_ERR_ALIGN, "vbq_swiglu: g, u and h must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = dtype == VBQ_DTYPE_BF16
+                      ? vbq::launch_swiglu(g, u, h, n, st)
+                      : vbq::launch_swiglu_f32(static_cast<const float*>(g), static_cast<const float*>(u),
+                                               static_cast<float*>(h), n, st);
+  if (e != cudaSuccess) return cuda_fail(e, "vbq_swiglu launch");
+  return ok();
+}

@@ -6,7 +6,7 @@
 // over the k slots, output sanitised).  The C++ engine's per-token loop
 // (cpp/src/fast_model.cpp:534-571, :844-903) computes the same thing one token and one
 // expert at a time; its slab stride (ggml_type_size per element, :852-854) is not used
-// here: slab e starts at e * tensor_nbytes(type, K, N).
+// here: slab e starts at e * K * row_bytes(type, N).
 //
 // Device pipeline (all on the caller's stream): route -> stable sort of the (token, slot)
 // entries by expert into row segments -> gather the rows of x as bf16 -> grouped GEMMs
@@ -159,6 +159,16 @@ __global__ void swiglu_kernel(const uint4* __restrict__ g, const uint4* __restri
   }
 }
 
+__global__ void swiglu_f32_kernel(const float4* __restrict__ g, const float4* __restrict__ u,
+                                  float4* __restrict__ h, int64_t n4) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 gv = g[i], uv = u[i];
+    h[i] = make_float4(silu_ref(sanitize(gv.x)) * sanitize(uv.x), silu_ref(sanitize(gv.y)) * sanitize(uv.y),
+                       silu_ref(sanitize(gv.z)) * sanitize(uv.z), silu_ref(sanitize(gv.w)) * sanitize(uv.w));
+  }
+}
+
 // out[t, d] = sanitize(((0 + w0 y0) + w1 y1) + ...), each product and sum rounded once,
 // in slot order as the reference's accumulation loop (vibeblade/moe.py:466-475)
 __global__ void combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ pos,
@@ -201,16 +211,28 @@ cudaError_t launch_moe_gather(const float* x, const int32_t* tok, int rows, int 
   return cudaGetLastError();
 }
 
-cudaError_t launch_swiglu(const void* g, const void* u, void* h, int64_t n, cudaStream_t st) {
-  const int64_t n8 = n / 8;
-  if (n8 <= 0) return cudaSuccess;
+static int grid_for(int64_t items) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t want = (n8 + 255) / 256;
-  const int blocks = (int)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
-  swiglu_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint4*>(g), static_cast<const uint4*>(u),
-                                        static_cast<uint4*>(h), n8);
+  const int64_t want = (items + 255) / 256;
+  return (int)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
+}
+
+cudaError_t launch_swiglu(const void* g, const void* u, void* h, int64_t n, cudaStream_t st) {
+  const int64_t n8 = n / 8;
+  if (n8 <= 0) return cudaSuccess;
+  swiglu_kernel<<<grid_for(n8), 256, 0, st>>>(static_cast<const uint4*>(g),
+                                              static_cast<const uint4*>(u), static_cast<uint4*>(h), n8);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu_f32(const float* g, const float* u, float* h, int64_t n, cudaStream_t st) {
+  const int64_t n4 = n / 4;
+  if (n4 <= 0) return cudaSuccess;
+  swiglu_f32_kernel<<<grid_for(n4), 256, 0, st>>>(reinterpret_cast<const float4*>(g),
+                                                  reinterpret_cast<const float4*>(u),
+                                                  reinterpret_cast<float4*>(h), n4);
   return cudaGetLastError();
 }
 

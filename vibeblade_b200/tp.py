@@ -1,0 +1,159 @@
+"""Tensor-parallel sharding of quantized weights and the TP FFN / attention projections.
+
+The reference runs on one host (its engine has no multi-GPU path); this module splits the
+same matmuls Megatron-style over the GPUs of one node, one process per GPU:
+
+* column split (Q, K, V, gate, up; ``kind="column"``): rank r owns output columns
+  [r N / W, (r + 1) N / W).  In the reference block layout (K x N, blocks along N) that
+  is the same byte range of every row, so the shard is a strided, block-aligned slice
+  packed into its own K x (N / W) matrix.  Outputs are disjoint: no communication.
+* row split (o, down; ``kind="row"``): rank r owns input rows [r K / W, (r + 1) K / W):
+  a contiguous byte range.  Each rank produces a partial [M, N] sum; one all-reduce (sum)
+  over the process group combines them, two per layer (after o and after down).
+
+``TPFFN`` is the SwiGLU FFN of one layer (gate / up column split, down row split);
+``TPAttentionProj`` the Q, K/V (column) and o (row) projections around the attention core,
+which is outside the quantized matmul path.  Prefill uses the tcgen05 GEMM (bf16
+activations), decode the fused GEMV (fp32).  The collective is torch.distributed's
+all_reduce on the process group (NCCL between GPUs).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from . import formats as F
+from .dequant import _require_cuda, _stream_ptr, _weights_u8, gemv_dequant
+from .gemm import gemm_dequant
+
+# GEMM tiles are 256 columns wide; a column shard must keep whole tiles
+SHARD_COLUMN_ALIGN = 256
+
+
+def check_split(kind: str, K: int, N: int, qtype, world: int) -> None:
+    t = F.parse_type(qtype)
+    if kind == "column":
+        if N % world or (N // world) % SHARD_COLUMN_ALIGN or (N // world) % F.BLOCK_VALUES[t]:
+            raise ValueError(f"column split: N={N} over {world} ranks must leave multiples of "
+                             f"{SHARD_COLUMN_ALIGN} columns per rank")
+        if F.row_bytes(t, N // world) % 16:
+            raise ValueError("column split: shard rows must be a multiple of 16 bytes "
+                             "(Q6_K: N / world % 2048 == 0)")
+    elif kind == "row":
+        if K % world or (K // world) % 8:
+            raise ValueError(f"row split: K={K} over {world} ranks must leave multiples of 8 rows")
+    else:
+        raise ValueError(kind)
+
+
+def shard(w: torch.Tensor, K: int, N: int, qtype, kind: str, rank: int, world: int) -> torch.Tensor:
+    """Rank `rank`'s shard of the K x N block matrix `w` (uint8 bytes, any device), packed
+    as its own block matrix: K x (N / world) for a column split, (K / world) x N for a row
+    split."""
+    t = F.parse_type(qtype)
+    check_split(kind, K, N, t, world)
+    rb = F.row_bytes(t, N)
+    m = _weights_u8(w).reshape(-1)[:K * rb].view(K, rb)
+    if kind == "column":
+        per = F.row_bytes(t, N // world)
+        return m[:, rank * per:(rank + 1) * per].contiguous()
+    kr = K // world
+    return m[rank * kr:(rank + 1) * kr].contiguous()
+
+
+def swiglu(g: torch.Tensor, u: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """silu(g) * u (fp32 or bf16 CUDA tensors, same shape), g and u sanitised first."""
+    _require_cuda("swiglu", g, u)
+    if g.shape != u.shape or g.dtype != u.dtype or g.dtype not in (torch.float32, torch.bfloat16):
+        raise RuntimeError("swiglu: g and u must be fp32 or bf16 tensors of one shape")
+    out = torch.empty_like(g) if out is None else out
+    lib = _lib.load()
+    dt = _lib.DTYPE_F32 if g.dtype == torch.float32 else _lib.DTYPE_BF16
+    _lib.check(lib.vbq_swiglu(g.data_ptr(), u.data_ptr(), out.data_ptr(), g.numel(), dt,
+                              _stream_ptr(g)), lib)
+    return out
+
+
+class TPLinear:
+    """One quantized matmul split over the group: y = x @ deq(W), W K x N."""
+
+    def __init__(self, w_full: torch.Tensor, K: int, N: int, qtype, kind: str, rank: int,
+                 world: int, device: torch.device):
+        self.t = F.parse_type(qtype)
+        self.kind, self.K, self.N, self.rank, self.world = kind, K, N, rank, world
+        self.w = shard(w_full, K, N, self.t, kind, rank, world).to(device)
+        self.k_loc = K // world if kind == "row" else K
+        self.n_loc = N // world if kind == "column" else N
+
+    def prefill(self, a: torch.Tensor, out_dtype=torch.float32) -> torch.Tensor:
+        """a: bf16 [M, k_loc] -> [M, n_loc] (row split: a partial sum)."""
+        return gemm_dequant(a, self.w, None, a.shape[0], self.k_loc, self.n_loc, self.t, out_dtype)
+
+    def decode(self, x: torch.Tensor) -> torch.Tensor:
+        """x: fp32 [B, k_loc] (B <= 16) -> fp32 [B, n_loc]."""
+        return gemv_dequant(x, self.w, None, self.k_loc, self.n_loc, self.t)
+
+
+def _all_reduce(y: torch.Tensor, group) -> torch.Tensor:
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group)
+    return y
+
+
+class TPFFN:
+    """SwiGLU FFN of one layer: out = down(silu(gate x) * up x), gate / up column split,
+    down row split, one all-reduce (cpp/src/fast_model.cpp:906-958)."""
+
+    def __init__(self, wg, wu, wd, H: int, I: int, qtype, rank: int, world: int, device,
+                 group=None):
+        self.gate = TPLinear(wg, H, I, qtype, "column", rank, world, device)
+        self.up = TPLinear(wu, H, I, qtype, "column", rank, world, device)
+        self.down = TPLinear(wd, I, H, qtype, "row", rank, world, device)
+        self.group = group
+
+    def prefill(self, x: torch.Tensor) -> torch.Tensor:
+        """x: bf16 [M, H] (replicated) -> fp32 [M, H] (replicated after the all-reduce)."""
+        g = self.gate.prefill(x, torch.bfloat16)
+        u = self.up.prefill(x, torch.bfloat16)
+        h = swiglu(g, u, out=g)
+        return _all_reduce(self.down.prefill(h, torch.float32), self.group)
+
+    def decode(self, x: torch.Tensor) -> torch.Tensor:
+        """x: fp32 [B, H] -> fp32 [B, H]."""
+        g = self.gate.decode(x)
+        u = self.up.decode(x)
+        h = swiglu(g, u, out=g)
+        return _all_reduce(self.down.decode(h), self.group)
+
+
+class TPAttentionProj:
+    """Q, K, V and o projections of one attention layer around the attention core.
+
+    Q, K and V are split by heads (columns), so rank r holds query heads r Hq / W .. and
+    the KV heads they attend to.  When a K / V shard would fall below the kernels'
+    256-column tiles (8 KV heads of 128 over 8 ranks) each rank computes all KV heads
+    instead (replicated).  o is split by rows and followed by the all-reduce."""
+
+    def __init__(self, wq, wk, wv, wo, H: int, kv_cols: int, qtype, rank: int, world: int,
+                 device, group=None):
+        self.q = TPLinear(wq, H, H, qtype, "column", rank, world, device)
+        try:
+            check_split("column", H, kv_cols, qtype, world)
+            kv_rank, kv_world = rank, world
+        except ValueError:
+            kv_rank, kv_world = 0, 1
+        self.kv_replicated = kv_world == 1 and world > 1
+        self.k = TPLinear(wk, H, kv_cols, qtype, "column", kv_rank, kv_world, device)
+        self.v = TPLinear(wv, H, kv_cols, qtype, "column", kv_rank, kv_world, device)
+        self.o = TPLinear(wo, H, H, qtype, "row", rank, world, device)
+        self.group = group
+
+    def qkv_prefill(self, x: torch.Tensor):
+        """x: bf16 [M, H] -> bf16 (q [M, H / W], k, v [M, kv_cols / W or kv_cols])."""
+        return (self.q.prefill(x, torch.bfloat16), self.k.prefill(x, torch.bfloat16),
+                self.v.prefill(x, torch.bfloat16))
+
+    def o_prefill(self, attn: torch.Tensor) -> torch.Tensor:
+        """attn: bf16 [M, H / world] (this rank's heads) -> fp32 [M, H] after all-reduce."""
+        return _all_reduce(self.o.prefill(attn, torch.float32), self.group)
