@@ -102,3 +102,35 @@ def test_tp_ffn_gloo_world2(qt):
     mp.spawn(_ffn_rank, args=(world, _free_port(), H, I, qt, res), nprocs=world, join=True)
     assert len(res) == world
     assert max(res.values()) <= 1e-9  # fp64 sums: only the split of the sum differs
+
+
+def _reduce_rank(rank, world, port, res):
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
+    try:
+        y = torch.full((4,), float(rank + 1))
+        # a TP = 1 layer on one rank only: no collective may start
+        if rank == 0:
+            assert torch.equal(tp.reduce_partial(y.clone(), 1), y)
+        # a layer split over a width that is not the group's: refused on every rank
+        try:
+            tp.reduce_partial(y.clone(), world + 1)
+            bad = False
+        except RuntimeError:
+            bad = True
+        s = tp.reduce_partial(y.clone(), world)  # the real split: summed over the ranks
+        res[rank] = (bad, s.tolist())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_reduce_partial_collective_decision():
+    """The all-reduce follows the layer's TP width, not the process group's size: a TP = 1
+    call made on one rank of a 2-rank job returns at once (a collective there would hang
+    the other rank; the 20 s group timeout turns such a regression into a failure)."""
+    import torch.multiprocessing as mp
+    res = mp.get_context("spawn").Manager().dict()
+    mp.spawn(_reduce_rank, args=(2, _free_port(), res), nprocs=2, join=True)
+    assert res[0] == (True, [3.0] * 4) and res[1] == (True, [3.0] * 4)

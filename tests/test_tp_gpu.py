@@ -72,7 +72,7 @@ def test_tp_ffn_prefill_emulated(cuda, ffn_setup, world):
     xb = x.to(torch.bfloat16)
     y = torch.zeros(256, H, device=cuda)
     for r in range(world):  # no process group: each rank's partial sum, added here
-        y += tp.TPFFN(wg, wu, wd, H, I, QT, r, world, cuda).prefill(xb)
+        y += tp.TPFFN(wg, wu, wd, H, I, QT, r, world, cuda).prefill(xb, reduce=False)
     torch.cuda.synchronize()
     assert vb.device_status() == 0
     assert _rel(y, ref_p) <= 2e-2
@@ -83,7 +83,7 @@ def test_tp_ffn_decode_emulated(cuda, ffn_setup, world):
     wg, wu, wd, x, _, ref_d = ffn_setup
     y = torch.zeros(4, H, device=cuda)
     for r in range(world):
-        y += tp.TPFFN(wg, wu, wd, H, I, QT, r, world, cuda).decode(x[:4].contiguous())
+        y += tp.TPFFN(wg, wu, wd, H, I, QT, r, world, cuda).decode(x[:4].contiguous(), reduce=False)
     torch.cuda.synchronize()
     assert _rel(y, ref_d) <= 1e-3
 
@@ -107,7 +107,7 @@ def test_tp_attention_projections_emulated(cuda):
         k = torch.cat([p.qkv_prefill(x)[1] for p in parts], dim=1) if world < 8 else parts[3].qkv_prefill(x)[1]
         assert torch.equal(k, k1)
         hq = H // world
-        o = sum(p.o_prefill(q1[:, r * hq:(r + 1) * hq].contiguous()) for r, p in enumerate(parts))
+        o = sum(p.o_prefill(q1[:, r * hq:(r + 1) * hq].contiguous(), reduce=False) for r, p in enumerate(parts))
         assert _rel(o, o1) <= 1e-5
     assert vb.device_status() == 0
 
@@ -129,11 +129,12 @@ def _nccl_rank(rank, world, port, res):
         dist.all_gather(ys, y)
         same = all(torch.equal(ys[0], t) for t in ys)
         rel = None
-        if rank == 0:
+        if rank == 0:  # TP = 1 layer: no collective (reduce_partial follows the layer width)
             y1 = tp.TPFFN(wg, wu, wd, H, I, QT, 0, 1, dev).prefill(x)
             rel = _rel(y, y1)
         torch.cuda.synchronize()
         res[rank] = (same, rel)
+        dist.barrier()  # every rank takes the same collective steps before teardown
     finally:
         dist.destroy_process_group()
 

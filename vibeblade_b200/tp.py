@@ -94,10 +94,22 @@ class TPLinear:
         return gemv_dequant(x, self.w, None, self.k_loc, self.n_loc, self.t)
 
 
-def _all_reduce(y: torch.Tensor, group) -> torch.Tensor:
+def reduce_partial(y: torch.Tensor, world: int, group=None) -> torch.Tensor:
+    """Sum a row-split layer's partial output over its `world` ranks.
+
+    The decision depends only on the layer's own TP width, never on the size of whatever
+    process group exists: a TP = 1 layer (for example a single-GPU reference computed on
+    one rank of a larger job) must not enter a collective the other ranks do not join.
+    A layer split over W > 1 ranks needs a process group of exactly W ranks."""
+    if world == 1:
+        return y
     import torch.distributed as dist
-    if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
-        dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group)
+    if not (dist.is_available() and dist.is_initialized()):
+        raise RuntimeError(f"a layer split over {world} ranks needs torch.distributed initialised")
+    if dist.get_world_size(group) != world:
+        raise RuntimeError(f"layer split over {world} ranks but the process group has "
+                           f"{dist.get_world_size(group)}")
+    dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group)
     return y
 
 
@@ -112,19 +124,22 @@ class TPFFN:
         self.down = TPLinear(wd, I, H, qtype, "row", rank, world, device)
         self.group = group
 
-    def prefill(self, x: torch.Tensor) -> torch.Tensor:
-        """x: bf16 [M, H] (replicated) -> fp32 [M, H] (replicated after the all-reduce)."""
+    def prefill(self, x: torch.Tensor, reduce: bool = True) -> torch.Tensor:
+        """x: bf16 [M, H] (replicated) -> fp32 [M, H], replicated after the all-reduce
+        (reduce=False returns this rank's partial sum and leaves the sum to the caller)."""
         g = self.gate.prefill(x, torch.bfloat16)
         u = self.up.prefill(x, torch.bfloat16)
         h = swiglu(g, u, out=g)
-        return _all_reduce(self.down.prefill(h, torch.float32), self.group)
+        y = self.down.prefill(h, torch.float32)
+        return reduce_partial(y, self.down.world, self.group) if reduce else y
 
-    def decode(self, x: torch.Tensor) -> torch.Tensor:
-        """x: fp32 [B, H] -> fp32 [B, H]."""
+    def decode(self, x: torch.Tensor, reduce: bool = True) -> torch.Tensor:
+        """x: fp32 [B, H] -> fp32 [B, H] (reduce as for prefill)."""
         g = self.gate.decode(x)
         u = self.up.decode(x)
         h = swiglu(g, u, out=g)
-        return _all_reduce(self.down.decode(h), self.group)
+        y = self.down.decode(h)
+        return reduce_partial(y, self.down.world, self.group) if reduce else y
 
 
 class TPAttentionProj:
@@ -154,6 +169,8 @@ class TPAttentionProj:
         return (self.q.prefill(x, torch.bfloat16), self.k.prefill(x, torch.bfloat16),
                 self.v.prefill(x, torch.bfloat16))
 
-    def o_prefill(self, attn: torch.Tensor) -> torch.Tensor:
-        """attn: bf16 [M, H / world] (this rank's heads) -> fp32 [M, H] after all-reduce."""
-        return _all_reduce(self.o.prefill(attn, torch.float32), self.group)
+    def o_prefill(self, attn: torch.Tensor, reduce: bool = True) -> torch.Tensor:
+        """attn: bf16 [M, H / world] (this rank's heads) -> fp32 [M, H] after all-reduce
+        (reduce=False: this rank's partial sum)."""
+        y = self.o.prefill(attn, torch.float32)
+        return reduce_partial(y, self.o.world, self.group) if reduce else y
