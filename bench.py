@@ -283,6 +283,27 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_only(args) -> None:
+    """One of the extra measurements on its own (a small, repeatable target for ncu)."""
+    import torch
+    import torch.distributed as dist
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if args.only == "prefill":
+        res = bench_prefill(dev, args.extras_steps)
+    elif args.only == "moe":
+        res = bench_moe(dev, args.extras_steps)
+    else:
+        res = bench_tp(dev, rank, world, args.extras_steps)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        res.update({"n_gpus": world, "only": args.only})
+        print(json.dumps(res), flush=True)
+
+
 def run_gpu(args) -> None:
     import torch
     import torch.distributed as dist
@@ -463,11 +484,15 @@ def main() -> None:
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the prefill GEMM, MoE and tensor-parallel FFN measurements")
     ap.add_argument("--extras-steps", type=int, default=10)
+    ap.add_argument("--only", choices=["prefill", "moe", "tp"],
+                    help="run just this measurement and print its JSON object")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.only:
+        run_only(args)
     else:
         run_gpu(args)
 

@@ -145,16 +145,13 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
       : "memory");
 }
-// Upper bound on how long one try_wait may keep the thread suspended (it resumes as soon
-// as the phase completes); waiting threads then spin far less often.
-constexpr unsigned kTryWaitSuspendNs = 1000000u;  // 1 ms
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity), "n"(kTryWaitSuspendNs)
+      : "r"(bar), "r"(parity)
       : "memory");
   return ok != 0;
 }

@@ -10,14 +10,14 @@
 // cta_group::2 tcgen05 MMAs: M = 256 spread over the pair (128 rows per CTA), N = 256,
 // K = 16, fp32 accumulators in tensor memory.  Each CTA holds two 128 x 256 accumulators
 // (pair rows 128r.. and 256 + 128r.., all 512 TMEM columns).  Each CTA dequantizes only
-// its 128-column half of the weight tile; the pair MMA reads both halves, so every bf16
-// weight is written to shared memory once and read once per pair.  Per 64-deep K step:
+// its 128-column half of the weight tile and holds 128 of the pair's A rows; the pair MMA
+// reads both CTAs' halves.  Per 64-deep K step:
 //   * warp 0 (one lane) TMA-loads the CTA's two 128 x 64 A boxes (128-byte swizzle); the
 //     bytes are reported to the leader's barrier (3-deep ring, freed by the MMAs);
-//   * warp 18 (one lane) TMA-loads the raw quant bytes of the 64 W rows into a 4-deep
+//   * warp 18 (one lane) TMA-loads the raw quant bytes of the 64 W rows into a 3-deep
 //     ring that the dequant warps free as soon as the bytes are in registers;
 //   * warps 2-17 dequantize the raw bytes to bf16 into the K-major, 128-byte swizzled B
-//     half-tile (3-deep ring): warps 2-9 take the even K steps, warps 10-17 the odd ones,
+//     half-tile (4-deep ring): warps 2-9 take the even K steps, warps 10-17 the odd ones,
 //     each warp 8 K rows x 128 columns; they arrive on the leader's B barrier;
 //   * the leader's warp 1 (one lane) issues 2 x 4 MMAs and commits them to barriers in
 //     both CTAs.
@@ -44,7 +44,7 @@ constexpr int kHalfN = BN / 2;               // columns dequantized per CTA
 constexpr int kDeqWarps = 16;                // two groups of 8, alternating K steps
 constexpr int kThreads = 32 * (3 + kDeqWarps);  // + A TMA, MMA, raw TMA warps
 constexpr int kRawWarp = 2 + kDeqWarps;
-constexpr int kAStages = 3, kRStages = 4, kBStages = 3;
+constexpr int kAStages = 3, kRStages = 3, kBStages = 4;
 constexpr int kABoxBytes = 128 * BK * 2;      // one 128 x 64 bf16 box
 constexpr int kBBytes = kHalfN * BK * 2;      // 128 x 64 bf16 B half-tile
 constexpr int kTableBytes = 384;              // per dequant warp
@@ -52,7 +52,7 @@ constexpr int kTmemCols = 512;
 
 template <int QT> struct Raw {
   static constexpr int kTileBytes = Tile<QT>::kBytes;                       // 144 / 210 / 272
-  static constexpr int kPitch = (QT == kQ6_K) ? 224 : kTileBytes;           // TMA box row
+  static constexpr int kPitch = (QT == kQ6_K) ? 240 : kTileBytes;           // TMA box row
   static constexpr int kBytes = kPitch * BK;                                // per stage
   static constexpr int kSlot = (kBytes + 1023) / 1024 * 1024;
 };
@@ -121,10 +121,10 @@ __device__ __forceinline__ void cluster_sync_all() {
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity), "n"(kTryWaitSuspendNs)
+      : "r"(bar), "r"(parity)
       : "memory");
   return ok != 0;
 }
@@ -308,7 +308,7 @@ template <> struct Producer<kQ4_K> {
 // 32r + 2lc, +1 and scale 8r + (lc >> 1).  The 6-bit codes are assembled byte-wise: even
 // columns in one word, odd columns in another.
 template <> struct Producer<kQ6_K> {
-  static constexpr int kPitch = 224;
+  static constexpr int kPitch = 240;
   // table: float2 (d*sc_r, d*sc_r+1) [4 row pairs][8 scales]
   __device__ __forceinline__ static void table(const uint8_t* wrows, int lane, int rank,
                                                uint8_t* tbl) {
