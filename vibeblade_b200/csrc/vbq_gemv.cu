@@ -530,6 +530,16 @@ static int split_override() {
   return v;
 }
 
+// VBQ_GEMV_SCALAR=1 routes Q4_K batch <= 4 to the scalar kernel (comparison runs).
+static bool scalar_override() {
+  static int v = -1;
+  if (v < 0) {
+    const char* env = getenv("VBQ_GEMV_SCALAR");
+    v = (env && atoi(env) == 1) ? 1 : 0;
+  }
+  return v == 1;
+}
+
 GemvPlan plan_gemv(int64_t K, int64_t N, int batch) {
   GemvPlan p{};
   const int64_t tiles = N / 256;
@@ -540,9 +550,9 @@ GemvPlan plan_gemv(int64_t K, int64_t N, int batch) {
   if (S > kGemvMaxSplit) S = kGemvMaxSplit;
   if (S < 1) S = 1;
   if (split_override()) S = split_override();
+  // K-slices of whole 128-row stages (the tensor-core kernel's stage height)
   int64_t kslice = (K + S - 1) / S;
-  kslice = (kslice + 15) / 16 * 16;
-  if (kslice < 16) kslice = 16;
+  kslice = (kslice + 127) / 128 * 128;
   S = (K + kslice - 1) / kslice;
   if (S < 1) S = 1;
   p.splits = (int)S;
@@ -607,7 +617,10 @@ cudaError_t launch_gemv(int qtype, const float* x, const void* w, float* y, int6
                         cudaStream_t st) {
   if (N % 256 != 0 || batch < 1 || batch > 16) return cudaErrorNotSupported;
   switch (qtype) {
-    case kQ4_K: return launch_gemv_q<kQ4_K>(x, w, y, K, N, row_bytes, batch, plan, scratch, st);
+    case kQ4_K:
+      if (!scalar_override() && gemv_mma_fits(x, K, N, batch, plan))
+        return launch_gemv_mma_q4k(x, w, y, K, N, row_bytes, batch, plan, scratch, st);
+      return launch_gemv_q<kQ4_K>(x, w, y, K, N, row_bytes, batch, plan, scratch, st);
     case kQ6_K: return launch_gemv_q<kQ6_K>(x, w, y, K, N, row_bytes, batch, plan, scratch, st);
     case kQ8_0: return launch_gemv_q<kQ8_0>(x, w, y, K, N, row_bytes, batch, plan, scratch, st);
     default: return cudaErrorInvalidValue;

@@ -24,6 +24,14 @@ cudaError_t launch_gemv(int qtype, const float* x, const void* w, float* y, int6
                         int64_t N, int64_t row_bytes, int batch, const GemvPlan& plan,
                         void* scratch, cudaStream_t st);
 
+// Tensor-core (mma.sync) Q4_K GEMV, batch 1..4, when gemv_mma_fits() (K-slices of whole
+// 128-row stages; the CTA's x rows fit in shared memory).  Same scratch layout as the
+// scalar kernel.
+bool gemv_mma_fits(const float* x, int64_t K, int64_t N, int batch, const GemvPlan& plan);
+cudaError_t launch_gemv_mma_q4k(const float* x, const void* w, float* y, int64_t K, int64_t N,
+                                int64_t row_bytes, int batch, const GemvPlan& plan,
+                                void* scratch, cudaStream_t st);
+
 // tcgen05 dequant-GEMM: a bf16 [M,K], W K x N blocks, c fp32 (c_dtype 0) / bf16 (1) [M,N].
 cudaError_t launch_gemm(int qtype, const void* a, const void* w, void* c, int64_t M, int64_t K,
                         int64_t N, int64_t row_bytes, int c_dtype, cudaStream_t st);
@@ -51,6 +59,8 @@ cudaError_t launch_swiglu_f32(const float* g, const float* u, float* h, int64_t 
 // out[t] = sum_slot weight[t, slot] * y[pos[t * topk + slot]], fp32 [T, H], sanitised
 cudaError_t launch_moe_combine(const float* y, const int32_t* pos, const float* weight, int T,
                                int topk, int H, float* out, cudaStream_t st);
+
+cudaError_t gemv_mma_status(unsigned* out, bool clear);
 
 // Sticky device status bits of the GEMV kernels (kStatusTimeout = 1); synchronous.
 cudaError_t gemv_status(unsigned* out, bool clear);
