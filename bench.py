@@ -451,7 +451,9 @@ def run_gpu(args) -> None:
                          "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
                          "traffic": traffic, "traffic_launch": "gate/up 4096x14336 (ncu)",
                          "peak_src": pk["src"] + " (MEASURED_PEAKS.json hbm_gbs)",
-                         "kernel": f"vbq::gemv_kernel<Q4_K,B={B}>",
+                         "kernel": (f"vbq::gmma::gemv_mma_kernel<{1 if B == 1 else 2 if B == 2 else 4}> "
+                                    "(u8 x s8 mma.sync, split-K in a thread-block cluster)" if B <= 4
+                                    else f"vbq::gemv_kernel<Q4_K,B={B}>"),
                          "gemv_4096x14336_gbs": round(big_gbs, 1),
                          "gemv_4096x14336_frac": round(big_gbs / pk["hbm_gbs"], 4)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,

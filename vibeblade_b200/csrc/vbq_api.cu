@@ -93,7 +93,7 @@ static int gemv_checks(int32_t type, int64_t K, int64_t N, int32_t batch) {
 int vbq_gemv_scratch_bytes(int64_t K, int64_t N, int32_t type, int32_t batch, size_t* bytes) {
   if (int rc = gemv_checks(type, K, N, batch)) return rc;
   if (!bytes) return fail(VBQ_ERR_NULL, "vbq_gemv_scratch_bytes: bytes is NULL");
-  *bytes = (K == 0 || N == 0 || N % 256 != 0) ? 0 : vbq::plan_gemv(K, N, batch).scratch_bytes;
+  *bytes = (K == 0 || N == 0 || N % 256 != 0) ? 0 : vbq::plan_gemv(K, N, batch, type).scratch_bytes;
   return ok();
 }
 
@@ -114,7 +114,7 @@ int vbq_gemv(const float* x, const void* w, float* y, int64_t K, int64_t N, int3
   if (N % 256 != 0)
     return fail(VBQ_ERR_UNSUPPORTED,
                 "vbq_gemv: N must be a multiple of 256 (Q8_0 rows of a partial 256-value tile are not implemented)");
-  const vbq::GemvPlan plan = vbq::plan_gemv(K, N, batch);
+  const vbq::GemvPlan plan = vbq::plan_gemv(K, N, batch, type);
   if (plan.scratch_bytes > 0) {
     if (!scratch || scratch_bytes < plan.scratch_bytes)
       return fail(VBQ_ERR_WORKSPACE, "vbq_gemv: scratch needs " + std::to_string(plan.scratch_bytes) +
@@ -230,7 +230,7 @@ extern "C" int vbq_gemv_static_scratch(const float* x, const void* w, float* y, 
     return fail(VBQ_ERR_ALIGN, "vbq_gemv_static_scratch: w and y must be 16-byte aligned, x 4-byte aligned");
   if (N % 256 != 0)
     return fail(VBQ_ERR_UNSUPPORTED, "vbq_gemv_static_scratch: N must be a multiple of 256");
-  const vbq::GemvPlan plan = vbq::plan_gemv(K, N, batch);
+  const vbq::GemvPlan plan = vbq::plan_gemv(K, N, batch, type);
   if (plan.scratch_bytes > kStaticScratchBytes)
     return fail(VBQ_ERR_WORKSPACE,
                 "vbq_gemv_static_scratch: this shape needs " + std::to_string(plan.scratch_bytes) +

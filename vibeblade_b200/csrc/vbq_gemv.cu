@@ -507,7 +507,7 @@ __global__ void __launch_bounds__(256, GemvCfg<QT, B, VPT>::kMinBlocks) gemv_ker
 // ---------------------------------------------------------------------------------
 constexpr int kGemvMinRows = 64, kGemvMaxSplit = 64;
 
-static int sm_count() {
+int sm_count() {
   static int cache[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
@@ -520,7 +520,7 @@ static int sm_count() {
   return cache[dev];
 }
 
-static int split_override() {
+int gemv_split_override() {
   static int v = -1;
   if (v < 0) {
     const char* env = getenv("VBQ_GEMV_SPLIT");  // tuning override, read once
@@ -540,8 +540,13 @@ static bool scalar_override() {
   return v == 1;
 }
 
-GemvPlan plan_gemv(int64_t K, int64_t N, int batch) {
+GemvPlan plan_gemv(int64_t K, int64_t N, int batch, int qtype) {
   GemvPlan p{};
+  if (qtype == kQ4_K && !scalar_override() && gemv_mma_fits(K, N, batch)) {
+    p.splits = 1;  // chosen at launch; the splits reduce in a cluster, without scratch
+    p.kslice = K;
+    return p;
+  }
   const int64_t tiles = N / 256;
   const int64_t slots = (batch <= 2 ? 2LL : 1LL) * sm_count();  // one wave (kMinBlocks)
   int64_t S = tiles > 0 ? slots / tiles : 1;
@@ -549,7 +554,7 @@ GemvPlan plan_gemv(int64_t K, int64_t N, int batch) {
   if (S > s_rows) S = s_rows;
   if (S > kGemvMaxSplit) S = kGemvMaxSplit;
   if (S < 1) S = 1;
-  if (split_override()) S = split_override();
+  if (gemv_split_override()) S = gemv_split_override();
   // K-slices of whole 128-row stages (the tensor-core kernel's stage height)
   int64_t kslice = (K + S - 1) / S;
   kslice = (kslice + 127) / 128 * 128;
@@ -618,8 +623,8 @@ cudaError_t launch_gemv(int qtype, const float* x, const void* w, float* y, int6
   if (N % 256 != 0 || batch < 1 || batch > 16) return cudaErrorNotSupported;
   switch (qtype) {
     case kQ4_K:
-      if (!scalar_override() && gemv_mma_fits(x, K, N, batch, plan))
-        return launch_gemv_mma_q4k(x, w, y, K, N, row_bytes, batch, plan, scratch, st);
+      if (!scalar_override() && gemv_mma_fits(K, N, batch))
+        return launch_gemv_mma_q4k(x, w, y, K, N, row_bytes, batch, st);
       return launch_gemv_q<kQ4_K>(x, w, y, K, N, row_bytes, batch, plan, scratch, st);
     case kQ6_K: return launch_gemv_q<kQ6_K>(x, w, y, K, N, row_bytes, batch, plan, scratch, st);
     case kQ8_0: return launch_gemv_q<kQ8_0>(x, w, y, K, N, row_bytes, batch, plan, scratch, st);

@@ -15,7 +15,7 @@
 //     n + 2^22 in the float mantissa, one XOR turns its two low bytes into signed digits
 //     (the top byte is already 0..127), one PRMT per digit packs two rows.  The digits sum
 //     to n + 4161408; column 3 (7) of B is all ones, so the MMA also yields sum q, and the
-//     offset comes off exactly in 64-bit integers.
+//     offset comes off in int32 (top digit centred) before fp32.
 //   * The s32 accumulators run across the CTA's stages (exact integer sums).  A stage
 //     whose |v| outgrows the scale (rare; warp-uniform) first moves the sums so far to
 //     fp32 and raises the scale.  The min term is summed in fp32 on the side.
@@ -25,9 +25,10 @@
 //
 // Decomposition: a CTA owns one 256-column tile (one Q4_K block per row) and every S-th
 // 128-row stage of the matrix (stages split, split + S, ...), so each CTA samples the
-// whole row range; its partial sums go to the caller's scratch and the CTA finishing a
-// tile last adds the S partials in split order (deterministic) and resets the tile's
-// counter.  Warp 8 TMA-loads the stages (144 B per row) into a 4-deep ring; warps 0-7 each
+// whole row range.  The S splits of a tile form one thread-block cluster (S <= 16): splits
+// 1 .. S-1 store their partial sums into split 0's shared memory with st.async, which
+// counts the bytes on split 0's mbarrier, and exit; split 0 adds them in split order
+// (deterministic) and writes y.  No global scratch, fence or atomic.  Warp 8 TMA-loads the stages (144 B per row) into a 4-deep ring; warps 0-7 each
 // take 32 rows x 128 columns of a stage: the B table for their rows, then 4 x 2 MMAs per
 // column set.  Each lane reads its two rows of x from global memory a stage ahead.  Waits
 // are bounded.
@@ -35,6 +36,7 @@
 #include <cuda_bf16.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "vbq_common.cuh"
 #include "vbq_internal.h"
@@ -53,7 +55,7 @@ constexpr int kThreads = 32 * (kConsumers + 1);
 constexpr int kRows = 16 * kConsumers;   // rows per stage
 constexpr int kPitch = 144;              // one Q4_K block per row
 constexpr int kStageBytes = kRows * kPitch;  // 18432
-constexpr int kStages = 4;
+constexpr int kStages = 4;  // a power of two (slot = stage & (kStages - 1))
 // B table per warp and column set: [4 local sub-blocks][8 columns][32 rows] s8.  Column
 // stride 48 B: the fragment loads (word 12 g + t) hit 32 different banks; sub-block stride
 // 416 B: the row-pair stores of the two lane halves land 16 banks apart.
@@ -63,11 +65,11 @@ constexpr int kTblBytes = 4 * kSbStride;  // 1664
 constexpr int kRedBytes = kConsumers * 4 * 128 * 4 + 4 * 256 * 4;  // per-warp outputs + CTA sum
 // fixed point: |v| < 2^(e + 1) <=> |n| < 2^22 with n = rint(v * 2^(21 - e))
 constexpr float kMagic = 12582912.f;       // 1.5 * 2^23
-constexpr long long kDigitOffset = 4161408;  // sum of the digits minus n
 constexpr int kExpMin = -100, kExpMax = 100;
 
 struct Bars {
   uint64_t full[kStages], empty[kStages];
+  uint64_t red;  // the cluster leader's: the other splits' partial sums have landed
   int abort;
 };
 constexpr int kTblOff = kStages * kStageBytes;
@@ -75,8 +77,11 @@ constexpr int kRedOff = 0;  // the per-warp outputs reuse the stage ring afterwa
 static_assert(kRedBytes <= kStages * kStageBytes, "reduction buffer inside the ring");
 template <int NSET> struct Lay {
   static constexpr int kBarOff = kTblOff + kConsumers * NSET * kTblBytes;
-  static constexpr int kSmem = kBarOff + 128 + 128;  // + alignment slack
+  // the leader's receive slots: splits 1 .. S-1, batch x 256 fp32 each (sized at launch)
+  static constexpr int kRecvOff = kBarOff + 128;
+  static constexpr int kSmem = kRecvOff + 128;  // + alignment slack; plus the slots
 };
+constexpr int kMaxSplit = 16;  // cluster size limit (non-portable above 8)
 
 __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t saddr, uint32_t& r0, uint32_t& r1,
                                                   uint32_t& r2, uint32_t& r3) {
@@ -99,6 +104,53 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
       : "memory");
 }
+// ---- thread-block cluster: one cluster = the K-splits of one tile, leader = split 0 ----
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t mapa_u32(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// 16 bytes into another CTA's shared memory; the bytes complete on its mbarrier
+__device__ __forceinline__ void st_async_v4(uint32_t remote, float4 v, uint32_t remote_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
+      ::"r"(remote), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(remote_bar)
+      : "memory");
+}
+
+// mbarrier wait that lets the hardware park the warp until the phase completes (up to
+// kSuspendNs per try), bounded by `budget` SM cycles overall
+constexpr uint32_t kSuspendNs = 20000;
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_hinted(uint32_t bar, uint32_t parity, long long budget) {
+  if (mbar_try_wait_hint(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait_hint(bar, parity)) {
+    if (clock64() - t0 > budget) return false;
+  }
+  return true;
+}
+
 __device__ __forceinline__ float pow2f(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }
 
 // |v| as the rescale test sees it: values past 2^100, inf and NaN count as 0 (they are
@@ -111,15 +163,13 @@ __device__ __forceinline__ float mag(float v) {
 template <int BATCH>
 __global__ void __launch_bounds__(kThreads, BATCH <= 2 ? 2 : 1)
 gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restrict__ x,
-                float* __restrict__ y, int K, int N, int batch, float* __restrict__ partials,
-                unsigned* __restrict__ counters) {
+                float* __restrict__ y, int K, int N, int batch) {
   constexpr int NSET = BATCH <= 2 ? 1 : 2;  // B column sets: two batch rows per set
   extern __shared__ uint8_t smem_raw[];
   // 128-byte aligned: TMA destinations and ldmatrix rows
   uint8_t* smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
   using L = Lay<NSET>;
   Bars& bars = *reinterpret_cast<Bars*>(smem + L::kBarOff);
-  __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y, S = gridDim.y;
   // CTA `split` takes the 128-row stages split, split + S, split + 2S, ... of the matrix
@@ -132,10 +182,12 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
       mbar_init(smem_u32(&bars.full[s]), 1);
       mbar_init(smem_u32(&bars.empty[s]), kConsumers);
     }
+    mbar_init(smem_u32(&bars.red), 1);
     bars.abort = 0;
     mbar_fence_init();
   }
   __syncthreads();
+  if (S > 1) cluster_arrive();  // barriers initialised; waited for before any remote store
   // Programmatic dependent launch: the next kernel may start filling SMs as this grid
   // drains; weights are streamed before waiting for the previous grid (they never depend
   // on it), x, y and the scratch only after.
@@ -146,9 +198,9 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
     atomicOr(&g_gemv_mma_status, kStatusTimeout);
   };
 
-  // flushed fp32 sums [set][chunk][low / high nibbles][row g / g + 8], min-term sums
-  // [batch][low / high sub-block], non-finite flags (bit 2 b + h)
-  float fac[NSET][4][2][2];
+  // flushed fp32 sums [set][chunk][low / high nibbles] of MMA row g (lanes t even) or
+  // g + 8 (t odd), min-term sums [batch][low / high sub-block], non-finite flags (bit b)
+  float fac[NSET][4][2];
   float mins[BATCH][2];
   unsigned nonfin = 0u;
 #pragma unroll
@@ -156,7 +208,7 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
 #pragma unroll
     for (int c = 0; c < 4; ++c)
 #pragma unroll
-      for (int h = 0; h < 2; ++h) fac[z][c][h][0] = fac[z][c][h][1] = 0.f;
+      for (int h = 0; h < 2; ++h) fac[z][c][h] = 0.f;
 #pragma unroll
   for (int b = 0; b < BATCH; ++b) mins[b][0] = mins[b][1] = 0.f;
 
@@ -167,7 +219,7 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
       for (; it < nst && !*abort_flag; ++it) {
         const int s = it % kStages;
         if (it == kStages) asm volatile("griddepcontrol.wait;" ::: "memory");
-        if (!mbar_wait_bounded(smem_u32(&bars.empty[s]), ((it / kStages) & 1) ^ 1, kWaitBudgetCycles)) {
+        if (!mbar_wait_hinted(smem_u32(&bars.empty[s]), ((it / kStages) & 1) ^ 1, kWaitBudgetCycles)) {
           give_up();
           break;
         }
@@ -182,193 +234,236 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
     asm volatile("griddepcontrol.wait;" ::: "memory");
   } else {
     // ------------------------------ consumers ------------------------------
-    const int gp = warp & 1;          // this warp's columns 128 gp .. + 127
-    const int rw = 32 * (warp >> 1);  // and its 32 rows of each stage
-    // table role: rows rw + 2 rp, + 1 and local group gl (sub-blocks 2 q, 2 q + 1 of the tile)
-    const int rp = lane & 15, gl = lane >> 4, q = 2 * gp + gl;
-    // MMA k index of row 2 rp: rows 8 i + 2 t' + e of matrix i sit at k = 16 (i >> 1) +
-    // 4 t' + 2 (i & 1) + e
-    const int kap0 = 16 * (rp >> 3) + 4 * (rp & 3) + 2 * ((rp >> 2) & 1);
-    const int g = lane >> 2, t = lane & 3;  // MMA fragment role
-    uint8_t* tbl = smem + kTblOff + warp * NSET * kTblBytes;
-    for (int i = lane; i < NSET * kTblBytes / 4; i += 32) reinterpret_cast<uint32_t*>(tbl)[i] = 0u;
-    __syncwarp();
-    for (int i = lane; i < NSET * 4 * 2 * 8; i += 32) {  // all-ones columns 3 and 7
-      const int w8 = i & 7, c2 = (i >> 3) & 1, sb = (i >> 4) & 3, z = i >> 6;
-      reinterpret_cast<uint32_t*>(tbl + z * kTblBytes + sb * kSbStride + (3 + 4 * c2) * kColStride)[w8] =
-          0x01010101u;
-    }
-    __syncwarp();
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-
-    const int row0 = rw + 2 * rp;  // stage row of this lane's first row
-    auto load_x = [&](int it, float2 (&xv)[BATCH]) {
-      const int k = (split + S * it) * kRows + row0;
-#pragma unroll
-      for (int b = 0; b < BATCH; ++b) {
-        const float* xb = x + (int64_t)b * K;
-        xv[b].x = (b < batch && k < K) ? __ldg(xb + k) : 0.f;
-        xv[b].y = (b < batch && k + 1 < K) ? __ldg(xb + k + 1) : 0.f;
+    // warp: columns 128 gp .. + 127 (gp = warp & 1, a template constant below) and rows
+    // rw .. rw + 31 of each stage
+    auto consumer = [&](auto gp_c) {
+      constexpr int GP = decltype(gp_c)::value;
+      const int rw = 32 * (warp >> 1);
+      // table role: rows rw + 2 rp, + 1 and local group gl (sub-blocks 2 q, 2 q + 1 of the
+      // tile, q = 2 GP + gl)
+      const int rp = lane & 15, gl = lane >> 4;
+      // MMA k index of row 2 rp: rows 8 i + 2 t' + e of matrix i sit at k = 16 (i >> 1) +
+      // 4 t' + 2 (i & 1) + e
+      const int kap0 = 16 * (rp >> 3) + 4 * (rp & 3) + 2 * ((rp >> 2) & 1);
+      const int g = lane >> 2, t = lane & 3;  // MMA fragment role
+      uint8_t* tbl = smem + kTblOff + warp * NSET * kTblBytes;
+      for (int i = lane; i < NSET * kTblBytes / 4; i += 32) reinterpret_cast<uint32_t*>(tbl)[i] = 0u;
+      __syncwarp();
+      for (int i = lane; i < NSET * 4 * 2 * 8; i += 32) {  // all-ones columns 3 and 7
+        const int w8 = i & 7, c2 = (i >> 3) & 1, sb = (i >> 4) & 3, z = i >> 6;
+        reinterpret_cast<uint32_t*>(tbl + z * kTblBytes + sb * kSbStride + (3 + 4 * c2) * kColStride)[w8] =
+            0x01010101u;
       }
-    };
-    int acc[NSET][4][2][4];  // [set][chunk][low / high nibbles][fragment]
+      __syncwarp();
+      // the lane's B-table bytes: (set, sub-block 2 gl + h, batch column 4 (b & 1), row pair)
+      uint8_t* const tcol = tbl + (2 * gl) * kSbStride + kap0;
+      // the lane's B fragments: column g, k = 4t .. 4t + 3 (+ 16 for the second register)
+      const uint8_t* const tfrag = tbl + g * kColStride + 4 * t;
+      const uint32_t sel_lo = 0x7440u | (uint32_t)(2 * gl), sel_hi = sel_lo + 1u;  // sub-block byte
+      const int row0 = rw + 2 * rp;  // stage row of this lane's first row
+      // ldmatrix: lane L gives row rw + L (matrix L >> 3, row L & 7) of the warp's qs bytes
+      const uint32_t lm_lane = smem_u32(smem) + (uint32_t)((rw + lane) * kPitch + 16 + 64 * GP);
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+
+      int acc[NSET][4][2][4];  // [set][chunk][low / high nibbles][fragment]
 #pragma unroll
-    for (int z = 0; z < NSET; ++z)
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) acc[z][c][h][0] = acc[z][c][h][1] = acc[z][c][h][2] = acc[z][c][h][3] = 0;
-    float scale[BATCH], step[BATCH], bound[BATCH];
-#pragma unroll
-    for (int b = 0; b < BATCH; ++b) {
-      scale[b] = 1.f;
-      step[b] = 1.f;
-      bound[b] = 0.f;  // the first stage sets the scale
-    }
-    // s32 sums -> fp32: lanes t even hold digits 0, 1 of batch row 2z + t/2, lanes t odd
-    // digit 2 and the code sum of the same row; each pair adds its halves in 64 bits
-    auto flush = [&]() {
-#pragma unroll
-      for (int z = 0; z < NSET; ++z) {
-        const float sb = (t >> 1) ? ((2 * z + 1 < BATCH) ? step[(2 * z + 1) % BATCH] : 0.f) : step[(2 * z) % BATCH];
+      for (int z = 0; z < NSET; ++z)
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            int* a = acc[z][c][h];
-            long long p0, p1;
-            if (t & 1) {
-              p0 = 65536LL * a[0] - kDigitOffset * a[1];
-              p1 = 65536LL * a[2] - kDigitOffset * a[3];
-            } else {
-              p0 = (long long)a[0] + 256LL * a[1];
-              p1 = (long long)a[2] + 256LL * a[3];
-            }
-            p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
-            p1 += __shfl_xor_sync(0xffffffffu, p1, 1);
-            const float f = h ? sb * 0.0625f : sb;  // high nibbles entered as 16 q
-            fac[z][c][h][0] = fmaf((float)p0, f, fac[z][c][h][0]);
-            fac[z][c][h][1] = fmaf((float)p1, f, fac[z][c][h][1]);
-            a[0] = a[1] = a[2] = a[3] = 0;
-          }
-      }
-    };
-
-    float2 xn[BATCH];
-    if (nst > 0) load_x(0, xn);
-    // ldmatrix: lane L gives row rw + L (matrix L >> 3, row L & 7) of the warp's qs bytes
-    const uint32_t lm_lane = (uint32_t)((rw + lane) * kPitch + 16 + 64 * gp);
-    for (int it = 0; it < nst; ++it) {
-      if (*abort_flag) break;
-      float2 xv[BATCH];
-#pragma unroll
-      for (int b = 0; b < BATCH; ++b) xv[b] = xn[b];
-      if (it + 1 < nst) load_x(it + 1, xn);  // a stage ahead
-      const int s = it % kStages;
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bars.full[s]), (it / kStages) & 1,
-                                                      kWaitBudgetCycles))) {
-        if (lane == 0) give_up();
-        break;
-      }
-      const uint8_t* st = stage(s);
-      // ---- scales of the lane's two rows (get_scale_min_k4, cpp/src/dequant.cpp:258-266,
-      // four sub-blocks per word) ----
-      const uint4 h0 = *reinterpret_cast<const uint4*>(st + row0 * kPitch);
-      const uint4 h1 = *reinterpret_cast<const uint4*>(st + (row0 + 1) * kPitch);
-      auto sc4 = [&](const uint4& h) {
-        return q < 2 ? (h.y & 0x3f3f3f3fu) : ((h.w & 0x0f0f0f0fu) | ((h.y >> 2) & 0x30303030u));
-      };
-      auto mn4 = [&](const uint4& h) {
-        return q < 2 ? (h.z & 0x3f3f3f3fu) : (((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u));
-      };
-      const uint32_t s0 = sc4(h0), s1 = sc4(h1), m0 = mn4(h0), m1 = mn4(h1);
-      const uint32_t sel_lo = 0x7440u | (uint32_t)((2 * q) & 3), sel_hi = 0x7440u | (uint32_t)((2 * q + 1) & 3);
-      // small integers as floats: byte into the 2^23 magic, minus 2^23 (exact)
-      const float2 kMag = make_float2(-8388608.f, -8388608.f);
-      const float2 sl = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(s0, 0x4b000000u, sel_lo)),
-                                               __uint_as_float(__byte_perm(s1, 0x4b000000u, sel_lo))), kMag);
-      const float2 sh = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(s0, 0x4b000000u, sel_hi)),
-                                               __uint_as_float(__byte_perm(s1, 0x4b000000u, sel_hi))), kMag);
-      const float2 mlo = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(m0, 0x4b000000u, sel_lo)),
-                                                __uint_as_float(__byte_perm(m1, 0x4b000000u, sel_lo))), kMag);
-      const float2 mhi = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(m0, 0x4b000000u, sel_hi)),
-                                                __uint_as_float(__byte_perm(m1, 0x4b000000u, sel_hi))), kMag);
-      const float2 d = make_float2(f16_ref(h0.x & 0xffffu), f16_ref(h1.x & 0xffffu));
-      const float2 dm = make_float2(f16_ref(h0.x >> 16), f16_ref(h1.x >> 16));
-      // dl = d * sc and ml = dmin * m: the reference's fp32 values (exact products)
-      const float2 dl[2] = {__fmul2_rn(d, sl), __fmul2_rn(d, sh)};
-      const float2 ml[2] = {__fmul2_rn(dm, mlo), __fmul2_rn(dm, mhi)};
-      float2 v[BATCH][2];
-      bool grow = false;
-#pragma unroll
-      for (int b = 0; b < BATCH; ++b)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          v[b][h] = __fmul2_rn(xv[b], dl[h]);
-          mins[b][h] = fmaf(xv[b].x, ml[h].x, fmaf(xv[b].y, ml[h].y, mins[b][h]));
-          const float a = fmaxf(fabsf(v[b][h].x), fabsf(v[b][h].y));
-          if (!(a < 0x1p100f)) nonfin |= 1u << (2 * b + h);  // inf, NaN or past 2^100
-          grow |= fmaxf(mag(v[b][h].x), mag(v[b][h].y)) >= bound[b];
-        }
-      if (__any_sync(0xffffffffu, grow)) {
-        // rare: move the sums to fp32, then scale each batch row to 4-8x its largest |v|
-        flush();
-#pragma unroll
-        for (int b = 0; b < BATCH; ++b) {
-          float m = fmaxf(fmaxf(mag(v[b][0].x), mag(v[b][0].y)), fmaxf(mag(v[b][1].x), mag(v[b][1].y)));
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-          int e = (int)((__float_as_uint(m) >> 23) & 0xffu) - 127 + 2;
-          e = e < kExpMin ? kExpMin : (e > kExpMax ? kExpMax : e);
-          scale[b] = pow2f(21 - e);
-          step[b] = pow2f(e - 21);
-          bound[b] = pow2f(e + 1);
-        }
-      }
-      // ---- B table: three signed digits of n per row pair, batch row b, sub-block ----
-#pragma unroll
-      for (int b = 0; b < BATCH; ++b)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t wx = __float_as_uint(fmaf(v[b][h].x, scale[b], kMagic)) ^ 0x8080u;
-          const uint32_t wy = __float_as_uint(fmaf(v[b][h].y, scale[b], kMagic)) ^ 0x8080u;
-          uint8_t* col = tbl + (b >> 1) * kTblBytes + (2 * gl + h) * kSbStride + 4 * (b & 1) * kColStride + kap0;
-#pragma unroll
-          for (int j = 0; j < 3; ++j)
-            *reinterpret_cast<uint16_t*>(col + j * kColStride) = (uint16_t)__byte_perm(wx, wy, j | ((4 + j) << 4));
-        }
-      __syncwarp();
-      // ---- 4 chunks of 16 byte columns x 32 rows: low- and high-nibble MMAs per set ----
-      const uint32_t lm = smem_u32(st) + lm_lane;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r0, r1, r2, r3;  // rows 0-7, 8-15, 16-23, 24-31 (pairs 2t, 2t+1), bytes 2g, 2g+1
-        ldmatrix_x4_trans(lm + 16 * c, r0, r1, r2, r3);
-        // A rows m = g: byte column 2g, m = g + 8: byte column 2g + 1
-        const uint32_t a0 = __byte_perm(r0, r1, 0x6420), a1 = __byte_perm(r0, r1, 0x7531);
-        const uint32_t a2 = __byte_perm(r2, r3, 0x6420), a3 = __byte_perm(r2, r3, 0x7531);
-#pragma unroll
-        for (int z = 0; z < NSET; ++z) {
-          const uint8_t* tz = tbl + z * kTblBytes + (2 * (c >> 1)) * kSbStride + g * kColStride + 4 * t;
-          const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(tz);
-          const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(tz + 16);
-          const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(tz + kSbStride);
-          const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(tz + kSbStride + 16);
-          mma_u8s8(acc[z][c][0], a0 & 0x0f0f0f0fu, a1 & 0x0f0f0f0fu, a2 & 0x0f0f0f0fu, a3 & 0x0f0f0f0fu, bl0, bl1);
-          mma_u8s8(acc[z][c][1], a0 & 0xf0f0f0f0u, a1 & 0xf0f0f0f0u, a2 & 0xf0f0f0f0u, a3 & 0xf0f0f0f0u, bh0, bh1);
-        }
-      }
-      __syncwarp();  // table and stage reads done
-      if (lane == 0) mbar_arrive(smem_u32(&bars.empty[s]));
-    }
-    flush();
-    // min-term sums and flags of the lane's group: add over its 16 lanes
-#pragma unroll
-    for (int o = 1; o < 16; o <<= 1) {
+          for (int h = 0; h < 2; ++h) acc[z][c][h][0] = acc[z][c][h][1] = acc[z][c][h][2] = acc[z][c][h][3] = 0;
+      float scale[BATCH], step[BATCH], bound[BATCH];
+      float2 mn2[BATCH][2];  // min-term sums, rows 2 rp / 2 rp + 1
 #pragma unroll
       for (int b = 0; b < BATCH; ++b) {
-        mins[b][0] += __shfl_xor_sync(0xffffffffu, mins[b][0], o);
-        mins[b][1] += __shfl_xor_sync(0xffffffffu, mins[b][1], o);
+        scale[b] = 1.f;
+        step[b] = 1.f;
+        bound[b] = 0.f;  // the first stage sets the scale
+        mn2[b][0] = mn2[b][1] = make_float2(0.f, 0.f);
+      }
+      // s32 sums -> fp32.  Lanes t even hold digits 0, 1 of batch row 2z + t/2, lanes t odd
+      // digit 2 and the code sum of the same row.  With the top digit centred (d2 - 64 per
+      // code) the pair's parts are (a0 + 256 a1) and (65536 (a2 - 64 S) + 32896 S), S = sum q:
+      // the int32 difference is exact and the fp32 terms stay within 2^-20 of the result.
+      auto flush = [&]() {
+        const int odd = t & 1;
+        const float c1 = odd ? 65536.f : 1.f, c2 = odd ? 32896.f : 256.f;
+        const int cen = odd ? 64 : 0;
+#pragma unroll
+        for (int z = 0; z < NSET; ++z) {
+          const float sb = (t >> 1) ? ((2 * z + 1 < BATCH) ? step[(2 * z + 1) % BATCH] : 0.f) : step[(2 * z) % BATCH];
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              int* a = acc[z][c][h];
+              float p0 = fmaf(c2, (float)a[1], c1 * (float)(a[0] - cen * a[1]));
+              float p1 = fmaf(c2, (float)a[3], c1 * (float)(a[2] - cen * a[3]));
+              // the pair's halves: lane t even keeps row g, lane t odd row g + 8
+              const float mine = odd ? p1 : p0, other = odd ? p0 : p1;
+              const float sum = mine + __shfl_xor_sync(0xffffffffu, other, 1);
+              const float f = h ? sb * 0.0625f : sb;  // high nibbles entered as 16 q
+              fac[z][c][h] = fmaf(sum, f, fac[z][c][h]);
+              a[0] = a[1] = a[2] = a[3] = 0;
+            }
+        }
+      };
+
+      // x rows of the lane, two stages ahead (L2 latency under a saturated HBM exceeds one
+      // stage): k = the lane's first row in the stage being loaded
+      int kx = split * kRows + row0;
+      const int kstep = S * kRows;
+      float2 xn[BATCH], xnn[BATCH];
+      auto load_x = [&](int k, float2 (&xv)[BATCH]) {
+#pragma unroll
+        for (int b = 0; b < BATCH; ++b) {
+          const float* xb = x + (int64_t)b * K;
+          xv[b].x = (b < batch && k < K) ? __ldg(xb + k) : 0.f;
+          xv[b].y = (b < batch && k + 1 < K) ? __ldg(xb + k + 1) : 0.f;
+        }
+      };
+      load_x(kx, xn);
+      kx += kstep;
+      load_x(kx, xnn);
+      // one stage per iteration, not unrolled: the loop body already fills the instruction
+      // cache (unrolling it 2x / 4x measured 3-7 % slower)
+#pragma unroll 1
+      for (int it = 0; it < nst; ++it) {
+        const int u = it & (kStages - 1);
+        const uint32_t par = (uint32_t)(it / kStages) & 1u;
+        {
+          float2 xv[BATCH];
+#pragma unroll
+          for (int b = 0; b < BATCH; ++b) {
+            xv[b] = xn[b];
+            xn[b] = xnn[b];
+          }
+          kx += kstep;
+          load_x(kx, xnn);  // rows of the stage after next (zero past K)
+          if (!__all_sync(0xffffffffu, mbar_wait_hinted(smem_u32(&bars.full[u]), par, kWaitBudgetCycles))) {
+            if (lane == 0) give_up();
+            break;
+          }
+          const uint8_t* st = smem + u * kStageBytes;
+          // ---- scales of the lane's two rows (get_scale_min_k4, cpp/src/dequant.cpp:258-266,
+          // four sub-blocks per word) ----
+          const uint4 h0 = *reinterpret_cast<const uint4*>(st + row0 * kPitch);
+          const uint4 h1 = *reinterpret_cast<const uint4*>(st + (row0 + 1) * kPitch);
+          uint32_t s0, s1, m0, m1;
+          if constexpr (GP == 0) {  // sub-blocks 0-3: 6-bit fields of scale bytes 0-3 / 4-7
+            s0 = h0.y & 0x3f3f3f3fu;
+            s1 = h1.y & 0x3f3f3f3fu;
+            m0 = h0.z & 0x3f3f3f3fu;
+            m1 = h1.z & 0x3f3f3f3fu;
+          } else {  // sub-blocks 4-7: low / high nibbles of bytes 8-11 + top bits of 0-7
+            s0 = (h0.w & 0x0f0f0f0fu) | ((h0.y >> 2) & 0x30303030u);
+            s1 = (h1.w & 0x0f0f0f0fu) | ((h1.y >> 2) & 0x30303030u);
+            m0 = ((h0.w >> 4) & 0x0f0f0f0fu) | ((h0.z >> 2) & 0x30303030u);
+            m1 = ((h1.w >> 4) & 0x0f0f0f0fu) | ((h1.z >> 2) & 0x30303030u);
+          }
+          // small integers as floats: byte into the 2^23 magic, minus 2^23 (exact)
+          const float2 kMag = make_float2(-8388608.f, -8388608.f);
+          const float2 sl = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(s0, 0x4b000000u, sel_lo)),
+                                                   __uint_as_float(__byte_perm(s1, 0x4b000000u, sel_lo))), kMag);
+          const float2 sh = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(s0, 0x4b000000u, sel_hi)),
+                                                   __uint_as_float(__byte_perm(s1, 0x4b000000u, sel_hi))), kMag);
+          const float2 mlo = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(m0, 0x4b000000u, sel_lo)),
+                                                    __uint_as_float(__byte_perm(m1, 0x4b000000u, sel_lo))), kMag);
+          const float2 mhi = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(m0, 0x4b000000u, sel_hi)),
+                                                    __uint_as_float(__byte_perm(m1, 0x4b000000u, sel_hi))), kMag);
+          const float2 d = make_float2(f16_ref(h0.x & 0xffffu), f16_ref(h1.x & 0xffffu));
+          const float2 dm = make_float2(f16_ref(h0.x >> 16), f16_ref(h1.x >> 16));
+          // dl = d * sc and ml = dmin * m: the reference's fp32 values (exact products)
+          const float2 dl0 = __fmul2_rn(d, sl), dl1 = __fmul2_rn(d, sh);
+          const float2 ml0 = __fmul2_rn(dm, mlo), ml1 = __fmul2_rn(dm, mhi);
+          float2 v[BATCH][2];
+          bool grow = false;
+#pragma unroll
+          for (int b = 0; b < BATCH; ++b) {
+            v[b][0] = __fmul2_rn(xv[b], dl0);
+            v[b][1] = __fmul2_rn(xv[b], dl1);
+            mn2[b][0] = __ffma2_rn(xv[b], ml0, mn2[b][0]);
+            mn2[b][1] = __ffma2_rn(xv[b], ml1, mn2[b][1]);
+            // NaN / inf propagate through the sum; the max ignores NaN and is capped so that
+            // huge values do not force a rescale every stage
+            const float sum = (fabsf(v[b][0].x) + fabsf(v[b][0].y)) + (fabsf(v[b][1].x) + fabsf(v[b][1].y));
+            nonfin |= (sum < 0x1p100f) ? 0u : (1u << b);
+            const float m = fminf(fmaxf(fmaxf(fabsf(v[b][0].x), fabsf(v[b][0].y)),
+                                        fmaxf(fabsf(v[b][1].x), fabsf(v[b][1].y))), 0x1p99f);
+            grow |= m >= bound[b];
+          }
+          if (__any_sync(0xffffffffu, grow)) {
+            // rare: move the sums to fp32, then scale each batch row to 4-8x its largest |v|
+            flush();
+#pragma unroll
+            for (int b = 0; b < BATCH; ++b) {
+              float m = fminf(fmaxf(fmaxf(fabsf(v[b][0].x), fabsf(v[b][0].y)),
+                                    fmaxf(fabsf(v[b][1].x), fabsf(v[b][1].y))), 0x1p99f);
+#pragma unroll
+              for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+              int e = (int)((__float_as_uint(m) >> 23) & 0xffu) - 127 + 2;
+              e = e < kExpMin ? kExpMin : (e > kExpMax ? kExpMax : e);
+              scale[b] = pow2f(21 - e);
+              step[b] = pow2f(e - 21);
+              bound[b] = pow2f(e + 1);
+            }
+          }
+          // ---- B table: three signed digits of n per row pair, batch row b, sub-block ----
+#pragma unroll
+          for (int b = 0; b < BATCH; ++b)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const uint32_t wx = __float_as_uint(fmaf(v[b][h].x, scale[b], kMagic)) ^ 0x8080u;
+              const uint32_t wy = __float_as_uint(fmaf(v[b][h].y, scale[b], kMagic)) ^ 0x8080u;
+              uint8_t* col = tcol + (b >> 1) * kTblBytes + h * kSbStride + 4 * (b & 1) * kColStride;
+#pragma unroll
+              for (int j = 0; j < 3; ++j)
+                *reinterpret_cast<uint16_t*>(col + j * kColStride) = (uint16_t)__byte_perm(wx, wy, j | ((4 + j) << 4));
+            }
+          __syncwarp();
+          // ---- 4 chunks of 16 byte columns x 32 rows: low- and high-nibble MMAs per set ----
+          const uint32_t lm = lm_lane + (uint32_t)(u * kStageBytes);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r0, r1, r2, r3;  // rows 0-7, 8-15, 16-23, 24-31 (pairs 2t, 2t+1), bytes 2g, 2g+1
+            ldmatrix_x4_trans(lm + 16 * c, r0, r1, r2, r3);
+            // A rows m = g: byte column 2g, m = g + 8: byte column 2g + 1
+            const uint32_t a0 = __byte_perm(r0, r1, 0x6420), a1 = __byte_perm(r0, r1, 0x7531);
+            const uint32_t a2 = __byte_perm(r2, r3, 0x6420), a3 = __byte_perm(r2, r3, 0x7531);
+#pragma unroll
+            for (int z = 0; z < NSET; ++z) {
+              const uint8_t* tz = tfrag + z * kTblBytes + (2 * (c >> 1)) * kSbStride;
+              const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(tz);
+              const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(tz + 16);
+              const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(tz + kSbStride);
+              const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(tz + kSbStride + 16);
+              mma_u8s8(acc[z][c][0], a0 & 0x0f0f0f0fu, a1 & 0x0f0f0f0fu, a2 & 0x0f0f0f0fu, a3 & 0x0f0f0f0fu, bl0, bl1);
+              mma_u8s8(acc[z][c][1], a0 & 0xf0f0f0f0u, a1 & 0xf0f0f0f0u, a2 & 0xf0f0f0f0u, a3 & 0xf0f0f0f0u, bh0, bh1);
+            }
+          }
+          __syncwarp();  // table and stage reads done
+          if (lane == 0) mbar_arrive(smem_u32(&bars.empty[u]));
+        }
+      }
+      flush();
+#pragma unroll
+      for (int b = 0; b < BATCH; ++b) {
+        mins[b][0] = mn2[b][0].x + mn2[b][0].y;
+        mins[b][1] = mn2[b][1].x + mn2[b][1].y;
+      }
+    };
+    if (warp & 1) consumer(std::integral_constant<int, 1>{});
+    else consumer(std::integral_constant<int, 0>{});
+    // min-term sums of the lane's group: add over its 16 lanes; flags over the warp (the
+    // warp's scale is shared by both groups)
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      if (o < 16) {
+#pragma unroll
+        for (int b = 0; b < BATCH; ++b) {
+          mins[b][0] += __shfl_xor_sync(0xffffffffu, mins[b][0], o);
+          mins[b][1] += __shfl_xor_sync(0xffffffffu, mins[b][1], o);
+        }
       }
       nonfin |= __shfl_xor_sync(0xffffffffu, nonfin, o);
     }
@@ -391,13 +486,13 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
           const float mB = __shfl_sync(0xffffffffu, mins[(2 * z + 1) % BATCH][h], 16 * gg);
           const unsigned nf = __shfl_sync(0xffffffffu, nonfin, 16 * gg);
           const int b = 2 * z + (t >> 1);
-          if ((t & 1) == 0 && b < BATCH && b < batch) {
+          if (b < BATCH && b < batch) {
             const float mn = (t >> 1) ? mB : mA;
-            const bool bad = (nf >> (2 * b + h)) & 1u;
-            // rows m = g, g + 8 of the chunk: byte columns 2g, 2g + 1 (+ 32: high nibbles)
-            float* dst = red + (warp * 4 + b) * 128 + 64 * gg + 16 * (c & 1) + 2 * g + 32 * h;
-            dst[0] = bad ? __int_as_float(0x7fc00000) : fac[z][c][h][0] - mn;
-            dst[1] = bad ? __int_as_float(0x7fc00000) : fac[z][c][h][1] - mn;
+            const bool bad = (nf >> b) & 1u;
+            // row m = g (t even) / g + 8 (t odd) of the chunk: byte column 2g / 2g + 1
+            // (+ 32: high nibbles)
+            red[(warp * 4 + b) * 128 + 64 * gg + 16 * (c & 1) + 2 * g + (t & 1) + 32 * h] =
+                bad ? __int_as_float(0x7fc00000) : fac[z][c][h] - mn;
           }
         }
   }
@@ -419,23 +514,25 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
       y[(int64_t)(e >> 8) * N + tile * 256 + (e & 255)] = outbuf[e];
     return;
   }
-  // ---- split-K: publish this CTA's partial; the last CTA of the tile adds them up ----
-  for (int e = threadIdx.x; e < E; e += kThreads)
-    partials[((int64_t)split * batch + (e >> 8)) * N + tile * 256 + (e & 255)] = outbuf[e];
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = (atomicAdd(&counters[tile], 1u) == (unsigned)(S - 1));
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  for (int e = threadIdx.x; e < E; e += kThreads) {
-    const int b = e >> 8, n = e & 255;
-    float sum = 0.f;
-    for (int sp = 0; sp < S; ++sp)
-      sum += __ldcg(partials + ((int64_t)sp * batch + b) * N + tile * 256 + n);
-    y[(int64_t)b * N + tile * 256 + n] = sum;
+  // ---- split-K inside the cluster: splits 1 .. S-1 push their partials into the leader's
+  // slots (st.async, counted on its barrier) and exit; the leader adds them in split order
+  cluster_wait();  // every CTA of the cluster has initialised its barriers
+  const uint32_t rank = cluster_rank();
+  float* recv = reinterpret_cast<float*>(smem + L::kRecvOff);
+  if (rank != 0) {
+    const uint32_t dst = mapa_u32(smem_u32(recv + (rank - 1) * E), 0u);
+    const uint32_t bar = mapa_u32(smem_u32(&bars.red), 0u);
+    for (int e4 = threadIdx.x; e4 < E / 4; e4 += kThreads)
+      st_async_v4(dst + 16u * (uint32_t)e4, reinterpret_cast<const float4*>(outbuf)[e4], bar);
+    return;
   }
-  if (threadIdx.x == 0) counters[tile] = 0u;  // leave the scratch ready for the next call
+  if (threadIdx.x == 0) mbar_arrive_expect_tx(smem_u32(&bars.red), (uint32_t)((S - 1) * E * 4));
+  if (!mbar_wait_bounded(smem_u32(&bars.red), 0, kWaitBudgetCycles) && threadIdx.x == 0) give_up();
+  for (int e = threadIdx.x; e < E; e += kThreads) {
+    float sum = outbuf[e];
+    for (int sp = 1; sp < S; ++sp) sum += recv[(sp - 1) * E + e];
+    y[(int64_t)(e >> 8) * N + tile * 256 + (e & 255)] = sum;
+  }
 }
 
 }  // namespace gmma
@@ -459,10 +556,66 @@ static EncodeTiledFnG encode_fn_g() {
   return fn;
 }
 
+// Splits per tile: at most one wave (two CTAs per SM up to batch 2) and 16 (one cluster),
+// the leader's receive slots inside the per-CTA shared memory budget, and room for every
+// tile's cluster at once with 25 % to spare (cudaOccupancyMaxActiveClusters, cached per
+// shape).  Measured on B200 (us per launch, batch 1): 4096 x 14336 S = 4: 11.6, S = 5
+// (56 clusters in 56-59 places): 16.3; 4096 x 6144 S = 8: 8.3, S = 12: 11.7.
+template <int BATCH>
+static int choose_splits(int64_t K, int64_t N, int batch, int smem_base) {
+  using namespace gmma;
+  const int tiles = (int)(N / 256);
+  const int64_t tot_st = (K + kRows - 1) / kRows;
+  const int slots = (BATCH <= 2 ? 2 : 1) * sm_count();
+  int S = tiles > 0 ? slots / tiles : 1;
+  if (S > kMaxSplit) S = kMaxSplit;
+  if (S > tot_st) S = (int)tot_st;
+  if (S < 1) S = 1;
+  const int cap = BATCH <= 2 ? 112 * 1024 : 220 * 1024;  // 2 / 1 CTAs per SM
+  if (gemv_split_override()) {
+    S = gemv_split_override() > kMaxSplit ? kMaxSplit : gemv_split_override();
+    if (S > tot_st) S = (int)tot_st;
+    while (S > 1 && smem_base + (S - 1) * batch * 1024 > cap) --S;
+    return S;
+  }
+  while (S > 1 && smem_base + (S - 1) * batch * 1024 > cap) --S;
+  struct Entry { int64_t tiles; int batch, s_in, s_out; };
+  static Entry cache[32];
+  static int n_cache = 0;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n_cache; ++i)
+    if (cache[i].tiles == tiles && cache[i].batch == batch && cache[i].s_in == S) return cache[i].s_out;
+  const int s_in = S;
+  for (; S > 1; --S) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)tiles, (unsigned)S, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem_base + (S - 1) * batch * 1024;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = (unsigned)S;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int active = 0;
+    if (cudaOccupancyMaxActiveClusters(&active, gmma::gemv_mma_kernel<BATCH>, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      active = 0;
+    }
+    // a quarter of headroom: clusters need S free slots in one GPC at once, and a grid
+    // that fills every GPC to the last cluster leaves some clusters to a second wave
+    // when the previous launch still holds slots (programmatic dependent launch)
+    if (active * 4 >= tiles * 5) break;
+  }
+  if (n_cache < 32) cache[n_cache++] = Entry{tiles, batch, s_in, S};
+  return S;
+}
+
 template <int BATCH>
 static cudaError_t launch_t(const float* x, const void* w, float* y, int64_t K, int64_t N,
-                            int64_t RB, int batch, const GemvPlan& plan, void* scratch,
-                            cudaStream_t st) {
+                            int64_t RB, int batch, cudaStream_t st) {
   using namespace gmma;
   auto enc = encode_fn_g();
   if (!enc) return cudaErrorNotSupported;
@@ -476,46 +629,48 @@ static cudaError_t launch_t(const float* x, const void* w, float* y, int64_t K, 
           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
   auto kern = gemv_mma_kernel<BATCH>;
-  constexpr int kSmem = Lay<(BATCH <= 2 ? 1 : 2)>::kSmem;
+  constexpr int kBase = Lay<(BATCH <= 2 ? 1 : 2)>::kSmem;
   static unsigned configured = 0;  // one bit per device ordinal
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= 32 || !(configured & (1u << dev))) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
     if (dev < 32) configured |= (1u << dev);
   }
-  unsigned* counters = static_cast<unsigned*>(scratch);
-  float* partials = plan.splits > 1
-                        ? reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + plan.counter_bytes)
-                        : nullptr;
+  const int S = choose_splits<BATCH>(K, N, batch, kBase);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(N / 256), (unsigned)plan.splits, 1);
+  cfg.gridDim = dim3((unsigned)(N / 256), (unsigned)S, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSmem;
+  cfg.dynamicSmemBytes = kBase + (S - 1) * batch * 1024;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = (unsigned)S;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, mw, x, y, (int)K, (int)N, batch, partials, counters);
+  cfg.numAttrs = S > 1 ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kern, mw, x, y, (int)K, (int)N, batch);
 }
 
 // Whether the tensor-core kernel takes this call (batch 1..4; any K below 2^31 - 2^8).
-bool gemv_mma_fits(const float*, int64_t K, int64_t N, int batch, const GemvPlan&) {
-  return batch >= 1 && batch <= 4 && K >= 1 && K <= 0x7fffff00LL && N % 256 == 0;
+bool gemv_mma_fits(int64_t K, int64_t N, int batch) {
+  return batch >= 1 && batch <= 4 && K >= 1 && K <= 0x7fffff00LL && N % 256 == 0 && N > 0;
 }
 
 // Tensor-core Q4_K GEMV for batch 1..4.
 cudaError_t launch_gemv_mma_q4k(const float* x, const void* w, float* y, int64_t K, int64_t N,
-                                int64_t row_bytes, int batch, const GemvPlan& plan,
-                                void* scratch, cudaStream_t st) {
-  if (!gemv_mma_fits(x, K, N, batch, plan) || row_bytes % 16 != 0) return cudaErrorNotSupported;
-  if (batch == 1) return launch_t<1>(x, w, y, K, N, row_bytes, batch, plan, scratch, st);
-  if (batch == 2) return launch_t<2>(x, w, y, K, N, row_bytes, batch, plan, scratch, st);
-  return launch_t<4>(x, w, y, K, N, row_bytes, batch, plan, scratch, st);
+                                int64_t row_bytes, int batch, cudaStream_t st) {
+  if (!gemv_mma_fits(K, N, batch) || row_bytes % 16 != 0) return cudaErrorNotSupported;
+  if (batch == 1) return launch_t<1>(x, w, y, K, N, row_bytes, batch, st);
+  if (batch == 2) return launch_t<2>(x, w, y, K, N, row_bytes, batch, st);
+  return launch_t<4>(x, w, y, K, N, row_bytes, batch, st);
 }
 
 cudaError_t gemv_mma_status(unsigned* out, bool clear) {

@@ -15,7 +15,11 @@ struct GemvPlan {
   int64_t counter_bytes; // scratch prefix holding one counter per tile (0 when splits == 1)
   size_t scratch_bytes;  // counters + splits * batch * N fp32 partial sums
 };
-GemvPlan plan_gemv(int64_t K, int64_t N, int batch);
+// `qtype` selects the kernel: the tensor-core Q4_K kernel (batch 1..4) reduces its K-splits
+// inside a thread-block cluster and needs no scratch.
+GemvPlan plan_gemv(int64_t K, int64_t N, int batch, int qtype);
+int sm_count();
+int gemv_split_override();  // VBQ_GEMV_SPLIT (tuning), 0 when unset
 
 // Fused dequant-GEMV; batch in 1..16.  `scratch` must hold plan.scratch_bytes with its
 // counter prefix zero (the kernel leaves it zero).  Returns cudaErrorNotSupported for
@@ -24,13 +28,11 @@ cudaError_t launch_gemv(int qtype, const float* x, const void* w, float* y, int6
                         int64_t N, int64_t row_bytes, int batch, const GemvPlan& plan,
                         void* scratch, cudaStream_t st);
 
-// Tensor-core (mma.sync) Q4_K GEMV, batch 1..4, when gemv_mma_fits() (K-slices of whole
-// 128-row stages; the CTA's x rows fit in shared memory).  Same scratch layout as the
-// scalar kernel.
-bool gemv_mma_fits(const float* x, int64_t K, int64_t N, int batch, const GemvPlan& plan);
+// Tensor-core (integer mma.sync) Q4_K GEMV, batch 1..4, when gemv_mma_fits(); the K-splits
+// of a tile form one thread-block cluster and add up in the leader's shared memory.
+bool gemv_mma_fits(int64_t K, int64_t N, int batch);
 cudaError_t launch_gemv_mma_q4k(const float* x, const void* w, float* y, int64_t K, int64_t N,
-                                int64_t row_bytes, int batch, const GemvPlan& plan,
-                                void* scratch, cudaStream_t st);
+                                int64_t row_bytes, int batch, cudaStream_t st);
 
 // tcgen05 dequant-GEMM: a bf16 [M,K], W K x N blocks, c fp32 (c_dtype 0) / bf16 (1) [M,N].
 cudaError_t launch_gemm(int qtype, const void* a, const void* w, void* c, int64_t M, int64_t K,
