@@ -21,7 +21,7 @@
 //     fp32 and raises the scale.  The min term is summed in fp32 on the side.
 // Accuracy: each v is rounded to 2^-19 of the warp's largest |v| for its batch row (headroom
 // 4-8x), products and sums are exact, fp32 at the end.  A v that is not finite (or beyond
-// 2^100) marks its batch row and sub-block, whose outputs are then NaN.
+// 2^100) marks its batch row in the warp, whose 128 outputs for that row are then NaN.
 //
 // Decomposition: a CTA owns one 256-column tile (one Q4_K block per row) and every S-th
 // 128-row stage of the matrix (stages split, split + S, ...), so each CTA samples the
@@ -56,12 +56,13 @@ constexpr int kRows = 16 * kConsumers;   // rows per stage
 constexpr int kPitch = 144;              // one Q4_K block per row
 constexpr int kStageBytes = kRows * kPitch;  // 18432
 constexpr int kStages = 4;  // a power of two (slot = stage & (kStages - 1))
-// B table per warp and column set: [4 local sub-blocks][8 columns][32 rows] s8.  Column
-// stride 48 B: the fragment loads (word 12 g + t) hit 32 different banks; sub-block stride
-// 416 B: the row-pair stores of the two lane halves land 16 banks apart.
-constexpr int kColStride = 48;
-constexpr int kSbStride = 416;
-constexpr int kTblBytes = 4 * kSbStride;  // 1664
+// B table per warp and column set: [4 local sub-blocks][8 columns][32 rows] s8, each
+// column's rows ordered so that lane (g, t)'s two fragment words (k = 4t.., 16 + 4t..) are
+// adjacent (one 8-byte load at byte 8t of column g; conflict-free per half warp).  Sub-block
+// stride 288 B: the row-pair stores of the two lane halves land 16 banks apart.
+constexpr int kColStride = 32;
+constexpr int kSbStride = 288;
+constexpr int kTblBytes = 4 * kSbStride;  // 1152
 constexpr int kRedBytes = kConsumers * 4 * 128 * 4 + 4 * 256 * 4;  // per-warp outputs + CTA sum
 // fixed point: |v| < 2^(e + 1) <=> |n| < 2^22 with n = rint(v * 2^(21 - e))
 constexpr float kMagic = 12582912.f;       // 1.5 * 2^23
@@ -243,8 +244,8 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
       // tile, q = 2 GP + gl)
       const int rp = lane & 15, gl = lane >> 4;
       // MMA k index of row 2 rp: rows 8 i + 2 t' + e of matrix i sit at k = 16 (i >> 1) +
-      // 4 t' + 2 (i & 1) + e
-      const int kap0 = 16 * (rp >> 3) + 4 * (rp & 3) + 2 * ((rp >> 2) & 1);
+      // 4 t' + 2 (i & 1) + e, stored at byte 8 t' + 4 (i >> 1) + 2 (i & 1) + e of a column
+      const int kap0 = 8 * (rp & 3) + 4 * (rp >> 3) + 2 * ((rp >> 2) & 1);
       const int g = lane >> 2, t = lane & 3;  // MMA fragment role
       uint8_t* tbl = smem + kTblOff + warp * NSET * kTblBytes;
       for (int i = lane; i < NSET * kTblBytes / 4; i += 32) reinterpret_cast<uint32_t*>(tbl)[i] = 0u;
@@ -257,8 +258,8 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
       __syncwarp();
       // the lane's B-table bytes: (set, sub-block 2 gl + h, batch column 4 (b & 1), row pair)
       uint8_t* const tcol = tbl + (2 * gl) * kSbStride + kap0;
-      // the lane's B fragments: column g, k = 4t .. 4t + 3 (+ 16 for the second register)
-      const uint8_t* const tfrag = tbl + g * kColStride + 4 * t;
+      // the lane's B fragments: column g, k = 4t .. 4t + 3 and 16 + 4t .. 16 + 4t + 3
+      const uint8_t* const tfrag = tbl + g * kColStride + 8 * t;
       const uint32_t sel_lo = 0x7440u | (uint32_t)(2 * gl), sel_hi = sel_lo + 1u;  // sub-block byte
       const int row0 = rw + 2 * rp;  // stage row of this lane's first row
       // ldmatrix: lane L gives row rw + L (matrix L >> 3, row L & 7) of the warp's qs bytes
@@ -272,13 +273,12 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
         for (int c = 0; c < 4; ++c)
 #pragma unroll
           for (int h = 0; h < 2; ++h) acc[z][c][h][0] = acc[z][c][h][1] = acc[z][c][h][2] = acc[z][c][h][3] = 0;
-      float scale[BATCH], step[BATCH], bound[BATCH];
+      float scale[BATCH], step[BATCH];
       float2 mn2[BATCH][2];  // min-term sums, rows 2 rp / 2 rp + 1
 #pragma unroll
       for (int b = 0; b < BATCH; ++b) {
-        scale[b] = 1.f;
+        scale[b] = 1.f;  // the first stage sets the scale
         step[b] = 1.f;
-        bound[b] = 0.f;  // the first stage sets the scale
         mn2[b][0] = mn2[b][1] = make_float2(0.f, 0.f);
       }
       // s32 sums -> fp32.  Lanes t even hold digits 0, 1 of batch row 2z + t/2, lanes t odd
@@ -376,27 +376,33 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
           // dl = d * sc and ml = dmin * m: the reference's fp32 values (exact products)
           const float2 dl0 = __fmul2_rn(d, sl), dl1 = __fmul2_rn(d, sh);
           const float2 ml0 = __fmul2_rn(dm, mlo), ml1 = __fmul2_rn(dm, mhi);
+          // v on the current scale: 1.5 * 2^23 + n in the float, in range exactly when the
+          // float keeps the exponent of 2^23 (|n| < 2^22); NaN, inf and overflow leave it
           float2 v[BATCH][2];
-          bool grow = false;
+          uint32_t w[BATCH][2][2];
+          uint32_t out = 0u;
 #pragma unroll
           for (int b = 0; b < BATCH; ++b) {
             v[b][0] = __fmul2_rn(xv[b], dl0);
             v[b][1] = __fmul2_rn(xv[b], dl1);
             mn2[b][0] = __ffma2_rn(xv[b], ml0, mn2[b][0]);
             mn2[b][1] = __ffma2_rn(xv[b], ml1, mn2[b][1]);
-            // NaN / inf propagate through the sum; the max ignores NaN and is capped so that
-            // huge values do not force a rescale every stage
-            const float sum = (fabsf(v[b][0].x) + fabsf(v[b][0].y)) + (fabsf(v[b][1].x) + fabsf(v[b][1].y));
-            nonfin |= (sum < 0x1p100f) ? 0u : (1u << b);
-            const float m = fminf(fmaxf(fmaxf(fabsf(v[b][0].x), fabsf(v[b][0].y)),
-                                        fmaxf(fabsf(v[b][1].x), fabsf(v[b][1].y))), 0x1p99f);
-            grow |= m >= bound[b];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              w[b][h][0] = __float_as_uint(fmaf(v[b][h].x, scale[b], kMagic));
+              w[b][h][1] = __float_as_uint(fmaf(v[b][h].y, scale[b], kMagic));
+              out |= (w[b][h][0] ^ 0x4b000000u) | (w[b][h][1] ^ 0x4b000000u);
+            }
           }
-          if (__any_sync(0xffffffffu, grow)) {
-            // rare: move the sums to fp32, then scale each batch row to 4-8x its largest |v|
-            flush();
+          if (__any_sync(0xffffffffu, out >= (1u << 23)) || it == 0) {
+            // rare (and the first stage): flag non-finite values, move the sums to fp32, then
+            // scale each batch row to 4-8x its largest finite |v| and encode again.  The
+            // max ignores NaN and is capped so that huge values do not rescale every stage.
+            if (it > 0) flush();  // nothing accumulated before the first stage
 #pragma unroll
             for (int b = 0; b < BATCH; ++b) {
+              const float sum = (fabsf(v[b][0].x) + fabsf(v[b][0].y)) + (fabsf(v[b][1].x) + fabsf(v[b][1].y));
+              nonfin |= (sum < 0x1p100f) ? 0u : (1u << b);  // NaN / inf propagate
               float m = fminf(fmaxf(fmaxf(fabsf(v[b][0].x), fabsf(v[b][0].y)),
                                     fmaxf(fabsf(v[b][1].x), fabsf(v[b][1].y))), 0x1p99f);
 #pragma unroll
@@ -405,7 +411,11 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
               e = e < kExpMin ? kExpMin : (e > kExpMax ? kExpMax : e);
               scale[b] = pow2f(21 - e);
               step[b] = pow2f(e - 21);
-              bound[b] = pow2f(e + 1);
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                w[b][h][0] = __float_as_uint(fmaf(v[b][h].x, scale[b], kMagic));
+                w[b][h][1] = __float_as_uint(fmaf(v[b][h].y, scale[b], kMagic));
+              }
             }
           }
           // ---- B table: three signed digits of n per row pair, batch row b, sub-block ----
@@ -413,8 +423,7 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
           for (int b = 0; b < BATCH; ++b)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const uint32_t wx = __float_as_uint(fmaf(v[b][h].x, scale[b], kMagic)) ^ 0x8080u;
-              const uint32_t wy = __float_as_uint(fmaf(v[b][h].y, scale[b], kMagic)) ^ 0x8080u;
+              const uint32_t wx = w[b][h][0] ^ 0x8080u, wy = w[b][h][1] ^ 0x8080u;
               uint8_t* col = tcol + (b >> 1) * kTblBytes + h * kSbStride + 4 * (b & 1) * kColStride;
 #pragma unroll
               for (int j = 0; j < 3; ++j)
@@ -433,12 +442,10 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
 #pragma unroll
             for (int z = 0; z < NSET; ++z) {
               const uint8_t* tz = tfrag + z * kTblBytes + (2 * (c >> 1)) * kSbStride;
-              const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(tz);
-              const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(tz + 16);
-              const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(tz + kSbStride);
-              const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(tz + kSbStride + 16);
-              mma_u8s8(acc[z][c][0], a0 & 0x0f0f0f0fu, a1 & 0x0f0f0f0fu, a2 & 0x0f0f0f0fu, a3 & 0x0f0f0f0fu, bl0, bl1);
-              mma_u8s8(acc[z][c][1], a0 & 0xf0f0f0f0u, a1 & 0xf0f0f0f0u, a2 & 0xf0f0f0f0u, a3 & 0xf0f0f0f0u, bh0, bh1);
+              const uint2 bl = *reinterpret_cast<const uint2*>(tz);
+              const uint2 bh = *reinterpret_cast<const uint2*>(tz + kSbStride);
+              mma_u8s8(acc[z][c][0], a0 & 0x0f0f0f0fu, a1 & 0x0f0f0f0fu, a2 & 0x0f0f0f0fu, a3 & 0x0f0f0f0fu, bl.x, bl.y);
+              mma_u8s8(acc[z][c][1], a0 & 0xf0f0f0f0u, a1 & 0xf0f0f0f0u, a2 & 0xf0f0f0f0u, a3 & 0xf0f0f0f0u, bh.x, bh.y);
             }
           }
           __syncwarp();  // table and stage reads done
