@@ -116,3 +116,46 @@ def test_gemv_linearity_and_row_independence(cuda, qtype):
     y_one = vb.gemv_dequant(x[2].contiguous(), w, None, K, N, qtype)
     # different kernel instantiations (batch 1 vs 4) add in different orders
     assert ((y_one - y[2]).abs().max() / y_one.abs().max()).item() <= 1e-4
+
+
+@pytest.mark.parametrize("qtype,batch", [(F.GGML_TYPE_Q4_K, 1), (F.GGML_TYPE_Q4_K, 4),
+                                         (F.GGML_TYPE_Q8_0, 1), (F.GGML_TYPE_Q6_K, 8)])
+def test_gemv_cuda_graph_replay(cuda, qtype, batch):
+    """A decode engine captures its GEMVs in a CUDA graph: the captured C-ABI call (cluster
+    split-K, or split-K scratch whose counters reset themselves) replays bit-identically to
+    the eager call, repeatedly, and follows new contents of the captured x buffer."""
+    import ctypes as C
+    from vibeblade_b200 import _lib
+    lib = _lib.load()
+    K, N = 4096, 6144
+    w = synthetic_weights(K, N, qtype, seed=21, device=cuda)
+    g = torch.Generator(device=cuda).manual_seed(22)
+    x = torch.randn(batch, K, generator=g, device=cuda)
+    y = torch.empty(batch, N, device=cuda)
+    v = C.c_size_t()
+    _lib.check(lib.vbq_gemv_scratch_bytes(K, N, qtype, batch, C.byref(v)), lib)
+    scratch = torch.zeros(max(int(v.value), 16), dtype=torch.uint8, device=cuda)
+    side = torch.cuda.Stream(cuda)
+
+    def call(stream_ptr):
+        _lib.check(lib.vbq_gemv(x.data_ptr(), w.data_ptr(), y.data_ptr(), K, N, qtype, batch,
+                                scratch.data_ptr(), scratch.numel(), stream_ptr), lib)
+
+    side.wait_stream(torch.cuda.current_stream(cuda))
+    with torch.cuda.stream(side):
+        call(side.cuda_stream)  # warm-up outside the capture (one-time attribute setup)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            call(side.cuda_stream)
+    torch.cuda.current_stream(cuda).wait_stream(side)
+    torch.cuda.synchronize()
+    for _ in range(2):
+        x.copy_(torch.randn(batch, K, generator=g, device=cuda))
+        call(torch.cuda.current_stream(cuda).cuda_stream)
+        torch.cuda.synchronize()
+        y_eager = y.clone()
+        y.fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(y, y_eager)
+    assert vb.device_status() == 0

@@ -560,6 +560,21 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       // tensor memory is freed only after the MMAs writing it have finished
       if (!mbar_wait_bounded(smem_u32(&bars.acc_full), 0, kWaitBudgetCycles)) give_up();
     }
+    // Tail, both CTAs: the last commits of every A / B slot arrive on this CTA's empty
+    // barriers through the pair's multicast, and nothing else waits for them.  The CTA may
+    // not exit (and a CTA of the next wave take its shared memory) while one of those
+    // arrivals is in flight, so wait for each slot's final phase.  After an abort some of
+    // those MMAs were never issued: skip.
+    if (lane == 0 && !*abort_flag) {
+      bool ok = true;
+      for (int j = (nk > kAStages ? nk - kAStages : 0); ok && j < nk; ++j)
+        ok = mbar_wait_bounded_cluster(smem_u32(&bars.empty_a[j % kAStages]), (j / kAStages) & 1,
+                                       kWaitBudgetCycles);
+      for (int j = (nk > kBStages ? nk - kBStages : 0); ok && j < nk; ++j)
+        ok = mbar_wait_bounded_cluster(smem_u32(&bars.empty_b[j % kBStages]), (j / kBStages) & 1,
+                                       kWaitBudgetCycles);
+      if (!ok && !*abort_flag) give_up();
+    }
   } else {
     // ------------------------------ dequant warps ------------------------------
     using P = Producer<QT>;
