@@ -68,7 +68,7 @@ def test_argument_errors_need_no_gpu(lib):
 
 def test_scratch_size_query(lib):
     """Split-K scratch: counters + splits * batch * N partials; none when K is tiny, and
-    none for the tensor-core Q4_K kernel (batch 1..4), whose splits add up inside a
+    none for the tensor-core Q4_K kernel (batch 1..16), whose splits add up inside a
     thread-block cluster."""
     v = C.c_size_t()
     assert lib.vbq_gemv_scratch_bytes(4096, 14336, 14, 1, C.byref(v)) == 0
@@ -76,8 +76,7 @@ def test_scratch_size_query(lib):
     big = v.value
     assert lib.vbq_gemv_scratch_bytes(4096, 14336, 14, 16, C.byref(v)) == 0
     assert v.value > big
-    assert lib.vbq_gemv_scratch_bytes(4096, 14336, 12, 16, C.byref(v)) == 0 and v.value > big
-    for batch in (1, 2, 3, 4):
+    for batch in (1, 2, 3, 4, 5, 8, 16):
         assert lib.vbq_gemv_scratch_bytes(4096, 14336, 12, batch, C.byref(v)) == 0 and v.value == 0
     assert lib.vbq_gemv_scratch_bytes(16, 256, 12, 1, C.byref(v)) == 0 and v.value == 0
     assert lib.vbq_gemv_scratch_bytes(4096, 14336, 9, 1, C.byref(v)) == 1

@@ -64,12 +64,12 @@ import ctypes as C, sys, torch
 sys.path.insert(0, sys.argv[1])
 from vibeblade_b200 import _lib
 lib = _lib.load()
-K, N, t, B = 4096, 14336, 12, 16
+K, N, t, B = 4096, 14336, 14, 16  # Q6_K: the split-K kernel with scratch
 v = C.c_size_t()
 assert lib.vbq_gemv_scratch_bytes(K, N, t, B, C.byref(v)) == 0
 assert v.value > (8 << 20), v.value
 x = torch.zeros(B, K, device="cuda")
-w = torch.zeros(K * (N // 256) * 144, dtype=torch.uint8, device="cuda")
+w = torch.zeros(K * (N // 256) * 210, dtype=torch.uint8, device="cuda")
 y = torch.zeros(B, N, device="cuda")
 rc = lib.vbq_gemv_static_scratch(x.data_ptr(), w.data_ptr(), y.data_ptr(), K, N, t, B,
                                  torch.cuda.current_stream().cuda_stream)

@@ -666,18 +666,27 @@ static cudaError_t launch_t(const float* x, const void* w, float* y, int64_t K, 
   return cudaLaunchKernelEx(&cfg, kern, mw, x, y, (int)K, (int)N, batch);
 }
 
-// Whether the tensor-core kernel takes this call (batch 1..4; any K below 2^31 - 2^8).
+// Whether the tensor-core kernel takes this call (batch 1..16; any K below 2^31 - 2^8).
 bool gemv_mma_fits(int64_t K, int64_t N, int batch) {
-  return batch >= 1 && batch <= 4 && K >= 1 && K <= 0x7fffff00LL && N % 256 == 0 && N > 0;
+  return batch >= 1 && batch <= 16 && K >= 1 && K <= 0x7fffff00LL && N % 256 == 0 && N > 0;
 }
 
-// Tensor-core Q4_K GEMV for batch 1..4.
+// Tensor-core Q4_K GEMV.  Batches above 4 run as consecutive launches over groups of 4
+// batch rows (each launch streams the weights again; matrices that fit in L2 are read
+// from HBM about once).
 cudaError_t launch_gemv_mma_q4k(const float* x, const void* w, float* y, int64_t K, int64_t N,
                                 int64_t row_bytes, int batch, cudaStream_t st) {
   if (!gemv_mma_fits(K, N, batch) || row_bytes % 16 != 0) return cudaErrorNotSupported;
-  if (batch == 1) return launch_t<1>(x, w, y, K, N, row_bytes, batch, st);
-  if (batch == 2) return launch_t<2>(x, w, y, K, N, row_bytes, batch, st);
-  return launch_t<4>(x, w, y, K, N, row_bytes, batch, st);
+  for (int b0 = 0; b0 < batch; b0 += 4) {
+    const int nb = batch - b0 < 4 ? batch - b0 : 4;
+    const float* xg = x + (int64_t)b0 * K;
+    float* yg = y + (int64_t)b0 * N;
+    cudaError_t e = nb == 1   ? launch_t<1>(xg, w, yg, K, N, row_bytes, nb, st)
+                    : nb == 2 ? launch_t<2>(xg, w, yg, K, N, row_bytes, nb, st)
+                              : launch_t<4>(xg, w, yg, K, N, row_bytes, nb, st);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 cudaError_t gemv_mma_status(unsigned* out, bool clear) {

@@ -28,7 +28,7 @@ cudaError_t launch_gemv(int qtype, const float* x, const void* w, float* y, int6
                         int64_t N, int64_t row_bytes, int batch, const GemvPlan& plan,
                         void* scratch, cudaStream_t st);
 
-// Tensor-core (integer mma.sync) Q4_K GEMV, batch 1..4, when gemv_mma_fits(); the K-splits
+// Tensor-core (integer mma.sync) Q4_K GEMV, batch 1..16, when gemv_mma_fits(); the K-splits
 // of a tile form one thread-block cluster and add up in the leader's shared memory.
 bool gemv_mma_fits(int64_t K, int64_t N, int batch);
 cudaError_t launch_gemv_mma_q4k(const float* x, const void* w, float* y, int64_t K, int64_t N,
