@@ -39,6 +39,7 @@
 #include <type_traits>
 
 #include "vbq_common.cuh"
+#include "vbq_gemv_mma.cuh"
 #include "vbq_internal.h"
 
 namespace vbq {
@@ -64,9 +65,6 @@ constexpr int kColStride = 32;
 constexpr int kSbStride = 288;
 constexpr int kTblBytes = 4 * kSbStride;  // 1152
 constexpr int kRedBytes = kConsumers * 4 * 128 * 4 + 4 * 256 * 4;  // per-warp outputs + CTA sum
-// fixed point: |v| < 2^(e + 1) <=> |n| < 2^22 with n = rint(v * 2^(21 - e))
-constexpr float kMagic = 12582912.f;       // 1.5 * 2^23
-constexpr int kExpMin = -100, kExpMax = 100;
 
 struct Bars {
   uint64_t full[kStages], empty[kStages];
@@ -83,83 +81,6 @@ template <int NSET> struct Lay {
   static constexpr int kSmem = kRecvOff + 128;  // + alignment slack; plus the slots
 };
 constexpr int kMaxSplit = 16;  // cluster size limit (non-portable above 8)
-
-__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t saddr, uint32_t& r0, uint32_t& r1,
-                                                  uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(saddr));
-}
-__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                         uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
-      "{%8, %9}, {%0, %1, %2, %3};"
-      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
-                                            uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-      : "memory");
-}
-// ---- thread-block cluster: one cluster = the K-splits of one tile, leader = split 0 ----
-__device__ __forceinline__ void cluster_arrive() {
-  asm volatile("barrier.cluster.arrive.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait() {
-  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t mapa_u32(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-// 16 bytes into another CTA's shared memory; the bytes complete on its mbarrier
-__device__ __forceinline__ void st_async_v4(uint32_t remote, float4 v, uint32_t remote_bar) {
-  asm volatile(
-      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
-      ::"r"(remote), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(remote_bar)
-      : "memory");
-}
-
-// mbarrier wait that lets the hardware park the warp until the phase completes (up to
-// kSuspendNs per try), bounded by `budget` SM cycles overall
-constexpr uint32_t kSuspendNs = 20000;
-__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(kSuspendNs)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_wait_hinted(uint32_t bar, uint32_t parity, long long budget) {
-  if (mbar_try_wait_hint(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (!mbar_try_wait_hint(bar, parity)) {
-    if (clock64() - t0 > budget) return false;
-  }
-  return true;
-}
-
-__device__ __forceinline__ float pow2f(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }
-
-// |v| as the rescale test sees it: values past 2^100, inf and NaN count as 0 (they are
-// flagged instead)
-__device__ __forceinline__ float mag(float v) {
-  const float a = fabsf(v);
-  return a < 0x1p100f ? a : 0.f;
-}
 
 template <int BATCH>
 __global__ void __launch_bounds__(kThreads, BATCH <= 2 ? 2 : 1)
@@ -671,12 +592,16 @@ bool gemv_mma_fits(int64_t K, int64_t N, int batch) {
   return batch >= 1 && batch <= 16 && K >= 1 && K <= 0x7fffff00LL && N % 256 == 0 && N > 0;
 }
 
-// Tensor-core Q4_K GEMV.  Batches above 4 run as consecutive launches over groups of 4
-// batch rows (each launch streams the weights again; matrices that fit in L2 are read
-// from HBM about once).
+// Tensor-core Q4_K GEMV.  Batches 9..16 go to the wide kernel (one pass over the weights)
+// when x's rows are 16-byte aligned; other batches above 4 run as consecutive launches over
+// groups of 4 batch rows (each streams the weights again).  Measured on B200, 4096 x 14336:
+// batch 8 grouped 32.4 us / wide 36.8 us; batch 16 grouped 64.5 us / wide 60.8 us (4096 x
+// 4096: 34.6 / 26.2 us).
 cudaError_t launch_gemv_mma_q4k(const float* x, const void* w, float* y, int64_t K, int64_t N,
                                 int64_t row_bytes, int batch, cudaStream_t st) {
   if (!gemv_mma_fits(K, N, batch) || row_bytes % 16 != 0) return cudaErrorNotSupported;
+  if (batch > 8 && gemv_wide_fits(x, K, N, batch))
+    return launch_gemv_wide_q4k(x, w, y, K, N, row_bytes, batch, st);
   for (int b0 = 0; b0 < batch; b0 += 4) {
     const int nb = batch - b0 < 4 ? batch - b0 : 4;
     const float* xg = x + (int64_t)b0 * K;
