@@ -186,10 +186,11 @@ def bench_moe(dev, steps: int) -> dict:
             "frac_of_bf16_peak": round(tf / peaks()["bf16_tflops"], 4)}
 
 
-def bench_tp(dev, rank: int, world: int, steps: int) -> dict:
+def bench_tp(dev, rank: int, world: int, steps: int, prefill: bool = True) -> dict:
     """70B FFN (hidden 8192, intermediate 28672, Q8_0) split over the
     `world` GPUs (gate / up column split, down row split, NCCL all-reduce of the fp32
-    output); prefill M = 2048 (whole-job TFLOP/s) and decode batch 1 (latency)."""
+    output); prefill M = 2048 (whole-job TFLOP/s, the 2-SM GEMM) and decode batch 1 and 16
+    (latency, the GEMV).  prefill=False measures the decode side only."""
     import torch
     from vibeblade_b200 import tp
     from vibeblade_b200.quantize import synthetic_weights
@@ -201,16 +202,24 @@ def bench_tp(dev, rank: int, world: int, steps: int) -> dict:
     del wg, wu, wd
     torch.cuda.empty_cache()
     g = torch.Generator(device=dev).manual_seed(2)
-    x = torch.randn(M, H, generator=g, device=dev).to(torch.bfloat16)
     xd = torch.randn(1, H, generator=g, device=dev)
+    xd16 = torch.randn(16, H, generator=g, device=dev)
     stream = torch.cuda.current_stream(dev)
+    dms = _time_steps(lambda _: ffn.decode(xd), 5 * steps, 5, stream, world)
+    dms16 = _time_steps(lambda _: ffn.decode(xd16), 5 * steps, 5, stream, world)
+    dec = {"decode_b1_us_per_ffn": round(1e3 * dms / (5 * steps), 1),
+           "decode_b16_us_per_ffn": round(1e3 * dms16 / (5 * steps), 1)}
+    if not prefill:
+        return {"metric": "70B FFN decode latency, batch 1 (Q8_0, TP over the job's GPUs)",
+                "value": dec["decode_b1_us_per_ffn"], "unit": "us", "higher_is_better": False,
+                "tp": world, "scaling": "strong", "steps": 5 * steps, **dec,
+                "collective": "torch.distributed all_reduce (NCCL) of the fp32 [B, 8192] partial sums"}
+    x = torch.randn(M, H, generator=g, device=dev).to(torch.bfloat16)
     ms = _time_steps(lambda _: ffn.prefill(x), steps, 3, stream, world)
     tf = 2 * M * 3 * H * I * steps / (ms * 1e-3) / 1e12
-    dms = _time_steps(lambda _: ffn.decode(xd), 5 * steps, 5, stream, world)
     return {"metric": "70B FFN prefill TFLOP/s (Q8_0, M=2048, TP over the job's GPUs)",
             "value": round(tf, 1), "unit": "TFLOP/s", "tp": world, "scaling": "strong",
-            "ms_per_step": round(ms / steps, 4), "steps": steps,
-            "decode_b1_us_per_ffn": round(1e3 * dms / (5 * steps), 1),
+            "ms_per_step": round(ms / steps, 4), "steps": steps, **dec,
             "collective": "torch.distributed all_reduce (NCCL) of the fp32 [M, 8192] partial sums"}
 
 
@@ -457,6 +466,8 @@ def run_gpu(args) -> None:
             extras["prefill"] = bench_prefill(dev, args.extras_steps)
             extras["moe"] = bench_moe(dev, args.extras_steps)
         extras["tp_ffn"] = bench_tp(dev, rank, world, args.extras_steps)
+    else:  # config 5's decode side runs on the GEMV alone
+        extras["tp_ffn_decode"] = bench_tp(dev, rank, world, args.extras_steps, prefill=False)
 
     pk = peaks()
     line = None

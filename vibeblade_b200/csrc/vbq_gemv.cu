@@ -530,7 +530,7 @@ int gemv_split_override() {
   return v;
 }
 
-// VBQ_GEMV_SCALAR=1 routes Q4_K batch <= 4 to the scalar kernel (comparison runs).
+// VBQ_GEMV_SCALAR=1 routes Q4_K and Q8_0 to the scalar kernel (comparison runs).
 static bool scalar_override() {
   static int v = -1;
   if (v < 0) {
@@ -542,7 +542,8 @@ static bool scalar_override() {
 
 GemvPlan plan_gemv(int64_t K, int64_t N, int batch, int qtype) {
   GemvPlan p{};
-  if (qtype == kQ4_K && !scalar_override() && gemv_mma_fits(K, N, batch)) {
+  if (!scalar_override() && ((qtype == kQ4_K && gemv_mma_fits(K, N, batch)) ||
+                             (qtype == kQ8_0 && gemv_q8_fits(K, N, batch)))) {
     p.splits = 1;  // chosen at launch; the splits reduce in a cluster, without scratch
     p.kslice = K;
     return p;
@@ -627,7 +628,10 @@ cudaError_t launch_gemv(int qtype, const float* x, const void* w, float* y, int6
         return launch_gemv_mma_q4k(x, w, y, K, N, row_bytes, batch, st);
       return launch_gemv_q<kQ4_K>(x, w, y, K, N, row_bytes, batch, plan, scratch, st);
     case kQ6_K: return launch_gemv_q<kQ6_K>(x, w, y, K, N, row_bytes, batch, plan, scratch, st);
-    case kQ8_0: return launch_gemv_q<kQ8_0>(x, w, y, K, N, row_bytes, batch, plan, scratch, st);
+    case kQ8_0:
+      if (!scalar_override() && gemv_q8_fits(K, N, batch))
+        return launch_gemv_q8_mma(x, w, y, K, N, row_bytes, batch, st);
+      return launch_gemv_q<kQ8_0>(x, w, y, K, N, row_bytes, batch, plan, scratch, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -1,0 +1,479 @@
+// vbq_gemv_q8.cu -- Q8_0 dequant-GEMV on the integer tensor cores (decode, batch 1..4).
+//
+//   y[b, n] = sum_k x[b, k] * d[k, j] * q[k, n]      (GGUF Q8_0: 34-byte blocks of 32 columns,
+//   fp16 scale d then 32 int8 codes; cpp/src/cuda_kernels.cu:718-735, vibeblade/loader.py:129)
+//
+// The codes are the s8 A operand of mma.sync m16n8k32 as they are; v = x * d per (row,
+// block) goes into the B columns as three signed byte digits of a 22-bit fixed-point
+// integer on a power-of-two scale per warp and batch row, with an all-ones column for the
+// digits' offset, as in the Q4_K kernel (vbq_gemv_mma.cu).  Accumulation is exact s32.
+//
+// Layout: a CTA owns one 256-column tile (8 blocks, 272 bytes of each row) and every S-th
+// 64-row stage.  A block's codes start 2 bytes into it, so rows are only 2-byte aligned
+// and ldmatrix cannot read them: each lane gathers its A fragment with 16-bit shared loads
+// (two rows x two codes per load pair) and byte permutes.  8 consumer warps = 2 row slices
+// (32 rows) x 4 column quarters (2 blocks = 64 columns); warp 8 TMA-loads the stages.
+// Split-K: the S splits of a tile form a cluster; splits 1..S-1 push their partial sums
+// into split 0's shared memory with st.async and exit, split 0 adds them in split order.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "vbq_common.cuh"
+#include "vbq_gemv_mma.cuh"
+#include "vbq_internal.h"
+
+namespace vbq {
+
+__device__ unsigned g_gemv_q8_status = 0;
+
+namespace gq8 {
+using namespace gmma;
+
+constexpr int kConsumers = 8;
+constexpr int kThreads = 32 * (kConsumers + 1);
+constexpr int kRows = 64;                 // rows per stage
+constexpr int kPitch = 272;               // 8 Q8_0 blocks per row
+constexpr int kStageBytes = kRows * kPitch;  // 17408 (a multiple of 128)
+constexpr int kStages = 4;
+constexpr int kColStride = 32;
+constexpr int kSbStride = 288;            // per block: 8 columns + pad (lane halves 8 banks apart)
+constexpr int kTblBytes = 2 * kSbStride;  // the warp's 2 blocks, one column set
+constexpr int kRedBytes = kConsumers * 4 * 64 * 4 + 4 * 256 * 4;  // [warp][b][64] + [b][256]
+
+struct Bars {
+  uint64_t full[kStages], empty[kStages];
+  uint64_t red;
+  int abort;
+};
+constexpr int kTblOff = kStages * kStageBytes;
+static_assert(kRedBytes <= kStages * kStageBytes, "reduction buffer inside the ring");
+template <int NSET> struct Lay {
+  static constexpr int kBarOff = kTblOff + kConsumers * NSET * kTblBytes;
+  static constexpr int kRecvOff = kBarOff + 128;
+  static constexpr int kSmem = kRecvOff + 128;  // + alignment slack; plus the receive slots
+};
+
+__device__ __forceinline__ void mma_s8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t lds_u16(uint32_t saddr) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(saddr));
+  return (uint32_t)v;
+}
+
+template <int BATCH>
+__global__ void __launch_bounds__(kThreads, 2)
+gemv_q8_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restrict__ x,
+               float* __restrict__ y, int K, int N, int batch) {
+  constexpr int NSET = BATCH <= 2 ? 1 : 2;  // B column sets: two batch rows per set
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
+  using L = Lay<NSET>;
+  Bars& bars = *reinterpret_cast<Bars*>(smem + L::kBarOff);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, split = blockIdx.y, S = gridDim.y;
+  // CTA `split` takes the 64-row stages split, split + S, ... of the matrix
+  const int tot_st = (K + kRows - 1) / kRows;
+  const int nst = split < tot_st ? (tot_st - split + S - 1) / S : 0;
+  auto stage = [&](int s) { return smem + s * kStageBytes; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&bars.full[s]), 1);
+      mbar_init(smem_u32(&bars.empty[s]), kConsumers);
+    }
+    mbar_init(smem_u32(&bars.red), 1);
+    bars.abort = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (S > 1) cluster_arrive();  // barriers initialised; waited for before any remote store
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  volatile int* abort_flag = &bars.abort;
+  auto give_up = [&]() {
+    *abort_flag = 1;
+    atomicOr(&g_gemv_q8_status, kStatusTimeout);
+  };
+
+  float fac[NSET][4];  // flushed fp32 sums [set][chunk]: MMA row g (lanes t even) / g + 8 (t odd)
+  unsigned nonfin = 0u;
+#pragma unroll
+  for (int z = 0; z < NSET; ++z)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) fac[z][k] = 0.f;
+
+  if (warp == kConsumers) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      int it = 0;
+      for (; it < nst && !*abort_flag; ++it) {
+        const int s = it % kStages;
+        if (it == kStages) asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (!mbar_wait_hinted(smem_u32(&bars.empty[s]), ((it / kStages) & 1) ^ 1, kWaitBudgetCycles)) {
+          give_up();
+          break;
+        }
+        const uint32_t fb = smem_u32(&bars.full[s]);
+        mbar_arrive_expect_tx(fb, kStageBytes);
+        tma_load_2d(smem_u32(stage(s)), &tmap_w, tile * (kPitch / 2), (split + S * it) * kRows, fb);
+      }
+      for (int j = (it > kStages ? it - kStages : 0); j < it; ++j)
+        mbar_wait_hinted(smem_u32(&bars.full[j % kStages]), (j / kStages) & 1, kWaitBudgetCycles);
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+  } else {
+    // ------------------------------ consumers ------------------------------
+    const int rw = 32 * (warp >> 2);  // row slice: rows rw .. rw + 31 of each stage
+    const int cq = warp & 3;          // column quarter: blocks 2cq, 2cq + 1
+    // table role: rows rw + 2 rp, + 1 and block 2cq + gl
+    const int rp = lane & 15, gl = lane >> 4;
+    const int kap0 = 8 * (rp & 3) + 4 * (rp >> 3) + 2 * ((rp >> 2) & 1);
+    const int g = lane >> 2, t = lane & 3;  // MMA fragment role
+    uint8_t* tbl = smem + kTblOff + warp * NSET * kTblBytes;
+    for (int i = lane; i < NSET * kTblBytes / 4; i += 32) reinterpret_cast<uint32_t*>(tbl)[i] = 0u;
+    __syncwarp();
+    for (int i = lane; i < NSET * 2 * 2 * 8; i += 32) {  // all-ones columns 3 and 7
+      const int w8 = i & 7, c2 = (i >> 3) & 1, jb = (i >> 4) & 1, z = i >> 5;
+      reinterpret_cast<uint32_t*>(tbl + z * kTblBytes + jb * kSbStride + (3 + 4 * c2) * kColStride)[w8] =
+          0x01010101u;
+    }
+    __syncwarp();
+    uint8_t* const tcol = tbl + gl * kSbStride + kap0;
+    const uint8_t* const tfrag = tbl + g * kColStride + 8 * t;
+    const int row0 = rw + 2 * rp;
+    const int blk = 2 * cq + gl;  // this lane's table block
+    // A gather: lane (g, t) reads codes 2g, 2g + 1 of rows rw + 8i + 2t (+1) of a chunk
+    const uint32_t a_lane = smem_u32(smem) + (uint32_t)((rw + 2 * t) * kPitch + 2 + 2 * g);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    int acc[NSET][4][4];  // [set][chunk][fragment]
+#pragma unroll
+    for (int z = 0; z < NSET; ++z)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc[z][k][0] = acc[z][k][1] = acc[z][k][2] = acc[z][k][3] = 0;
+    float scale[BATCH], step[BATCH];
+#pragma unroll
+    for (int b = 0; b < BATCH; ++b) scale[b] = step[b] = 1.f;
+    // s32 sums -> fp32 (see vbq_gemv_mma.cu): lanes t even hold digits 0, 1 of batch row
+    // 2z + t/2, lanes t odd digit 2 and the code sum; the pair adds its halves
+    auto flush = [&]() {
+      const int odd = t & 1;
+      const float c1 = odd ? 65536.f : 1.f, c2 = odd ? 32896.f : 256.f;
+      const int cen = odd ? 64 : 0;
+#pragma unroll
+      for (int z = 0; z < NSET; ++z) {
+        const float sb = (t >> 1) ? ((2 * z + 1 < BATCH) ? step[(2 * z + 1) % BATCH] : 0.f) : step[(2 * z) % BATCH];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          int* a = acc[z][k];
+          const float p0 = fmaf(c2, (float)a[1], c1 * (float)(a[0] - cen * a[1]));
+          const float p1 = fmaf(c2, (float)a[3], c1 * (float)(a[2] - cen * a[3]));
+          const float mine = odd ? p1 : p0, other = odd ? p0 : p1;
+          const float sum = mine + __shfl_xor_sync(0xffffffffu, other, 1);
+          fac[z][k] = fmaf(sum, sb, fac[z][k]);
+          a[0] = a[1] = a[2] = a[3] = 0;
+        }
+      }
+    };
+
+    int kx = split * kRows + row0;
+    const int kstep = S * kRows;
+    auto load_x = [&](int k, float2 (&xv)[BATCH]) {
+#pragma unroll
+      for (int b = 0; b < BATCH; ++b) {
+        const float* xb = x + (int64_t)b * K;
+        xv[b].x = (b < batch && k < K) ? __ldg(xb + k) : 0.f;
+        xv[b].y = (b < batch && k + 1 < K) ? __ldg(xb + k + 1) : 0.f;
+      }
+    };
+    float2 xn[BATCH], xnn[BATCH];
+    load_x(kx, xn);
+    kx += kstep;
+    load_x(kx, xnn);
+#pragma unroll 1
+    for (int it = 0; it < nst; ++it) {
+      const int s = it & (kStages - 1);
+      float2 xv[BATCH];
+#pragma unroll
+      for (int b = 0; b < BATCH; ++b) {
+        xv[b] = xn[b];
+        xn[b] = xnn[b];
+      }
+      kx += kstep;
+      load_x(kx, xnn);
+      if (!__all_sync(0xffffffffu, mbar_wait_hinted(smem_u32(&bars.full[s]), (uint32_t)(it / kStages) & 1u,
+                                                      kWaitBudgetCycles))) {
+        if (lane == 0) give_up();
+        break;
+      }
+      const uint8_t* st = stage(s);
+      // ---- v = x * d for the lane's two rows of its block (fp16 scale, IEEE) ----
+      const float2 d = make_float2(f16_ieee(*reinterpret_cast<const uint16_t*>(st + row0 * kPitch + 34 * blk)),
+                                   f16_ieee(*reinterpret_cast<const uint16_t*>(st + (row0 + 1) * kPitch + 34 * blk)));
+      float2 v[BATCH];
+      uint32_t w[BATCH][2];
+      uint32_t out = 0u;
+#pragma unroll
+      for (int b = 0; b < BATCH; ++b) {
+        v[b] = __fmul2_rn(xv[b], d);
+        w[b][0] = __float_as_uint(fmaf(v[b].x, scale[b], kMagic));
+        w[b][1] = __float_as_uint(fmaf(v[b].y, scale[b], kMagic));
+        out |= (w[b][0] ^ 0x4b000000u) | (w[b][1] ^ 0x4b000000u);
+      }
+      if (__any_sync(0xffffffffu, out >= (1u << 23)) || it == 0) {
+        // rare (and the first stage): see vbq_gemv_mma.cu
+        if (it > 0) flush();
+#pragma unroll
+        for (int b = 0; b < BATCH; ++b) {
+          const float sum = fabsf(v[b].x) + fabsf(v[b].y);
+          nonfin |= (sum < 0x1p100f) ? 0u : (1u << b);
+          float m = fminf(fmaxf(fabsf(v[b].x), fabsf(v[b].y)), 0x1p99f);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          int e = (int)((__float_as_uint(m) >> 23) & 0xffu) - 127 + 2;
+          e = e < kExpMin ? kExpMin : (e > kExpMax ? kExpMax : e);
+          scale[b] = pow2f(21 - e);
+          step[b] = pow2f(e - 21);
+          w[b][0] = __float_as_uint(fmaf(v[b].x, scale[b], kMagic));
+          w[b][1] = __float_as_uint(fmaf(v[b].y, scale[b], kMagic));
+        }
+      }
+      // ---- B table: three signed digits of n per row pair ----
+#pragma unroll
+      for (int b = 0; b < BATCH; ++b) {
+        const uint32_t wx = w[b][0] ^ 0x8080u, wy = w[b][1] ^ 0x8080u;
+        uint8_t* col = tcol + (b >> 1) * kTblBytes + 4 * (b & 1) * kColStride;
+#pragma unroll
+        for (int dg = 0; dg < 3; ++dg)
+          *reinterpret_cast<uint16_t*>(col + dg * kColStride) = (uint16_t)__byte_perm(wx, wy, dg | ((4 + dg) << 4));
+      }
+      __syncwarp();
+      // ---- 4 chunks of 16 codes x 32 rows: one MMA per set ----
+      const uint32_t sbase = a_lane + (uint32_t)(s * kStageBytes);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t cb = sbase + (uint32_t)(34 * (2 * cq + (k >> 1)) + 16 * (k & 1));
+        uint32_t r[4];  // rows 8i + 2t (low half) and 8i + 2t + 1 (high half), codes 2g, 2g + 1
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          r[i] = __byte_perm(lds_u16(cb + (uint32_t)(8 * i * kPitch)), lds_u16(cb + (uint32_t)((8 * i + 1) * kPitch)),
+                             0x5410);
+        // A rows m = g: code column 2g, m = g + 8: code column 2g + 1
+        const uint32_t a0 = __byte_perm(r[0], r[1], 0x6420), a1 = __byte_perm(r[0], r[1], 0x7531);
+        const uint32_t a2 = __byte_perm(r[2], r[3], 0x6420), a3 = __byte_perm(r[2], r[3], 0x7531);
+#pragma unroll
+        for (int z = 0; z < NSET; ++z) {
+          const uint2 bf = *reinterpret_cast<const uint2*>(tfrag + z * kTblBytes + (k >> 1) * kSbStride);
+          mma_s8s8(acc[z][k], a0, a1, a2, a3, bf.x, bf.y);
+        }
+      }
+      __syncwarp();  // table and stage reads done
+      if (lane == 0) mbar_arrive(smem_u32(&bars.empty[s]));
+    }
+    flush();
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) nonfin |= __shfl_xor_sync(0xffffffffu, nonfin, o);
+  }
+
+  // ---- per-warp outputs -> shared memory (the stage ring, now idle) ----
+  __syncthreads();
+  float* red = reinterpret_cast<float*>(smem);  // [warp][b][64 columns of the warp]
+  if (warp < kConsumers) {
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int z = 0; z < NSET; ++z)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int b = 2 * z + (t >> 1);
+        if (b < BATCH && b < batch)
+          red[(warp * 4 + b) * 64 + 32 * (k >> 1) + 16 * (k & 1) + 2 * g + (t & 1)] =
+              ((nonfin >> b) & 1u) ? __int_as_float(0x7fc00000) : fac[z][k];
+      }
+  }
+  __syncthreads();
+  // ---- sum the two row slices in order: this CTA's partial y ----
+  const int E = batch * 256;
+  float* outbuf = red + kConsumers * 4 * 64;
+  for (int e = threadIdx.x; e < E; e += kThreads) {
+    const int b = e >> 8, n = e & 255, cq = n >> 6, cl = n & 63;
+    outbuf[e] = red[(cq * 4 + b) * 64 + cl] + red[((cq + 4) * 4 + b) * 64 + cl];
+  }
+  __syncthreads();
+  if (S == 1) {
+    for (int e = threadIdx.x; e < E; e += kThreads)
+      y[(int64_t)(e >> 8) * N + tile * 256 + (e & 255)] = outbuf[e];
+    return;
+  }
+  // ---- split-K inside the cluster (as vbq_gemv_mma.cu) ----
+  cluster_wait();
+  const uint32_t rank = cluster_rank();
+  float* recv = reinterpret_cast<float*>(smem + L::kRecvOff);
+  if (rank != 0) {
+    const uint32_t dst = mapa_u32(smem_u32(recv + (rank - 1) * E), 0u);
+    const uint32_t bar = mapa_u32(smem_u32(&bars.red), 0u);
+    for (int e4 = threadIdx.x; e4 < E / 4; e4 += kThreads)
+      st_async_v4(dst + 16u * (uint32_t)e4, reinterpret_cast<const float4*>(outbuf)[e4], bar);
+    return;
+  }
+  if (threadIdx.x == 0) mbar_arrive_expect_tx(smem_u32(&bars.red), (uint32_t)((S - 1) * E * 4));
+  if (!mbar_wait_bounded(smem_u32(&bars.red), 0, kWaitBudgetCycles) && threadIdx.x == 0) give_up();
+  for (int e = threadIdx.x; e < E; e += kThreads) {
+    float sum = outbuf[e];
+    for (int sp = 1; sp < S; ++sp) sum += recv[(sp - 1) * E + e];
+    y[(int64_t)(e >> 8) * N + tile * 256 + (e & 255)] = sum;
+  }
+}
+
+}  // namespace gq8
+
+// ---- host side -----------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFnQ)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFnQ encode_fn_q() {
+  static EncodeTiledFnQ fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFnQ>(p);
+  });
+  return fn;
+}
+
+// Splits per tile as for the Q4_K kernel: one wave of two CTAs per SM, at most 16, the
+// leader's receive slots inside the shared memory budget, 25 % spare cluster places.
+template <int BATCH>
+static int choose_splits_q8(int64_t K, int64_t N, int batch, int smem_base) {
+  using namespace gq8;
+  const int tiles = (int)(N / 256);
+  const int64_t tot_st = (K + kRows - 1) / kRows;
+  int S = tiles > 0 ? 2 * sm_count() / tiles : 1;
+  if (S > 16) S = 16;
+  if (S > tot_st) S = (int)tot_st;
+  if (S < 1) S = 1;
+  const int cap = 112 * 1024;  // two CTAs per SM
+  if (gemv_split_override()) {
+    S = gemv_split_override() > 16 ? 16 : gemv_split_override();
+    if (S > tot_st) S = (int)tot_st;
+    while (S > 1 && smem_base + (S - 1) * batch * 1024 > cap) --S;
+    return S;
+  }
+  while (S > 1 && smem_base + (S - 1) * batch * 1024 > cap) --S;
+  struct Entry { int64_t tiles; int batch, s_in, s_out; };
+  static Entry cache[32];
+  static int n_cache = 0;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n_cache; ++i)
+    if (cache[i].tiles == tiles && cache[i].batch == batch && cache[i].s_in == S) return cache[i].s_out;
+  const int s_in = S;
+  for (; S > 1; --S) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)tiles, (unsigned)S, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem_base + (S - 1) * batch * 1024;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = (unsigned)S;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int active = 0;
+    if (cudaOccupancyMaxActiveClusters(&active, gemv_q8_kernel<BATCH>, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      active = 0;
+    }
+    if (active * 4 >= tiles * 5) break;
+  }
+  if (n_cache < 32) cache[n_cache++] = Entry{tiles, batch, s_in, S};
+  return S;
+}
+
+template <int BATCH>
+static cudaError_t launch_q8_t(const float* x, const void* w, float* y, int64_t K, int64_t N,
+                               int64_t RB, int batch, cudaStream_t st) {
+  using namespace gq8;
+  auto enc = encode_fn_q();
+  if (!enc) return cudaErrorNotSupported;
+  CUtensorMap mw;
+  cuuint64_t dims[2] = {(cuuint64_t)(RB / 2), (cuuint64_t)K};
+  cuuint64_t strides[1] = {(cuuint64_t)RB};
+  cuuint32_t box[2] = {(cuuint32_t)(kPitch / 2), (cuuint32_t)kRows};
+  cuuint32_t es[2] = {1, 1};
+  if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(w), dims, strides, box, es,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  auto kern = gemv_q8_kernel<BATCH>;
+  constexpr int kBase = Lay<(BATCH <= 2 ? 1 : 2)>::kSmem;
+  static unsigned configured = 0;  // one bit per device ordinal
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 32 || !(configured & (1u << dev))) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+    if (dev < 32) configured |= (1u << dev);
+  }
+  const int S = choose_splits_q8<BATCH>(K, N, batch, kBase);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(N / 256), (unsigned)S, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kBase + (S - 1) * batch * 1024;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = (unsigned)S;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = S > 1 ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kern, mw, x, y, (int)K, (int)N, batch);
+}
+
+bool gemv_q8_fits(int64_t K, int64_t N, int batch) {
+  return batch >= 1 && batch <= 16 && K >= 1 && K <= 0x7fffff00LL && N % 256 == 0 && N > 0;
+}
+
+// Tensor-core Q8_0 GEMV; batches above 4 run as launches over groups of 4 batch rows.
+cudaError_t launch_gemv_q8_mma(const float* x, const void* w, float* y, int64_t K, int64_t N,
+                               int64_t row_bytes, int batch, cudaStream_t st) {
+  if (!gemv_q8_fits(K, N, batch) || row_bytes % 16 != 0) return cudaErrorNotSupported;
+  for (int b0 = 0; b0 < batch; b0 += 4) {
+    const int nb = batch - b0 < 4 ? batch - b0 : 4;
+    const float* xg = x + (int64_t)b0 * K;
+    float* yg = y + (int64_t)b0 * N;
+    cudaError_t e = nb == 1   ? launch_q8_t<1>(xg, w, yg, K, N, row_bytes, nb, st)
+                    : nb == 2 ? launch_q8_t<2>(xg, w, yg, K, N, row_bytes, nb, st)
+                              : launch_q8_t<4>(xg, w, yg, K, N, row_bytes, nb, st);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t gemv_q8_status(unsigned* out, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_gemv_q8_status, sizeof(unsigned));
+  if (e != cudaSuccess || !clear) return e;
+  const unsigned zero = 0;
+  return cudaMemcpyToSymbol(g_gemv_q8_status, &zero, sizeof(unsigned));
+}
+
+}  // namespace vbq

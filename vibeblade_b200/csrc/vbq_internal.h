@@ -31,6 +31,11 @@ cudaError_t launch_gemv(int qtype, const float* x, const void* w, float* y, int6
 // Tensor-core (integer mma.sync) Q4_K GEMV, batch 1..16, when gemv_mma_fits(); the K-splits
 // of a tile form one thread-block cluster and add up in the leader's shared memory.
 bool gemv_mma_fits(int64_t K, int64_t N, int batch);
+// Tensor-core Q8_0 GEMV (vbq_gemv_q8.cu), batch 1..16 (groups of 4 above 4), no scratch.
+bool gemv_q8_fits(int64_t K, int64_t N, int batch);
+cudaError_t launch_gemv_q8_mma(const float* x, const void* w, float* y, int64_t K, int64_t N,
+                               int64_t row_bytes, int batch, cudaStream_t st);
+cudaError_t gemv_q8_status(unsigned* out, bool clear);
 // Batch 5..16 kernel (vbq_gemv_wide.cu): x read by TMA, so rows of x 16-byte aligned.
 bool gemv_wide_fits(const float* x, int64_t K, int64_t N, int batch);
 cudaError_t launch_gemv_wide_q4k(const float* x, const void* w, float* y, int64_t K, int64_t N,
