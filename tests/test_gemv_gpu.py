@@ -62,6 +62,37 @@ def test_gemv_ragged_k(cuda, oracle, qtype, K):
     assert max_rel(y, ref) <= TOL
 
 
+@pytest.mark.parametrize("qtype", [F.GGML_TYPE_Q4_K, F.GGML_TYPE_Q8_0])
+@pytest.mark.parametrize("K,batch", [(63, 8), (65, 16), (1000, 13), (1000, 16), (300, 9)])
+def test_gemv_batch_routing_ragged_k(cuda, oracle, qtype, K, batch):
+    """Batches 5-16 take the one-pass kernel when x rows are 16-byte aligned (K % 4 == 0)
+    and groups of 4 otherwise; every route matches the reference."""
+    N = 768
+    rng = np.random.default_rng(K * 17 + batch + qtype)
+    w = quantize(rng.normal(0, 0.3, (K, N)).astype(np.float32), qtype).numpy()
+    x = rng.normal(0, 1, (batch, K)).astype(np.float32)
+    ref = oracle.gemv_dequant(x, w, K, N, qtype)
+    y = vb.gemv_dequant(torch.from_numpy(x).to(cuda), torch.from_numpy(w).to(cuda), None, K, N,
+                        qtype).cpu().numpy()
+    assert max_rel(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("batch", [12, 16])
+def test_gemv_misaligned_x_view(cuda, batch):
+    """x as a view starting 4 bytes into its buffer: not 16-byte aligned, so batch 9-16
+    cannot use the TMA read of x and runs in groups of 4; same result as an aligned copy."""
+    K, N, t = 4096, 4096, F.GGML_TYPE_Q4_K
+    w = synthetic_weights(K, N, t, seed=3, device=cuda)
+    g = torch.Generator(device=cuda).manual_seed(5)
+    buf = torch.randn(batch * K + 1, generator=g, device=cuda)
+    x_view = buf[1:].view(batch, K)
+    assert x_view.data_ptr() % 16 != 0
+    y_view = vb.gemv_dequant(x_view, w, None, K, N, t)
+    y_copy = vb.gemv_dequant(x_view.clone(), w, None, K, N, t)
+    assert ((y_view - y_copy).abs().max() / y_copy.abs().max()).item() <= 1e-5
+    assert vb.device_status() == 0
+
+
 def test_gemv_1d_x_and_out_buffer(cuda, oracle):
     K, N, t = 256, 768, F.GGML_TYPE_Q4_K
     rng = np.random.default_rng(3)
