@@ -461,7 +461,7 @@ def run_gpu(args) -> None:
 
     # ---- configs 3-5: prefill GEMM, MoE (one GPU) and the tensor-parallel 70B FFN ----
     extras = {}
-    if args.extras and not args.no_extras:
+    if not args.no_extras:
         if world == 1:
             extras["prefill"] = bench_prefill(dev, args.extras_steps)
             extras["moe"] = bench_moe(dev, args.extras_steps)
@@ -525,12 +525,10 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch the decode step's GEMVs eagerly instead of replaying a CUDA graph")
-    # The prefill GEMM, MoE and tensor-parallel FFN measurements launch the 2-SM GEMM, which
-    # is kept off the GPU while an intermittent device fault at M = 8192 is unexplained:
-    # they run only when asked for.
     ap.add_argument("--extras", action="store_true",
-                    help="also measure the prefill GEMM, MoE and tensor-parallel FFN (2-SM GEMM)")
-    ap.add_argument("--no-extras", action="store_true", help="(default) skip those measurements")
+                    help="(default) also measure the prefill GEMM, MoE and tensor-parallel FFN")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip those; config 5 is then measured on its decode side only")
     ap.add_argument("--extras-steps", type=int, default=10)
     ap.add_argument("--only", choices=["prefill", "moe", "tp"],
                     help="run just this measurement and print its JSON object")

@@ -14,14 +14,6 @@ if str(ROOT) not in sys.path:
 
 GOLDEN = ROOT / "tests" / "golden"
 
-# The 2-SM tcgen05 GEMM (vbq_gemm.cu: dense, grouped / MoE, tensor-parallel prefill) is kept
-# off the GPU: an unexplained "unspecified launch failure" at M = 8192 (dense, 12 waves of
-# CTA pairs) recurred in a self-checking build, so the kernel does not run again until the
-# cause is found.  Its host-side checks and CPU tests still run.
-GEMM_OFF_GPU = pytest.mark.skip(
-    reason="2-SM GEMM kept off the GPU until an intermittent device fault at M=8192 is explained")
-
-
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA B200 GPU (runs the sm_100a kernels)")
 

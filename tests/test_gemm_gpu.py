@@ -14,7 +14,7 @@ import pytest
 import torch
 
 import vibeblade_b200 as vb
-from conftest import max_rel, GEMM_OFF_GPU
+from conftest import max_rel
 from vibeblade_b200 import formats as F
 from vibeblade_b200.quantize import quantize, synthetic_weights
 
@@ -35,7 +35,6 @@ def _case(cuda, oracle, qtype, M, K, N, seed, out_dtype=torch.float32):
     return c.float().cpu().numpy(), ref
 
 
-@GEMM_OFF_GPU
 def test_gemm_first_tile(cuda, oracle):
     """One CTA, one K step: the smallest case the pipeline has."""
     c, ref = _case(cuda, oracle, F.GGML_TYPE_Q4_K, 256, 64, 256, 0)
@@ -44,20 +43,17 @@ def test_gemm_first_tile(cuda, oracle):
 
 @pytest.mark.parametrize("qtype,N", [(F.GGML_TYPE_Q4_K, 512), (F.GGML_TYPE_Q8_0, 512),
                                      (F.GGML_TYPE_Q6_K, 2048)])
-@GEMM_OFF_GPU
 @pytest.mark.parametrize("M,K", [(256, 512), (1, 256), (100, 320), (300, 1024), (512, 64)])
 def test_gemm_vs_oracle(cuda, oracle, qtype, N, M, K):
     c, ref = _case(cuda, oracle, qtype, M, K, N, M * 7 + K + qtype)
     assert max_rel(c, ref) <= TOL
 
 
-@GEMM_OFF_GPU
 def test_gemm_bf16_output(cuda, oracle):
     c, ref = _case(cuda, oracle, F.GGML_TYPE_Q4_K, 256, 512, 512, 3, out_dtype=torch.bfloat16)
     assert max_rel(c, ref) <= TOL
 
 
-@GEMM_OFF_GPU
 def test_gemm_ragged_k_tail(cuda, oracle):
     """K not a multiple of the 64-deep K step: the tail rows come in as zeros."""
     c, ref = _case(cuda, oracle, F.GGML_TYPE_Q8_0, 128, 200, 256, 5)
@@ -69,7 +65,6 @@ FULL = [(F.GGML_TYPE_Q6_K, 512, 4096, 14336), (F.GGML_TYPE_Q6_K, 512, 14336, 409
         (F.GGML_TYPE_Q4_K, 512, 4096, 14336), (F.GGML_TYPE_Q8_0, 256, 8192, 28672)]
 
 
-@GEMM_OFF_GPU
 @pytest.mark.parametrize("qtype,M,K,N", FULL)
 def test_gemm_full_size_vs_fp32_matmul(cuda, qtype, M, K, N):
     w = synthetic_weights(K, N, qtype, seed=0, device=cuda)

@@ -10,7 +10,7 @@ import pytest
 import torch
 
 import vibeblade_b200 as vb
-from conftest import GEMM_OFF_GPU, load_golden, max_rel
+from conftest import load_golden, max_rel
 from oracle.moe_oracle import moe_ffn as oracle_moe_ffn
 from oracle.moe_oracle import route as oracle_route
 from vibeblade_b200 import formats as F
@@ -46,7 +46,6 @@ def test_route_vs_oracle(cuda):
         np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
 
 
-@GEMM_OFF_GPU
 def test_moe_ffn_matches_reference_golden(cuda):
     g = load_golden("moe_q4_k")
     T, H, I, E, k, t = (int(g[n]) for n in ("T", "H", "I", "E", "topk", "type"))
@@ -60,7 +59,6 @@ def test_moe_ffn_matches_reference_golden(cuda):
 
 @pytest.mark.parametrize("qtype,K,N", [(F.GGML_TYPE_Q4_K, 256, 512), (F.GGML_TYPE_Q8_0, 320, 256),
                                        (F.GGML_TYPE_Q6_K, 128, 2048)])
-@GEMM_OFF_GPU
 def test_gemm_grouped_vs_oracle(cuda, oracle, qtype, K, N):
     rng = np.random.default_rng(K + N + qtype)
     E = 5
@@ -90,7 +88,6 @@ def test_gemm_grouped_vs_oracle(cuda, oracle, qtype, K, N):
 @pytest.mark.parametrize("qtype,T,H,I,E,k", [(F.GGML_TYPE_Q4_K, 300, 512, 768, 6, 2),
                                              (F.GGML_TYPE_Q8_0, 129, 256, 512, 4, 3),
                                              (F.GGML_TYPE_Q6_K, 40, 2048, 2048, 3, 1)])
-@GEMM_OFF_GPU
 def test_moe_ffn_vs_oracle(cuda, oracle, qtype, T, H, I, E, k):
     rng = np.random.default_rng(T + H + I)
     wg, wu, wd = _slabs(rng, E, H, I, qtype), _slabs(rng, E, H, I, qtype), _slabs(rng, E, I, H, qtype)
@@ -107,7 +104,6 @@ def test_moe_ffn_vs_oracle(cuda, oracle, qtype, T, H, I, E, k):
     assert max_rel(out.cpu().numpy(), ref) <= TOL
 
 
-@GEMM_OFF_GPU
 def test_moe_ffn_config4_sampled_tokens(cuda):
     """BASELINE config 4 (8 experts, top-2, hidden 4096, expert intermediate 14336, Q4_K,
     4096 tokens): full-size device run; 12 sampled tokens recomputed with torch fp32

@@ -20,7 +20,6 @@ import torch
 import vibeblade_b200 as vb
 from vibeblade_b200 import formats as F
 from vibeblade_b200 import tp
-from conftest import GEMM_OFF_GPU
 from vibeblade_b200.quantize import synthetic_weights
 
 pytestmark = pytest.mark.gpu
@@ -67,7 +66,6 @@ def ffn_setup(cuda):
     return wg, wu, wd, x, ref_p, ref_d
 
 
-@GEMM_OFF_GPU
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
 def test_tp_ffn_prefill_emulated(cuda, ffn_setup, world):
     wg, wu, wd, x, ref_p, _ = ffn_setup
@@ -90,7 +88,6 @@ def test_tp_ffn_decode_emulated(cuda, ffn_setup, world):
     assert _rel(y, ref_d) <= 1e-3
 
 
-@GEMM_OFF_GPU
 def test_tp_attention_projections_emulated(cuda):
     """Q / K / V column split by heads (K / V replicated at TP = 8), o row split."""
     KV = 1024  # 8 KV heads x 128
@@ -142,7 +139,6 @@ def _nccl_rank(rank, world, port, res):
         dist.destroy_process_group()
 
 
-@GEMM_OFF_GPU
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
 def test_tp_ffn_nccl():
     import torch.multiprocessing as mp

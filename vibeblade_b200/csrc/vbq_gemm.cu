@@ -15,7 +15,13 @@
 //   * warp 0 (one lane) TMA-loads the CTA's two 128 x 64 A boxes (128-byte swizzle); the
 //     bytes are reported to the leader's barrier (3-deep ring, freed by the MMAs);
 //   * warp 18 (one lane) TMA-loads the raw quant bytes of the 64 W rows into a 3-deep
-//     ring that the dequant warps free as soon as the bytes are in registers;
+//     ring that the dequant warps free as soon as the bytes are in registers.  With an odd
+//     depth a slot alternates between the two dequant groups, so each slot has one "full"
+//     barrier per group.  A parity wait for phase k also passes while the barrier is still
+//     in phase k - 1 (same test, other parity); on a barrier shared with the other group,
+//     a group could reach its next visit of a slot (phase k) before the other group's
+//     load (phase k - 1) had landed, read stale bytes, release the slot early and let the
+//     producer arrive again on a phase whose arrival was spent;
 //   * warps 2-17 dequantize the raw bytes to bf16 into the K-major, 128-byte swizzled B
 //     half-tile (4-deep ring): warps 2-9 take the even K steps, warps 10-17 the odd ones,
 //     each warp 8 K rows x 128 columns; they arrive on the leader's B barrier;
@@ -45,6 +51,9 @@ constexpr int kDeqWarps = 16;                // two groups of 8, alternating K s
 constexpr int kThreads = 32 * (3 + kDeqWarps);  // + A TMA, MMA, raw TMA warps
 constexpr int kRawWarp = 2 + kDeqWarps;
 constexpr int kAStages = 3, kRStages = 3, kBStages = 4;
+// raw steps it and it + kRCycle use the same slot and the same dequant group (it & 1)
+constexpr int kRCycle = (kRStages % 2) ? 2 * kRStages : kRStages;
+static_assert(kBStages % 2 == 0, "each B slot belongs to one dequant group");
 constexpr int kABoxBytes = 128 * BK * 2;      // one 128 x 64 bf16 box
 constexpr int kBBytes = kHalfN * BK * 2;      // 128 x 64 bf16 B half-tile
 constexpr int kTableBytes = 384;              // per dequant warp
@@ -59,7 +68,7 @@ template <int QT> struct Raw {
 
 struct Bars {
   uint64_t full_a[kAStages], empty_a[kAStages];
-  uint64_t full_raw[kRStages], empty_raw[kRStages];
+  uint64_t full_raw[kRStages][2], empty_raw[kRStages];  // full: per slot and dequant group
   uint64_t full_b[kBStages], empty_b[kBStages];
   uint64_t acc_full;
   uint32_t tmem_base;
@@ -464,7 +473,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       mbar_init(smem_u32(&bars.empty_a[s]), 1);  // MMA commit
     }
     for (int q = 0; q < kRStages; ++q) {
-      mbar_init(smem_u32(&bars.full_raw[q]), 1);
+      mbar_init(smem_u32(&bars.full_raw[q][0]), 1);
+      mbar_init(smem_u32(&bars.full_raw[q][1]), 1);
       mbar_init(smem_u32(&bars.empty_raw[q]), kDeqWarps / 2);  // the warps of one group
     }
     for (int t = 0; t < kBStages; ++t) {
@@ -523,14 +533,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           give_up();
           break;
         }
-        const uint32_t fb = smem_u32(&bars.full_raw[q]);
+        const uint32_t fb = smem_u32(&bars.full_raw[q][it & 1]);  // the consuming group's
         mbar_arrive_expect_tx(fb, R::kBytes);
         if constexpr (GROUPED) tma_load_3d(smem_u32(raw_stage(q)), &tmap_w, tile_x / 2, it * BK, slab, fb);
         else tma_load_2d(smem_u32(raw_stage(q)), &tmap_w, tile_x / 2, it * BK, fb);
       }
       // drain: every issued raw stage must land before the CTA may exit
       for (int j = (it > kRStages ? it - kRStages : 0); j < it; ++j)
-        mbar_wait_bounded(smem_u32(&bars.full_raw[j % kRStages]), (j / kRStages) & 1, kWaitBudgetCycles);
+        mbar_wait_bounded(smem_u32(&bars.full_raw[j % kRStages][j & 1]), (j / kRCycle) & 1, kWaitBudgetCycles);
     }
   } else if (warp == 1) {
     // --------------------------- MMA issuer (leader) ---------------------------
@@ -594,7 +604,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     for (int it = grp; it < nk; it += 2) {
       if (*abort_flag) break;
       const int q = it % kRStages, t = it % kBStages;
-      if (!mbar_wait_bounded(smem_u32(&bars.full_raw[q]), (it / kRStages) & 1, kWaitBudgetCycles)) {
+      // this group's own barrier of the slot: its phases are exactly this group's visits
+      if (!mbar_wait_bounded(smem_u32(&bars.full_raw[q][grp]), (it / kRCycle) & 1, kWaitBudgetCycles)) {
         give_up();
         break;
       }
