@@ -6,10 +6,10 @@
 //   y[b, n] = sum_k q[k, n] * v[b, k, s]  -  sum_k x[b, k] * ml[k, s],   v = x * dl,
 // the first term runs on mma.sync m16n8k32 (u8 x s8 -> s32), two instructions per 1024
 // weights:
-//   * A (16 columns x 32 rows): the 4-bit codes as exact u8.  ldmatrix.trans of four
-//     8-row matrices hands each lane the bytes of rows (2t, 2t+1) of two adjacent byte
-//     columns from each matrix; one PRMT per register gathers four rows of one byte
-//     column, one LOP keeps the low nibbles (q) or the high nibbles in place (16 q).
+//   * A (16 columns x 32 rows): the 4-bit codes as exact u8.  One byte-granular
+//     ldmatrix.trans (m16n16, two matrices) hands each lane four rows of one byte column
+//     per register, the MMA's A fragment as it stands; one LOP keeps the low nibbles (q)
+//     or the high nibbles in place (16 q).
 //   * B (32 rows x 8): v as a 22-bit fixed-point integer n on a power-of-two scale per warp
 //     and batch row, in three signed byte digits.  One FFMA with the 1.5 * 2^23 magic puts
 //     n + 2^22 in the float mantissa, one XOR turns its two low bytes into signed digits
@@ -164,9 +164,10 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
       // table role: rows rw + 2 rp, + 1 and local group gl (sub-blocks 2 q, 2 q + 1 of the
       // tile, q = 2 GP + gl)
       const int rp = lane & 15, gl = lane >> 4;
-      // MMA k index of row 2 rp: rows 8 i + 2 t' + e of matrix i sit at k = 16 (i >> 1) +
-      // 4 t' + 2 (i & 1) + e, stored at byte 8 t' + 4 (i >> 1) + 2 (i & 1) + e of a column
-      const int kap0 = 8 * (rp & 3) + 4 * (rp >> 3) + 2 * ((rp >> 2) & 1);
+      // the MMA's k index is the row (0..31); row r is stored at byte 8 ((r & 15) >> 2) +
+      // 4 (r >> 4) + (r & 3) of a column, so lane t's fragment words (rows 4t.., 16 + 4t..)
+      // are adjacent; rows 2 rp, 2 rp + 1 are one 16-bit slot
+      const int kap0 = 8 * ((rp & 7) >> 1) + 4 * (rp >> 3) + 2 * (rp & 1);
       const int g = lane >> 2, t = lane & 3;  // MMA fragment role
       uint8_t* tbl = smem + kTblOff + warp * NSET * kTblBytes;
       for (int i = lane; i < NSET * kTblBytes / 4; i += 32) reinterpret_cast<uint32_t*>(tbl)[i] = 0u;
@@ -355,11 +356,8 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
           const uint32_t lm = lm_lane + (uint32_t)(u * kStageBytes);
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            uint32_t r0, r1, r2, r3;  // rows 0-7, 8-15, 16-23, 24-31 (pairs 2t, 2t+1), bytes 2g, 2g+1
-            ldmatrix_x4_trans(lm + 16 * c, r0, r1, r2, r3);
-            // A rows m = g: byte column 2g, m = g + 8: byte column 2g + 1
-            const uint32_t a0 = __byte_perm(r0, r1, 0x6420), a1 = __byte_perm(r0, r1, 0x7531);
-            const uint32_t a2 = __byte_perm(r2, r3, 0x6420), a3 = __byte_perm(r2, r3, 0x7531);
+            uint32_t a0, a1, a2, a3;  // A rows m = g / g + 8: byte columns g / g + 8
+            ldmatrix_a8_trans(lm + 16 * c, a0, a1, a2, a3);
 #pragma unroll
             for (int z = 0; z < NSET; ++z) {
               const uint8_t* tz = tfrag + z * kTblBytes + (2 * (c >> 1)) * kSbStride;
@@ -417,9 +415,9 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
           if (b < BATCH && b < batch) {
             const float mn = (t >> 1) ? mB : mA;
             const bool bad = (nf >> b) & 1u;
-            // row m = g (t even) / g + 8 (t odd) of the chunk: byte column 2g / 2g + 1
+            // row m = g (t even) / g + 8 (t odd) of the chunk: byte column g / g + 8
             // (+ 32: high nibbles)
-            red[(warp * 4 + b) * 128 + 64 * gg + 16 * (c & 1) + 2 * g + (t & 1) + 32 * h] =
+            red[(warp * 4 + b) * 128 + 64 * gg + 16 * (c & 1) + g + 8 * (t & 1) + 32 * h] =
                 bad ? __int_as_float(0x7fc00000) : fac[z][c][h] - mn;
           }
         }

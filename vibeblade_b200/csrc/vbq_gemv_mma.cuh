@@ -14,9 +14,12 @@ namespace gmma {
 constexpr float kMagic = 12582912.f;  // 1.5 * 2^23
 constexpr int kExpMin = -100, kExpMax = 100;
 
-__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t saddr, uint32_t& r0, uint32_t& r1,
+// 32 rows x 16 bytes (lane L gives the address of row L) as the m16n8k32 8-bit A fragment:
+// r0 / r1 = rows 4t .. 4t + 3 of byte column g / g + 8, r2 / r3 = rows 16 + 4t .. (g = lane / 4,
+// t = lane % 4); byte-granular transpose, so the codes need no permute after the load
+__device__ __forceinline__ void ldmatrix_a8_trans(uint32_t saddr, uint32_t& r0, uint32_t& r1,
                                                   uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+  asm volatile("ldmatrix.sync.aligned.m16n16.x2.trans.shared.b8 {%0, %1, %2, %3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(saddr));
 }

@@ -146,7 +146,7 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
     const int G = c >> 1;          // 64-column group: sub-blocks 2G (low), 2G + 1 (high)
     // table role: rows 2 rp, 2 rp + 1 of the stage, batch rows bh * HB .. + HB - 1
     const int rp = lane & 15, bh = lane >> 4;
-    const int kap0 = 8 * (rp & 3) + 4 * (rp >> 3) + 2 * ((rp >> 2) & 1);
+    const int kap0 = 8 * ((rp & 7) >> 1) + 4 * (rp >> 3) + 2 * (rp & 1);  // as in vbq_gemv_mma.cu
     const int g = lane >> 2, t = lane & 3;  // MMA fragment role
     uint8_t* tbl = smem + C::kTblOff + warp * C::kTbl;
     float* fac = reinterpret_cast<float*>(smem + C::kFacOff + warp * C::kFac);  // [set][h][lane]
@@ -298,10 +298,8 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
       __syncwarp();
       // ---- the chunk: 16 byte columns x 32 rows, low- and high-nibble MMAs per set ----
       {
-        uint32_t r0, r1, r2, r3;
-        ldmatrix_x4_trans(lm_lane + (uint32_t)(s * C::kSlot), r0, r1, r2, r3);
-        const uint32_t a0 = __byte_perm(r0, r1, 0x6420), a1 = __byte_perm(r0, r1, 0x7531);
-        const uint32_t a2 = __byte_perm(r2, r3, 0x6420), a3 = __byte_perm(r2, r3, 0x7531);
+        uint32_t a0, a1, a2, a3;  // A rows m = g / g + 8: byte columns g / g + 8
+        ldmatrix_a8_trans(lm_lane + (uint32_t)(s * C::kSlot), a0, a1, a2, a3);
         const uint32_t l0 = a0 & 0x0f0f0f0fu, l1 = a1 & 0x0f0f0f0fu, l2 = a2 & 0x0f0f0f0fu, l3 = a3 & 0x0f0f0f0fu;
         const uint32_t u0 = a0 & 0xf0f0f0f0u, u1 = a1 & 0xf0f0f0f0u, u2 = a2 & 0xf0f0f0f0u, u3 = a3 & 0xf0f0f0f0u;
 #pragma unroll
@@ -349,8 +347,8 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
     const float* fac = reinterpret_cast<const float*>(smem + C::kFacOff + warp * C::kFac);
     const float* mns = reinterpret_cast<const float*>(smem + C::kMinOff) + warp * BATCH * 2;
     const unsigned nf = __float_as_uint(reinterpret_cast<const float*>(smem + C::kStepOff)[warp * BATCH]);
-    // MMA row g (t even) / g + 8 (t odd) = byte column 2g / 2g + 1 of the chunk
-    const int colb = 64 * G + 16 * (c & 1) + 2 * g + (t & 1);
+    // MMA row g (t even) / g + 8 (t odd) = byte column g / g + 8 of the chunk
+    const int colb = 64 * G + 16 * (c & 1) + g + 8 * (t & 1);
 #pragma unroll
     for (int z = 0; z < NSET; ++z)
 #pragma unroll

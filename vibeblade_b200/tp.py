@@ -16,6 +16,11 @@ same matmuls Megatron-style over the GPUs of one node, one process per GPU:
 which is outside the quantized matmul path.  Prefill uses the tcgen05 GEMM (bf16
 activations), decode the fused GEMV (fp32).  The collective is torch.distributed's
 all_reduce on the process group (NCCL between GPUs).
+
+Prefill overlaps work the dependencies allow: gate and up (independent GEMMs over the same
+x) run on two streams, so at TP >= 4, where each fills only part of the GPU's CTA-pair
+slots, the second fills what the first leaves; a row-split layer's GEMM runs in two row
+halves and the first half's all-reduce (on NCCL's stream) overlaps the second half's GEMM.
 """
 from __future__ import annotations
 
@@ -85,32 +90,83 @@ class TPLinear:
         self.k_loc = K // world if kind == "row" else K
         self.n_loc = N // world if kind == "column" else N
 
-    def prefill(self, a: torch.Tensor, out_dtype=torch.float32) -> torch.Tensor:
+    def prefill(self, a: torch.Tensor, out_dtype=torch.float32,
+                out: torch.Tensor | None = None) -> torch.Tensor:
         """a: bf16 [M, k_loc] -> [M, n_loc] (row split: a partial sum)."""
-        return gemm_dequant(a, self.w, None, a.shape[0], self.k_loc, self.n_loc, self.t, out_dtype)
+        return gemm_dequant(a, self.w, out, a.shape[0], self.k_loc, self.n_loc, self.t, out_dtype)
 
     def decode(self, x: torch.Tensor) -> torch.Tensor:
         """x: fp32 [B, k_loc] (B <= 16) -> fp32 [B, n_loc]."""
         return gemv_dequant(x, self.w, None, self.k_loc, self.n_loc, self.t)
 
 
-def reduce_partial(y: torch.Tensor, world: int, group=None) -> torch.Tensor:
-    """Sum a row-split layer's partial output over its `world` ranks.
+def reduce_partial(y: torch.Tensor, world: int, group=None, async_op: bool = False):
+    """Sum a row-split layer's partial output over its `world` ranks (in place).
 
     The decision depends only on the layer's own TP width, never on the size of whatever
     process group exists: a TP = 1 layer (for example a single-GPU reference computed on
     one rank of a larger job) must not enter a collective the other ranks do not join.
-    A layer split over W > 1 ranks needs a process group of exactly W ranks."""
+    A layer split over W > 1 ranks needs a process group of exactly W ranks.  async_op
+    returns the collective's work handle (None at W = 1) instead of y."""
     if world == 1:
-        return y
+        return None if async_op else y
     import torch.distributed as dist
     if not (dist.is_available() and dist.is_initialized()):
         raise RuntimeError(f"a layer split over {world} ranks needs torch.distributed initialised")
     if dist.get_world_size(group) != world:
         raise RuntimeError(f"layer split over {world} ranks but the process group has "
                            f"{dist.get_world_size(group)}")
-    dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group)
+    work = dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group, async_op=async_op)
+    return work if async_op else y
+
+
+# rows of a GEMM pair tile: a split at a multiple keeps both halves in whole tiles
+_PAIR_TILE_ROWS = 512
+
+
+def row_split_prefill_reduced(lin: "TPLinear", a: torch.Tensor, group=None) -> torch.Tensor:
+    """fp32 [M, N] = all-reduce over the ranks of lin.prefill(a) for a row-split layer.
+
+    The GEMM runs in two row halves (split at whole 512-row pair tiles); the first half's
+    all-reduce is issued as soon as its GEMM is enqueued and runs on NCCL's stream while
+    the second half computes.  Every rank takes the same collective steps for the same M."""
+    M, W = a.shape[0], lin.world
+    y = torch.empty((M, lin.n_loc), dtype=torch.float32, device=a.device)
+    split = ((M // 2 + _PAIR_TILE_ROWS - 1) // _PAIR_TILE_ROWS) * _PAIR_TILE_ROWS
+    if W == 1 or split >= M:
+        lin.prefill(a, torch.float32, out=y)
+        return reduce_partial(y, W, group)
+    lin.prefill(a[:split], torch.float32, out=y[:split])
+    work = reduce_partial(y[:split], W, group, async_op=True)
+    lin.prefill(a[split:], torch.float32, out=y[split:])
+    reduce_partial(y[split:], W, group)
+    work.wait()
     return y
+
+
+_side_streams: dict = {}
+
+
+def _side_stream(device: torch.device) -> torch.cuda.Stream:
+    key = torch.device(device).index
+    if key not in _side_streams:
+        _side_streams[key] = torch.cuda.Stream(device)
+    return _side_streams[key]
+
+
+def column_pair_prefill(lin_a: "TPLinear", lin_b: "TPLinear", x: torch.Tensor, out_dtype):
+    """(lin_a.prefill(x), lin_b.prefill(x)), the second on a side stream so that the two
+    independent GEMMs share the GPU; the caller's stream waits for both."""
+    cur = torch.cuda.current_stream(x.device)
+    side = _side_stream(x.device)
+    side.wait_stream(cur)
+    ya = lin_a.prefill(x, out_dtype)
+    with torch.cuda.stream(side):
+        yb = lin_b.prefill(x, out_dtype)
+    cur.wait_stream(side)
+    yb.record_stream(cur)  # yb was allocated on the side stream and is used on this one
+    x.record_stream(side)
+    return ya, yb
 
 
 class TPFFN:
@@ -127,11 +183,11 @@ class TPFFN:
     def prefill(self, x: torch.Tensor, reduce: bool = True) -> torch.Tensor:
         """x: bf16 [M, H] (replicated) -> fp32 [M, H], replicated after the all-reduce
         (reduce=False returns this rank's partial sum and leaves the sum to the caller)."""
-        g = self.gate.prefill(x, torch.bfloat16)
-        u = self.up.prefill(x, torch.bfloat16)
+        g, u = column_pair_prefill(self.gate, self.up, x, torch.bfloat16)
         h = swiglu(g, u, out=g)
-        y = self.down.prefill(h, torch.float32)
-        return reduce_partial(y, self.down.world, self.group) if reduce else y
+        if not reduce:
+            return self.down.prefill(h, torch.float32)
+        return row_split_prefill_reduced(self.down, h, self.group)
 
     def decode(self, x: torch.Tensor, reduce: bool = True) -> torch.Tensor:
         """x: fp32 [B, H] -> fp32 [B, H] (reduce as for prefill)."""
@@ -172,5 +228,6 @@ class TPAttentionProj:
     def o_prefill(self, attn: torch.Tensor, reduce: bool = True) -> torch.Tensor:
         """attn: bf16 [M, H / world] (this rank's heads) -> fp32 [M, H] after all-reduce
         (reduce=False: this rank's partial sum)."""
-        y = self.o.prefill(attn, torch.float32)
-        return reduce_partial(y, self.o.world, self.group) if reduce else y
+        if not reduce:
+            return self.o.prefill(attn, torch.float32)
+        return row_split_prefill_reduced(self.o, attn, self.group)
