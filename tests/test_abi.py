@@ -80,6 +80,10 @@ def test_scratch_size_query(lib):
         assert lib.vbq_gemv_scratch_bytes(4096, 14336, 12, batch, C.byref(v)) == 0 and v.value == 0
     assert lib.vbq_gemv_scratch_bytes(16, 256, 12, 1, C.byref(v)) == 0 and v.value == 0
     assert lib.vbq_gemv_scratch_bytes(4096, 14336, 9, 1, C.byref(v)) == 1
+    # past the integer kernels' K cap (exact s32 sums) the fp32 kernel takes the call
+    for t in (12, 8):
+        assert lib.vbq_gemv_scratch_bytes(3 * 65536, 1024, t, 1, C.byref(v)) == 0 and v.value == 0
+        assert lib.vbq_gemv_scratch_bytes(3 * 65536 + 256, 1024, t, 1, C.byref(v)) == 0 and v.value > 0
 
 
 def test_python_face_rejects_host_tensors():

@@ -93,6 +93,21 @@ def test_gemv_misaligned_x_view(cuda, batch):
     assert vb.device_status() == 0
 
 
+@pytest.mark.parametrize("qtype", [F.GGML_TYPE_Q4_K, F.GGML_TYPE_Q8_0])
+def test_gemv_k_past_integer_cap(cuda, qtype):
+    """K above the integer-MMA kernels' cap (their s32 sums must stay exact) runs on the
+    fp32 kernel with caller scratch; same bar against the fp64 product."""
+    K, N, B = 3 * 65536 + 2048, 512, 2
+    w = synthetic_weights(K, N, qtype, seed=9, device=cuda)
+    g = torch.Generator(device=cuda).manual_seed(10)
+    x = torch.randn(B, K, generator=g, device=cuda)
+    assert vb.gemv_scratch_bytes(K, N, qtype, B) > 0
+    y = vb.gemv_dequant(x, w, None, K, N, qtype)
+    ref = x.double() @ vb.dequantize(w, K, N, qtype).double()
+    assert ((y.double() - ref).abs().max() / ref.abs().max()).item() <= TOL
+    assert vb.device_status() == 0
+
+
 def test_gemv_1d_x_and_out_buffer(cuda, oracle):
     K, N, t = 256, 768, F.GGML_TYPE_Q4_K
     rng = np.random.default_rng(3)

@@ -585,9 +585,12 @@ static cudaError_t launch_t(const float* x, const void* w, float* y, int64_t K, 
   return cudaLaunchKernelEx(&cfg, kern, mw, x, y, (int)K, (int)N, batch);
 }
 
-// Whether the tensor-core kernel takes this call (batch 1..16; any K below 2^31 - 2^8).
+// Whether the tensor-core kernel takes this call (batch 1..16).  The s32 sums run over up
+// to K / 4 rows per accumulator with terms below 240 * 128 in magnitude, so K is capped
+// at 3 * 2^16 (exact below 2^31 with room to spare); longer rows take the fp32 kernel.
+constexpr int64_t kMmaMaxK = 3 * 65536;
 bool gemv_mma_fits(int64_t K, int64_t N, int batch) {
-  return batch >= 1 && batch <= 16 && K >= 1 && K <= 0x7fffff00LL && N % 256 == 0 && N > 0;
+  return batch >= 1 && batch <= 16 && K >= 1 && K <= kMmaMaxK && N % 256 == 0 && N > 0;
 }
 
 // Tensor-core Q4_K GEMV.  Batches 9..16 go to the wide kernel (one pass over the weights)

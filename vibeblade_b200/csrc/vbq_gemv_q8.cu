@@ -449,8 +449,10 @@ static cudaError_t launch_q8_t(const float* x, const void* w, float* y, int64_t 
   return cudaLaunchKernelEx(&cfg, kern, mw, x, y, (int)K, (int)N, batch);
 }
 
+// The s32 sums run over up to K / 2 rows per accumulator with terms of at most 128 * 128
+// in magnitude: K is capped at 3 * 2^16 (longer rows take the fp32 kernel).
 bool gemv_q8_fits(int64_t K, int64_t N, int batch) {
-  return batch >= 1 && batch <= 16 && K >= 1 && K <= 0x7fffff00LL && N % 256 == 0 && N > 0;
+  return batch >= 1 && batch <= 16 && K >= 1 && K <= 3 * 65536 && N % 256 == 0 && N > 0;
 }
 
 // Tensor-core Q8_0 GEMV; batches above 4 run as launches over groups of 4 batch rows.

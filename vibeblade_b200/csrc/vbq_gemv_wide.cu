@@ -509,8 +509,10 @@ static cudaError_t launch_wide_t(const float* x, const void* w, float* y, int64_
 }
 
 // The wide kernel reads x through a TMA tensor map: rows of x 16-byte aligned.
+// A warp's s32 sums run over up to K rows with terms below 240 * 128 in magnitude: K is
+// capped at 2^16 (longer rows run as groups of 4 on the batch 1..4 kernel).
 bool gemv_wide_fits(const float* x, int64_t K, int64_t N, int batch) {
-  return batch >= 5 && batch <= 16 && K >= 1 && K <= 0x7fffff00LL && K % 4 == 0 && N % 256 == 0 &&
+  return batch >= 5 && batch <= 16 && K >= 1 && K <= 65536 && K % 4 == 0 && N % 256 == 0 &&
          N > 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
 }
 
