@@ -593,15 +593,15 @@ bool gemv_mma_fits(int64_t K, int64_t N, int batch) {
   return batch >= 1 && batch <= 16 && K >= 1 && K <= kMmaMaxK && N % 256 == 0 && N > 0;
 }
 
-// Tensor-core Q4_K GEMV.  Batches 9..16 go to the wide kernel (one pass over the weights)
-// when x's rows are 16-byte aligned; other batches above 4 run as consecutive launches over
-// groups of 4 batch rows (each streams the weights again).  Measured on B200, 4096 x 14336:
-// batch 8 grouped 32.4 us / wide 36.8 us; batch 16 grouped 64.5 us / wide 60.8 us (4096 x
-// 4096: 34.6 / 26.2 us).
+// Tensor-core Q4_K GEMV.  Batches 5..16 go to the wide kernel (one pass over the weights)
+// when x's rows are 16-byte aligned (and K within its cap); otherwise batches above 4 run as
+// consecutive launches over groups of 4 batch rows (each streams the weights again).
+// Measured on B200, 4096 x 14336: batch 8 grouped 33.2 us / wide 31.3 us; batch 16
+// grouped 64.5 us / wide 51.9 us.
 cudaError_t launch_gemv_mma_q4k(const float* x, const void* w, float* y, int64_t K, int64_t N,
                                 int64_t row_bytes, int batch, cudaStream_t st) {
   if (!gemv_mma_fits(K, N, batch) || row_bytes % 16 != 0) return cudaErrorNotSupported;
-  if (batch > 8 && gemv_wide_fits(x, K, N, batch))
+  if (batch > 4 && gemv_wide_fits(x, K, N, batch))
     return launch_gemv_wide_q4k(x, w, y, K, N, row_bytes, batch, st);
   for (int b0 = 0; b0 < batch; b0 += 4) {
     const int nb = batch - b0 < 4 ? batch - b0 : 4;

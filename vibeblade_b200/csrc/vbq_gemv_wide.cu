@@ -9,9 +9,12 @@
 // What changes with 8 or 16 batch rows is the shape of a warp's work: its accumulators
 // grow with the batch (4 or 8 column sets), so a warp takes one 16-byte chunk of the
 // tile's quant bytes (32 columns: 16 low + 16 high nibbles) instead of four, and the 8
-// consumer warps cover the 256-column tile over 32-row stages.  Each warp builds the B
-// table for its chunk's two sub-blocks; lanes 0-15 / 16-31 take the two halves of the
-// batch.  The stage's x rows ([batch][32] fp32) come by TMA with the weights, so nothing
+// consumer warps cover the 256-column tile over 32-row stages.  Warps 2G and 2G + 1 read
+// the same two sub-blocks (2G, 2G + 1) and share one B table: each builds the digits of
+// half the batch rows (lanes 0-15 / 16-31 a quarter each), a 64-thread named barrier per
+// pair separates the table's writes from the MMAs' reads, and the pair agrees on every
+// per-stage decision (a rescale, a bounded wait that gave up) through shared flags before
+// that barrier, so neither warp can wait for one the other skips.  The stage's x rows ([batch][32] fp32) come by TMA with the weights, so nothing
 // is prefetched in registers.  Flushed fp32 sums and the per-batch-row scales live in
 // shared memory (they change only when a scale does).
 //
@@ -52,14 +55,16 @@ template <int BATCH> struct Cfg {
   static constexpr int kSlot = kWBytes + kXBytes;          // stage slot (multiple of 128)
   // set stride: a batch row's lane-half partner (B/4 sets apart) writes 16 banks away
   static constexpr int kSetStride = BATCH == 16 ? 592 : 608;
-  static constexpr int kTbl = kSets * kSetStride;          // per warp
+  static constexpr int kTbl = kSets * kSetStride;          // per warp pair
   static constexpr int kFac = kSets * 2 * 32 * 4;          // per warp: [set][lo/hi][lane]
   static constexpr int kRingOff = 0;
   static constexpr int kTblOff = kStages * kSlot;
-  static constexpr int kFacOff = kTblOff + kConsumers * kTbl;
-  static constexpr int kStepOff = kFacOff + kConsumers * kFac;          // [warp][BATCH] fp32
-  static constexpr int kMinOff = kStepOff + kConsumers * BATCH * 4;     // [warp][BATCH][2]
-  static constexpr int kBarOff = kMinOff + kConsumers * BATCH * 2 * 4;
+  static constexpr int kPairs = kConsumers / 2;
+  static constexpr int kFacOff = kTblOff + kPairs * kTbl;
+  static constexpr int kStepOff = kFacOff + kConsumers * kFac;          // [pair][BATCH] fp32
+  static constexpr int kMinOff = kStepOff + kPairs * BATCH * 4;         // [pair][BATCH][2]
+  static constexpr int kFlagOff = kMinOff + kPairs * BATCH * 2 * 4;     // [warp][2] u32
+  static constexpr int kBarOff = kFlagOff + kConsumers * 2 * 4;
   static constexpr int kSmem = kBarOff + 128 + 128;                     // + alignment slack
   static constexpr int kOutBytes = BATCH * 256 * 4;                     // partial sums
   static_assert(kSlot % 128 == 0, "TMA destinations 128-byte aligned");
@@ -141,26 +146,31 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
     asm volatile("griddepcontrol.wait;" ::: "memory");
   } else {
     // ------------------------------ consumers ------------------------------
-    constexpr int HB = BATCH / 2;  // batch rows per lane half
+    constexpr int QB = BATCH / 4;  // batch rows per lane (a quarter of the batch)
     const int c = warp;            // the tile's quant bytes 16c .. 16c + 15
     const int G = c >> 1;          // 64-column group: sub-blocks 2G (low), 2G + 1 (high)
-    // table role: rows 2 rp, 2 rp + 1 of the stage, batch rows bh * HB .. + HB - 1
-    const int rp = lane & 15, bh = lane >> 4;
+    const int pr = G, par = c & 1; // warp pair (shares the B table) and the warp in it
+    // table role: rows 2 rp, 2 rp + 1 of the stage, batch rows qd * QB .. + QB - 1
+    const int rp = lane & 15, qd = 2 * par + (lane >> 4);
     const int kap0 = 8 * ((rp & 7) >> 1) + 4 * (rp >> 3) + 2 * (rp & 1);  // as in vbq_gemv_mma.cu
     const int g = lane >> 2, t = lane & 3;  // MMA fragment role
-    uint8_t* tbl = smem + C::kTblOff + warp * C::kTbl;
+    uint8_t* tbl = smem + C::kTblOff + pr * C::kTbl;
     float* fac = reinterpret_cast<float*>(smem + C::kFacOff + warp * C::kFac);  // [set][h][lane]
-    float* stp = reinterpret_cast<float*>(smem + C::kStepOff) + warp * BATCH;   // step per row
-    for (int i = lane; i < C::kTbl / 4; i += 32) reinterpret_cast<uint32_t*>(tbl)[i] = 0u;
+    float* stp = reinterpret_cast<float*>(smem + C::kStepOff) + pr * BATCH;     // step per row
+    volatile uint32_t* flags = reinterpret_cast<volatile uint32_t*>(smem + C::kFlagOff);  // [warp][2]
+    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + pr) : "memory"); };
+    // the pair's table: each warp zeroes half and writes the all-ones columns 3 and 7 of
+    // its half of the sets, then the pair meets before any digit is written
+    for (int i = par * 32 + lane; i < C::kTbl / 4; i += 64) reinterpret_cast<uint32_t*>(tbl)[i] = 0u;
     for (int i = lane; i < NSET * 2 * 32; i += 32) fac[i] = 0.f;
-    if (lane < BATCH) stp[lane] = 1.f;
-    __syncwarp();
-    for (int i = lane; i < NSET * 2 * 2 * 8; i += 32) {  // all-ones columns 3 and 7
+    if (par == 0 && lane < BATCH) stp[lane] = 1.f;
+    pair_sync();
+    for (int i = par * 32 + lane; i < NSET * 2 * 2 * 8; i += 64) {
       const int w8 = i & 7, c2 = (i >> 3) & 1, h = (i >> 4) & 1, z = i >> 5;
       reinterpret_cast<uint32_t*>(tbl + z * C::kSetStride + h * kSbStride + (3 + 4 * c2) * kColStride)[w8] =
           0x01010101u;
     }
-    __syncwarp();
+    pair_sync();
     const uint32_t sel_lo = 0x7440u | (uint32_t)((2 * G) & 3), sel_hi = 0x7440u | (uint32_t)((2 * G + 1) & 3);
     const uint8_t* const tfrag = tbl + g * kColStride + 8 * t;
     const uint32_t lm_lane = smem_u32(smem) + (uint32_t)(C::kRingOff + lane * kPitch + 16 + 16 * c);
@@ -170,9 +180,9 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
     for (int z = 0; z < NSET; ++z)
 #pragma unroll
       for (int h = 0; h < 2; ++h) acc[z][h][0] = acc[z][h][1] = acc[z][h][2] = acc[z][h][3] = 0;
-    float scale[HB], mins[HB][2];
+    float scale[QB], mins[QB][2];
 #pragma unroll
-    for (int j = 0; j < HB; ++j) {
+    for (int j = 0; j < QB; ++j) {
       scale[j] = 1.f;
       mins[j][0] = mins[j][1] = 0.f;
     }
@@ -203,11 +213,10 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
 
     for (int it = 0; it < nst; ++it) {
       const int s = it % kStages;
-      if (!__all_sync(0xffffffffu, mbar_wait_hinted(smem_u32(&bars.full[s]), (it / kStages) & 1,
-                                                      kWaitBudgetCycles))) {
-        if (lane == 0) give_up();
-        break;
-      }
+      // a wait that gives up is acted on only after the pair's flag exchange below (the
+      // stage's bytes are then stale but in bounds)
+      const bool ok = __all_sync(0xffffffffu, mbar_wait_hinted(smem_u32(&bars.full[s]), (it / kStages) & 1,
+                                                                kWaitBudgetCycles));
       const uint8_t* st = slot(s);
       // ---- scales of the lane's two rows, sub-blocks 2G and 2G + 1
       // (get_scale_min_k4, cpp/src/dequant.cpp:258-266) ----
@@ -240,12 +249,12 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
       const float2 ml0 = __fmul2_rn(dm, mlo), ml1 = __fmul2_rn(dm, mhi);
       // ---- v = x * dl on the current scales (x rows from the stage slot) ----
       const float* xs = reinterpret_cast<const float*>(st + kWBytes);  // [BATCH][32]
-      float2 v[HB][2];
-      uint32_t w[HB][2][2];
+      float2 v[QB][2];
+      uint32_t w[QB][2][2];
       uint32_t out = 0u;
 #pragma unroll
-      for (int j = 0; j < HB; ++j) {
-        const int b = bh * HB + j;
+      for (int j = 0; j < QB; ++j) {
+        const int b = qd * QB + j;
         const float2 xv = *reinterpret_cast<const float2*>(xs + b * kRows + 2 * rp);
         v[j][0] = __fmul2_rn(xv, dl0);
         v[j][1] = __fmul2_rn(xv, dl1);
@@ -258,15 +267,26 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
           out |= (w[j][h][0] ^ 0x4b000000u) | (w[j][h][1] ^ 0x4b000000u);
         }
       }
-      if (__any_sync(0xffffffffu, out >= (1u << 23)) || it == 0) {
-        // rare (and the first stage): flag non-finite values, move the sums to fp32, scale
-        // each batch row to 4-8x its largest finite |v| over the lane half, encode again
+      // the pair's decisions: either warp's wait gave up -> both leave; either warp's
+      // digits left their range (or the first stage) -> both flush, then rescale
+      const bool need = __any_sync(0xffffffffu, out >= (1u << 23)) || it == 0;
+      if (lane == 0) flags[2 * warp] = (need ? 1u : 0u) | (ok ? 0u : 2u);
+      pair_sync();
+      const uint32_t fl = flags[2 * warp] | flags[2 * (warp ^ 1)];
+      if (fl & 2u) {
+        if (!ok && lane == 0) give_up();
+        break;
+      }
+      if (fl & 1u) {
+        // rare (and the first stage): flag non-finite values, move the sums to fp32 with
+        // the old steps (both warps, before either changes them), then scale each batch row
+        // of this warp's half to 4-8x its largest finite |v| over the lane half, encode again
         if (it > 0) flush();
-        __syncwarp();
+        pair_sync();
 #pragma unroll
-        for (int j = 0; j < HB; ++j) {
+        for (int j = 0; j < QB; ++j) {
           const float sum = (fabsf(v[j][0].x) + fabsf(v[j][0].y)) + (fabsf(v[j][1].x) + fabsf(v[j][1].y));
-          nonfin |= (sum < 0x1p100f) ? 0u : (1u << (bh * HB + j));
+          nonfin |= (sum < 0x1p100f) ? 0u : (1u << (qd * QB + j));
           float m = fminf(fmaxf(fmaxf(fabsf(v[j][0].x), fabsf(v[j][0].y)),
                                 fmaxf(fabsf(v[j][1].x), fabsf(v[j][1].y))), 0x1p99f);
 #pragma unroll
@@ -274,7 +294,7 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
           int e = (int)((__float_as_uint(m) >> 23) & 0xffu) - 127 + 2;
           e = e < kExpMin ? kExpMin : (e > kExpMax ? kExpMax : e);
           scale[j] = pow2f(21 - e);
-          if (rp == 0) stp[bh * HB + j] = pow2f(e - 21);
+          if (rp == 0) stp[qd * QB + j] = pow2f(e - 21);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             w[j][h][0] = __float_as_uint(fmaf(v[j][h].x, scale[j], kMagic));
@@ -282,10 +302,10 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
           }
         }
       }
-      // ---- B table: three signed digits of n per row pair ----
+      // ---- B table: three signed digits of n per row pair (this warp's batch rows) ----
 #pragma unroll
-      for (int j = 0; j < HB; ++j) {
-        const int b = bh * HB + j;
+      for (int j = 0; j < QB; ++j) {
+        const int b = qd * QB + j;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const uint32_t wx = w[j][h][0] ^ 0x8080u, wy = w[j][h][1] ^ 0x8080u;
@@ -295,7 +315,7 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
             *reinterpret_cast<uint16_t*>(col + dg * kColStride) = (uint16_t)__byte_perm(wx, wy, dg | ((4 + dg) << 4));
         }
       }
-      __syncwarp();
+      pair_sync();  // the pair's table is complete (and the steps, after a rescale)
       // ---- the chunk: 16 byte columns x 32 rows, low- and high-nibble MMAs per set ----
       {
         uint32_t a0, a1, a2, a3;  // A rows m = g / g + 8: byte columns g / g + 8
@@ -321,22 +341,22 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
     for (int o = 1; o < 32; o <<= 1) {
       if (o < 16) {
 #pragma unroll
-        for (int j = 0; j < HB; ++j) {
+        for (int j = 0; j < QB; ++j) {
           mins[j][0] += __shfl_xor_sync(0xffffffffu, mins[j][0], o);
           mins[j][1] += __shfl_xor_sync(0xffffffffu, mins[j][1], o);
         }
       }
       nonfin |= __shfl_xor_sync(0xffffffffu, nonfin, o);
     }
-    float* mns = reinterpret_cast<float*>(smem + C::kMinOff) + warp * BATCH * 2;  // [b][h]
+    float* mns = reinterpret_cast<float*>(smem + C::kMinOff) + pr * BATCH * 2;  // [b][h]
     if (rp == 0) {
 #pragma unroll
-      for (int j = 0; j < HB; ++j) {
-        mns[(bh * HB + j) * 2 + 0] = mins[j][0];
-        mns[(bh * HB + j) * 2 + 1] = mins[j][1];
+      for (int j = 0; j < QB; ++j) {
+        mns[(qd * QB + j) * 2 + 0] = mins[j][0];
+        mns[(qd * QB + j) * 2 + 1] = mins[j][1];
       }
     }
-    if (lane == 0) stp[0] = __uint_as_float(nonfin);  // reused: the flag word (steps are done)
+    if (lane == 0) flags[2 * warp + 1] = nonfin;  // this warp's batch rows' flags
   }
 
   // ---- this CTA's partial sums [BATCH][256] into the ring (idle now) ----
@@ -345,8 +365,9 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
   if (warp < kConsumers) {
     const int c = warp, G = c >> 1, g = lane >> 2, t = lane & 3;
     const float* fac = reinterpret_cast<const float*>(smem + C::kFacOff + warp * C::kFac);
-    const float* mns = reinterpret_cast<const float*>(smem + C::kMinOff) + warp * BATCH * 2;
-    const unsigned nf = __float_as_uint(reinterpret_cast<const float*>(smem + C::kStepOff)[warp * BATCH]);
+    const float* mns = reinterpret_cast<const float*>(smem + C::kMinOff) + G * BATCH * 2;
+    const volatile uint32_t* flg = reinterpret_cast<const volatile uint32_t*>(smem + C::kFlagOff);
+    const unsigned nf = flg[2 * warp + 1] | flg[2 * (warp ^ 1) + 1];  // the pair's rows
     // MMA row g (t even) / g + 8 (t odd) = byte column g / g + 8 of the chunk
     const int colb = 64 * G + 16 * (c & 1) + g + 8 * (t & 1);
 #pragma unroll
