@@ -475,6 +475,51 @@ def run_gpu(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_value = layer_bytes(B) * args.steps * world / (float(t.item()) * 1e-3) / 1e9
 
+    # ---- config 2's other batch sizes: the same rotated layers at batch 4 and 16 ----
+    decode_batches = {}
+    if B == 1 and not args.no_extras:
+        for bx in (4, 16):
+            xb = {K: torch.randn(bx, K, generator=g, device=dev) for _, K, _ in LAYER_8B}
+            yb = [torch.empty(bx, N, device=dev) for _, _, N in LAYER_8B]
+            need_b = max(vb.gemv_scratch_bytes(K, N, QTYPE, bx) for _, K, N in LAYER_8B)
+            scr_b = torch.zeros(max(need_b, 16), dtype=torch.uint8, device=dev)
+
+            def layer_b(c: int, stream_ptr: int):
+                for (K, N, w), y in zip(layers[c], yb):
+                    rc = lib.vbq_gemv(xb[K].data_ptr(), w.data_ptr(), y.data_ptr(), K, N, QTYPE, bx,
+                                      scr_b.data_ptr(), scr_b.numel(), stream_ptr)
+                    if rc:
+                        _lib.check(rc, lib)
+
+            cap_b = torch.cuda.Stream(dev)
+            cap_b.wait_stream(stream)
+            with torch.cuda.stream(cap_b):
+                for c in range(n_copies):
+                    layer_b(c, cap_b.cuda_stream)
+                graph_b = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph_b, stream=cap_b):
+                    for c in range(n_copies):
+                        layer_b(c, cap_b.cuda_stream)
+            stream.wait_stream(cap_b)
+            graph_b.replay()
+            torch.cuda.synchronize()
+            reps = max(1, args.steps // n_copies)
+            a_b, b_b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a_b.record(stream)
+            for _ in range(reps):
+                graph_b.replay()
+            b_b.record(stream)
+            torch.cuda.synchronize()
+            t_b = torch.tensor([a_b.elapsed_time(b_b)], device=dev, dtype=torch.float64)
+            if world > 1:
+                dist.all_reduce(t_b, op=dist.ReduceOp.MAX)
+            ms_b = float(t_b.item())
+            gbs_b = layer_bytes(bx) * reps * n_copies * world / (ms_b * 1e-3) / 1e9
+            decode_batches[str(bx)] = {"value": round(gbs_b, 1), "unit": "GB/s",
+                                       "us_per_step": round(1e3 * ms_b / (reps * n_copies), 2),
+                                       "frac_of_hbm": round(gbs_b / world / peaks()["hbm_gbs"], 4)}
+            del graph_b
+
     # ---- configs 3-5: prefill GEMM, MoE (one GPU) and the tensor-parallel 70B FFN ----
     extras = {}
     if not args.no_extras:
@@ -509,7 +554,8 @@ def run_gpu(args) -> None:
                          "peak_src": pk["src"] + " (MEASURED_PEAKS.json hbm_gbs)",
                          "kernel": (f"vbq::gmma::gemv_mma_kernel<{1 if B == 1 else 2 if B == 2 else 4}> "
                                     "(u8 x s8 mma.sync, split-K in a thread-block cluster)" if B <= 4
-                                    else f"vbq::gemv_kernel<Q4_K,B={B}>"),
+                                    else f"vbq::gwide::gemv_wide_kernel<{8 if B <= 8 else 16}> "
+                                    "(u8 x s8 mma.sync, B table shared by warp pairs)"),
                          "gemv_4096x14336_gbs": round(big_gbs, 1),
                          "gemv_4096x14336_frac": round(big_gbs / pk["hbm_gbs"], 4)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
@@ -517,6 +563,8 @@ def run_gpu(args) -> None:
             "gpu_launches": args.steps * len(LAYER_8B),
             "clocks": clk.summary(),
         }
+        if decode_batches:  # outside the timed region above; same layers, graph-replayed
+            line["decode_layer_by_batch"] = decode_batches
         line.update(extras)
     if world > 1:
         dist.barrier()

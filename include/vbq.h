@@ -190,6 +190,17 @@ int vbq_moe_ffn(const float* x, const float* logits, const void* w_gate, const v
 int vbq_swiglu(const void* g, const void* u, void* h, int64_t n, int32_t dtype, void* stream);
 
 /*
+ * SwiGLU over the output of one matmul whose weight columns hold the gate and up
+ * projections side by side (a tensor-parallel rank's gate and up shards packed into one
+ * K x 2n block matrix, so that one GEMM / GEMV computes both): gu is [rows, 2n] (gate
+ * values in columns 0..n-1, up values in n..2n-1), h is [rows, n], h[r, i] =
+ * silu(gu[r, i]) * gu[r, n + i] with the same sanitising and rounding as vbq_swiglu.
+ * n % 8 == 0; gu and h 16-byte aligned; h must not overlap gu.
+ */
+int vbq_swiglu_rows(const void* gu, void* h, int64_t rows, int64_t n, int32_t dtype,
+                    void* stream);
+
+/*
  * Device-side status of the library's kernels on the current device: bit 0 set means a
  * bounded wait inside a kernel gave up (VBQ_ERR_TIMEOUT is returned then), which leaves
  * that call's outputs undefined and its scratch in need of re-zeroing.  Reads

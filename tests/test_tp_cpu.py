@@ -47,6 +47,25 @@ def test_row_shard_is_row_slice(oracle, qt):
         np.testing.assert_array_equal(oracle.dequantize(s.numpy(), k, N, qt), full[r * k:(r + 1) * k])
 
 
+@pytest.mark.parametrize("qt,H,I", [(F.GGML_TYPE_Q8_0, 256, 1024), (F.GGML_TYPE_Q4_K, 256, 1024),
+                                    (F.GGML_TYPE_Q6_K, 256, 8192)])
+def test_packed_gate_up_is_side_by_side_shards(oracle, qt, H, I):
+    """The FFN's packed gate | up matrix of a rank: each row is the gate shard's blocks then
+    the up shard's, so its dequantization is the two shards' dequantizations side by side."""
+    rng = np.random.default_rng(qt)
+    wg = quantize(rng.normal(0, 0.02, (H, I)).astype(np.float32), qt)
+    wu = quantize(rng.normal(0, 0.02, (H, I)).astype(np.float32), qt)
+    for world in (1, 2, 4):
+        for r in range(world):
+            gs, us = (tp.shard(w, H, I, qt, "column", r, world) for w in (wg, wu))
+            lin = tp.TPLinear.packed_columns([gs, us], H, qt, torch.device("cpu"))
+            n = I // world
+            assert (lin.k_loc, lin.n_loc) == (H, 2 * n)
+            full = oracle.dequantize(lin.w.numpy(), H, 2 * n, qt)
+            np.testing.assert_array_equal(full[:, :n], oracle.dequantize(gs.numpy(), H, n, qt))
+            np.testing.assert_array_equal(full[:, n:], oracle.dequantize(us.numpy(), H, n, qt))
+
+
 def test_split_rules():
     # 70B shapes (hidden 8192, intermediate 28672, Q8_0) split at 1, 2, 4, 8
     for world in (1, 2, 4, 8):

@@ -413,3 +413,19 @@ extern "C" int vbq_swiglu(const void* g, const void* u, void* h, int64_t n, int3
   if (e != cudaSuccess) return cuda_fail(e, "vbq_swiglu launch");
   return ok();
 }
+
+extern "C" int vbq_swiglu_rows(const void* gu, void* h, int64_t rows, int64_t n, int32_t dtype,
+                               void* stream) {
+  if (dtype != VBQ_DTYPE_F32 && dtype != VBQ_DTYPE_BF16)
+    return fail(VBQ_ERR_SHAPE, "vbq_swiglu_rows: dtype must be VBQ_DTYPE_F32 or VBQ_DTYPE_BF16");
+  if (rows < 0 || n < 0) return fail(VBQ_ERR_SHAPE, "vbq_swiglu_rows: negative size");
+  if (rows == 0 || n == 0) return ok();
+  if (!gu || !h) return fail(VBQ_ERR_NULL, "vbq_swiglu_rows: NULL pointer");
+  if (n % 8 != 0) return fail(VBQ_ERR_SHAPE, "vbq_swiglu_rows: n must be a multiple of 8");
+  if (!aligned(gu, 16) || !aligned(h, 16))
+    return fail(VBQ_ERR_ALIGN, "vbq_swiglu_rows: gu and h must be 16-byte aligned");
+  cudaError_t e = vbq::launch_swiglu_rows(gu, h, rows, n, dtype == VBQ_DTYPE_BF16,
+                                          static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "vbq_swiglu_rows launch");
+  return ok();
+}

@@ -68,6 +68,8 @@ cudaError_t launch_moe_gather(const float* x, const int32_t* tok, int rows, int 
 // h = bf16(silu(g) * u) over n bf16 values, with the reference's clipping (in place in g ok)
 cudaError_t launch_swiglu(const void* g, const void* u, void* h, int64_t n, cudaStream_t st);
 cudaError_t launch_swiglu_f32(const float* g, const float* u, float* h, int64_t n, cudaStream_t st);
+cudaError_t launch_swiglu_rows(const void* gu, void* h, int64_t rows, int64_t n, bool bf16,
+                               cudaStream_t st);
 // out[t] = sum_slot weight[t, slot] * y[pos[t * topk + slot]], fp32 [T, H], sanitised
 cudaError_t launch_moe_combine(const float* y, const int32_t* pos, const float* weight, int T,
                                int topk, int H, float* out, cudaStream_t st);

@@ -15,6 +15,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "vbq_internal.h"
 
 namespace vbq {
@@ -140,32 +142,46 @@ __device__ __forceinline__ float silu_ref(float x) {
   return x * s;
 }
 
-__global__ void swiglu_kernel(const uint4* __restrict__ g, const uint4* __restrict__ u,
-                              uint4* __restrict__ h, int64_t n8) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const uint4 gv = g[i], uv = u[i];
-    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
-    uint32_t o[4];
+// silu(g) * u on 8 bf16 / 4 fp32 values (one 16-byte vector of each), inputs sanitised
+__device__ __forceinline__ uint4 swiglu_vec(uint4 gv, uint4 uv, std::true_type /*bf16*/) {
+  const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
+  uint32_t o[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const __nv_bfloat162 g2 = *reinterpret_cast<const __nv_bfloat162*>(&gw[q]);
-      const __nv_bfloat162 u2 = *reinterpret_cast<const __nv_bfloat162*>(&uw[q]);
-      const float2 gf = __bfloat1622float2(g2), uf = __bfloat1622float2(u2);
-      o[q] = pack_bf16(silu_ref(sanitize(gf.x)) * sanitize(uf.x),
-                       silu_ref(sanitize(gf.y)) * sanitize(uf.y));
-    }
-    h[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  for (int q = 0; q < 4; ++q) {
+    const __nv_bfloat162 g2 = *reinterpret_cast<const __nv_bfloat162*>(&gw[q]);
+    const __nv_bfloat162 u2 = *reinterpret_cast<const __nv_bfloat162*>(&uw[q]);
+    const float2 gf = __bfloat1622float2(g2), uf = __bfloat1622float2(u2);
+    o[q] = pack_bf16(silu_ref(sanitize(gf.x)) * sanitize(uf.x), silu_ref(sanitize(gf.y)) * sanitize(uf.y));
   }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+__device__ __forceinline__ uint4 swiglu_vec(uint4 gq, uint4 uq, std::false_type /*fp32*/) {
+  const float4 gv = *reinterpret_cast<const float4*>(&gq), uv = *reinterpret_cast<const float4*>(&uq);
+  const float4 r = make_float4(silu_ref(sanitize(gv.x)) * sanitize(uv.x), silu_ref(sanitize(gv.y)) * sanitize(uv.y),
+                               silu_ref(sanitize(gv.z)) * sanitize(uv.z), silu_ref(sanitize(gv.w)) * sanitize(uv.w));
+  return *reinterpret_cast<const uint4*>(&r);
 }
 
-__global__ void swiglu_f32_kernel(const float4* __restrict__ g, const float4* __restrict__ u,
-                                  float4* __restrict__ h, int64_t n4) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
+template <bool BF16>
+__global__ void swiglu_kernel(const uint4* __restrict__ g, const uint4* __restrict__ u,
+                              uint4* __restrict__ h, int64_t nv) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nv;
+       i += (int64_t)gridDim.x * blockDim.x)
+    h[i] = swiglu_vec(g[i], u[i], std::integral_constant<bool, BF16>{});
+}
+
+// rows of [g | u] (each row: the gate half then the up half, w vectors each) -> rows of
+// h = silu(g) * u (w vectors each): the output of one GEMM / GEMV over gate and up packed
+// side by side
+template <bool BF16>
+__global__ void swiglu_rows_kernel(const uint4* __restrict__ gu, uint4* __restrict__ h,
+                                   int64_t rows, int64_t w) {
+  const int64_t total = rows * w;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const float4 gv = g[i], uv = u[i];
-    h[i] = make_float4(silu_ref(sanitize(gv.x)) * sanitize(uv.x), silu_ref(sanitize(gv.y)) * sanitize(uv.y),
-                       silu_ref(sanitize(gv.z)) * sanitize(uv.z), silu_ref(sanitize(gv.w)) * sanitize(uv.w));
+    const int64_t r = i / w, c = i - r * w;
+    const uint4* row = gu + r * 2 * w;
+    h[i] = swiglu_vec(row[c], row[w + c], std::integral_constant<bool, BF16>{});
   }
 }
 
@@ -222,17 +238,30 @@ static int grid_for(int64_t items) {
 cudaError_t launch_swiglu(const void* g, const void* u, void* h, int64_t n, cudaStream_t st) {
   const int64_t n8 = n / 8;
   if (n8 <= 0) return cudaSuccess;
-  swiglu_kernel<<<grid_for(n8), 256, 0, st>>>(static_cast<const uint4*>(g),
-                                              static_cast<const uint4*>(u), static_cast<uint4*>(h), n8);
+  swiglu_kernel<true><<<grid_for(n8), 256, 0, st>>>(static_cast<const uint4*>(g),
+                                                    static_cast<const uint4*>(u), static_cast<uint4*>(h), n8);
   return cudaGetLastError();
 }
 
 cudaError_t launch_swiglu_f32(const float* g, const float* u, float* h, int64_t n, cudaStream_t st) {
   const int64_t n4 = n / 4;
   if (n4 <= 0) return cudaSuccess;
-  swiglu_f32_kernel<<<grid_for(n4), 256, 0, st>>>(reinterpret_cast<const float4*>(g),
-                                                  reinterpret_cast<const float4*>(u),
-                                                  reinterpret_cast<float4*>(h), n4);
+  swiglu_kernel<false><<<grid_for(n4), 256, 0, st>>>(reinterpret_cast<const uint4*>(g),
+                                                     reinterpret_cast<const uint4*>(u),
+                                                     reinterpret_cast<uint4*>(h), n4);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu_rows(const void* gu, void* h, int64_t rows, int64_t n, bool bf16,
+                               cudaStream_t st) {
+  const int64_t w = bf16 ? n / 8 : n / 4;  // 16-byte vectors per half row
+  if (rows <= 0 || w <= 0) return cudaSuccess;
+  if (bf16)
+    swiglu_rows_kernel<true><<<grid_for(rows * w), 256, 0, st>>>(static_cast<const uint4*>(gu),
+                                                                 static_cast<uint4*>(h), rows, w);
+  else
+    swiglu_rows_kernel<false><<<grid_for(rows * w), 256, 0, st>>>(static_cast<const uint4*>(gu),
+                                                                  static_cast<uint4*>(h), rows, w);
   return cudaGetLastError();
 }
 

@@ -17,10 +17,11 @@ which is outside the quantized matmul path.  Prefill uses the tcgen05 GEMM (bf16
 activations), decode the fused GEMV (fp32).  The collective is torch.distributed's
 all_reduce on the process group (NCCL between GPUs).
 
-Prefill overlaps work the dependencies allow: gate and up (independent GEMMs over the same
-x) run on two streams, so at TP >= 4, where each fills only part of the GPU's CTA-pair
-slots, the second fills what the first leaves; a row-split layer's GEMM runs in two row
-halves and the first half's all-reduce (on NCCL's stream) overlaps the second half's GEMM.
+Gate and up (independent column splits over the same x) are one matmul over their packed
+shards: one launch instead of two, and at TP >= 4, where each alone fills only part of the
+GPU's CTA-pair slots, together they fill 1.5 waves instead of two.  A row-split layer's
+GEMM runs in two row halves and the first half's all-reduce (on NCCL's stream) overlaps
+the second half's GEMM.
 """
 from __future__ import annotations
 
@@ -66,6 +67,21 @@ def shard(w: torch.Tensor, K: int, N: int, qtype, kind: str, rank: int, world: i
     return m[rank * kr:(rank + 1) * kr].contiguous()
 
 
+def swiglu_rows(gu: torch.Tensor, n: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """silu(gate) * up for rows of [gate | up] (gu: fp32 or bf16 CUDA [rows, 2n], the output of
+    one matmul over gate and up packed side by side) -> [rows, n]."""
+    _require_cuda("swiglu_rows", gu)
+    if gu.dim() != 2 or gu.shape[1] != 2 * n or gu.dtype not in (torch.float32, torch.bfloat16) \
+            or not gu.is_contiguous():
+        raise RuntimeError("swiglu_rows: gu must be a contiguous fp32 or bf16 [rows, 2n] tensor")
+    out = torch.empty((gu.shape[0], n), dtype=gu.dtype, device=gu.device) if out is None else out
+    lib = _lib.load()
+    dt = _lib.DTYPE_F32 if gu.dtype == torch.float32 else _lib.DTYPE_BF16
+    _lib.check(lib.vbq_swiglu_rows(gu.data_ptr(), out.data_ptr(), gu.shape[0], n, dt,
+                                   _stream_ptr(gu)), lib)
+    return out
+
+
 def swiglu(g: torch.Tensor, u: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """silu(g) * u (fp32 or bf16 CUDA tensors, same shape), g and u sanitised first."""
     _require_cuda("swiglu", g, u)
@@ -98,6 +114,20 @@ class TPLinear:
     def decode(self, x: torch.Tensor) -> torch.Tensor:
         """x: fp32 [B, k_loc] (B <= 16) -> fp32 [B, n_loc]."""
         return gemv_dequant(x, self.w, None, self.k_loc, self.n_loc, self.t)
+
+    @classmethod
+    def packed_columns(cls, parts, K: int, qtype, device: torch.device) -> "TPLinear":
+        """One matmul over several column-split layers of the same input: the shards
+        ``parts`` (uint8 K x row-bytes block matrices of this rank) packed side by side,
+        each row holding the parts' blocks in order, so one GEMM / GEMV computes all of
+        them and its output columns are the parts' outputs in order."""
+        t = F.parse_type(qtype)
+        self = cls.__new__(cls)
+        self.t, self.kind, self.K, self.rank, self.world = t, "column", K, 0, 1
+        self.w = torch.cat([p.reshape(K, -1) for p in parts], dim=1).contiguous().to(device)
+        self.N = self.n_loc = self.w.shape[1] // F.BLOCK_BYTES[t] * F.BLOCK_VALUES[t]
+        self.k_loc = K
+        return self
 
 
 def reduce_partial(y: torch.Tensor, world: int, group=None, async_op: bool = False):
@@ -144,56 +174,37 @@ def row_split_prefill_reduced(lin: "TPLinear", a: torch.Tensor, group=None) -> t
     return y
 
 
-_side_streams: dict = {}
-
-
-def _side_stream(device: torch.device) -> torch.cuda.Stream:
-    key = torch.device(device).index
-    if key not in _side_streams:
-        _side_streams[key] = torch.cuda.Stream(device)
-    return _side_streams[key]
-
-
-def column_pair_prefill(lin_a: "TPLinear", lin_b: "TPLinear", x: torch.Tensor, out_dtype):
-    """(lin_a.prefill(x), lin_b.prefill(x)), the second on a side stream so that the two
-    independent GEMMs share the GPU; the caller's stream waits for both."""
-    cur = torch.cuda.current_stream(x.device)
-    side = _side_stream(x.device)
-    side.wait_stream(cur)
-    ya = lin_a.prefill(x, out_dtype)
-    with torch.cuda.stream(side):
-        yb = lin_b.prefill(x, out_dtype)
-    cur.wait_stream(side)
-    yb.record_stream(cur)  # yb was allocated on the side stream and is used on this one
-    x.record_stream(side)
-    return ya, yb
-
-
 class TPFFN:
     """SwiGLU FFN of one layer: out = down(silu(gate x) * up x), gate / up column split,
-    down row split, one all-reduce (cpp/src/fast_model.cpp:906-958)."""
+    down row split, one all-reduce (cpp/src/fast_model.cpp:906-958).
+
+    The rank's gate and up shards are packed side by side into one K x (2 I / W) matrix
+    (no requantisation: each row is the gate shard's blocks, then the up shard's), so one
+    GEMM (prefill) or GEMV (decode) launch computes both and SwiGLU reads the two halves
+    of each output row (``swiglu_rows``)."""
 
     def __init__(self, wg, wu, wd, H: int, I: int, qtype, rank: int, world: int, device,
                  group=None):
-        self.gate = TPLinear(wg, H, I, qtype, "column", rank, world, device)
-        self.up = TPLinear(wu, H, I, qtype, "column", rank, world, device)
+        t = F.parse_type(qtype)
+        check_split("column", H, I, t, world)
+        self.i_loc = I // world
+        self.gate_up = TPLinear.packed_columns(
+            [shard(wg, H, I, t, "column", rank, world), shard(wu, H, I, t, "column", rank, world)],
+            H, t, device)
         self.down = TPLinear(wd, I, H, qtype, "row", rank, world, device)
         self.group = group
 
     def prefill(self, x: torch.Tensor, reduce: bool = True) -> torch.Tensor:
         """x: bf16 [M, H] (replicated) -> fp32 [M, H], replicated after the all-reduce
         (reduce=False returns this rank's partial sum and leaves the sum to the caller)."""
-        g, u = column_pair_prefill(self.gate, self.up, x, torch.bfloat16)
-        h = swiglu(g, u, out=g)
+        h = swiglu_rows(self.gate_up.prefill(x, torch.bfloat16), self.i_loc)
         if not reduce:
             return self.down.prefill(h, torch.float32)
         return row_split_prefill_reduced(self.down, h, self.group)
 
     def decode(self, x: torch.Tensor, reduce: bool = True) -> torch.Tensor:
         """x: fp32 [B, H] -> fp32 [B, H] (reduce as for prefill)."""
-        g = self.gate.decode(x)
-        u = self.up.decode(x)
-        h = swiglu(g, u, out=g)
+        h = swiglu_rows(self.gate_up.decode(x), self.i_loc)
         y = self.down.decode(h)
         return reduce_partial(y, self.down.world, self.group) if reduce else y
 
