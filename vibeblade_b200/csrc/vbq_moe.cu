@@ -129,18 +129,12 @@ __device__ __forceinline__ float sanitize(float v) {
   if (v != v) return 0.0f;
   return fminf(fmaxf(v, -65504.0f), 65504.0f);
 }
-// x * sigmoid(x) with the stable two-sided form of vibeblade/moe.py:36-50
-__device__ __forceinline__ float silu_ref(float x) {
-  float s;
-  if (x >= 0.0f) {
-    s = 1.0f / (1.0f + expf(-x));
-  } else {
-    const float e = expf(x);
-    s = e / (1.0f + e);
-  }
-  if (s != s) s = 0.0f;
-  return x * s;
-}
+// x * sigmoid(x) = x / (1 + e^-x), the reference's two-sided form (vibeblade/moe.py:36-50)
+// written without its branch: for the sanitised inputs (|x| <= 65504) e^-x is +inf only
+// where x < -88, and the quotient is then -0, as in the two-sided form.  expf is the full-
+// precision exponential; __fdividef is within 2 ulp for every denominator here (>= 1).
+// Branch-free, so a warp whose inputs have both signs does not run both halves.
+__device__ __forceinline__ float silu_ref(float x) { return __fdividef(x, 1.0f + expf(-x)); }
 
 // silu(g) * u on 8 bf16 / 4 fp32 values (one 16-byte vector of each), inputs sanitised
 __device__ __forceinline__ uint4 swiglu_vec(uint4 gv, uint4 uv, std::true_type /*bf16*/) {
