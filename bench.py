@@ -220,11 +220,14 @@ def bench_tp(dev, rank: int, world: int, steps: int, prefill: bool = True) -> di
     g = torch.Generator(device=dev).manual_seed(2)
     xd = torch.randn(1, H, generator=g, device=dev)
     xd16 = torch.randn(16, H, generator=g, device=dev)
+    xd32 = torch.randn(32, H, generator=g, device=dev)
     stream = torch.cuda.current_stream(dev)
     dms = _time_steps(lambda _: ffn.decode(xd), 5 * steps, 5, stream, world)
     dms16 = _time_steps(lambda _: ffn.decode(xd16), 5 * steps, 5, stream, world)
+    dms32 = _time_steps(lambda _: ffn.decode(xd32), 5 * steps, 5, stream, world)
     dec = {"decode_b1_us_per_ffn": round(1e3 * dms / (5 * steps), 1),
-           "decode_b16_us_per_ffn": round(1e3 * dms16 / (5 * steps), 1)}
+           "decode_b16_us_per_ffn": round(1e3 * dms16 / (5 * steps), 1),
+           "decode_b32_us_per_ffn": round(1e3 * dms32 / (5 * steps), 1)}
     if not prefill:
         return {"metric": "70B FFN decode latency, batch 1 (Q8_0, TP over the job's GPUs)",
                 "value": dec["decode_b1_us_per_ffn"], "unit": "us", "higher_is_better": False,

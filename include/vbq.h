@@ -85,7 +85,8 @@ int vbq_gemv_scratch_bytes(int64_t K, int64_t N, int32_t type, int32_t batch, si
  *                    ggml_type, float* scratch)` (cpp/include/dequant.h:27-35) and of
  * `cuda::gemv_dequant(d_x, d_weights, d_y, K, M, ggml_type, d_scratch, stream)`
  * (cpp/include/cuda_kernels.h:191-199):
- *     y[b, n] = sum_k x[b, k] * deq(W)[k, n],  b < batch (1..16).
+ *     y[b, n] = sum_k x[b, k] * deq(W)[k, n],  b < batch (1..32; above 16 the call runs
+ *     consecutive launches over groups of up to 16 batch rows).
  * x is fp32 [batch, K], y fp32 [batch, N], both row-major.  N must be a multiple of
  * the block size (256 for Q4_K/Q6_K, 32 for Q8_0; this build needs 256 for all);
  * W and y must be 16-byte aligned, x 4-byte aligned.
@@ -157,6 +158,18 @@ int vbq_gemm_grouped(const void* a, const void* w, int64_t slab_bytes, void* c, 
  */
 int vbq_moe_route(const float* logits, int64_t T, int32_t E, int32_t topk, int32_t* idx,
                   float* weight, void* stream);
+
+/*
+ * The MoE dispatch's grouping of (token, slot) entries by expert (the reference sends each
+ * slot's tokens to their experts one slot at a time, vibeblade/moe.py:462-475; here one
+ * stable counting sort on the device): idx int32 [T, topk] is the expert of each entry
+ * (entries outside 0..E-1 are skipped); seg int32 [E + 1] receives the row ranges (expert
+ * e owns rows seg[e] .. seg[e + 1] - 1), pos int32 [T * topk] the row of entry j (-1 when
+ * skipped) and tok int32 [T * topk] the token of each row (j / topk).  Within an expert,
+ * rows follow entry order.  All device memory; E <= 4096.
+ */
+int vbq_moe_sort(const int32_t* idx, int64_t T, int32_t E, int32_t topk, int32_t* seg,
+                 int32_t* pos, int32_t* tok, void* stream);
 
 /* Workspace bytes vbq_moe_ffn needs for these sizes. */
 int vbq_moe_workspace_bytes(int64_t T, int64_t H, int64_t I, int32_t E, int32_t topk,

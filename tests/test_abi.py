@@ -56,7 +56,7 @@ def test_argument_errors_need_no_gpu(lib):
     # unsupported type: reference message (cpp/src/dequant.cpp:764)
     assert lib.vbq_gemv(None, None, None, 16, 256, 2, 1, None, 0, None) == _lib.VBQ_ERR_TYPE
     assert lib.vbq_last_error() == b"gemv_dequant: unsupported type 2"
-    assert lib.vbq_gemv(None, None, None, 16, 256, 12, 17, None, 0, None) == _lib.VBQ_ERR_SHAPE
+    assert lib.vbq_gemv(None, None, None, 16, 256, 12, 33, None, 0, None) == _lib.VBQ_ERR_SHAPE
     assert lib.vbq_gemv(None, None, None, 16, 300, 12, 1, None, 0, None) == _lib.VBQ_ERR_SHAPE
     assert lib.vbq_gemv(None, None, None, 16, 256, 12, 1, None, 0, None) == _lib.VBQ_ERR_NULL
     assert lib.vbq_gemv(16, 16, 8, 16, 256, 12, 1, None, 0, None) == _lib.VBQ_ERR_ALIGN

@@ -108,6 +108,22 @@ def test_gemv_k_past_integer_cap(cuda, qtype):
     assert vb.device_status() == 0
 
 
+@pytest.mark.parametrize("qtype", TYPES)
+@pytest.mark.parametrize("batch", [17, 24, 32])
+def test_gemv_batch_above_16(cuda, qtype, batch):
+    """Batches 17..32 run as launches over groups of up to 16 rows: the same bar against
+    the fp64 product, and each group bit-identical to a separate call on its rows."""
+    K, N = 4096, 2048
+    w = synthetic_weights(K, N, qtype, seed=31, device=cuda)
+    g = torch.Generator(device=cuda).manual_seed(32)
+    x = torch.randn(batch, K, generator=g, device=cuda)
+    y = vb.gemv_dequant(x, w, None, K, N, qtype)
+    ref = x.double() @ vb.dequantize(w, K, N, qtype).double()
+    assert ((y.double() - ref).abs().max() / ref.abs().max()).item() <= TOL
+    assert torch.equal(y[:16], vb.gemv_dequant(x[:16].contiguous(), w, None, K, N, qtype))
+    assert torch.equal(y[16:], vb.gemv_dequant(x[16:].contiguous(), w, None, K, N, qtype))
+
+
 def test_gemv_1d_x_and_out_buffer(cuda, oracle):
     K, N, t = 256, 768, F.GGML_TYPE_Q4_K
     rng = np.random.default_rng(3)

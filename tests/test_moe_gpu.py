@@ -46,6 +46,43 @@ def test_route_vs_oracle(cuda):
         np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
 
 
+def _stable_sort_ref(idx: np.ndarray, E: int):
+    """Stable counting sort of the flattened entries by expert (entries outside 0..E-1
+    skipped): the row layout the device MoE uses."""
+    flat = idx.reshape(-1)
+    k = idx.shape[1]
+    seg = np.zeros(E + 1, np.int32)
+    for e in range(E):
+        seg[e + 1] = seg[e] + int(np.sum(flat == e))
+    pos = np.full(flat.size, -1, np.int32)
+    tok = np.full(flat.size, -1, np.int32)
+    nxt = seg[:-1].copy()
+    for j, e in enumerate(flat):
+        if 0 <= e < E:
+            pos[j] = nxt[e]
+            tok[nxt[e]] = j // k
+            nxt[e] += 1
+    return seg, pos, tok
+
+
+@pytest.mark.parametrize("T,E,k", [(1, 8, 1), (33, 8, 2), (1000, 8, 2), (4096, 8, 2), (777, 64, 4),
+                                   (300, 200, 8), (50, 1000, 2)])
+def test_moe_sort_is_stable_counting_sort(cuda, T, E, k):
+    """vbq_moe_sort (one CTA, 32 warps on contiguous chunks; the single-warp form above
+    384 experts) against a plain stable counting sort, with skipped (out-of-range) entries
+    and sizes that do not divide evenly among the warps."""
+    rng = np.random.default_rng(T * 7 + E + k)
+    idx = rng.integers(0, E, (T, k)).astype(np.int32)
+    idx.reshape(-1)[::13] = -1
+    idx.reshape(-1)[5::29] = E + 3
+    seg, pos, tok = vb.moe_sort(torch.from_numpy(idx).to(cuda), E)
+    rseg, rpos, rtok = _stable_sort_ref(idx, E)
+    assert np.array_equal(seg.cpu().numpy(), rseg)
+    assert np.array_equal(pos.cpu().numpy(), rpos)
+    n = int(rseg[-1])
+    assert np.array_equal(tok.cpu().numpy()[:n], rtok[:n])
+
+
 def test_moe_ffn_matches_reference_golden(cuda):
     g = load_golden("moe_q4_k")
     T, H, I, E, k, t = (int(g[n]) for n in ("T", "H", "I", "E", "topk", "type"))

@@ -9,13 +9,13 @@ from . import formats
 from .formats import GGML_TYPE_Q4_K, GGML_TYPE_Q6_K, GGML_TYPE_Q8_0, row_bytes, tensor_nbytes
 from .dequant import dequantize, dequantize_row, gemv_dequant, gemv_dequant_mt, gemv_scratch_bytes
 from .gemm import gemm_dequant, device_status
-from .moe import gemm_grouped, moe_ffn, moe_route, moe_workspace_bytes
+from .moe import gemm_grouped, moe_ffn, moe_route, moe_sort, moe_workspace_bytes
 from ._lib import VbqError
 
 __all__ = [
     "formats", "GGML_TYPE_Q4_K", "GGML_TYPE_Q6_K", "GGML_TYPE_Q8_0", "row_bytes",
     "tensor_nbytes", "dequantize", "dequantize_row", "gemv_dequant", "gemv_dequant_mt",
     "gemv_scratch_bytes", "gemm_dequant", "device_status", "gemm_grouped", "moe_ffn",
-    "moe_route", "moe_workspace_bytes",
+    "moe_route", "moe_sort", "moe_workspace_bytes",
     "VbqError",
 ]

@@ -44,6 +44,8 @@ SIGNATURES = {
     "vbq_gemm_grouped": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
                                    C.c_int64, C.c_int64, C.c_int32, C.c_int32, C.c_void_p,
                                    C.c_int32, C.c_void_p]),
+    "vbq_moe_sort": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_void_p,
+                               C.c_void_p, C.c_void_p, C.c_void_p]),
     "vbq_moe_route": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_void_p,
                                 C.c_void_p, C.c_void_p]),
     "vbq_moe_workspace_bytes": (C.c_int, [C.c_int64, C.c_int64, C.c_int64, C.c_int32,

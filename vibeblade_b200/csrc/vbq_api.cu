@@ -78,11 +78,15 @@ int vbq_dequantize(const void* w, void* out, int64_t rows, int64_t n, int32_t ty
   return ok();
 }
 
+// Batches above 16 run as launches over groups of up to 16 rows (the kernels' limit), in
+// order on the stream, sharing the scratch (each launch leaves it zero-filled).
+constexpr int32_t kMaxBatch = 32, kLaunchBatch = 16;
+
 static int gemv_checks(int32_t type, int64_t K, int64_t N, int32_t batch) {
   if (!supported(type)) return fail(VBQ_ERR_TYPE, "gemv_dequant: unsupported type " + std::to_string(type));
   if (K < 0 || N < 0) return fail(VBQ_ERR_SHAPE, "vbq_gemv: negative size");
-  if (batch < 1 || batch > 16)
-    return fail(VBQ_ERR_SHAPE, "vbq_gemv: batch must be in 1..16, got " + std::to_string(batch));
+  if (batch < 1 || batch > kMaxBatch)
+    return fail(VBQ_ERR_SHAPE, "vbq_gemv: batch must be in 1..32, got " + std::to_string(batch));
   const int64_t bv = block_values(type);
   if (N % bv != 0)
     return fail(VBQ_ERR_SHAPE, "vbq_gemv: N = " + std::to_string(N) +
@@ -90,10 +94,34 @@ static int gemv_checks(int32_t type, int64_t K, int64_t N, int32_t batch) {
   return VBQ_OK;
 }
 
+// the largest plan among the launches of a call (a full group of 16 and the remainder)
+static vbq::GemvPlan gemv_call_plan(int64_t K, int64_t N, int32_t batch, int32_t type) {
+  vbq::GemvPlan p = vbq::plan_gemv(K, N, batch < kLaunchBatch ? batch : kLaunchBatch, type);
+  const int32_t rem = batch % kLaunchBatch;
+  if (batch > kLaunchBatch && rem != 0) {
+    const vbq::GemvPlan q = vbq::plan_gemv(K, N, rem, type);
+    if (q.scratch_bytes > p.scratch_bytes) p = q;
+  }
+  return p;
+}
+
+static cudaError_t launch_gemv_groups(int32_t type, const float* x, const void* w, float* y,
+                                      int64_t K, int64_t N, int64_t rb, int32_t batch,
+                                      void* scratch, cudaStream_t st) {
+  for (int32_t b0 = 0; b0 < batch; b0 += kLaunchBatch) {
+    const int32_t nb = batch - b0 < kLaunchBatch ? batch - b0 : kLaunchBatch;
+    const vbq::GemvPlan plan = vbq::plan_gemv(K, N, nb, type);
+    cudaError_t e = vbq::launch_gemv(type, x + (int64_t)b0 * K, w, y + (int64_t)b0 * N, K, N, rb, nb,
+                                     plan, scratch, st);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
 int vbq_gemv_scratch_bytes(int64_t K, int64_t N, int32_t type, int32_t batch, size_t* bytes) {
   if (int rc = gemv_checks(type, K, N, batch)) return rc;
   if (!bytes) return fail(VBQ_ERR_NULL, "vbq_gemv_scratch_bytes: bytes is NULL");
-  *bytes = (K == 0 || N == 0 || N % 256 != 0) ? 0 : vbq::plan_gemv(K, N, batch, type).scratch_bytes;
+  *bytes = (K == 0 || N == 0 || N % 256 != 0) ? 0 : gemv_call_plan(K, N, batch, type).scratch_bytes;
   return ok();
 }
 
@@ -114,7 +142,7 @@ int vbq_gemv(const float* x, const void* w, float* y, int64_t K, int64_t N, int3
   if (N % 256 != 0)
     return fail(VBQ_ERR_UNSUPPORTED,
                 "vbq_gemv: N must be a multiple of 256 (Q8_0 rows of a partial 256-value tile are not implemented)");
-  const vbq::GemvPlan plan = vbq::plan_gemv(K, N, batch, type);
+  const vbq::GemvPlan plan = gemv_call_plan(K, N, batch, type);
   if (plan.scratch_bytes > 0) {
     if (!scratch || scratch_bytes < plan.scratch_bytes)
       return fail(VBQ_ERR_WORKSPACE, "vbq_gemv: scratch needs " + std::to_string(plan.scratch_bytes) +
@@ -123,7 +151,7 @@ int vbq_gemv(const float* x, const void* w, float* y, int64_t K, int64_t N, int3
     if (!aligned(scratch, 16)) return fail(VBQ_ERR_ALIGN, "vbq_gemv: scratch must be 16-byte aligned");
   }
   const int64_t rb = (N / block_values(type)) * block_bytes(type);
-  cudaError_t e = vbq::launch_gemv(type, x, w, y, K, N, rb, batch, plan, scratch, st);
+  cudaError_t e = launch_gemv_groups(type, x, w, y, K, N, rb, batch, scratch, st);
   if (e != cudaSuccess) return cuda_fail(e, "vbq_gemv launch");
   return ok();
 }
@@ -232,7 +260,7 @@ extern "C" int vbq_gemv_static_scratch(const float* x, const void* w, float* y, 
     return fail(VBQ_ERR_ALIGN, "vbq_gemv_static_scratch: w and y must be 16-byte aligned, x 4-byte aligned");
   if (N % 256 != 0)
     return fail(VBQ_ERR_UNSUPPORTED, "vbq_gemv_static_scratch: N must be a multiple of 256");
-  const vbq::GemvPlan plan = vbq::plan_gemv(K, N, batch, type);
+  const vbq::GemvPlan plan = gemv_call_plan(K, N, batch, type);
   if (plan.scratch_bytes > kStaticScratchBytes)
     return fail(VBQ_ERR_WORKSPACE,
                 "vbq_gemv_static_scratch: this shape needs " + std::to_string(plan.scratch_bytes) +
@@ -247,7 +275,7 @@ extern "C" int vbq_gemv_static_scratch(const float* x, const void* w, float* y, 
     if (e != cudaSuccess) return cuda_fail(e, "vbq_gemv_static_scratch counter reset");
   }
   const int64_t rb = (N / block_values(type)) * block_bytes(type);
-  cudaError_t e = vbq::launch_gemv(type, x, w, y, K, N, rb, batch, plan, scratch, st);
+  cudaError_t e = launch_gemv_groups(type, x, w, y, K, N, rb, batch, scratch, st);
   if (e != cudaSuccess) return cuda_fail(e, "vbq_gemv_static_scratch launch");
   return ok();
 }
@@ -332,6 +360,17 @@ int vbq_moe_route(const float* logits, int64_t T, int32_t E, int32_t topk, int32
   cudaError_t e = vbq::launch_moe_route(logits, (int)T, E, topk, idx, weight,
                                         static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "vbq_moe_route launch");
+  return ok();
+}
+
+int vbq_moe_sort(const int32_t* idx, int64_t T, int32_t E, int32_t topk, int32_t* seg,
+                 int32_t* pos, int32_t* tok, void* stream) {
+  if (T < 0 || E <= 0 || E > 4096 || topk < 1 || topk > 8 || T * topk > (int64_t)INT32_MAX)
+    return fail(VBQ_ERR_SHAPE, "vbq_moe_sort: need T >= 0, 1 <= E <= 4096, 1 <= topk <= 8");
+  if (!idx || !seg || !pos || !tok) return fail(VBQ_ERR_NULL, "vbq_moe_sort: NULL pointer");
+  cudaError_t e = vbq::launch_moe_sort(idx, (int)T, E, topk, seg, pos, tok,
+                                       static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "vbq_moe_sort launch");
   return ok();
 }
 

@@ -106,6 +106,72 @@ __global__ void sort_kernel(const int32_t* __restrict__ idx, int n, int E, int32
   }
 }
 
+// Single CTA, every warp busy: warp w takes the contiguous entries [w c, (w + 1) c) and
+// counts them per expert; a scan over (expert, warp) in warp order gives each warp its
+// first row per expert; each warp then assigns rows to its entries in entry order, 32 at
+// a time.  The same stable order as sort_kernel (entry order within an expert).
+constexpr int kSortWarps = 32;
+__global__ void sort_parallel_kernel(const int32_t* __restrict__ idx, int n, int E,
+                                     int32_t* __restrict__ seg, int32_t* __restrict__ pos,
+                                     int32_t* __restrict__ tok, int topk) {
+  extern __shared__ int32_t sh[];  // cnt[kSortWarps][E]: counts, then each warp's next row
+  const int warp = threadIdx.x >> 5;
+  const unsigned lane = threadIdx.x & 31u;
+  for (int i = threadIdx.x; i < kSortWarps * E; i += blockDim.x) sh[i] = 0;
+  __syncthreads();
+  const int chunk = (n + kSortWarps - 1) / kSortWarps;
+  const int j0 = warp * chunk, j1 = min(n, j0 + chunk);
+  int32_t* mine = sh + warp * E;
+  for (int base = j0; base < j1; base += 32) {
+    const int j = base + (int)lane;
+    const int e = (j < j1) ? idx[j] : -1;
+    const bool valid = e >= 0 && e < E;
+    const unsigned same = __match_any_sync(0xffffffffu, valid ? e : -1);
+    if (valid && __popc(same & ((1u << lane) - 1u)) == 0) mine[e] += __popc(same);
+    __syncwarp();
+  }
+  __syncthreads();
+  // expert e: the warps' first rows in warp order, then the segment offsets
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < kSortWarps; ++w) {
+      const int c = sh[w * E + e];
+      sh[w * E + e] = run;
+      run += c;
+    }
+    seg[e + 1] = run;  // the expert's total, scanned below
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0;
+    seg[0] = 0;
+    for (int e = 0; e < E; ++e) {
+      const int c = seg[e + 1];
+      seg[e] = run;
+      run += c;
+    }
+    seg[E] = run;
+  }
+  __syncthreads();
+  for (int e = (int)lane; e < E; e += 32) mine[e] += seg[e];  // + the segment start
+  __syncwarp();
+  for (int base = j0; base < j1; base += 32) {
+    const int j = base + (int)lane;
+    const int e = (j < j1) ? idx[j] : -1;
+    const bool valid = e >= 0 && e < E;
+    const unsigned same = __match_any_sync(0xffffffffu, valid ? e : -1);
+    const int rank = __popc(same & ((1u << lane) - 1u));
+    const int row = valid ? mine[e] + rank : -1;
+    __syncwarp();
+    if (valid && rank == 0) mine[e] += __popc(same);
+    __syncwarp();
+    if (j < j1) {
+      pos[j] = row;
+      if (valid) tok[row] = j / topk;
+    }
+  }
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&p);
@@ -196,6 +262,27 @@ __global__ void combine_kernel(const float* __restrict__ y, const int32_t* __res
   }
 }
 
+// combine_kernel on 16-byte vectors (H % 4 == 0, aligned rows): the same products and sums
+// per value, in the same order
+__global__ void combine4_kernel(const float4* __restrict__ y, const int32_t* __restrict__ pos,
+                                const float* __restrict__ weight, int topk, int H4,
+                                float4* __restrict__ out) {
+  const int t = blockIdx.x;
+  for (int d = threadIdx.x; d < H4; d += blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < topk; ++k) {
+      const int r = pos[(int64_t)t * topk + k];
+      const float4 v = r >= 0 ? y[(int64_t)r * H4 + d] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float w = weight[(int64_t)t * topk + k];
+      acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(w, v.w));
+    }
+    out[(int64_t)t * H4 + d] = make_float4(sanitize(acc.x), sanitize(acc.y), sanitize(acc.z), sanitize(acc.w));
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_moe_route(const float* logits, int T, int E, int topk, int32_t* idx,
@@ -208,6 +295,11 @@ cudaError_t launch_moe_route(const float* logits, int T, int E, int topk, int32_
 
 cudaError_t launch_moe_sort(const int32_t* idx, int T, int E, int topk, int32_t* seg,
                             int32_t* pos, int32_t* tok, cudaStream_t st) {
+  const size_t shm_par = (size_t)kSortWarps * E * sizeof(int32_t);
+  if (shm_par <= 48 * 1024) {
+    sort_parallel_kernel<<<1, 32 * kSortWarps, shm_par, st>>>(idx, T * topk, E, seg, pos, tok, topk);
+    return cudaGetLastError();
+  }
   const size_t shm = (size_t)2 * E * sizeof(int32_t);
   if (shm > 48 * 1024) return cudaErrorInvalidValue;
   sort_kernel<<<1, 1024, shm, st>>>(idx, T * topk, E, seg, pos, tok, topk);
@@ -262,7 +354,11 @@ cudaError_t launch_swiglu_rows(const void* gu, void* h, int64_t rows, int64_t n,
 cudaError_t launch_moe_combine(const float* y, const int32_t* pos, const float* weight, int T,
                                int topk, int H, float* out, cudaStream_t st) {
   if (T <= 0) return cudaSuccess;
-  combine_kernel<<<T, 256, 0, st>>>(y, pos, weight, topk, H, out);
+  if (H % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0)
+    combine4_kernel<<<T, 256, 0, st>>>(reinterpret_cast<const float4*>(y), pos, weight, topk, H / 4,
+                                       reinterpret_cast<float4*>(out));
+  else
+    combine_kernel<<<T, 256, 0, st>>>(y, pos, weight, topk, H, out);
   return cudaGetLastError();
 }
 

@@ -98,7 +98,7 @@ def gemv_dequant(x: torch.Tensor, weights: torch.Tensor, out: torch.Tensor | Non
     """``gemv_dequant(x, W, out, K, N, wtype, scratch)`` (cpp/include/dequant.h:27-35):
     out[n] = sum_k x[k] * deq(W)[k, n].
 
-    ``x`` may also be a batch [B, K] with B <= 16 (the reference engine makes B calls,
+    ``x`` may also be a batch [B, K] with B <= 32 (the reference engine makes B calls,
     cpp/src/fast_model.cpp:645-660); ``out`` is then [B, N].  ``scratch`` is the
     caller-owned split-K buffer, as in the reference: a CUDA tensor of at least
     ``gemv_scratch_bytes(K, N, wtype, B)`` bytes, zero-filled before its first use (each
@@ -114,8 +114,8 @@ def gemv_dequant(x: torch.Tensor, weights: torch.Tensor, out: torch.Tensor | Non
         batch = x.numel() // K
     else:
         batch = x.shape[0] if x.dim() > 1 else 1
-    if not 1 <= batch <= 16:
-        raise RuntimeError(f"gemv_dequant: batch must be in 1..16, got {batch}")
+    if not 1 <= batch <= 32:
+        raise RuntimeError(f"gemv_dequant: batch must be in 1..32, got {batch}")
     w = _weights_u8(weights)
     need = F.row_bytes(t, N) * K
     if w.numel() < need:

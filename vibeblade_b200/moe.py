@@ -33,6 +33,24 @@ def moe_route(logits: torch.Tensor, topk: int) -> tuple[torch.Tensor, torch.Tens
     return idx, w
 
 
+def moe_sort(idx: torch.Tensor, E: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Stable counting sort of the (token, slot) entries of idx (int32 [T, topk]) by expert.
+    Returns (seg int32 [E + 1], pos int32 [T * topk], tok int32 [T * topk]): expert e owns
+    rows seg[e] .. seg[e + 1] - 1, entry j sits at row pos[j] (-1 if its expert is outside
+    0..E-1), row r holds token tok[r]; rows of an expert follow entry order."""
+    _require_cuda("moe_sort", idx)
+    if idx.dtype != torch.int32 or idx.dim() != 2 or not idx.is_contiguous():
+        raise RuntimeError("moe_sort: idx must be a contiguous int32 [T, topk] tensor")
+    T, k = idx.shape
+    seg = torch.empty(E + 1, dtype=torch.int32, device=idx.device)
+    pos = torch.empty(T * k, dtype=torch.int32, device=idx.device)
+    tok = torch.full((T * k,), -1, dtype=torch.int32, device=idx.device)
+    lib = _lib.load()
+    _lib.check(lib.vbq_moe_sort(idx.data_ptr(), T, E, k, seg.data_ptr(), pos.data_ptr(),
+                                tok.data_ptr(), _stream_ptr(idx)), lib)
+    return seg, pos, tok
+
+
 def gemm_grouped(a: torch.Tensor, slabs: torch.Tensor, seg: torch.Tensor, K: int, N: int, wtype,
                  out: torch.Tensor | None = None, out_dtype=torch.float32,
                  slab_bytes: int | None = None) -> torch.Tensor:

@@ -112,7 +112,7 @@ class TPLinear:
         return gemm_dequant(a, self.w, out, a.shape[0], self.k_loc, self.n_loc, self.t, out_dtype)
 
     def decode(self, x: torch.Tensor) -> torch.Tensor:
-        """x: fp32 [B, k_loc] (B <= 16) -> fp32 [B, n_loc]."""
+        """x: fp32 [B, k_loc] (B <= 32) -> fp32 [B, n_loc]."""
         return gemv_dequant(x, self.w, None, self.k_loc, self.n_loc, self.t)
 
     @classmethod
