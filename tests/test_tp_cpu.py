@@ -153,3 +153,50 @@ def test_reduce_partial_collective_decision():
     res = mp.get_context("spawn").Manager().dict()
     mp.spawn(_reduce_rank, args=(2, _free_port(), res), nprocs=2, join=True)
     assert res[0] == (True, [3.0] * 4) and res[1] == (True, [3.0] * 4)
+
+
+class _CpuRowLinear:
+    """Stand-in for a row-split TPLinear on the CPU: rank r's rows of a dense weight."""
+
+    def __init__(self, w_full: torch.Tensor, rank: int, world: int):
+        K = w_full.shape[0]
+        self.world, self.n_loc = world, w_full.shape[1]
+        self.w = w_full[rank * K // world:(rank + 1) * K // world]
+
+    def prefill(self, a, out_dtype=torch.float32, out=None):
+        r = a.float() @ self.w
+        if out is None:
+            return r
+        out.copy_(r)
+        return out
+
+
+def _row_split_rank(rank, world, port, res):
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
+    try:
+        g = torch.Generator().manual_seed(5)
+        out = {}
+        for M in (300, 600, 2048):  # no split, split at 512, split at 1024
+            a = torch.randn(M, 64, generator=g)
+            w = torch.randn(64, 48, generator=g)
+            lin = _CpuRowLinear(w, rank, world)
+            k = 64 // world
+            y = tp.row_split_prefill_reduced(lin, a[:, rank * k:(rank + 1) * k].contiguous())
+            out[M] = float((y - a @ w).abs().max())
+        res[rank] = out
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_split_prefill_reduced_gloo():
+    """The row-split prefill with its first half's all-reduce in flight while the second
+    half computes (split at whole 512-row pair tiles): the sum over ranks equals the full
+    product for M with no split, an uneven split and an even one."""
+    import torch.multiprocessing as mp
+    res = mp.get_context("spawn").Manager().dict()
+    mp.spawn(_row_split_rank, args=(2, _free_port(), res), nprocs=2, join=True)
+    for rank in (0, 1):
+        assert all(v < 1e-4 for v in res[rank].values()), res[rank]
