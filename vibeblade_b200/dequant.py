@@ -37,12 +37,23 @@ def _weights_u8(w: torch.Tensor) -> torch.Tensor:
 _SCRATCH: dict[tuple[int, int], torch.Tensor] = {}
 
 
+# scratch sizes per (device, K, N, type, batch): the plan depends on the device's SM count
+_SCRATCH_BYTES: dict[tuple[int, int, int, int, int], int] = {}
+
+
 def gemv_scratch_bytes(K: int, N: int, wtype, batch: int = 1) -> int:
     """Bytes of scratch ``gemv_dequant`` needs for this shape on the current device."""
+    t = F.parse_type(wtype)
+    dev = torch.cuda.current_device() if torch.cuda.is_available() else -1
+    key = (dev, K, N, t, batch)
+    hit = _SCRATCH_BYTES.get(key)
+    if hit is not None:
+        return hit
     import ctypes as C
     lib = _lib.load()
     v = C.c_size_t()
-    _lib.check(lib.vbq_gemv_scratch_bytes(K, N, F.parse_type(wtype), batch, C.byref(v)), lib)
+    _lib.check(lib.vbq_gemv_scratch_bytes(K, N, t, batch, C.byref(v)), lib)
+    _SCRATCH_BYTES[key] = int(v.value)
     return int(v.value)
 
 
