@@ -136,6 +136,17 @@ def _time_steps(step, steps: int, warmup: int, stream, world: int):
     return float(t.item())
 
 
+def _soft(fn, *args, **kw) -> dict:
+    """A one-GPU extra measurement whose failure is reported on the line instead of ending
+    the run (the headline is measured before the extras)."""
+    try:
+        return fn(*args, **kw)
+    except Exception as e:  # noqa: BLE001 - reported on the line, not hidden
+        import torch
+        torch.cuda.synchronize()
+        return {"error": f"{type(e).__name__}: {e}"[:300]}
+
+
 def bench_prefill(dev, steps: int) -> dict:
     """the 8B layer's five matrices in Q6_K times bf16 activations of
     M = 2048 tokens (tcgen05 GEMM, bf16 out).  Whole layer per step."""
@@ -566,8 +577,8 @@ def run_gpu(args) -> None:
     extras = {}
     if not args.no_extras:
         if world == 1:
-            extras["prefill"] = bench_prefill(dev, args.extras_steps)
-            extras["moe"] = bench_moe(dev, args.extras_steps)
+            extras["prefill"] = _soft(bench_prefill, dev, args.extras_steps)
+            extras["moe"] = _soft(bench_moe, dev, args.extras_steps)
         extras["tp_ffn"] = bench_tp(dev, rank, world, args.extras_steps)
     else:  # config 5's decode side runs on the GEMV alone
         extras["tp_ffn_decode"] = bench_tp(dev, rank, world, args.extras_steps, prefill=False)
