@@ -15,7 +15,14 @@ from . import _lib
 from . import formats as F
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream_ptr(t: torch.Tensor) -> int:
+    """The current CUDA stream of t's device as a raw handle (no Stream object per call:
+    this runs once per operator call on the decode path)."""
+    if _raw_stream is not None:
+        return _raw_stream(t.device.index if t.device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
@@ -37,6 +44,15 @@ def _weights_u8(w: torch.Tensor) -> torch.Tensor:
 _SCRATCH: dict[tuple[int, int], torch.Tensor] = {}
 
 
+_CUDA_AVAILABLE: list[bool] = []
+
+
+def _cuda_available() -> bool:
+    if not _CUDA_AVAILABLE:
+        _CUDA_AVAILABLE.append(torch.cuda.is_available())
+    return _CUDA_AVAILABLE[0]
+
+
 # scratch sizes per (device, K, N, type, batch): the plan depends on the device's SM count
 _SCRATCH_BYTES: dict[tuple[int, int, int, int, int], int] = {}
 
@@ -44,7 +60,7 @@ _SCRATCH_BYTES: dict[tuple[int, int, int, int, int], int] = {}
 def gemv_scratch_bytes(K: int, N: int, wtype, batch: int = 1) -> int:
     """Bytes of scratch ``gemv_dequant`` needs for this shape on the current device."""
     t = F.parse_type(wtype)
-    dev = torch.cuda.current_device() if torch.cuda.is_available() else -1
+    dev = torch.cuda.current_device() if _cuda_available() else -1
     key = (dev, K, N, t, batch)
     hit = _SCRATCH_BYTES.get(key)
     if hit is not None:
