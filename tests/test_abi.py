@@ -66,6 +66,22 @@ def test_argument_errors_need_no_gpu(lib):
     assert lib.vbq_dequantize(0, 0, 0, 256, 12, 0, None) == _lib.VBQ_OK  # empty: no work
 
 
+def test_newer_entry_points_validate_before_any_cuda_call(lib):
+    """vbq_swiglu_rows and vbq_moe_sort check their arguments before touching the GPU."""
+    from vibeblade_b200 import _lib
+    assert lib.vbq_swiglu_rows(None, None, 4, 16, 9, None) == _lib.VBQ_ERR_SHAPE      # dtype
+    assert lib.vbq_swiglu_rows(None, None, -1, 16, 0, None) == _lib.VBQ_ERR_SHAPE     # rows < 0
+    assert lib.vbq_swiglu_rows(None, None, 0, 16, 0, None) == _lib.VBQ_OK             # nothing to do
+    assert lib.vbq_swiglu_rows(None, None, 4, 16, 0, None) == _lib.VBQ_ERR_NULL
+    assert lib.vbq_swiglu_rows(16, 16, 4, 12, 0, None) == _lib.VBQ_ERR_SHAPE          # n % 8
+    assert lib.vbq_swiglu_rows(8, 16, 4, 16, 0, None) == _lib.VBQ_ERR_ALIGN
+    assert lib.vbq_moe_sort(None, 10, 8, 2, None, None, None, None) == _lib.VBQ_ERR_NULL
+    assert lib.vbq_moe_sort(None, 10, 0, 2, None, None, None, None) == _lib.VBQ_ERR_SHAPE   # E
+    assert lib.vbq_moe_sort(None, 10, 5000, 2, None, None, None, None) == _lib.VBQ_ERR_SHAPE
+    assert lib.vbq_moe_sort(None, 10, 8, 9, None, None, None, None) == _lib.VBQ_ERR_SHAPE   # topk
+    assert b"vbq_moe_sort" in lib.vbq_last_error()
+
+
 def test_scratch_size_query(lib):
     """Split-K scratch: counters + splits * batch * N partials; none when K is tiny, and
     none for the tensor-core Q4_K kernel (batch 1..16), whose splits add up inside a
