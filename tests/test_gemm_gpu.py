@@ -94,3 +94,57 @@ def test_gemm_rejects_bad_shapes(cuda):
     w6 = torch.zeros(64 * 210 * 4, dtype=torch.uint8, device=cuda)
     with pytest.raises(vb.VbqError, match="16 bytes"):
         vb.gemm_dequant(a, w6, None, 4, 64, 1024, "Q6_K")
+
+
+# Several 512-row pair tiles and several waves of the 74 CTA pairs: config 3's M = 2048
+# and M = 8192 (the benched sizes; M = 8192 is where the raw-weight ring race once
+# showed), Q4_K at M = 8192, and ragged M that ends inside a pair tile and inside a
+# CTA's 128-row quarter.
+MULTI = [(F.GGML_TYPE_Q6_K, 2048, 4096, 14336), (F.GGML_TYPE_Q6_K, 2048, 14336, 4096),
+         (F.GGML_TYPE_Q6_K, 2048, 4096, 6144), (F.GGML_TYPE_Q6_K, 8192, 4096, 14336),
+         (F.GGML_TYPE_Q6_K, 8192, 14336, 4096), (F.GGML_TYPE_Q4_K, 8192, 4096, 14336),
+         (F.GGML_TYPE_Q4_K, 1573, 4096, 14336), (F.GGML_TYPE_Q4_K, 2000, 14336, 4096),
+         (F.GGML_TYPE_Q8_0, 2048 + 37, 8192, 10240)]
+
+
+@pytest.mark.parametrize("qtype,M,K,N", MULTI)
+def test_gemm_multi_tile_vs_fp32_matmul(cuda, qtype, M, K, N):
+    """Two bars: the north star's 2e-2 against an fp32 product of the bit-exact
+    dequantization, and 1e-4 against the same product over the weights rounded to bf16
+    (the kernel's operands), which only accumulation order separates, so a wrong or stale
+    tile anywhere in the grid shows.  Three calls give the same bits and a clean status."""
+    w = synthetic_weights(K, N, qtype, seed=7, device=cuda)
+    g = torch.Generator(device=cuda).manual_seed(8)
+    a = torch.randn(M, K, generator=g, device=cuda).to(torch.bfloat16)
+    c = vb.gemm_dequant(a, w, None, M, K, N, qtype)
+    deq = vb.dequantize(w, K, N, qtype)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        af = a.float()
+        ref = af @ deq
+        den = ref.abs().max()
+        assert ((c - ref).abs().max() / den).item() <= TOL
+        del ref
+        ref_b = af @ deq.to(torch.bfloat16).float()
+        assert ((c - ref_b).abs().max() / den).item() <= 1e-4
+        del ref_b
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    assert vb.device_status() == 0
+    for _ in range(2):
+        c2 = vb.gemm_dequant(a, w, None, M, K, N, qtype)
+        assert torch.equal(c, c2)
+    assert vb.device_status() == 0
+
+
+def test_gemm_multi_tile_bf16_out_matches_fp32_out(cuda):
+    """bf16 output at M = 8192 is the fp32 output rounded to nearest-even, tile by tile."""
+    qtype, M, K, N = F.GGML_TYPE_Q6_K, 8192, 4096, 6144
+    w = synthetic_weights(K, N, qtype, seed=9, device=cuda)
+    g = torch.Generator(device=cuda).manual_seed(10)
+    a = torch.randn(M, K, generator=g, device=cuda).to(torch.bfloat16)
+    c32 = vb.gemm_dequant(a, w, None, M, K, N, qtype)
+    c16 = vb.gemm_dequant(a, w, None, M, K, N, qtype, out_dtype=torch.bfloat16)
+    assert torch.equal(c16, c32.to(torch.bfloat16))
+    assert vb.device_status() == 0

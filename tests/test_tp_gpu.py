@@ -112,6 +112,40 @@ def test_tp_attention_projections_emulated(cuda):
     assert vb.device_status() == 0
 
 
+@pytest.mark.parametrize("world", [1, 8])
+def test_tp_ffn_prefill_emulated_m2048(cuda, world):
+    """Config 5's prefill size: 2048 rows = four 512-row pair tiles per GEMM, and at TP = 8
+    the gate|up GEMM's 1.5 waves.  Same bar and reference as above, plus bit-identical
+    repeats."""
+    wg, wu, wd = _weights(cuda)
+    g = torch.Generator(device=cuda).manual_seed(12)
+    M = 2048
+    xb = torch.randn(M, H, generator=g, device=cuda).to(torch.bfloat16)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        xf = xb.float()
+        gp = (xf @ vb.dequantize(wg, H, I, QT)).to(torch.bfloat16).float()
+        up = (xf @ vb.dequantize(wu, H, I, QT)).to(torch.bfloat16).float()
+        hp = (torch.nn.functional.silu(gp) * up).to(torch.bfloat16).float()
+        del gp, up
+        ref = hp @ vb.dequantize(wd, I, H, QT)
+        del hp
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    ranks = [tp.TPFFN(wg, wu, wd, H, I, QT, r, world, cuda) for r in range(world)]
+    y = torch.zeros(M, H, device=cuda)
+    for f in ranks:
+        y += f.prefill(xb, reduce=False)
+    torch.cuda.synchronize()
+    assert vb.device_status() == 0
+    assert _rel(y, ref) <= 2e-2
+    y2 = torch.zeros(M, H, device=cuda)
+    for f in ranks:
+        y2 += f.prefill(xb, reduce=False)
+    assert torch.equal(y, y2)
+
+
 def _nccl_rank(rank, world, port, res):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
