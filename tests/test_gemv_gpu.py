@@ -221,3 +221,55 @@ def test_gemv_cuda_graph_replay(cuda, qtype, batch):
         torch.cuda.synchronize()
         assert torch.equal(y, y_eager)
     assert vb.device_status() == 0
+
+
+def _outlier_x(rng, batch, K, frac, lo=100.0, hi=1000.0):
+    """N(0, 1) activations with outlier channels, like real hidden states: `frac` of the
+    entries of every row scaled by lo..hi (random sign), scattered, so many 32-row warp
+    slices hold one outlier among 31 ordinary rows; one extra outlier is placed at the
+    last row of the first slice."""
+    x = rng.normal(0, 1, (batch, K)).astype(np.float32)
+    n = max(1, int(frac * K))
+    for b in range(batch):
+        idx = rng.choice(K, n, replace=False)
+        x[b, idx] *= (rng.uniform(lo, hi, n) * rng.choice([-1.0, 1.0], n)).astype(np.float32)
+        x[b, 31] = np.float32(hi)
+    return x
+
+
+def _check_columns(y, ref, what):
+    """Max-norm bar (1e-3 of the largest output) and a per-column bar: every output with
+    |ref| >= 1e-2 of its row's largest keeps 1e-3 relative accuracy."""
+    y = np.asarray(y, np.float64)
+    ref = np.asarray(ref, np.float64)
+    mx = np.abs(ref).max(axis=1, keepdims=True)
+    err = np.abs(y - ref)
+    assert (err / mx).max() <= TOL, f"{what}: max-norm {(err / mx).max():.3g}"
+    big = np.abs(ref) >= 1e-2 * mx
+    rel = err[big] / np.abs(ref[big])
+    assert rel.max() <= TOL, f"{what}: per-column {rel.max():.3g}"
+
+
+OUTLIER = [(F.GGML_TYPE_Q4_K, 4096, 14336), (F.GGML_TYPE_Q4_K, 14336, 4096),
+           (F.GGML_TYPE_Q8_0, 8192, 10240), (F.GGML_TYPE_Q8_0, 28672, 8192),
+           (F.GGML_TYPE_Q6_K, 4096, 4096)]
+
+
+@pytest.mark.parametrize("qtype,K,N", OUTLIER)
+@pytest.mark.parametrize("batch", [1, 4, 16])
+@pytest.mark.parametrize("frac", [0.001, 0.01])
+def test_gemv_outlier_activations(cuda, oracle, qtype, K, N, batch, frac):
+    """The integer kernels round x * scale per (warp, batch row) to a fixed point set by
+    the slice's largest value, so an outlier coarsens its 31 neighbours: checked per
+    column against the fp64 product and against the reference's sequential fp32 sum."""
+    rng = np.random.default_rng(K + N + batch + int(frac * 1e4) + qtype)
+    w = synthetic_weights(K, N, qtype, seed=K + qtype, device=cuda)
+    x = _outlier_x(rng, batch, K, frac)
+    y = vb.gemv_dequant(torch.from_numpy(x).to(cuda), w, None, K, N, qtype).cpu().numpy()
+    assert vb.device_status() == 0
+    deq = vb.dequantize(w, K, N, qtype).double()
+    ref64 = (torch.from_numpy(x).to(cuda).double() @ deq).cpu().numpy()
+    del deq
+    _check_columns(y, ref64, "fp64")
+    ref = oracle.gemv_dequant(x, w.cpu().numpy(), K, N, qtype)
+    _check_columns(y, ref, "oracle")

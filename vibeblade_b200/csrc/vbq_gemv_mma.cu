@@ -17,11 +17,17 @@
 //     to n + 4161408; column 3 (7) of B is all ones, so the MMA also yields sum q, and the
 //     offset comes off in int32 (top digit centred) before fp32.
 //   * The s32 accumulators run across the CTA's stages (exact integer sums).  A stage
-//     whose |v| outgrows the scale (rare; warp-uniform) first moves the sums so far to
-//     fp32 and raises the scale.  The min term is summed in fp32 on the side.
-// Accuracy: each v is rounded to 2^-19 of the warp's largest |v| for its batch row (headroom
-// 4-8x), products and sums are exact, fp32 at the end.  A v that is not finite (or beyond
-// 2^100) marks its batch row in the warp, whose 128 outputs for that row are then NaN.
+//     whose |v| outgrows the scale, or whose sampled |v| for some batch row (one value per
+//     lane) all sit 16x or more below the value the scale was set from (warp-uniform
+//     decisions; both rare on ordinary activations), first moves the sums so far to fp32
+//     and then sets the scales again from this stage's full maximum.  The min term is
+//     summed in fp32 on the side.
+// Accuracy: each v is rounded to 2^-20 of the warp's largest |v| for its batch row in the
+// stage that set the scale (headroom 2-4x), products and sums are exact, fp32 at the end.
+// Because the scale also comes back down, an outlier activation (a channel 100-1000x its
+// neighbours) coarsens only the rows of its own stage, not the rest of the warp's stages.
+// A v that is not finite (or beyond 2^100) marks its batch row in the warp, whose 128
+// outputs for that row are then NaN.
 //
 // Decomposition: a CTA owns one 256-column tile (one Q4_K block per row) and every S-th
 // 128-row stage of the matrix (stages split, split + S, ...), so each CTA samples the
@@ -195,12 +201,14 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
         for (int c = 0; c < 4; ++c)
 #pragma unroll
           for (int h = 0; h < 2; ++h) acc[z][c][h][0] = acc[z][c][h][1] = acc[z][c][h][2] = acc[z][c][h][3] = 0;
-      float scale[BATCH], step[BATCH];
+      float scale[BATCH];  // powers of two; the step of batch row b is 1 / scale[b]
+      // bit b: batch row b may be rescaled down (a row below `batch` whose scale was not set
+      // from an all-zero stage)
+      uint32_t down_ok = 0u;
       float2 mn2[BATCH][2];  // min-term sums, rows 2 rp / 2 rp + 1
 #pragma unroll
       for (int b = 0; b < BATCH; ++b) {
         scale[b] = 1.f;  // the first stage sets the scale
-        step[b] = 1.f;
         mn2[b][0] = mn2[b][1] = make_float2(0.f, 0.f);
       }
       // s32 sums -> fp32.  Lanes t even hold digits 0, 1 of batch row 2z + t/2, lanes t odd
@@ -213,7 +221,8 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
         const int cen = odd ? 64 : 0;
 #pragma unroll
         for (int z = 0; z < NSET; ++z) {
-          const float sb = (t >> 1) ? ((2 * z + 1 < BATCH) ? step[(2 * z + 1) % BATCH] : 0.f) : step[(2 * z) % BATCH];
+          const float sb = (t >> 1) ? ((2 * z + 1 < BATCH) ? inv_pow2(scale[(2 * z + 1) % BATCH]) : 0.f)
+                                  : inv_pow2(scale[(2 * z) % BATCH]);
 #pragma unroll
           for (int c = 0; c < 4; ++c)
 #pragma unroll
@@ -302,7 +311,7 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
           // float keeps the exponent of 2^23 (|n| < 2^22); NaN, inf and overflow leave it
           float2 v[BATCH][2];
           uint32_t w[BATCH][2][2];
-          uint32_t out = 0u;
+          uint32_t out = 0u, small = 0u;
 #pragma unroll
           for (int b = 0; b < BATCH; ++b) {
             v[b][0] = __fmul2_rn(xv[b], dl0);
@@ -315,10 +324,16 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
               w[b][h][1] = __float_as_uint(fmaf(v[b][h].y, scale[b], kMagic));
               out |= (w[b][h][0] ^ 0x4b000000u) | (w[b][h][1] ^ 0x4b000000u);
             }
+            // one of the lane's four values is the sample (the test only decides whether to
+            // rescale; the rescale itself takes the full maximum): |n| < 2^16
+            // (the word holds 1.5 * 2^23 + n when in range: |n| < 2^16 <=> w - (1.5 * 2^23 - 2^16)
+            // below 2^17; an out-of-range word fails it and rescales through `out` anyway)
+            small |= (w[b][0][0] - 0x4b3f0000u < 0x20000u) ? (1u << b) : 0u;
           }
-          if (__any_sync(0xffffffffu, out >= (1u << 23)) || it == 0) {
+          if (__any_sync(0xffffffffu, out >= (1u << 23)) ||
+              __reduce_and_sync(0xffffffffu, small & down_ok) != 0u || it == 0) {
             // rare (and the first stage): flag non-finite values, move the sums to fp32, then
-            // scale each batch row to 4-8x its largest finite |v| and encode again.  The
+            // scale each batch row to 2-4x its largest finite |v| and encode again.  The
             // max ignores NaN and is capped so that huge values do not rescale every stage.
             if (it > 0) flush();  // nothing accumulated before the first stage
 #pragma unroll
@@ -329,10 +344,10 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
                                     fmaxf(fabsf(v[b][1].x), fabsf(v[b][1].y))), 0x1p99f);
 #pragma unroll
               for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-              int e = (int)((__float_as_uint(m) >> 23) & 0xffu) - 127 + 2;
+              int e = (int)((__float_as_uint(m) >> 23) & 0xffu) - 127 + 1;
               e = e < kExpMin ? kExpMin : (e > kExpMax ? kExpMax : e);
               scale[b] = pow2f(21 - e);
-              step[b] = pow2f(e - 21);
+              down_ok = (b < batch && e > kExpMin) ? (down_ok | (1u << b)) : (down_ok & ~(1u << b));
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
                 w[b][h][0] = __float_as_uint(fmaf(v[b][h].x, scale[b], kMagic));
@@ -556,16 +571,16 @@ static cudaError_t launch_t(const float* x, const void* w, float* y, int64_t K, 
     return cudaErrorInvalidValue;
   auto kern = gemv_mma_kernel<BATCH>;
   constexpr int kBase = Lay<(BATCH <= 2 ? 1 : 2)>::kSmem;
-  static unsigned configured = 0;  // one bit per device ordinal
+  static DeviceOnce configured;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev >= 32 || !(configured & (1u << dev))) {
+  if (!configured.done(dev)) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
-    if (dev < 32) configured |= (1u << dev);
+    configured.mark(dev);
   }
   const int S = choose_splits<BATCH>(K, N, batch, kBase);
   cudaLaunchConfig_t cfg = {};

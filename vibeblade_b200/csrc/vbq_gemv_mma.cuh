@@ -97,6 +97,8 @@ __device__ __forceinline__ bool mbar_wait_hinted(uint32_t bar, uint32_t parity, 
 }
 
 __device__ __forceinline__ float pow2f(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }
+// 1 / s for a power of two s = 2^k with |k| <= 126 (exact: the exponent field is negated)
+__device__ __forceinline__ float inv_pow2(float s) { return __uint_as_float(0x7f000000u - __float_as_uint(s)); }
 
 }  // namespace gmma
 }  // namespace vbq

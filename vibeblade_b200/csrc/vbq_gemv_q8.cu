@@ -7,6 +7,9 @@
 // block) goes into the B columns as three signed byte digits of a 22-bit fixed-point
 // integer on a power-of-two scale per warp and batch row, with an all-ones column for the
 // digits' offset, as in the Q4_K kernel (vbq_gemv_mma.cu).  Accumulation is exact s32.
+// As there, the scale is set again (after a flush to fp32) when a stage's |v| outgrows it
+// or sits 16x or more below the value it was set from, so an outlier activation coarsens
+// only its own stage's rows.
 //
 // Layout: a CTA owns one 256-column tile (8 blocks, 272 bytes of each row) and every S-th
 // 64-row stage.  A block's codes start 2 bytes into it, so rows are only 2-byte aligned
@@ -159,9 +162,10 @@ gemv_q8_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restri
     for (int z = 0; z < NSET; ++z)
 #pragma unroll
       for (int k = 0; k < 4; ++k) acc[z][k][0] = acc[z][k][1] = acc[z][k][2] = acc[z][k][3] = 0;
-    float scale[BATCH], step[BATCH];
+    float scale[BATCH];  // powers of two; the step of batch row b is 1 / scale[b]
+    uint32_t down_ok = 0u;  // rows that may be rescaled down (see vbq_gemv_mma.cu)
 #pragma unroll
-    for (int b = 0; b < BATCH; ++b) scale[b] = step[b] = 1.f;
+    for (int b = 0; b < BATCH; ++b) scale[b] = 1.f;
     // s32 sums -> fp32 (see vbq_gemv_mma.cu): lanes t even hold digits 0, 1 of batch row
     // 2z + t/2, lanes t odd digit 2 and the code sum; the pair adds its halves
     auto flush = [&]() {
@@ -170,7 +174,8 @@ gemv_q8_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restri
       const int cen = odd ? 64 : 0;
 #pragma unroll
       for (int z = 0; z < NSET; ++z) {
-        const float sb = (t >> 1) ? ((2 * z + 1 < BATCH) ? step[(2 * z + 1) % BATCH] : 0.f) : step[(2 * z) % BATCH];
+        const float sb = (t >> 1) ? ((2 * z + 1 < BATCH) ? inv_pow2(scale[(2 * z + 1) % BATCH]) : 0.f)
+                                  : inv_pow2(scale[(2 * z) % BATCH]);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           int* a = acc[z][k];
@@ -220,15 +225,17 @@ gemv_q8_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restri
                                    f16_ieee(*reinterpret_cast<const uint16_t*>(st + (row0 + 1) * kPitch + 34 * blk)));
       float2 v[BATCH];
       uint32_t w[BATCH][2];
-      uint32_t out = 0u;
+      uint32_t out = 0u, small = 0u;
 #pragma unroll
       for (int b = 0; b < BATCH; ++b) {
         v[b] = __fmul2_rn(xv[b], d);
         w[b][0] = __float_as_uint(fmaf(v[b].x, scale[b], kMagic));
         w[b][1] = __float_as_uint(fmaf(v[b].y, scale[b], kMagic));
         out |= (w[b][0] ^ 0x4b000000u) | (w[b][1] ^ 0x4b000000u);
+        small |= (fabsf(v[b].x) * scale[b] < 65536.f) ? (1u << b) : 0u;  // a sample, as there
       }
-      if (__any_sync(0xffffffffu, out >= (1u << 23)) || it == 0) {
+      if (__any_sync(0xffffffffu, out >= (1u << 23)) ||
+          __reduce_and_sync(0xffffffffu, small & down_ok) != 0u || it == 0) {
         // rare (and the first stage): see vbq_gemv_mma.cu
         if (it > 0) flush();
 #pragma unroll
@@ -238,10 +245,10 @@ gemv_q8_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restri
           float m = fminf(fmaxf(fabsf(v[b].x), fabsf(v[b].y)), 0x1p99f);
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-          int e = (int)((__float_as_uint(m) >> 23) & 0xffu) - 127 + 2;
+          int e = (int)((__float_as_uint(m) >> 23) & 0xffu) - 127 + 1;
           e = e < kExpMin ? kExpMin : (e > kExpMax ? kExpMax : e);
           scale[b] = pow2f(21 - e);
-          step[b] = pow2f(e - 21);
+          down_ok = (b < batch && e > kExpMin) ? (down_ok | (1u << b)) : (down_ok & ~(1u << b));
           w[b][0] = __float_as_uint(fmaf(v[b].x, scale[b], kMagic));
           w[b][1] = __float_as_uint(fmaf(v[b].y, scale[b], kMagic));
         }
@@ -420,16 +427,16 @@ static cudaError_t launch_q8_t(const float* x, const void* w, float* y, int64_t 
     return cudaErrorInvalidValue;
   auto kern = gemv_q8_kernel<BATCH>;
   constexpr int kBase = Lay<(BATCH <= 2 ? 1 : 2)>::kSmem;
-  static unsigned configured = 0;  // one bit per device ordinal
+  static DeviceOnce configured;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev >= 32 || !(configured & (1u << dev))) {
+  if (!configured.done(dev)) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
-    if (dev < 32) configured |= (1u << dev);
+    configured.mark(dev);
   }
   const int S = choose_splits_q8<BATCH>(K, N, batch, kBase);
   cudaLaunchConfig_t cfg = {};

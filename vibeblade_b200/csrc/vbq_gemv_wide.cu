@@ -181,6 +181,7 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
 #pragma unroll
       for (int h = 0; h < 2; ++h) acc[z][h][0] = acc[z][h][1] = acc[z][h][2] = acc[z][h][3] = 0;
     float scale[QB], mins[QB][2];
+    uint32_t down_ok = 0u;  // bit b: batch row b may be rescaled down (see vbq_gemv_mma.cu)
 #pragma unroll
     for (int j = 0; j < QB; ++j) {
       scale[j] = 1.f;
@@ -251,7 +252,10 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
       const float* xs = reinterpret_cast<const float*>(st + kWBytes);  // [BATCH][32]
       float2 v[QB][2];
       uint32_t w[QB][2][2];
-      uint32_t out = 0u;
+      // small: bit b = batch row b's sample is 16x or more below its scale.  Each lane
+      // half owns one quarter of the rows; the bits of the other half's quarter start at 1,
+      // so the warp-wide AND below is each row's AND over the lanes that own it.
+      uint32_t out = 0u, small = 0u;
 #pragma unroll
       for (int j = 0; j < QB; ++j) {
         const int b = qd * QB + j;
@@ -266,10 +270,15 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
           w[j][h][1] = __float_as_uint(fmaf(v[j][h].y, scale[j], kMagic));
           out |= (w[j][h][0] ^ 0x4b000000u) | (w[j][h][1] ^ 0x4b000000u);
         }
+        // one sampled value per lane (see vbq_gemv_mma.cu): |n| < 2^16
+        small |= (fabsf(v[j][0].x) * scale[j] < 65536.f) ? (1u << b) : 0u;
       }
+      small = (small & down_ok) | (((1u << QB) - 1u) << ((qd ^ 1) * QB));
       // the pair's decisions: either warp's wait gave up -> both leave; either warp's
-      // digits left their range (or the first stage) -> both flush, then rescale
-      const bool need = __any_sync(0xffffffffu, out >= (1u << 23)) || it == 0;
+      // digits left their range, or some batch row of the warp sits 16x or more below its
+      // scale in every lane (or the first stage) -> both flush, then rescale
+      const bool need = __any_sync(0xffffffffu, out >= (1u << 23)) ||
+                        __reduce_and_sync(0xffffffffu, small) != 0u || it == 0;
       if (lane == 0) flags[2 * warp] = (need ? 1u : 0u) | (ok ? 0u : 2u);
       pair_sync();
       const uint32_t fl = flags[2 * warp] | flags[2 * (warp ^ 1)];
@@ -280,7 +289,7 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
       if (fl & 1u) {
         // rare (and the first stage): flag non-finite values, move the sums to fp32 with
         // the old steps (both warps, before either changes them), then scale each batch row
-        // of this warp's half to 4-8x its largest finite |v| over the lane half, encode again
+        // of this warp's half to 2-4x its largest finite |v| over the lane half, encode again
         if (it > 0) flush();
         pair_sync();
 #pragma unroll
@@ -291,9 +300,13 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
                                 fmaxf(fabsf(v[j][1].x), fabsf(v[j][1].y))), 0x1p99f);
 #pragma unroll
           for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-          int e = (int)((__float_as_uint(m) >> 23) & 0xffu) - 127 + 2;
+          int e = (int)((__float_as_uint(m) >> 23) & 0xffu) - 127 + 1;
           e = e < kExpMin ? kExpMin : (e > kExpMax ? kExpMax : e);
           scale[j] = pow2f(21 - e);
+          {
+            const uint32_t bit = 1u << (qd * QB + j);
+            down_ok = (qd * QB + j < batch && e > kExpMin) ? (down_ok | bit) : (down_ok & ~bit);
+          }
           if (rp == 0) stp[qd * QB + j] = pow2f(e - 21);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
@@ -500,16 +513,16 @@ static cudaError_t launch_wide_t(const float* x, const void* w, float* y, int64_
       return cudaErrorInvalidValue;
   }
   auto kern = gemv_wide_kernel<BATCH>;
-  static unsigned configured = 0;  // one bit per device ordinal
+  static DeviceOnce configured;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev >= 32 || !(configured & (1u << dev))) {
+  if (!configured.done(dev)) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
-    if (dev < 32) configured |= (1u << dev);
+    configured.mark(dev);
   }
   const int S = choose_splits_wide<BATCH>(K, N);
   cudaLaunchConfig_t cfg = {};
