@@ -759,14 +759,14 @@ static cudaError_t launch_gemm_t(const void* a, const void* w, void* c, int64_t 
       return cudaErrorInvalidValue;
   }
   auto kern = gemm_kernel<QT, BF16_OUT, GROUPED>;
-  static unsigned configured = 0;
+  static DeviceOnce configured;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev >= 32 || !(configured & (1u << dev))) {
+  if (!configured.done(dev)) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
     if (e != cudaSuccess) return e;
-    if (dev < 32) configured |= (1u << dev);
+    configured.mark(dev);
   }
   // two CTAs (one cluster) per 512 x 256 tile of C; grouped: an upper bound on the
   // segments' tile count (each segment adds at most one partial tile)

@@ -574,17 +574,17 @@ static cudaError_t launch_gemv_t(const float* x, const void* w, float* y, int64_
                                  cudaStream_t st) {
   using C = GemvCfg<QT, B, VPT>;
   auto kern = gemv_kernel<QT, B, VPT>;
-  static unsigned configured = 0;  // one bit per device ordinal
+  static DeviceOnce configured;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev >= 32 || !(configured & (1u << dev))) {
+  if (!configured.done(dev)) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     if (e != cudaSuccess) return e;
     // keep shared memory to what two CTAs need; the rest stays L1 for the weight stream
     e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 25);
     if (e != cudaSuccess) return e;
-    if (dev < 32) configured |= (1u << dev);
+    configured.mark(dev);
   }
   unsigned* counters = static_cast<unsigned*>(scratch);
   float* partials = plan.splits > 1

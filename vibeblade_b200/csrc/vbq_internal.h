@@ -3,7 +3,24 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace vbq {
+
+// One-time per-device set-up of a kernel's launch attributes.  Each launcher keeps one
+// of these (a function-local static): `done(dev)` tells whether device `dev` is set up,
+// `mark(dev)` records it.  The flag word is atomic, so first calls from several host
+// threads never race on it; at worst two of them both run the set-up, which only sets
+// the same attributes twice.  Devices past 63 are set up on every call.
+struct DeviceOnce {
+  std::atomic<uint64_t> bits{0};
+  bool done(int dev) const {
+    return dev < 64 && (bits.load(std::memory_order_acquire) >> dev & 1u);
+  }
+  void mark(int dev) {
+    if (dev < 64) bits.fetch_or(uint64_t(1) << dev, std::memory_order_acq_rel);
+  }
+};
 
 cudaError_t launch_dequant(int qtype, const void* w, void* out, int64_t rows, int64_t n,
                            int64_t row_bytes, int out_dtype, cudaStream_t st);
