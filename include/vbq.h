@@ -125,7 +125,9 @@ int vbq_gemm(const void* a, const void* w, void* c, int64_t M, int64_t K, int64_
  * the library until the process exits); shapes whose scratch would exceed it return
  * VBQ_ERR_WORKSPACE.  The call allocates nothing.  Its first call on a device looks up
  * the array's device address once (cudaGetSymbolAddress, with that device current); make
- * that first call before any stream capture.  Every call on a device shares the array
+ * that first call before any stream capture.  The address belongs to the device's current
+ * context: after cudaDeviceReset (or any new primary context) the next call looks it up
+ * again, so make that call before a capture as well.  Every call on a device shares the array
  * and the array keeps the previous call's contents (the call zeroes the part that must
  * start at zero), so calls that may overlap on the GPU -- different streams, or graphs
  * replayed concurrently -- race and must be serialised by the caller.
@@ -221,6 +223,16 @@ int vbq_swiglu_rows(const void* gu, void* h, int64_t rows, int64_t n, int32_t dt
  * path throws on the host, cpp/src/cuda_kernels.cu:24-40).
  */
 int vbq_device_status(int32_t* status, int32_t clear);
+
+/*
+ * Diagnostic of the failure report above (no counterpart in the reference): launches one
+ * warp that waits on a shared-memory mbarrier with the same bounded wait the GEMV kernels
+ * use.  arrive = 1: the warp completes the barrier's phase itself and the wait succeeds.
+ * arrive = 0: nothing arrives, the wait gives up after budget_cycles SM clock cycles
+ * (1 .. 2^31, about 1 s at most) and records the timeout bit that vbq_device_status then
+ * reports as VBQ_ERR_TIMEOUT.  The kernel always returns; the context stays usable.
+ */
+int vbq_debug_wait_probe(int64_t budget_cycles, int32_t arrive, void* stream);
 
 #ifdef __cplusplus
 }

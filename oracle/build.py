@@ -6,9 +6,10 @@ Two shared libraries come out of this file:
 * ``oracle/_ref/libvbref.so`` -- the reference's own CPU path, compiled straight from
   its sources ``cpp/src/dequant.cpp`` and ``cpp/src/fp16_compat.cpp`` with the
   reference's release flags ``-O3 -DNDEBUG`` (cpp/CMakeLists.txt:177), without the
-  reference's build system.  The sources are read where they lie (``$VB_REF``, default
-  the mounted reference checkout); nothing is copied into this repository.  The GPU
-  box has no reference checkout, so there only the prebuilt ``.so`` is used.
+  reference's build system.  The sources are read where they lie: ``$VB_REF`` when set,
+  else a checkout named ``reference`` beside this repository's directory; nothing is
+  copied into this repository.  Where neither exists (a machine without the reference
+  checkout), only a prebuilt ``.so`` is used.
 
 Run ``python -m oracle.build`` or call :func:`build_all`.
 """
@@ -23,11 +24,17 @@ ORACLE_SRC = HERE / "vbq_oracle.c"
 ORACLE_SO = HERE / "liboracle.so"
 REF_DIR = HERE / "_ref"
 REF_SO = REF_DIR / "libvbref.so"
-DEFAULT_REF = "/root/reference"  # the read-only mount of the build container
+# the same sources with the reference's x86 release flags on an AVX2 host
+# (cpp/CMakeLists.txt:177 and :206-208: -O3 -DNDEBUG -mavx2 -mfma); used for timing only,
+# and only where the host CPU reports avx2 and fma
+REF_AVX2_SO = REF_DIR / "libvbref_avx2.so"
+# a reference checkout beside this repository's directory, unless $VB_REF names one
+DEFAULT_REF = HERE.parent.parent / "reference"
 
 
-def _ref_root() -> Path:
-    return Path(os.environ.get("VB_REF", DEFAULT_REF))
+def ref_root() -> Path:
+    """The reference checkout: ``$VB_REF``, else ``reference`` beside this repository."""
+    return Path(os.environ.get("VB_REF", str(DEFAULT_REF)))
 
 
 def _stale(target: Path, sources: list[Path]) -> bool:
@@ -52,17 +59,31 @@ def build_ref(force: bool = False) -> Path | None:
 
     Returns None when the reference checkout is absent (for example on the GPU box,
     which relies on the library built in the container and shipped with the tree)."""
-    root = _ref_root() / "cpp"
+    root = ref_root() / "cpp"
     srcs = [root / "src" / "dequant.cpp", root / "src" / "fp16_compat.cpp"]
     if not all(s.exists() for s in srcs):
         return REF_SO if REF_SO.exists() else None
     REF_DIR.mkdir(exist_ok=True)
-    if force or _stale(REF_SO, srcs):
-        cmd = ["g++", "-O3", "-DNDEBUG", "-fPIC", "-shared", "-std=c++17",
-               "-I", str(root / "include"), "-I", str(root / "src"),
-               *map(str, srcs), "-o", str(REF_SO)]
-        subprocess.run(cmd, check=True)
+    for target, extra in ((REF_SO, []), (REF_AVX2_SO, ["-mavx2", "-mfma"])):
+        if force or _stale(target, srcs):
+            cmd = ["g++", "-O3", "-DNDEBUG", *extra, "-fPIC", "-shared", "-std=c++17",
+                   "-I", str(root / "include"), "-I", str(root / "src"),
+                   *map(str, srcs), "-o", str(target)]
+            subprocess.run(cmd, check=True)
     return REF_SO
+
+
+def host_has_avx2() -> bool:
+    """Whether this host's CPU reports AVX2 and FMA (Linux /proc/cpuinfo)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("flags"):
+                    flags = set(line.split(":", 1)[1].split())
+                    return "avx2" in flags and "fma" in flags
+    except OSError:
+        pass
+    return False
 
 
 def build_all(force: bool = False) -> None:

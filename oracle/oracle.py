@@ -193,6 +193,16 @@ def load_oracle() -> Oracle:
 
 
 @lru_cache(maxsize=1)
+def load_ref_avx2() -> RefLib | None:
+    """The reference built with its AVX2 release flags (timing only), when the library
+    exists and this host's CPU has AVX2 and FMA; else None."""
+    if load_ref() is None or not _build.host_has_avx2():
+        return None
+    p = _build.REF_AVX2_SO
+    return RefLib(str(p)) if p.exists() else None
+
+
+@lru_cache(maxsize=1)
 def load_ref() -> RefLib | None:
     """The compiled reference, or None when neither its sources nor a prebuilt copy
     exist."""

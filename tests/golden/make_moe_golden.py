@@ -31,11 +31,12 @@ ROOT = HERE.parents[1]
 sys.path.insert(0, str(ROOT))
 sys.dont_write_bytecode = True  # never write into the read-only reference checkout
 
+from oracle.build import ref_root  # noqa: E402
 from oracle.oracle import load_ref  # noqa: E402
 from vibeblade_b200 import formats as F  # noqa: E402
 from vibeblade_b200.quantize import quantize  # noqa: E402
 
-REF = Path(os.environ.get("VB_REF", "/root/reference"))
+REF = ref_root()
 T, H, I, E, TOPK = 48, 256, 512, 4, 2
 QT = F.GGML_TYPE_Q4_K
 

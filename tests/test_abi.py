@@ -111,3 +111,11 @@ def test_python_face_rejects_host_tensors():
         vb.gemv_dequant(x, w, None, 4096, 4096, "Q4_K")
     with pytest.raises(RuntimeError, match="Unsupported dequant type"):
         vb.gemv_dequant(x, w, None, 4096, 4096, 13)
+
+
+def test_wait_probe_argument_errors_need_no_gpu(lib):
+    from vibeblade_b200 import _lib
+    assert lib.vbq_debug_wait_probe(0, 0, None) == _lib.VBQ_ERR_SHAPE
+    assert lib.vbq_debug_wait_probe((1 << 31) + 1, 0, None) == _lib.VBQ_ERR_SHAPE
+    assert lib.vbq_debug_wait_probe(1000, 2, None) == _lib.VBQ_ERR_SHAPE
+    assert b"arrive" in lib.vbq_last_error()

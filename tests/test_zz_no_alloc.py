@@ -28,6 +28,8 @@ SHAPES = [
     (14, 4096, 4096, 2),    # Q6_K
     (8, 8192, 10240, 16),   # Q8_0 70B-shape QKV, batch 16
     (12, 300, 1024, 3),     # ragged K: a single split, no scratch at all
+    (14, 4096, 4096, 24),   # Q6_K batch 24: two launches (16 + 8 rows) over the array
+    (14, 14336, 4096, 5),   # Q6_K down projection, batch 5
 ]
 
 
@@ -92,3 +94,50 @@ def test_static_scratch_rejects_shapes_beyond_its_size(cuda):
     r = subprocess.run([sys.executable, "-c", _REJECT_SCRIPT, root], env=env,
                        capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "rejected" in r.stdout, r.stdout + r.stderr
+
+
+_SCALAR_SCRIPT = r"""
+import ctypes as C, sys, torch
+sys.path.insert(0, sys.argv[1])
+from vibeblade_b200 import _lib
+from vibeblade_b200.quantize import synthetic_weights
+lib = _lib.load()
+dev = torch.device("cuda", 0)
+stream = torch.cuda.current_stream(dev).cuda_stream
+g = torch.Generator(device=dev).manual_seed(13)
+for t, K, N, B in [(12, 4096, 14336, 1), (12, 14336, 4096, 20), (8, 8192, 10240, 4)]:
+    v = C.c_size_t()
+    assert lib.vbq_gemv_scratch_bytes(K, N, t, B, C.byref(v)) == 0
+    assert v.value > 0, (t, K, N, B)  # the scratch-using kernel is the one under test
+    w = synthetic_weights(K, N, t, seed=17, device=dev)
+    scratch = torch.zeros(v.value, dtype=torch.uint8, device=dev)
+    for call in range(2):
+        x = torch.randn(B, K, generator=g, device=dev)
+        y_ref = torch.empty(B, N, device=dev)
+        assert lib.vbq_gemv(x.data_ptr(), w.data_ptr(), y_ref.data_ptr(), K, N, t, B,
+                            scratch.data_ptr(), scratch.numel(), stream) == 0
+        y = torch.full((B, N), float("nan"), device=dev)
+        rc = lib.vbq_gemv_static_scratch(x.data_ptr(), w.data_ptr(), y.data_ptr(), K, N, t, B, stream)
+        assert rc == 0, lib.vbq_last_error()
+        torch.cuda.synchronize()
+        assert torch.isfinite(y).all(), (t, call)
+        err = ((y.double() - y_ref.double()).abs().max() / y_ref.double().abs().max()).item()
+        assert err <= 1e-3, (t, call, err)
+print("scalar ok")
+"""
+
+
+def test_static_scratch_on_the_split_k_kernel_for_all_types(cuda):
+    """Q4_K and Q8_0 normally run on tensor-core kernels that need no scratch; the
+    comparison switch VBQ_GEMV_SCALAR=1 (read once per process, hence the child process)
+    sends them to the split-K kernel, so the array is used for every type, twice per shape
+    (batch 20 also as two launches)."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = str(Path(__file__).resolve().parents[1])
+    env = dict(os.environ, VBQ_GEMV_SCALAR="1")
+    r = subprocess.run([sys.executable, "-c", _SCALAR_SCRIPT, root], env=env,
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "scalar ok" in r.stdout, r.stdout + r.stderr

@@ -5,6 +5,8 @@
 //     and "gemv_dequant: unsupported type <id>" (cpp/src/dequant.cpp:764);
 //   * CUDA failures -> the runtime's error string, like CUDA_CHECK
 //     (cpp/src/cuda_kernels.cu:24-40), but returned as a status instead of thrown.
+#include <cuda.h>
+
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -94,13 +96,16 @@ static int gemv_checks(int32_t type, int64_t K, int64_t N, int32_t batch) {
   return VBQ_OK;
 }
 
-// the largest plan among the launches of a call (a full group of 16 and the remainder)
+// the largest plan among the launches of a call (a full group of 16 and the remainder):
+// the most scratch, and the longest counter prefix any of the launches uses
 static vbq::GemvPlan gemv_call_plan(int64_t K, int64_t N, int32_t batch, int32_t type) {
   vbq::GemvPlan p = vbq::plan_gemv(K, N, batch < kLaunchBatch ? batch : kLaunchBatch, type);
   const int32_t rem = batch % kLaunchBatch;
   if (batch > kLaunchBatch && rem != 0) {
     const vbq::GemvPlan q = vbq::plan_gemv(K, N, rem, type);
+    const int64_t counters = q.counter_bytes > p.counter_bytes ? q.counter_bytes : p.counter_bytes;
     if (q.scratch_bytes > p.scratch_bytes) p = q;
+    p.counter_bytes = counters;
   }
   return p;
 }
@@ -200,6 +205,15 @@ int vbq_device_status(int32_t* status, int32_t clear) {
   return ok();
 }
 
+int vbq_debug_wait_probe(int64_t budget_cycles, int32_t arrive, void* stream) {
+  if (budget_cycles < 1 || budget_cycles > (int64_t)1 << 31)
+    return fail(VBQ_ERR_SHAPE, "vbq_debug_wait_probe: budget_cycles must be in 1..2^31");
+  if (arrive != 0 && arrive != 1) return fail(VBQ_ERR_SHAPE, "vbq_debug_wait_probe: arrive must be 0 or 1");
+  cudaError_t e = vbq::launch_wait_probe((long long)budget_cycles, arrive, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "vbq_debug_wait_probe launch");
+  return ok();
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------------------------
@@ -219,24 +233,56 @@ constexpr size_t kStaticScratchBytes = 8u << 20;  // 8 MiB per device
 static __device__ __align__(256) unsigned char g_gemv_static_scratch[kStaticScratchBytes];
 
 std::mutex g_static_mu;
-void* g_static_ptr[64] = {nullptr};  // device address of the array, per device ordinal
+// device address of the array per device ordinal, and the id of the context it was looked
+// up in (a context created anew, e.g. after cudaDeviceReset, gets a new id and a new
+// lookup: the old address would point into freed memory)
+void* g_static_ptr[64] = {nullptr};
+unsigned long long g_static_ctx[64] = {0};
+
+// id of the context current on this thread (0 when none is current yet).  The two driver
+// calls come through the runtime's driver entry point, so the library needs no libcuda
+// link (it loads on machines without a driver; its calls then fail with a status).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+unsigned long long current_context_id() {
+  static const CtxGetCurrentFn get_current = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    return (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) ? reinterpret_cast<CtxGetCurrentFn>(p) : nullptr;
+  }();
+  static const CtxGetIdFn get_id = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    return (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) ? reinterpret_cast<CtxGetIdFn>(p) : nullptr;
+  }();
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id) return 0;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
 
 // Device address of the array on the current device.  Host code must not pass
 // g_gemv_static_scratch itself to a kernel: on the host it names a stand-in, not device
-// memory.  The address is looked up once per device, with that device current.
+// memory.  The address is looked up once per device and context, with that device current.
 int static_scratch(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "vbq_gemv_static_scratch: cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(VBQ_ERR_UNSUPPORTED, "vbq_gemv_static_scratch: device ordinal >= 64");
   std::lock_guard<std::mutex> lock(g_static_mu);
-  if (!g_static_ptr[dev]) {
+  const unsigned long long ctx = current_context_id();
+  if (!g_static_ptr[dev] || ctx == 0 || ctx != g_static_ctx[dev]) {
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_gemv_static_scratch);
+    e = cudaGetSymbolAddress(&p, g_gemv_static_scratch);  // makes the primary context current
     if (e != cudaSuccess || !p)
       return cuda_fail(e != cudaSuccess ? e : cudaErrorInvalidSymbol,
                        "vbq_gemv_static_scratch: cudaGetSymbolAddress");
     g_static_ptr[dev] = p;
+    g_static_ctx[dev] = current_context_id();
   }
   *out = g_static_ptr[dev];
   return VBQ_OK;

@@ -32,6 +32,8 @@
 #include <cstdlib>
 
 #include "vbq_common.cuh"
+#include <atomic>
+
 #include "vbq_internal.h"
 
 namespace vbq {
@@ -507,37 +509,37 @@ __global__ void __launch_bounds__(256, GemvCfg<QT, B, VPT>::kMinBlocks) gemv_ker
 // ---------------------------------------------------------------------------------
 constexpr int kGemvMinRows = 64, kGemvMaxSplit = 64;
 
+// SM count per device ordinal (atomic cache: first calls may come from several threads)
 int sm_count() {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (cache[dev] == 0) {
-    int n = 0;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
       n = 148;
-    cache[dev] = n;
+    cache[dev].store(n, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return n;
 }
 
 int gemv_split_override() {
-  static int v = -1;
-  if (v < 0) {
-    const char* env = getenv("VBQ_GEMV_SPLIT");  // tuning override, read once
+  // tuning override, read once (thread-safe static initialisation)
+  static const int v = [] {
+    const char* env = getenv("VBQ_GEMV_SPLIT");
     const int e = env ? atoi(env) : 0;
-    v = (e >= 1 && e <= kGemvMaxSplit) ? e : 0;
-  }
+    return (e >= 1 && e <= kGemvMaxSplit) ? e : 0;
+  }();
   return v;
 }
 
 // VBQ_GEMV_SCALAR=1 routes Q4_K and Q8_0 to the scalar kernel (comparison runs).
 static bool scalar_override() {
-  static int v = -1;
-  if (v < 0) {
+  static const bool v = [] {
     const char* env = getenv("VBQ_GEMV_SCALAR");
-    v = (env && atoi(env) == 1) ? 1 : 0;
-  }
-  return v == 1;
+    return env && atoi(env) == 1;
+  }();
+  return v;
 }
 
 GemvPlan plan_gemv(int64_t K, int64_t N, int batch, int qtype) {

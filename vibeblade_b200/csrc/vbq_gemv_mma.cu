@@ -630,6 +630,38 @@ cudaError_t launch_gemv_mma_q4k(const float* x, const void* w, float* y, int64_t
   return cudaSuccess;
 }
 
+// ---------------------------------------------------------------------------------
+// Diagnostic of the bounded-wait path: one warp waits on an mbarrier with the GEMV
+// kernel's own hinted, bounded wait and, when the wait gives up, raises kStatusTimeout in
+// this file's status word, as the kernel's give_up() does.  With arrive = 0 nothing ever
+// arrives, so the wait runs out after `budget` cycles and the kernel returns normally:
+// the timeout report is tested without a fault or a hang.  With arrive = 1 lane 0
+// completes the phase first and the wait succeeds.
+// ---------------------------------------------------------------------------------
+namespace gmma {
+__global__ void __launch_bounds__(32) wait_probe_kernel(long long budget, int arrive) {
+  __shared__ uint64_t bar;
+  const uint32_t b = smem_u32(&bar);
+  if (threadIdx.x == 0) {
+    mbar_init(b, 1);
+    mbar_fence_init();
+  }
+  __syncwarp();
+  if (arrive && threadIdx.x == 0) mbar_arrive(b);
+  __syncwarp();
+  const bool ok = __all_sync(0xffffffffu, mbar_wait_hinted(b, 0u, budget));
+  if (threadIdx.x == 0) {
+    if (!ok) atomicOr(&g_gemv_mma_status, kStatusTimeout);
+    mbar_inval(b);
+  }
+}
+}  // namespace gmma
+
+cudaError_t launch_wait_probe(long long budget_cycles, int arrive, cudaStream_t st) {
+  gmma::wait_probe_kernel<<<1, 32, 0, st>>>(budget_cycles, arrive);
+  return cudaGetLastError();
+}
+
 cudaError_t gemv_mma_status(unsigned* out, bool clear) {
   cudaError_t e = cudaMemcpyFromSymbol(out, g_gemv_mma_status, sizeof(unsigned));
   if (e != cudaSuccess || !clear) return e;

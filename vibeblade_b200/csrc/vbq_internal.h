@@ -92,6 +92,8 @@ cudaError_t launch_moe_combine(const float* y, const int32_t* pos, const float* 
                                int topk, int H, float* out, cudaStream_t st);
 
 cudaError_t gemv_mma_status(unsigned* out, bool clear);
+// One warp waiting on an mbarrier with the GEMV's bounded wait (vbq_debug_wait_probe).
+cudaError_t launch_wait_probe(long long budget_cycles, int arrive, cudaStream_t st);
 
 // Sticky device status bits of the GEMV kernels (kStatusTimeout = 1); synchronous.
 cudaError_t gemv_status(unsigned* out, bool clear);
