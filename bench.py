@@ -42,6 +42,36 @@ def layer_bytes(batch: int) -> int:
     return sum(int(K * N * BPW) + batch * K * 4 + batch * N * 4 for _, K, N in LAYER_8B)
 
 
+def weight_seed(rank: int, copy: int, matrix: int) -> int:
+    """Seed of one synthetic weight matrix; both bench arms use these."""
+    return 1000 * rank + 10 * copy + matrix
+
+
+def make_inputs(dev, batch: int, n_copies: int, rank: int):
+    """The decode workload's inputs: n_copies distinct copies of the layer's five Q4_K
+    matrices (N(0, 0.02) quantized by this library, seeds weight_seed) and x N(0, 1) per
+    input width (torch generator seed 1), all on `dev`.  Both bench arms call this, so the
+    reference arm times the same bytes the GPU arm streams."""
+    import torch
+    from vibeblade_b200.quantize import synthetic_weights
+    layers = [[(K, N, synthetic_weights(K, N, QTYPE, seed=weight_seed(rank, c, i), device=dev))
+               for i, (_, K, N) in enumerate(LAYER_8B)] for c in range(n_copies)]
+    g = torch.Generator(device=dev).manual_seed(1)
+    xs = {K: torch.randn(batch, K, generator=g, device=dev) for _, K, _ in LAYER_8B}
+    return layers, xs
+
+
+def bench_config(batch: int, n_copies: int, world: int) -> dict:
+    """The workload description both arms print (the same dict in both)."""
+    return {"workload": "llama8b_decode_layer_q4k", "batch": batch,
+            "matrices": [f"{n} {k}x{m}" for n, k, m in LAYER_8B],
+            "weights": "N(0,0.02) quantized Q4_K, seed 1000*rank + 10*copy + matrix; x N(0,1) seed 1",
+            "layer_copies_rotated": n_copies,
+            "l2": f"inputs larger than L2: {n_copies} distinct layer copies "
+                  f"({n_copies * layer_bytes(batch) / 1e6:.0f} MB) rotate per step",
+            "parallelism": f"{world} independent GPU(s), own layer copies each (no collective)"}
+
+
 def peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -253,50 +283,101 @@ def bench_tp(dev, rank: int, world: int, steps: int, prefill: bool = True) -> di
             "collective": "torch.distributed all_reduce (NCCL) of the fp32 [M, 8192] partial sums"}
 
 
-def cpu_reference_gbs(batch: int, seconds: float, threads: int, steps: int | None = None,
-                      warmup: int = 0):
-    """Time the reference's gemv_dequant over the decode layer on host cores.
+def _ref_libs():
+    """(timed library, its build flags, plain library) of the compiled reference: the AVX2
+    release build where the host has AVX2 and FMA, else the plain -O3 build; (None, ...)
+    when neither library exists (the C restatement is timed then)."""
+    from oracle import load_ref
+    from oracle.oracle import load_ref_avx2
+    plain = load_ref()
+    fast = load_ref_avx2()
+    if fast is not None:
+        return fast, "-O3 -DNDEBUG -mavx2 -mfma", plain
+    return plain, "-O3 -DNDEBUG", plain
 
-    Returns (gb_per_s, kind, cores, sample_description, per_step_seconds)."""
-    import numpy as np
-    from oracle import load_oracle, load_ref
+
+def cpu_reference_gbs(layers_np, xs_np, batch: int, seconds: float, threads: int,
+                      steps: int | None = None, warmup: int = 0):
+    """Time the reference's gemv_dequant over the decode layer on host cores: passes over
+    the rotated layer copies `layers_np` ([[(K, N, uint8 array)] per copy]) with inputs
+    xs_np ({K: fp32 [batch, K]}), K split across `threads` threads (ctypes releases the
+    GIL; the reference's own gemv_dequant_mt ignores its thread count, so this only lets
+    the baseline use the host's cores).  Returns (gb_per_s, kind, cores, sample,
+    per_step_seconds, flags)."""
     from concurrent.futures import ThreadPoolExecutor
-    from vibeblade_b200.quantize import synthetic_weights
+    from oracle import load_oracle
 
-    ref = load_ref()
+    ref, flags, _ = _ref_libs()
     kind = "reference" if ref is not None else "port"
-    mats = [(K, N, synthetic_weights(K, N, QTYPE, seed=i).numpy()) for i, (_, K, N) in enumerate(LAYER_8B)]
-    rng = np.random.default_rng(1)
-    xs = {K: rng.normal(0, 1, (batch, K)).astype(np.float32) for _, K, _ in LAYER_8B}
     pool = ThreadPoolExecutor(threads)
+    n_copies = len(layers_np)
 
     if ref is not None:
-        def one_layer():
-            for K, N, w in mats:
-                ref.gemv_dequant_sliced(xs[K], w, K, N, QTYPE, threads, pool)
+        def one_layer(step):
+            for K, N, w in layers_np[step % n_copies]:
+                ref.gemv_dequant_sliced(xs_np[K], w, K, N, QTYPE, threads, pool)
     else:
         orc = load_oracle()
         threads = 1
+        flags = "C restatement (oracle/vbq_oracle.c)"
 
-        def one_layer():
-            for K, N, w in mats:
-                orc.gemv_dequant(xs[K], w, K, N, QTYPE)
+        def one_layer(step):
+            for K, N, w in layers_np[step % n_copies]:
+                orc.gemv_dequant(xs_np[K], w, K, N, QTYPE)
 
-    for _ in range(warmup):
-        one_layer()
+    for i in range(warmup):
+        one_layer(i)
     times = []
     t_end = time.perf_counter() + seconds
     while (steps is None and (time.perf_counter() < t_end or not times)) or \
             (steps is not None and len(times) < steps):
         t0 = time.perf_counter()
-        one_layer()
+        one_layer(warmup + len(times))
         times.append(time.perf_counter() - t0)
     pool.shutdown()
     total = sum(times)
     gbs = layer_bytes(batch) * len(times) / total / 1e9
-    sample = (f"{len(times)} passes over the Llama-8B Q4_K decode layer (5 GEMVs, batch {batch}), "
-              f"{total:.1f} s; gemv_dequant split over K across {threads} threads")
-    return gbs, kind, threads, sample, times
+    sample = (f"{len(times)} passes over {n_copies} rotated copies of the Llama-8B Q4_K decode layer "
+              f"(5 GEMVs, batch {batch}), {total:.1f} s; reference gemv_dequant built with {flags}, "
+              f"K split across {threads} threads")
+    return gbs, kind, threads, sample, times, flags
+
+
+def cpu_single_thread(layers_np, xs_np, batch: int, seconds: float) -> dict:
+    """The reference's stock path as it runs in its engine: gemv_dequant_mt, which ignores
+    its thread count (cpp/src/dequant.cpp:783-792), i.e. one core; the plain -O3 build and,
+    where the host supports it, the AVX2 release build."""
+    fast, flags, plain = _ref_libs()
+    out = {"cores": 1}
+    builds = [("O3", plain, "-O3 -DNDEBUG")]
+    if fast is not None and fast is not plain:
+        builds.append(("avx2", fast, flags))
+    for name, lib, fl in builds:
+        if lib is None:
+            continue
+        times = []
+        t_end = time.perf_counter() + seconds
+        while time.perf_counter() < t_end or not times:
+            t0 = time.perf_counter()
+            for K, N, w in layers_np[len(times) % len(layers_np)]:
+                lib.gemv_dequant(xs_np[K], w, K, N, QTYPE)
+            times.append(time.perf_counter() - t0)
+        out[name] = {"value": round(layer_bytes(batch) * len(times) / sum(times) / 1e9, 3),
+                     "unit": "GB/s", "flags": fl, "passes": len(times)}
+    return out
+
+
+def _host_inputs(batch: int, n_copies: int, rank: int):
+    """make_inputs() generated where it is fastest (the GPU when one is visible; the host's
+    torch quantizer takes ~10 s per large matrix) and handed over as numpy arrays."""
+    import torch
+    dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
+    if dev.type == "cpu":
+        n_copies = 1
+    layers, xs = make_inputs(dev, batch, n_copies, rank)
+    layers_np = [[(K, N, w.cpu().numpy()) for K, N, w in layer] for layer in layers]
+    xs_np = {K: x.cpu().numpy() for K, x in xs.items()}
+    return layers_np, xs_np
 
 
 def run_reference(args) -> None:
@@ -304,18 +385,19 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    gbs, kind, cores, sample, times = cpu_reference_gbs(args.batch, 0.0, threads, steps=args.steps,
-                                                        warmup=args.warmup)
+    layers_np, xs_np = _host_inputs(args.batch, args.copies, 0)
+    gbs, kind, cores, sample, times, flags = cpu_reference_gbs(
+        layers_np, xs_np, args.batch, 0.0, threads, steps=args.steps, warmup=args.warmup)
     ms = 1e3 * sum(times) / len(times)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (N(0,0.02) weights, seed 0, quantized Q4_K; x N(0,1) seed 1)",
-        "config": {"workload": "llama8b_decode_layer_q4k", "batch": args.batch,
-                   "matrices": [f"{n} {k}x{m}" for n, k, m in LAYER_8B]},
+        "data": "synthetic (N(0,0.02) weights quantized Q4_K; x N(0,1))",
+        "config": bench_config(args.batch, len(layers_np), args.gpus),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
-                         "sample": sample},
+                         "sample": sample,
+                         "single_thread": cpu_single_thread(layers_np, xs_np, args.batch, 3.0)},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -348,7 +430,6 @@ def run_gpu(args) -> None:
     import torch.distributed as dist
     import vibeblade_b200 as vb
     from vibeblade_b200 import _lib
-    from vibeblade_b200.quantize import synthetic_weights
 
     rank, world, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
@@ -357,15 +438,8 @@ def run_gpu(args) -> None:
     B = args.batch
     n_copies = args.copies
     # weights: n_copies distinct layers (distinct seeds per rank and copy)
-    layers = []
-    for c in range(n_copies):
-        mats = []
-        for i, (name, K, N) in enumerate(LAYER_8B):
-            seed = 1000 * rank + 10 * c + i
-            mats.append((K, N, synthetic_weights(K, N, QTYPE, seed=seed, device=dev)))
-        layers.append(mats)
-    g = torch.Generator(device=dev).manual_seed(1)
-    xs = {K: torch.randn(B, K, generator=g, device=dev) for _, K, _ in LAYER_8B}
+    layers, xs = make_inputs(dev, B, n_copies, rank)
+    g = torch.Generator(device=dev).manual_seed(101)  # other batch sizes' activations
     ys = [torch.empty(B, N, device=dev) for _, _, N in LAYER_8B]
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
@@ -591,16 +665,11 @@ def run_gpu(args) -> None:
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms_total / args.steps, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (N(0,0.02) weights, seed 0+, quantized Q4_K; x N(0,1) seed 1)",
-            "config": {"workload": "llama8b_decode_layer_q4k", "batch": B,
-                       "matrices": [f"{n} {k}x{m}" for n, k, m in LAYER_8B],
-                       "layer_copies_rotated": n_copies,
-                       "launch": (f"CUDA graph of {n_copies} steps ({5 * n_copies} GEMV kernels chained by "
-                                  "programmatic dependent launch), replayed; remainder eager"
-                                  if graph is not None else "eager, one C-ABI call per GEMV"),
-                       "l2": f"inputs larger than L2: {n_copies} distinct layer copies "
-                             f"({n_copies * layer_bytes(B) / 1e6:.0f} MB) rotate per step",
-                       "parallelism": f"{world} independent GPUs, own layers each (no collective)"},
+            "data": "synthetic (N(0,0.02) weights quantized Q4_K; x N(0,1))",
+            "config": bench_config(B, n_copies, world),
+            "launch": (f"CUDA graph of {n_copies} steps ({5 * n_copies} GEMV kernels chained by "
+                       "programmatic dependent launch), replayed; remainder eager"
+                       if graph is not None else "eager, one C-ABI call per GEMV"),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
                          "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
                          "traffic": traffic, "traffic_launch": "gate/up 4096x14336 (ncu)",
@@ -626,9 +695,14 @@ def run_gpu(args) -> None:
         dist.destroy_process_group()
     if rank == 0:
         if not args.no_cpu_baseline:
-            gbs, kind, cores, sample, _ = cpu_reference_gbs(B, args.cpu_seconds, os.cpu_count() or 1)
+            # the same bytes the GPU streamed (rank 0's copies), rotated the same way
+            layers_np = [[(K, N, w.cpu().numpy()) for K, N, w in layer] for layer in layers]
+            xs_np = {K: x.cpu().numpy() for K, x in xs.items()}
+            gbs, kind, cores, sample, _, _ = cpu_reference_gbs(layers_np, xs_np, B, args.cpu_seconds,
+                                                               os.cpu_count() or 1)
             line["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores,
-                                    "kind": kind, "sample": sample}
+                                    "kind": kind, "sample": sample,
+                                    "single_thread": cpu_single_thread(layers_np, xs_np, B, 3.0)}
         print(json.dumps(line), flush=True)
 
 
