@@ -31,10 +31,15 @@
 extern "C" {
 #endif
 
-/* ggml type ids (cpp/include/ggml_types.h:17,21,23) */
+/* ggml type ids (cpp/include/ggml_types.h:12-13,17,21,23,26).  The quantized types are
+ * the path's; the unquantized ones are read by vbq_dequantize and vbq_gemv (GGUF files keep
+ * small tensors such as the MoE router, ffn_gate_inp, unquantized). */
+#define VBQ_TYPE_F32 0
+#define VBQ_TYPE_F16 1
 #define VBQ_TYPE_Q8_0 8
 #define VBQ_TYPE_Q4_K 12
 #define VBQ_TYPE_Q6_K 14
+#define VBQ_TYPE_BF16 30
 
 /* element types of outputs / activations */
 #define VBQ_DTYPE_F32 0
@@ -85,11 +90,15 @@ int vbq_gemv_scratch_bytes(int64_t K, int64_t N, int32_t type, int32_t batch, si
  *                    ggml_type, float* scratch)` (cpp/include/dequant.h:27-35) and of
  * `cuda::gemv_dequant(d_x, d_weights, d_y, K, M, ggml_type, d_scratch, stream)`
  * (cpp/include/cuda_kernels.h:191-199):
- *     y[b, n] = sum_k x[b, k] * deq(W)[k, n],  b < batch (1..32; above 16 the call runs
- *     consecutive launches over groups of up to 16 batch rows).
+ *     y[b, n] = sum_k x[b, k] * deq(W)[k, n],  b < batch (1..32 on the tiled kernels, above
+ *     16 as consecutive launches over groups of up to 16 batch rows; any batch up to
+ *     262140 on the generic kernel below, e.g. a prefill's tokens through the MoE router).
  * x is fp32 [batch, K], y fp32 [batch, N], both row-major.  N must be a multiple of
- * the block size (256 for Q4_K/Q6_K, 32 for Q8_0; this build needs 256 for all);
- * W and y must be 16-byte aligned, x 4-byte aligned.
+ * the block size (256 for Q4_K/Q6_K, 32 for Q8_0, 1 for F32/F16/BF16); widths that are
+ * whole 256-column tiles of a quantized type run on the tiled kernels, the rest (the MoE
+ * router's N = n_experts, unquantized weights) on a generic kernel without scratch.
+ * W and y must be 16-byte aligned, x 4-byte aligned.  F16 weights are read through the
+ * reference's f16_to_f32 (fp16 subnormals doubled), BF16 as the top half of an fp32.
  * scratch: caller-owned device memory of at least vbq_gemv_scratch_bytes(); it must be
  * zero-filled before its first use, every call leaves it zero-filled again, and two
  * calls that may run at the same time must not share it.  NULL is allowed when the

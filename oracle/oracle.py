@@ -19,8 +19,8 @@ _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _f64p = np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")
 _u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
 
-BLOCK_VALUES = {8: 32, 12: 256, 14: 256}
-BLOCK_BYTES = {8: 34, 12: 144, 14: 210}
+BLOCK_VALUES = {0: 1, 1: 1, 30: 1, 8: 32, 12: 256, 14: 256}
+BLOCK_BYTES = {0: 4, 1: 2, 30: 2, 8: 34, 12: 144, 14: 210}
 
 
 def row_bytes(qtype: int, n: int) -> int:

@@ -19,11 +19,12 @@
 #include <math.h>
 
 /* ggml type ids: cpp/include/ggml_types.h:11-27 */
-enum { VBO_Q8_0 = 8, VBO_Q4_K = 12, VBO_Q6_K = 14 };
+enum { VBO_F32 = 0, VBO_F16 = 1, VBO_Q8_0 = 8, VBO_Q4_K = 12, VBO_Q6_K = 14, VBO_BF16 = 30 };
 
 /* Block geometry: cpp/include/ggml_types.h:31-71 (block sizes 32/256, byte sizes 34/144/210). */
 int64_t vbo_block_values(int32_t type) {
     switch (type) {
+        case VBO_F32: case VBO_F16: case VBO_BF16: return 1;
         case VBO_Q8_0: return 32;
         case VBO_Q4_K: return 256;
         case VBO_Q6_K: return 256;
@@ -33,6 +34,8 @@ int64_t vbo_block_values(int32_t type) {
 
 int64_t vbo_block_bytes(int32_t type) {
     switch (type) {
+        case VBO_F32: return 4;
+        case VBO_F16: case VBO_BF16: return 2;
         case VBO_Q8_0: return 34;
         case VBO_Q4_K: return 144;
         case VBO_Q6_K: return 210;
@@ -201,10 +204,27 @@ void vbo_dequantize_row_q8_0_f32scale(const uint8_t* row, float* out, int64_t n)
     }
 }
 
+/* Unquantized rows (cpp/src/dequant.cpp:407-411): F32 copied, F16 through the
+ * reference's own conversion (so subnormals double, fp16_compat.cpp:13-35), BF16 as the
+ * top half of an fp32 (bf16_to_f32, cpp/include/ggml_types.h:175-180). */
+static void vbo_row_f32(const uint8_t* row, float* out, int64_t n) { memcpy(out, row, (size_t)n * 4); }
+static void vbo_row_f16(const uint8_t* row, float* out, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) out[i] = vbo_f16_to_f32(rd16(row + 2 * i));
+}
+static void vbo_row_bf16(const uint8_t* row, float* out, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) {
+        const uint32_t bits = (uint32_t)rd16(row + 2 * i) << 16;
+        memcpy(out + i, &bits, 4);
+    }
+}
+
 /* Dispatcher (cpp/src/dequant.cpp:407-425).  Returns 0, or -1 for an unsupported type
  * where the reference throws "Unsupported dequant type". */
 int vbo_dequantize_row(const void* row, float* out, int64_t n, int32_t type) {
     switch (type) {
+        case VBO_F32: vbo_row_f32((const uint8_t*)row, out, n); return 0;
+        case VBO_F16: vbo_row_f16((const uint8_t*)row, out, n); return 0;
+        case VBO_BF16: vbo_row_bf16((const uint8_t*)row, out, n); return 0;
         case VBO_Q4_K: vbo_dequantize_row_q4_K((const uint8_t*)row, out, n); return 0;
         case VBO_Q6_K: vbo_dequantize_row_q6_K((const uint8_t*)row, out, n); return 0;
         case VBO_Q8_0: vbo_dequantize_row_q8_0((const uint8_t*)row, out, n); return 0;

@@ -95,3 +95,28 @@ def test_dequant_empty_is_noop(cuda):
     w = torch.zeros(144, dtype=torch.uint8, device=cuda)
     out = vb.dequantize(w, 0, 256, F.GGML_TYPE_Q4_K)
     assert out.shape == (0, 256)
+
+
+@pytest.mark.parametrize("qtype", [F.GGML_TYPE_F32, F.GGML_TYPE_F16, F.GGML_TYPE_BF16])
+@pytest.mark.parametrize("K,N", [(1, 65536), (3, 1000), (17, 8)])
+def test_dequant_unquantized_rows_bitexact(cuda, oracle, qtype, K, N):
+    """F32 / F16 / BF16 weights: every 16-bit pattern (F16 subnormals doubled as the
+    reference's f16_to_f32 does), widths that end inside a lane's 8 values, and a single
+    ragged row; bit-exact against the oracle (pinned to the compiled reference)."""
+    rng = np.random.default_rng(K * 7 + N + qtype)
+    eb = F.BLOCK_BYTES[qtype]
+    if qtype == F.GGML_TYPE_F32:
+        w = rng.normal(0, 1, K * N).astype(np.float32).view(np.uint8)
+    else:
+        w = rng.integers(0, 65536, K * N, dtype=np.uint16)
+        w[:min(w.size, 65536)] = np.arange(min(w.size, 65536), dtype=np.uint16)
+        w = w.view(np.uint8)
+    want = oracle.dequantize(w, K, N, qtype)
+    got = vb.dequantize(torch.from_numpy(w).to(cuda), K, N, qtype).cpu().numpy()
+    assert bits_equal(got, want)
+    gb = vb.dequantize(torch.from_numpy(w).to(cuda), K, N, qtype, dtype=torch.bfloat16).float().cpu().numpy()
+    assert bits_equal(gb, bf16_rne(want))
+    # one ragged row
+    n1 = N - 3 if N > 3 else N
+    row = vb.dequantize_row(torch.from_numpy(w[:N * eb].copy()).to(cuda), None, n1, qtype).cpu().numpy()
+    assert bits_equal(row, want[0, :n1])

@@ -273,3 +273,54 @@ def test_gemv_outlier_activations(cuda, oracle, qtype, K, N, batch, frac):
     _check_columns(y, ref64, "fp64")
     ref = oracle.gemv_dequant(x, w.cpu().numpy(), K, N, qtype)
     _check_columns(y, ref, "oracle")
+
+
+# The generic kernel: the MoE router (hidden 4096 -> 8 experts) as GGUF files store it
+# (F32 / F16 / BF16), Q8_0 widths that are multiples of 32 but not of 256, and unquantized
+# weights of odd widths.
+GENERIC = [(F.GGML_TYPE_F32, 4096, 8), (F.GGML_TYPE_F16, 4096, 8), (F.GGML_TYPE_BF16, 4096, 8),
+           (F.GGML_TYPE_F32, 6144, 64), (F.GGML_TYPE_F16, 300, 1001), (F.GGML_TYPE_BF16, 2048, 4104),
+           (F.GGML_TYPE_Q8_0, 4096, 32), (F.GGML_TYPE_Q8_0, 4096, 1184), (F.GGML_TYPE_Q8_0, 1000, 8288)]
+
+
+def _weights_of(rng, qtype, K, N):
+    vals = rng.normal(0, 0.05, (K, N)).astype(np.float32)
+    if qtype == F.GGML_TYPE_F32:
+        return vals.view(np.uint8).reshape(K, -1)
+    if qtype == F.GGML_TYPE_F16:
+        return vals.astype(np.float16).view(np.uint8).reshape(K, -1)
+    if qtype == F.GGML_TYPE_BF16:
+        return (vals.view(np.uint32) >> 16).astype(np.uint16).view(np.uint8).reshape(K, -1)
+    return quantize(vals, qtype).numpy()
+
+
+@pytest.mark.parametrize("qtype,K,N", GENERIC)
+@pytest.mark.parametrize("batch", [1, 3, 4, 16, 32, 37])
+def test_gemv_generic_kernel_vs_oracle(cuda, oracle, qtype, K, N, batch):
+    rng = np.random.default_rng(K + N + batch + qtype)
+    w = _weights_of(rng, qtype, K, N)
+    x = rng.normal(0, 1, (batch, K)).astype(np.float32)
+    assert vb.gemv_scratch_bytes(K, N, qtype, batch) == 0  # no scratch on this path
+    wd = torch.from_numpy(np.ascontiguousarray(w)).to(cuda)
+    y = vb.gemv_dequant(torch.from_numpy(x).to(cuda), wd, None, K, N, qtype).cpu().numpy()
+    ref = oracle.gemv_dequant(x, w, K, N, qtype)
+    _check_columns(y, ref, "oracle")
+    y2 = vb.gemv_dequant(torch.from_numpy(x).to(cuda), wd, None, K, N, qtype).cpu().numpy()
+    assert np.array_equal(y, y2)  # deterministic (split order fixed)
+
+
+def test_gemv_router_feeds_moe_routing(cuda, oracle):
+    """The reference's MoE router step (cpp/src/fast_model.cpp:861-872) for a prefill's
+    tokens in one call: the F32 router GEMV over hidden 4096 -> 8 experts, then softmax and
+    top-2; the device routing of the device logits picks the oracle's experts."""
+    T, H, E = 300, 4096, 8
+    rng = np.random.default_rng(3)
+    w = _weights_of(rng, F.GGML_TYPE_F32, H, E)
+    x = rng.normal(0, 1, (T, H)).astype(np.float32)
+    lg = vb.gemv_dequant(torch.from_numpy(x).to(cuda), torch.from_numpy(w).to(cuda), None, H, E,
+                         F.GGML_TYPE_F32)
+    ref = oracle.gemv_dequant(x, w, H, E, F.GGML_TYPE_F32)
+    _check_columns(lg.cpu().numpy(), ref, "router")
+    idx, _ = vb.moe_route(lg, 2)
+    idx_ref, _ = vb.moe_route(torch.from_numpy(ref).to(cuda), 2)
+    assert torch.equal(idx.sort(dim=1).values, idx_ref.sort(dim=1).values)

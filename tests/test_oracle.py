@@ -102,3 +102,24 @@ def test_oracle_vs_compiled_reference_random(oracle, reflib, qtype, std):
         assert bits_equal(oracle.dequantize(wm, K, N, qtype), ref)
         x = rng.normal(0, 1, (2, K)).astype(np.float32)
         assert bits_equal(oracle.gemv_dequant(x, wm, K, N, qtype), reflib.gemv_dequant(x, wm, K, N, qtype))
+
+
+@pytest.mark.parametrize("qtype", [F.GGML_TYPE_F32, F.GGML_TYPE_F16, F.GGML_TYPE_BF16])
+def test_oracle_unquantized_rows_vs_compiled_reference(oracle, reflib, qtype):
+    """F32 / F16 / BF16 rows (the reference's dequantize_row, cpp/src/dequant.cpp:407-411):
+    every 16-bit pattern once (F16 subnormals double, NaN and inf pass through), and a GEMV
+    over random weights, bit for bit against the compiled reference."""
+    rng = np.random.default_rng(qtype + 5)
+    if qtype == F.GGML_TYPE_F32:
+        row = rng.normal(0, 1, 4096).astype(np.float32).view(np.uint8)
+        n = 4096
+    else:
+        row = np.arange(65536, dtype=np.uint16).view(np.uint8)
+        n = 65536
+    assert bits_equal(oracle.dequantize_row(row, n, qtype), reflib.dequantize_row(row, n, qtype))
+    K, N = 64, 40  # a width that is no multiple of any block but the unquantized one
+    vals = rng.normal(0, 0.05, (K, N)).astype(np.float32)
+    w = {F.GGML_TYPE_F32: vals, F.GGML_TYPE_F16: vals.astype(np.float16),
+         F.GGML_TYPE_BF16: (vals.view(np.uint32) >> 16).astype(np.uint16)}[qtype]
+    x = rng.normal(0, 1, (3, K)).astype(np.float32)
+    assert bits_equal(oracle.gemv_dequant(x, w, K, N, qtype), reflib.gemv_dequant(x, w, K, N, qtype))

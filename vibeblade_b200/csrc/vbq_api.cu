@@ -29,12 +29,27 @@ int ok() {
   return VBQ_OK;
 }
 
-bool supported(int32_t t) { return t == VBQ_TYPE_Q4_K || t == VBQ_TYPE_Q6_K || t == VBQ_TYPE_Q8_0; }
-
-int64_t block_values(int32_t t) { return t == VBQ_TYPE_Q8_0 ? 32 : 256; }
-int64_t block_bytes(int32_t t) {
-  return t == VBQ_TYPE_Q8_0 ? 34 : (t == VBQ_TYPE_Q4_K ? 144 : 210);
+// the quantized weight types (tiled GEMV kernels, tensor-core GEMM, MoE)
+bool quantized(int32_t t) { return t == VBQ_TYPE_Q4_K || t == VBQ_TYPE_Q6_K || t == VBQ_TYPE_Q8_0; }
+// every weight type the library reads (dequantize, GEMV): plus F32 / F16 / BF16
+bool supported(int32_t t) {
+  return quantized(t) || t == VBQ_TYPE_F32 || t == VBQ_TYPE_F16 || t == VBQ_TYPE_BF16;
 }
+
+int64_t block_values(int32_t t) { return t == VBQ_TYPE_Q8_0 ? 32 : (quantized(t) ? 256 : 1); }
+int64_t block_bytes(int32_t t) {
+  switch (t) {
+    case VBQ_TYPE_Q8_0: return 34;
+    case VBQ_TYPE_Q4_K: return 144;
+    case VBQ_TYPE_Q6_K: return 210;
+    case VBQ_TYPE_F32: return 4;
+    default: return 2;  // F16, BF16
+  }
+}
+
+// The generic GEMV kernel takes unquantized weights and widths that are not whole
+// 256-column tiles; the tiled kernels the rest.
+bool gemv_generic(int32_t t, int64_t N) { return !quantized(t) || N % 256 != 0; }
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
@@ -84,11 +99,16 @@ int vbq_dequantize(const void* w, void* out, int64_t rows, int64_t n, int32_t ty
 // order on the stream, sharing the scratch (each launch leaves it zero-filled).
 constexpr int32_t kMaxBatch = 32, kLaunchBatch = 16;
 
+// batch limit of the generic kernel (groups of 4 rows on a grid dimension of 65535)
+constexpr int32_t kMaxBatchGeneric = 4 * 65535;
+
 static int gemv_checks(int32_t type, int64_t K, int64_t N, int32_t batch) {
   if (!supported(type)) return fail(VBQ_ERR_TYPE, "gemv_dequant: unsupported type " + std::to_string(type));
   if (K < 0 || N < 0) return fail(VBQ_ERR_SHAPE, "vbq_gemv: negative size");
-  if (batch < 1 || batch > kMaxBatch)
-    return fail(VBQ_ERR_SHAPE, "vbq_gemv: batch must be in 1..32, got " + std::to_string(batch));
+  const int32_t max_batch = gemv_generic(type, N) ? kMaxBatchGeneric : kMaxBatch;
+  if (batch < 1 || batch > max_batch)
+    return fail(VBQ_ERR_SHAPE, "vbq_gemv: batch must be in 1.." + std::to_string(max_batch) + ", got " +
+                                   std::to_string(batch));
   const int64_t bv = block_values(type);
   if (N % bv != 0)
     return fail(VBQ_ERR_SHAPE, "vbq_gemv: N = " + std::to_string(N) +
@@ -126,7 +146,7 @@ static cudaError_t launch_gemv_groups(int32_t type, const float* x, const void* 
 int vbq_gemv_scratch_bytes(int64_t K, int64_t N, int32_t type, int32_t batch, size_t* bytes) {
   if (int rc = gemv_checks(type, K, N, batch)) return rc;
   if (!bytes) return fail(VBQ_ERR_NULL, "vbq_gemv_scratch_bytes: bytes is NULL");
-  *bytes = (K == 0 || N == 0 || N % 256 != 0) ? 0 : gemv_call_plan(K, N, batch, type).scratch_bytes;
+  *bytes = (K == 0 || N == 0 || gemv_generic(type, N)) ? 0 : gemv_call_plan(K, N, batch, type).scratch_bytes;
   return ok();
 }
 
@@ -144,9 +164,15 @@ int vbq_gemv(const float* x, const void* w, float* y, int64_t K, int64_t N, int3
   if (!x || !w || !y) return fail(VBQ_ERR_NULL, "vbq_gemv: NULL pointer");
   if (!aligned(x, 4) || !aligned(y, 16) || !aligned(w, 16))
     return fail(VBQ_ERR_ALIGN, "vbq_gemv: w and y must be 16-byte aligned, x 4-byte aligned");
-  if (N % 256 != 0)
-    return fail(VBQ_ERR_UNSUPPORTED,
-                "vbq_gemv: N must be a multiple of 256 (Q8_0 rows of a partial 256-value tile are not implemented)");
+  if (K > (int64_t)INT32_MAX || N > (int64_t)INT32_MAX)
+    return fail(VBQ_ERR_SHAPE, "vbq_gemv: sizes above 2^31 are not supported");
+  if (gemv_generic(type, N)) {
+    const int64_t rbg = (N / block_values(type)) * block_bytes(type);
+    cudaError_t e = vbq::launch_gemv_any(type, x, w, y, nullptr, nullptr, K, N, rbg, batch,
+                                         static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "vbq_gemv launch");
+    return ok();
+  }
   const vbq::GemvPlan plan = gemv_call_plan(K, N, batch, type);
   if (plan.scratch_bytes > 0) {
     if (!scratch || scratch_bytes < plan.scratch_bytes)
@@ -163,7 +189,7 @@ int vbq_gemv(const float* x, const void* w, float* y, int64_t K, int64_t N, int3
 
 int vbq_gemm(const void* a, const void* w, void* c, int64_t M, int64_t K, int64_t N, int32_t type,
              int32_t c_dtype, void* stream) {
-  if (!supported(type)) return fail(VBQ_ERR_TYPE, "gemm_dequant: unsupported type " + std::to_string(type));
+  if (!quantized(type)) return fail(VBQ_ERR_TYPE, "gemm_dequant: unsupported type " + std::to_string(type));
   if (c_dtype != VBQ_DTYPE_F32 && c_dtype != VBQ_DTYPE_BF16)
     return fail(VBQ_ERR_SHAPE, "vbq_gemm: c_dtype must be VBQ_DTYPE_F32 or VBQ_DTYPE_BF16");
   if (M < 0 || K < 0 || N < 0) return fail(VBQ_ERR_SHAPE, "vbq_gemm: negative size");
@@ -304,8 +330,14 @@ extern "C" int vbq_gemv_static_scratch(const float* x, const void* w, float* y, 
   if (!x || !w || !y) return fail(VBQ_ERR_NULL, "vbq_gemv_static_scratch: NULL pointer");
   if (!aligned(x, 4) || !aligned(y, 16) || !aligned(w, 16))
     return fail(VBQ_ERR_ALIGN, "vbq_gemv_static_scratch: w and y must be 16-byte aligned, x 4-byte aligned");
-  if (N % 256 != 0)
-    return fail(VBQ_ERR_UNSUPPORTED, "vbq_gemv_static_scratch: N must be a multiple of 256");
+  if (K > (int64_t)INT32_MAX || N > (int64_t)INT32_MAX)
+    return fail(VBQ_ERR_SHAPE, "vbq_gemv_static_scratch: sizes above 2^31 are not supported");
+  if (gemv_generic(type, N)) {  // the generic kernel needs no scratch
+    const int64_t rbg = (N / block_values(type)) * block_bytes(type);
+    cudaError_t e = vbq::launch_gemv_any(type, x, w, y, nullptr, nullptr, K, N, rbg, batch, st);
+    if (e != cudaSuccess) return cuda_fail(e, "vbq_gemv_static_scratch launch");
+    return ok();
+  }
   const vbq::GemvPlan plan = gemv_call_plan(K, N, batch, type);
   if (plan.scratch_bytes > kStaticScratchBytes)
     return fail(VBQ_ERR_WORKSPACE,
@@ -334,7 +366,7 @@ namespace {
 // Shape rules of the tcgen05 GEMM for one K x N weight slab; *rb gets the row bytes.
 int gemm_shape_checks(const char* who, int32_t type, int64_t K, int64_t N, int64_t* rb) {
   const std::string w(who);
-  if (!supported(type)) return fail(VBQ_ERR_TYPE, w + ": unsupported type " + std::to_string(type));
+  if (!quantized(type)) return fail(VBQ_ERR_TYPE, w + ": unsupported type " + std::to_string(type));
   if (K <= 0 || N <= 0) return fail(VBQ_ERR_SHAPE, w + ": K and N must be positive");
   if (N % 256 != 0) return fail(VBQ_ERR_SHAPE, w + ": N must be a multiple of 256");
   if (K % 8 != 0) return fail(VBQ_ERR_SHAPE, w + ": K must be a multiple of 8 (16-byte rows of A)");

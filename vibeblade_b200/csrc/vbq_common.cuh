@@ -12,14 +12,21 @@
 
 namespace vbq {
 
+constexpr int kF32 = 0;
+constexpr int kF16 = 1;
 constexpr int kQ8_0 = 8;
 constexpr int kQ4_K = 12;
 constexpr int kQ6_K = 14;
+constexpr int kBF16 = 30;
 
 template <int QT> struct Fmt;
 template <> struct Fmt<kQ4_K> { static constexpr int kValues = 256, kBytes = 144; };
 template <> struct Fmt<kQ6_K> { static constexpr int kValues = 256, kBytes = 210; };
 template <> struct Fmt<kQ8_0> { static constexpr int kValues = 32, kBytes = 34; };
+// unquantized weights (small GGUF tensors such as the MoE router): one value per "block"
+template <> struct Fmt<kF32> { static constexpr int kValues = 1, kBytes = 4; };
+template <> struct Fmt<kF16> { static constexpr int kValues = 1, kBytes = 2; };
+template <> struct Fmt<kBF16> { static constexpr int kValues = 1, kBytes = 2; };
 
 // Bytes holding one 256-value column tile of a row: one Q4_K / Q6_K block, or eight
 // Q8_0 blocks.

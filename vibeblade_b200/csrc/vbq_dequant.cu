@@ -10,71 +10,10 @@
 // one warp per unit, 8 values per lane, so each warp writes 1 KB (fp32) or 512 B (bf16)
 // of contiguous output.  The kernel is HBM-bound on its writes.
 #include "vbq_common.cuh"
+#include "vbq_decode.cuh"
 #include "vbq_internal.h"
 
 namespace vbq {
-
-template <int QT>
-__device__ __forceinline__ void decode8(const uint8_t* __restrict__ tile, int lane, float v[8]);
-
-// Q4_K: lane covers values 8*lane..8*lane+7 -> sub-block s = lane/4, nibble half s&1,
-// qs bytes 32*(s/2) + 8*(lane%4) .. +7.
-template <>
-__device__ __forceinline__ void decode8<kQ4_K>(const uint8_t* __restrict__ blk, int lane,
-                                               float v[8]) {
-  const float d = f16_ref(ld_u16(blk));
-  const float dmin = f16_ref(ld_u16(blk + 2));
-  const uint32_t s0 = ld_u32_a2(blk + 4), s1 = ld_u32_a2(blk + 8), s2 = ld_u32_a2(blk + 12);
-  const int s = lane >> 2;
-  int sc, mn;
-  q4k_scale_min(s, s0, s1, s2, sc, mn);
-  const float dl = __fmul_rn(d, (float)sc);
-  const float ml = __fmul_rn(dmin, (float)mn);
-  const uint8_t* q = blk + 16 + 32 * (s >> 1) + 8 * (lane & 3);
-  const uint32_t w0 = ld_u32_a2(q), w1 = ld_u32_a2(q + 4);
-  const int hs = (s & 1) * 4;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const uint32_t w = i < 4 ? w0 : w1;
-    const uint32_t nib = (w >> (8 * (i & 3) + hs)) & 0xfu;
-    v[i] = __fsub_rn(__fmul_rn(dl, (float)nib), ml);
-  }
-}
-
-// Q6_K (reference layout): value i -> ql nibble i&1 of byte i>>1, qh field i&3 of byte
-// i>>2, int8 scale i>>4, out = (d*scale)*(q-32).  Lane: ql bytes 4*lane..+3, qh bytes
-// 2*lane..+1, scale 192 + lane/2.
-template <>
-__device__ __forceinline__ void decode8<kQ6_K>(const uint8_t* __restrict__ blk, int lane,
-                                               float v[8]) {
-  const float d = f16_ref(ld_u16(blk + 208));
-  const int sc = (int)(int8_t)blk[192 + (lane >> 1)];
-  const float ds = __fmul_rn(d, (float)sc);
-  const uint32_t ql = ld_u32_a2(blk + 4 * lane);
-  const uint32_t qh = ld_u16(blk + 128 + 2 * lane);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int lo = (int)((ql >> (4 * i)) & 0xfu);
-    const int hi = (int)((qh >> (2 * i)) & 0x3u);
-    v[i] = __fmul_rn(ds, (float)((lo | (hi << 4)) - 32));
-  }
-}
-
-// Q8_0 (GGUF block, fp16 d): the 256-value unit spans blocks lane/4, values 8*(lane%4)..
-template <>
-__device__ __forceinline__ void decode8<kQ8_0>(const uint8_t* __restrict__ unit, int lane,
-                                               float v[8]) {
-  const uint8_t* blk = unit + 34 * (lane >> 2);
-  const float d = f16_ieee(ld_u16(blk));
-  const uint8_t* q = blk + 2 + 8 * (lane & 3);
-  const uint32_t w0 = ld_u32_a2(q), w1 = ld_u32_a2(q + 4);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const uint32_t w = i < 4 ? w0 : w1;
-    const int qv = (int)(int8_t)(uint8_t)(w >> (8 * (i & 3)));
-    v[i] = __fmul_rn((float)qv, d);
-  }
-}
 
 template <int QT, typename OutT>
 __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict__ w,
@@ -94,7 +33,12 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict_
     if (v0 >= n) continue;                  // ragged tail of a single row
     const uint8_t* unit = w + r * row_bytes + j * kUnitBytes;
     float v[8];
-    decode8<QT>(unit, lane, v);
+    if constexpr (Fmt<QT>::kValues == 1) {
+      if (v0 + 8 > n) decode_tail<QT>(unit, lane, (int)(n - v0), v);
+      else decode8<QT>(unit, lane, v);
+    } else {
+      decode8<QT>(unit, lane, v);
+    }
     OutT* o = out + r * n + v0;
     if (vec_ok && v0 + 8 <= n) {
       if constexpr (sizeof(OutT) == 4) {
@@ -146,6 +90,15 @@ cudaError_t launch_dequant(int qtype, const void* w, void* out, int64_t rows, in
     case kQ8_0:
       return bf ? launch_dequant_t<kQ8_0, __nv_bfloat16>(w, out, rows, n, row_bytes, st)
                 : launch_dequant_t<kQ8_0, float>(w, out, rows, n, row_bytes, st);
+    case kF32:
+      return bf ? launch_dequant_t<kF32, __nv_bfloat16>(w, out, rows, n, row_bytes, st)
+                : launch_dequant_t<kF32, float>(w, out, rows, n, row_bytes, st);
+    case kF16:
+      return bf ? launch_dequant_t<kF16, __nv_bfloat16>(w, out, rows, n, row_bytes, st)
+                : launch_dequant_t<kF16, float>(w, out, rows, n, row_bytes, st);
+    case kBF16:
+      return bf ? launch_dequant_t<kBF16, __nv_bfloat16>(w, out, rows, n, row_bytes, st)
+                : launch_dequant_t<kBF16, float>(w, out, rows, n, row_bytes, st);
     default:
       return cudaErrorInvalidValue;
   }

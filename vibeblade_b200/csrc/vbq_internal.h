@@ -45,6 +45,13 @@ cudaError_t launch_gemv(int qtype, const float* x, const void* w, float* y, int6
                         int64_t N, int64_t row_bytes, int batch, const GemvPlan& plan,
                         void* scratch, cudaStream_t st);
 
+// Generic GEMV (vbq_gemv_any.cu): any type (F32, F16, BF16, Q8_0, Q4_K, Q6_K), any N that
+// is a multiple of the block, any batch (groups of 4 rows on the grid), optional bias [N]
+// and residual [batch, N] added to the output; no scratch.
+cudaError_t launch_gemv_any(int qtype, const float* x, const void* w, float* y, const float* bias,
+                            const float* res, int64_t K, int64_t N, int64_t row_bytes, int batch,
+                            cudaStream_t st);
+
 // Tensor-core (integer mma.sync) Q4_K GEMV, batch 1..16, when gemv_mma_fits(); the K-splits
 // of a tile form one thread-block cluster and add up in the leader's shared memory.
 bool gemv_mma_fits(int64_t K, int64_t N, int batch);

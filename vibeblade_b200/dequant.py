@@ -141,8 +141,10 @@ def gemv_dequant(x: torch.Tensor, weights: torch.Tensor, out: torch.Tensor | Non
         batch = x.numel() // K
     else:
         batch = x.shape[0] if x.dim() > 1 else 1
-    if not 1 <= batch <= 32:
-        raise RuntimeError(f"gemv_dequant: batch must be in 1..32, got {batch}")
+    generic = t not in F.QUANTIZED or N % 256 != 0  # the generic kernel: any batch
+    limit = 4 * 65535 if generic else 32
+    if not 1 <= batch <= limit:
+        raise RuntimeError(f"gemv_dequant: batch must be in 1..{limit}, got {batch}")
     w = _weights_u8(weights)
     need = F.row_bytes(t, N) * K
     if w.numel() < need:

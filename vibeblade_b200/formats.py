@@ -8,17 +8,27 @@ a run of blocks along N and rows are ``row_bytes(type, N)`` apart, exactly the l
 """
 from __future__ import annotations
 
+GGML_TYPE_F32 = 0
+GGML_TYPE_F16 = 1
 GGML_TYPE_Q8_0 = 8
 GGML_TYPE_Q4_K = 12
 GGML_TYPE_Q6_K = 14
+GGML_TYPE_BF16 = 30
 
-TYPE_NAMES = {GGML_TYPE_Q8_0: "Q8_0", GGML_TYPE_Q4_K: "Q4_K", GGML_TYPE_Q6_K: "Q6_K"}
+TYPE_NAMES = {GGML_TYPE_F32: "F32", GGML_TYPE_F16: "F16", GGML_TYPE_BF16: "BF16",
+              GGML_TYPE_Q8_0: "Q8_0", GGML_TYPE_Q4_K: "Q4_K", GGML_TYPE_Q6_K: "Q6_K"}
 NAME_TO_TYPE = {v: k for k, v in TYPE_NAMES.items()}
 
 # values per block (cpp/include/ggml_types.h:31-50)
-BLOCK_VALUES = {GGML_TYPE_Q8_0: 32, GGML_TYPE_Q4_K: 256, GGML_TYPE_Q6_K: 256}
+BLOCK_VALUES = {GGML_TYPE_F32: 1, GGML_TYPE_F16: 1, GGML_TYPE_BF16: 1,
+                GGML_TYPE_Q8_0: 32, GGML_TYPE_Q4_K: 256, GGML_TYPE_Q6_K: 256}
 # bytes per block (cpp/include/ggml_types.h:52-71); Q8_0 is the 34-byte GGUF block
-BLOCK_BYTES = {GGML_TYPE_Q8_0: 34, GGML_TYPE_Q4_K: 144, GGML_TYPE_Q6_K: 210}
+BLOCK_BYTES = {GGML_TYPE_F32: 4, GGML_TYPE_F16: 2, GGML_TYPE_BF16: 2,
+               GGML_TYPE_Q8_0: 34, GGML_TYPE_Q4_K: 144, GGML_TYPE_Q6_K: 210}
+# the quantized types (the tensor-core GEMM, MoE and the tiled GEMV kernels take these;
+# F32 / F16 / BF16 weights -- small tensors such as the MoE router in GGUF files -- take
+# the generic GEMV)
+QUANTIZED = (GGML_TYPE_Q8_0, GGML_TYPE_Q4_K, GGML_TYPE_Q6_K)
 
 # byte offsets inside a block
 Q4K_D, Q4K_DMIN, Q4K_SCALES, Q4K_QS = 0, 2, 4, 16          # block_q4_K :118-124
