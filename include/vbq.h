@@ -55,6 +55,9 @@ extern "C" {
 #define VBQ_ERR_TIMEOUT 6     /* a bounded device-side wait gave up (see vbq_gemm) */
 #define VBQ_ERR_UNSUPPORTED 7 /* a valid request this build does not implement */
 #define VBQ_ERR_WORKSPACE 8   /* workspace missing or too small */
+#define VBQ_ERR_FORMAT 9      /* a GGUF file is malformed (vbq_gguf.h; the reference's messages) */
+#define VBQ_ERR_IO 10         /* a file cannot be opened, read or mapped */
+#define VBQ_ERR_NOT_FOUND 11  /* no GGUF metadata key of the asked kind */
 
 /* Message of the last failing call on this thread ("" after success). */
 const char* vbq_last_error(void);

@@ -28,6 +28,9 @@ REF_SO = REF_DIR / "libvbref.so"
 # (cpp/CMakeLists.txt:177 and :206-208: -O3 -DNDEBUG -mavx2 -mfma); used for timing only,
 # and only where the host CPU reports avx2 and fma
 REF_AVX2_SO = REF_DIR / "libvbref_avx2.so"
+# the reference's GGUF reader (cpp/src/gguf.cpp) behind oracle/ref_gguf_shim.cpp
+REF_GGUF_SO = REF_DIR / "libvbref_gguf.so"
+GGUF_SHIM = HERE / "ref_gguf_shim.cpp"
 # a reference checkout beside this repository's directory, unless $VB_REF names one
 DEFAULT_REF = HERE.parent.parent / "reference"
 
@@ -73,6 +76,22 @@ def build_ref(force: bool = False) -> Path | None:
     return REF_SO
 
 
+def build_ref_gguf(force: bool = False) -> Path | None:
+    """Compile the reference's GGUF reader with the C shim into oracle/_ref/libvbref_gguf.so
+    (None when neither the sources nor a prebuilt library exist)."""
+    root = ref_root() / "cpp"
+    srcs = [root / "src" / "gguf.cpp"]
+    if not srcs[0].exists():
+        return REF_GGUF_SO if REF_GGUF_SO.exists() else None
+    REF_DIR.mkdir(exist_ok=True)
+    if force or _stale(REF_GGUF_SO, srcs + [GGUF_SHIM]):
+        cmd = ["g++", "-O2", "-DNDEBUG", "-fPIC", "-shared", "-std=c++17",
+               "-I", str(root / "include"), "-I", str(root / "src"),
+               str(GGUF_SHIM), *map(str, srcs), "-o", str(REF_GGUF_SO)]
+        subprocess.run(cmd, check=True)
+    return REF_GGUF_SO
+
+
 def host_has_avx2() -> bool:
     """Whether this host's CPU reports AVX2 and FMA (Linux /proc/cpuinfo)."""
     try:
@@ -89,6 +108,7 @@ def host_has_avx2() -> bool:
 def build_all(force: bool = False) -> None:
     build_oracle(force)
     build_ref(force)
+    build_ref_gguf(force)
 
 
 if __name__ == "__main__":

@@ -209,3 +209,97 @@ def load_ref() -> RefLib | None:
     p = _build.build_ref() if os.environ.get("VB_NO_REF_BUILD") is None else (
         _build.REF_SO if _build.REF_SO.exists() else None)
     return RefLib(str(p)) if p is not None and os.path.exists(p) else None
+
+
+class RefGGUF:
+    """The reference's own GGUF reader (vibeblade::GGUFFile) through oracle/ref_gguf_shim.cpp."""
+
+    def __init__(self, path: str):
+        lib = C.CDLL(path)
+        self.lib = lib
+        sig = {
+            "vbr_gguf_error": (C.c_char_p, []),
+            "vbr_gguf_open": (C.c_void_p, [C.c_char_p]),
+            "vbr_gguf_close": (None, [C.c_void_p]),
+            "vbr_gguf_version": (C.c_int64, [C.c_void_p]),
+            "vbr_gguf_n_tensors": (C.c_int64, [C.c_void_p]),
+            "vbr_gguf_tensor": (C.c_int, [C.c_void_p, C.c_int64, C.c_char_p, C.c_int64, C.POINTER(C.c_int32),
+                                          C.POINTER(C.c_int64), C.POINTER(C.c_int32), C.POINTER(C.c_uint64),
+                                          C.POINTER(C.c_uint64)]),
+            "vbr_gguf_tensor_data": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_void_p)]),
+            "vbr_gguf_has_tensor": (C.c_int, [C.c_void_p, C.c_char_p]),
+            "vbr_gguf_meta_int": (C.c_int64, [C.c_void_p, C.c_char_p, C.c_int64]),
+            "vbr_gguf_meta_float": (C.c_double, [C.c_void_p, C.c_char_p, C.c_double]),
+            "vbr_gguf_meta_bool": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int]),
+            "vbr_gguf_meta_string": (C.c_int64, [C.c_void_p, C.c_char_p, C.c_char_p, C.c_int64]),
+            "vbr_gguf_meta_int_array": (C.c_int64, [C.c_void_p, C.c_char_p, C.POINTER(C.c_int64), C.c_int64]),
+            "vbr_gguf_meta_float_array": (C.c_int64, [C.c_void_p, C.c_char_p, C.POINTER(C.c_float), C.c_int64]),
+            "vbr_gguf_meta_string_array_len": (C.c_int64, [C.c_void_p, C.c_char_p]),
+            "vbr_gguf_meta_string_at": (C.c_int64, [C.c_void_p, C.c_char_p, C.c_int64, C.c_char_p, C.c_int64]),
+        }
+        for name, (res, args) in sig.items():
+            f = getattr(lib, name)
+            f.restype, f.argtypes = res, args
+
+    def open(self, path: str):
+        """(handle, None) or (None, the reference's exception message)."""
+        h = self.lib.vbr_gguf_open(str(path).encode())
+        return (h, None) if h else (None, self.lib.vbr_gguf_error().decode())
+
+    def close(self, h) -> None:
+        self.lib.vbr_gguf_close(h)
+
+    def tensors(self, h) -> list[tuple]:
+        out = []
+        buf = C.create_string_buffer(4096)
+        for i in range(self.lib.vbr_gguf_n_tensors(h)):
+            nd, ty = C.c_int32(), C.c_int32()
+            dims = (C.c_int64 * 4)()
+            off, size = C.c_uint64(), C.c_uint64()
+            self.lib.vbr_gguf_tensor(h, i, buf, 4096, C.byref(nd), dims, C.byref(ty), C.byref(off), C.byref(size))
+            out.append((buf.value.decode(errors="surrogateescape"), nd.value, tuple(dims), ty.value, off.value,
+                        size.value))
+        return out
+
+    def tensor_data(self, h, name: str, size: int):
+        """bytes, None when absent, or the exception message (str) when it throws"""
+        p = C.c_void_p()
+        rc = self.lib.vbr_gguf_tensor_data(h, name.encode(), C.byref(p))
+        if rc < 0:
+            return self.lib.vbr_gguf_error().decode()
+        return None if rc == 0 else C.string_at(p.value, size)
+
+    def meta_string(self, h, key):
+        n = self.lib.vbr_gguf_meta_string(h, key.encode(), None, 0)
+        buf = C.create_string_buffer(n + 1)
+        self.lib.vbr_gguf_meta_string(h, key.encode(), buf, n + 1)
+        return buf.raw[:n].decode(errors="surrogateescape")
+
+    def meta_int_array(self, h, key):
+        n = self.lib.vbr_gguf_meta_int_array(h, key.encode(), None, 0)
+        a = (C.c_int64 * max(n, 1))()
+        self.lib.vbr_gguf_meta_int_array(h, key.encode(), a, n)
+        return [int(v) for v in a[:n]]
+
+    def meta_float_array(self, h, key):
+        n = self.lib.vbr_gguf_meta_float_array(h, key.encode(), None, 0)
+        a = (C.c_float * max(n, 1))()
+        self.lib.vbr_gguf_meta_float_array(h, key.encode(), a, n)
+        return [float(v) for v in a[:n]]
+
+    def meta_string_array(self, h, key):
+        res = []
+        for j in range(self.lib.vbr_gguf_meta_string_array_len(h, key.encode())):
+            n = self.lib.vbr_gguf_meta_string_at(h, key.encode(), j, None, 0)
+            buf = C.create_string_buffer(n + 1)
+            self.lib.vbr_gguf_meta_string_at(h, key.encode(), j, buf, n + 1)
+            res.append(buf.raw[:n].decode(errors="surrogateescape"))
+        return res
+
+
+@lru_cache(maxsize=1)
+def load_ref_gguf() -> RefGGUF | None:
+    """The reference's GGUF reader, or None when it cannot be built or found."""
+    p = _build.build_ref_gguf() if os.environ.get("VB_NO_REF_BUILD") is None else (
+        _build.REF_GGUF_SO if _build.REF_GGUF_SO.exists() else None)
+    return RefGGUF(str(p)) if p is not None and os.path.exists(p) else None

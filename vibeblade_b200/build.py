@@ -34,7 +34,8 @@ def nvcc() -> str:
 
 
 def sources() -> list[Path]:
-    return sorted(CSRC.glob("*.cu"))
+    """CUDA sources and the host-only C++ sources (the GGUF reader), all through nvcc."""
+    return sorted(list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cpp")))
 
 
 def headers() -> list[Path]:
