@@ -218,6 +218,30 @@ def bench_prefill(dev, steps: int) -> dict:
             "kernel": "vbq::gemm::gemm_kernel (2-SM tcgen05, cta_group::2)"}
 
 
+def bench_lm_head(dev, steps: int) -> dict:
+    """The lm_head GEMV at a Llama-3 vocabulary (4096 x 128256, batch 1; the reference's
+    gemv_dequant_mt at cpp/src/fast_model.cpp:1022) in Q6_K -- the usual type of
+    output.weight in Q4_K_M files -- and Q4_K; two weight copies alternate (> L2)."""
+    import torch
+    import vibeblade_b200 as vb
+    from vibeblade_b200.quantize import synthetic_weights
+    K, N = 4096, 128256
+    out = {"shape": f"{K}x{N}", "batch": 1}
+    g = torch.Generator(device=dev).manual_seed(6)
+    x = torch.randn(1, K, generator=g, device=dev)
+    y = torch.empty(1, N, device=dev)
+    for t, name in ((14, "q6_k"), (12, "q4_k")):
+        ws = [synthetic_weights(K, N, t, seed=300 + i, device=dev) for i in range(2)]
+        ms = _time_steps(lambda i: vb.gemv_dequant(x, ws[i % 2], y, K, N, t), 5 * steps, 4,
+                         torch.cuda.current_stream(dev), 1)
+        nbytes = K * N * (210 if t == 14 else 144) // 256 + 4 * (K + N)
+        gbs = nbytes * 5 * steps / (ms * 1e-3) / 1e9
+        out[name] = {"value": round(gbs, 1), "unit": "GB/s", "us_per_call": round(1e3 * ms / (5 * steps), 2),
+                     "frac_of_hbm": round(gbs / peaks()["hbm_gbs"], 4)}
+        del ws
+    return out
+
+
 def bench_moe(dev, steps: int) -> dict:
     """MoE FFN, 8 experts top-2, hidden 4096, intermediate 14336, Q4_K,
     4096 tokens routed by N(0,1) logits (seed 3)."""
@@ -653,6 +677,7 @@ def run_gpu(args) -> None:
         if world == 1:
             extras["prefill"] = _soft(bench_prefill, dev, args.extras_steps)
             extras["moe"] = _soft(bench_moe, dev, args.extras_steps)
+            extras["lm_head"] = _soft(bench_lm_head, dev, args.extras_steps)
         extras["tp_ffn"] = bench_tp(dev, rank, world, args.extras_steps)
     else:  # config 5's decode side runs on the GEMV alone
         extras["tp_ffn_decode"] = bench_tp(dev, rank, world, args.extras_steps, prefill=False)

@@ -112,6 +112,26 @@ int vbq_gemv(const float* x, const void* w, float* y, int64_t K, int64_t N, int3
              int32_t batch, void* scratch, size_t scratch_bytes, void* stream);
 
 /*
+ * vbq_gemv with the FFN's element-wise steps fused in (no counterpart call in the
+ * reference, which runs them as separate loops around its gemv_dequant calls):
+ *   * flags & VBQ_GEMV_X_SWIGLU: x points at a [batch, 2K] buffer holding the output of a
+ *     gate | up matmul (gate values in columns 0..K-1, up in K..2K-1), and the GEMV's input
+ *     is x'[b, k] = silu(gate[b, k]) * up[b, k], computed where the kernel reads it, with
+ *     vbq_swiglu's sanitising and arithmetic (cpp/src/fast_model.cpp:946-953) -- the down
+ *     projection without a SwiGLU pass of its own;
+ *   * bias (fp32 [N], may be NULL) is added to every output row (the Q/K/V biases,
+ *     cpp/src/fast_model.cpp:659-668);
+ *   * residual (fp32 [batch, N], may be NULL) is added as well (the residual adds after o
+ *     and down, :813-824, :990-998); it may be y itself, but must not overlap y otherwise.
+ * Same shapes, scratch and results as vbq_gemv otherwise (K >= 1 when an addend is given).
+ * Q4_K batches above 4 with the SwiGLU input run as groups of 4 rows.
+ */
+#define VBQ_GEMV_X_SWIGLU 1
+int vbq_gemv_ex(const float* x, const void* w, float* y, int64_t K, int64_t N, int32_t type,
+                int32_t batch, int32_t flags, const float* bias, const float* residual,
+                void* scratch, size_t scratch_bytes, void* stream);
+
+/*
  * Quantized-weight GEMM on the tcgen05 tensor cores (prefill):
  *     C[m, n] = sum_k A[m, k] * deq(W)[k, n]
  * A is bf16 [M, K] row-major, C fp32 (VBQ_DTYPE_F32) or bf16 (VBQ_DTYPE_BF16) [M, N]
@@ -125,6 +145,18 @@ int vbq_gemv(const float* x, const void* w, float* y, int64_t K, int64_t N, int3
  */
 int vbq_gemm(const void* a, const void* w, void* c, int64_t M, int64_t K, int64_t N,
              int32_t type, int32_t c_dtype, void* stream);
+
+/*
+ * vbq_gemm with the adds that follow the reference's matmuls fused into the epilogue (no
+ * counterpart call in the reference): bias (fp32 [N], 16-byte aligned, may be NULL) is
+ * added to every row, the Q/K/V biases (cpp/src/fast_model.cpp:659-668); residual ([M, N]
+ * of c's element type, 16-byte aligned, may be NULL, may be c itself but must not overlap
+ * it otherwise) is added too, the residual adds after o and down (:813-824, :990-998).
+ * The sums are formed in fp32 on the accumulator and rounded once to c's type.
+ */
+int vbq_gemm_ex(const void* a, const void* w, void* c, int64_t M, int64_t K, int64_t N,
+                int32_t type, int32_t c_dtype, const float* bias, const void* residual,
+                void* stream);
 
 /*
  * vbq_gemv with library-owned scratch, for callers that cannot allocate device memory --

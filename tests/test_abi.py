@@ -119,3 +119,11 @@ def test_wait_probe_argument_errors_need_no_gpu(lib):
     assert lib.vbq_debug_wait_probe((1 << 31) + 1, 0, None) == _lib.VBQ_ERR_SHAPE
     assert lib.vbq_debug_wait_probe(1000, 2, None) == _lib.VBQ_ERR_SHAPE
     assert b"arrive" in lib.vbq_last_error()
+
+
+def test_fused_entry_argument_errors_need_no_gpu(lib):
+    from vibeblade_b200 import _lib
+    assert lib.vbq_gemv_ex(None, None, None, 16, 256, 12, 1, 4, None, None, None, 0, None) == _lib.VBQ_ERR_SHAPE
+    assert b"flags" in lib.vbq_last_error()
+    assert lib.vbq_gemv_ex(None, None, None, 16, 256, 2, 1, 0, None, None, None, 0, None) == _lib.VBQ_ERR_TYPE
+    assert lib.vbq_gemm_ex(None, None, None, 4, 64, 300, 12, 0, None, None, None) == _lib.VBQ_ERR_SHAPE

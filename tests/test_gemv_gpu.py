@@ -324,3 +324,21 @@ def test_gemv_router_feeds_moe_routing(cuda, oracle):
     idx, _ = vb.moe_route(lg, 2)
     idx_ref, _ = vb.moe_route(torch.from_numpy(ref).to(cuda), 2)
     assert torch.equal(idx.sort(dim=1).values, idx_ref.sort(dim=1).values)
+
+
+@pytest.mark.parametrize("qtype", [F.GGML_TYPE_Q6_K, F.GGML_TYPE_Q4_K, F.GGML_TYPE_Q8_0])
+@pytest.mark.parametrize("batch", [1, 4])
+def test_gemv_lm_head_vocab_size(cuda, qtype, batch):
+    """The lm_head projection at a Llama-3 vocabulary (cpp/src/fast_model.cpp:1022, 1058:
+    gemv_dequant_mt over N = vocab): 4096 x 128256 (501 column tiles) in Q6_K, the usual
+    type of output.weight in Q4_K_M files, and in Q4_K / Q8_0; against the fp64 product with
+    the per-column bar, and bitwise repeatable."""
+    K, N = 4096, 128256
+    w = synthetic_weights(K, N, qtype, seed=77, device=cuda)
+    g = torch.Generator(device=cuda).manual_seed(78)
+    x = torch.randn(batch, K, generator=g, device=cuda)
+    y = vb.gemv_dequant(x, w, None, K, N, qtype)
+    ref = (x.double() @ vb.dequantize(w, K, N, qtype).double()).cpu().numpy()
+    _check_columns(y.cpu().numpy(), ref, "fp64")
+    assert torch.equal(y, vb.gemv_dequant(x, w, None, K, N, qtype))
+    assert vb.device_status() == 0

@@ -132,12 +132,16 @@ static vbq::GemvPlan gemv_call_plan(int64_t K, int64_t N, int32_t batch, int32_t
 
 static cudaError_t launch_gemv_groups(int32_t type, const float* x, const void* w, float* y,
                                       int64_t K, int64_t N, int64_t rb, int32_t batch,
-                                      void* scratch, cudaStream_t st) {
+                                      void* scratch, cudaStream_t st,
+                                      const vbq::GemvFuse& f = vbq::GemvFuse{}) {
+  const int64_t xrow = f.swiglu_x ? 2 * K : K;
   for (int32_t b0 = 0; b0 < batch; b0 += kLaunchBatch) {
     const int32_t nb = batch - b0 < kLaunchBatch ? batch - b0 : kLaunchBatch;
     const vbq::GemvPlan plan = vbq::plan_gemv(K, N, nb, type);
-    cudaError_t e = vbq::launch_gemv(type, x + (int64_t)b0 * K, w, y + (int64_t)b0 * N, K, N, rb, nb,
-                                     plan, scratch, st);
+    vbq::GemvFuse fg = f;
+    if (f.res) fg.res = f.res + (int64_t)b0 * N;
+    cudaError_t e = vbq::launch_gemv(type, x + (int64_t)b0 * xrow, w, y + (int64_t)b0 * N, K, N, rb, nb,
+                                     plan, scratch, st, fg);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -150,45 +154,66 @@ int vbq_gemv_scratch_bytes(int64_t K, int64_t N, int32_t type, int32_t batch, si
   return ok();
 }
 
-int vbq_gemv(const float* x, const void* w, float* y, int64_t K, int64_t N, int32_t type,
-             int32_t batch, void* scratch, size_t scratch_bytes, void* stream) {
+// vbq_gemv and vbq_gemv_ex: `who` names the entry in messages, `f` the optional fusions
+static int gemv_impl(const char* who, const float* x, const void* w, float* y, int64_t K, int64_t N,
+                     int32_t type, int32_t batch, void* scratch, size_t scratch_bytes, void* stream,
+                     const vbq::GemvFuse& f) {
+  const std::string nm(who);
   if (int rc = gemv_checks(type, K, N, batch)) return rc;
   if (N == 0) return ok();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool epi = f.bias || f.res;
   if (K == 0) {  // empty sum: the reference zeroes out and adds nothing (dequant.cpp:767)
-    if (!y) return fail(VBQ_ERR_NULL, "vbq_gemv: NULL pointer");
+    if (!y) return fail(VBQ_ERR_NULL, nm + ": NULL pointer");
+    if (epi) return fail(VBQ_ERR_SHAPE, nm + ": K must be positive when a bias or residual is added");
     cudaError_t e = cudaMemsetAsync(y, 0, (size_t)batch * (size_t)N * sizeof(float), st);
-    if (e != cudaSuccess) return cuda_fail(e, "vbq_gemv memset");
+    if (e != cudaSuccess) return cuda_fail(e, (nm + " memset").c_str());
     return ok();
   }
-  if (!x || !w || !y) return fail(VBQ_ERR_NULL, "vbq_gemv: NULL pointer");
+  if (!x || !w || !y) return fail(VBQ_ERR_NULL, nm + ": NULL pointer");
   if (!aligned(x, 4) || !aligned(y, 16) || !aligned(w, 16))
-    return fail(VBQ_ERR_ALIGN, "vbq_gemv: w and y must be 16-byte aligned, x 4-byte aligned");
+    return fail(VBQ_ERR_ALIGN, nm + ": w and y must be 16-byte aligned, x 4-byte aligned");
+  if ((f.bias && !aligned(f.bias, 4)) || (f.res && !aligned(f.res, 4)))
+    return fail(VBQ_ERR_ALIGN, nm + ": bias and residual must be 4-byte aligned");
   if (K > (int64_t)INT32_MAX || N > (int64_t)INT32_MAX)
-    return fail(VBQ_ERR_SHAPE, "vbq_gemv: sizes above 2^31 are not supported");
+    return fail(VBQ_ERR_SHAPE, nm + ": sizes above 2^31 are not supported");
   if (gemv_generic(type, N)) {
     const int64_t rbg = (N / block_values(type)) * block_bytes(type);
-    cudaError_t e = vbq::launch_gemv_any(type, x, w, y, nullptr, nullptr, K, N, rbg, batch,
-                                         static_cast<cudaStream_t>(stream));
-    if (e != cudaSuccess) return cuda_fail(e, "vbq_gemv launch");
+    cudaError_t e = vbq::launch_gemv_any(type, x, w, y, K, N, rbg, batch, st, f);
+    if (e != cudaSuccess) return cuda_fail(e, (nm + " launch").c_str());
     return ok();
   }
   const vbq::GemvPlan plan = gemv_call_plan(K, N, batch, type);
   if (plan.scratch_bytes > 0) {
     if (!scratch || scratch_bytes < plan.scratch_bytes)
-      return fail(VBQ_ERR_WORKSPACE, "vbq_gemv: scratch needs " + std::to_string(plan.scratch_bytes) +
-                                          " bytes (vbq_gemv_scratch_bytes), got " +
-                                          std::to_string(scratch_bytes));
-    if (!aligned(scratch, 16)) return fail(VBQ_ERR_ALIGN, "vbq_gemv: scratch must be 16-byte aligned");
+      return fail(VBQ_ERR_WORKSPACE, nm + ": scratch needs " + std::to_string(plan.scratch_bytes) +
+                                         " bytes (vbq_gemv_scratch_bytes), got " + std::to_string(scratch_bytes));
+    if (!aligned(scratch, 16)) return fail(VBQ_ERR_ALIGN, nm + ": scratch must be 16-byte aligned");
   }
   const int64_t rb = (N / block_values(type)) * block_bytes(type);
-  cudaError_t e = launch_gemv_groups(type, x, w, y, K, N, rb, batch, scratch, st);
-  if (e != cudaSuccess) return cuda_fail(e, "vbq_gemv launch");
+  cudaError_t e = launch_gemv_groups(type, x, w, y, K, N, rb, batch, scratch, st, f);
+  if (e != cudaSuccess) return cuda_fail(e, (nm + " launch").c_str());
   return ok();
 }
 
-int vbq_gemm(const void* a, const void* w, void* c, int64_t M, int64_t K, int64_t N, int32_t type,
-             int32_t c_dtype, void* stream) {
+int vbq_gemv(const float* x, const void* w, float* y, int64_t K, int64_t N, int32_t type,
+             int32_t batch, void* scratch, size_t scratch_bytes, void* stream) {
+  return gemv_impl("vbq_gemv", x, w, y, K, N, type, batch, scratch, scratch_bytes, stream, vbq::GemvFuse{});
+}
+
+int vbq_gemv_ex(const float* x, const void* w, float* y, int64_t K, int64_t N, int32_t type,
+                int32_t batch, int32_t flags, const float* bias, const float* residual, void* scratch,
+                size_t scratch_bytes, void* stream) {
+  if (flags & ~VBQ_GEMV_X_SWIGLU) return fail(VBQ_ERR_SHAPE, "vbq_gemv_ex: unknown flags " + std::to_string(flags));
+  vbq::GemvFuse f;
+  f.swiglu_x = (flags & VBQ_GEMV_X_SWIGLU) != 0;
+  f.bias = bias;
+  f.res = residual;
+  return gemv_impl("vbq_gemv_ex", x, w, y, K, N, type, batch, scratch, scratch_bytes, stream, f);
+}
+
+static int gemm_impl(const void* a, const void* w, void* c, int64_t M, int64_t K, int64_t N, int32_t type,
+                     int32_t c_dtype, void* stream, const vbq::GemmEpi& ep) {
   if (!quantized(type)) return fail(VBQ_ERR_TYPE, "gemm_dequant: unsupported type " + std::to_string(type));
   if (c_dtype != VBQ_DTYPE_F32 && c_dtype != VBQ_DTYPE_BF16)
     return fail(VBQ_ERR_SHAPE, "vbq_gemm: c_dtype must be VBQ_DTYPE_F32 or VBQ_DTYPE_BF16");
@@ -197,6 +222,7 @@ int vbq_gemm(const void* a, const void* w, void* c, int64_t M, int64_t K, int64_
   if (M == 0 || N == 0) return ok();
   if (K == 0) {
     if (!c) return fail(VBQ_ERR_NULL, "vbq_gemm: NULL pointer");
+    if (ep.bias || ep.res) return fail(VBQ_ERR_SHAPE, "vbq_gemm_ex: K must be positive when a bias or residual is added");
     cudaError_t e = cudaMemsetAsync(c, 0, (size_t)M * N * (c_dtype == VBQ_DTYPE_F32 ? 4 : 2),
                                     static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "vbq_gemm memset");
@@ -211,9 +237,24 @@ int vbq_gemm(const void* a, const void* w, void* c, int64_t M, int64_t K, int64_
     return fail(VBQ_ERR_UNSUPPORTED, "vbq_gemm: weight rows must be a multiple of 16 bytes (Q6_K: N % 2048 == 0)");
   if (!aligned(a, 16) || !aligned(w, 16) || !aligned(c, 16))
     return fail(VBQ_ERR_ALIGN, "vbq_gemm: a, w and c must be 16-byte aligned");
-  cudaError_t e = vbq::launch_gemm(type, a, w, c, M, K, N, rb, c_dtype, static_cast<cudaStream_t>(stream));
+  if ((ep.bias && !aligned(ep.bias, 16)) || (ep.res && !aligned(ep.res, 16)))
+    return fail(VBQ_ERR_ALIGN, "vbq_gemm_ex: bias and residual must be 16-byte aligned");
+  cudaError_t e = vbq::launch_gemm(type, a, w, c, M, K, N, rb, c_dtype, static_cast<cudaStream_t>(stream), ep);
   if (e != cudaSuccess) return cuda_fail(e, "vbq_gemm launch");
   return ok();
+}
+
+int vbq_gemm(const void* a, const void* w, void* c, int64_t M, int64_t K, int64_t N, int32_t type,
+             int32_t c_dtype, void* stream) {
+  return gemm_impl(a, w, c, M, K, N, type, c_dtype, stream, vbq::GemmEpi{});
+}
+
+int vbq_gemm_ex(const void* a, const void* w, void* c, int64_t M, int64_t K, int64_t N, int32_t type,
+                int32_t c_dtype, const float* bias, const void* residual, void* stream) {
+  vbq::GemmEpi ep;
+  ep.bias = bias;
+  ep.res = residual;
+  return gemm_impl(a, w, c, M, K, N, type, c_dtype, stream, ep);
 }
 
 int vbq_device_status(int32_t* status, int32_t clear) {
@@ -334,7 +375,7 @@ extern "C" int vbq_gemv_static_scratch(const float* x, const void* w, float* y, 
     return fail(VBQ_ERR_SHAPE, "vbq_gemv_static_scratch: sizes above 2^31 are not supported");
   if (gemv_generic(type, N)) {  // the generic kernel needs no scratch
     const int64_t rbg = (N / block_values(type)) * block_bytes(type);
-    cudaError_t e = vbq::launch_gemv_any(type, x, w, y, nullptr, nullptr, K, N, rbg, batch, st);
+    cudaError_t e = vbq::launch_gemv_any(type, x, w, y, K, N, rbg, batch, st);
     if (e != cudaSuccess) return cuda_fail(e, "vbq_gemv_static_scratch launch");
     return ok();
   }

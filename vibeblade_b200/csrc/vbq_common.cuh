@@ -49,6 +49,48 @@ __device__ __forceinline__ float f16_ieee(uint32_t h) {
 
 __device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xffu; }
 
+// nan -> 0, +-inf -> +-65504, then clip to +-65504 (vibeblade/moe.py:472-473)
+__device__ __forceinline__ float sanitize(float v) {
+  if (v != v) return 0.0f;
+  return fminf(fmaxf(v, -65504.0f), 65504.0f);
+}
+// x * sigmoid(x) = x / (1 + e^-x), the reference's two-sided form (vibeblade/moe.py:36-50)
+// written without its branch: for the sanitised inputs (|x| <= 65504) e^-x is +inf only
+// where x < -88, and the quotient is then -0, as in the two-sided form.  expf is the full-
+// precision exponential; __fdividef is within 2 ulp for every denominator here (>= 1).
+// Branch-free, so a warp whose inputs have both signs does not run both halves.
+__device__ __forceinline__ float silu_ref(float x) { return __fdividef(x, 1.0f + expf(-x)); }
+// One SwiGLU value, silu(g) * u of the sanitised inputs (the FFN's gate and up,
+// cpp/src/fast_model.cpp:946-953; the same arithmetic as vbq_swiglu).
+__device__ __forceinline__ float swiglu1(float g, float u) { return silu_ref(sanitize(g)) * sanitize(u); }
+
+// Input of a fused GEMV: x[b, k] itself, or, with SWIGLU, silu(gu[b, k]) * gu[b, K + k]
+// where x points at a [batch, 2K] buffer holding a gate | up matmul's output (the down
+// projection's input, computed where it is read instead of in a pass of its own).
+template <bool SWIGLU>
+__device__ __forceinline__ float gemv_x(const float* __restrict__ x, int64_t b, int64_t K, int64_t k) {
+  if constexpr (SWIGLU) {
+    const float* r = x + b * 2 * K;
+    return swiglu1(__ldg(r + k), __ldg(r + K + k));
+  } else {
+    return __ldg(x + b * K + k);
+  }
+}
+
+// Output epilogue of the GEMV kernels: y[b, n] = acc + bias[n] + res[b, n], each term only
+// when its pointer is set (the reference adds the Q/K/V biases after its GEMVs,
+// cpp/src/fast_model.cpp:659-668, and the residual after o and down, :813-824, :990-998).
+// res is [batch, N] like y and may be y itself (read before the write, same thread).
+struct Epi {
+  const float* bias;
+  const float* res;
+};
+__device__ __forceinline__ float epi_apply(const Epi& e, float v, int64_t b, int64_t N, int64_t n) {
+  if (e.bias) v += __ldg(e.bias + n);
+  if (e.res) v += e.res[b * N + n];
+  return v;
+}
+
 // Q4_K sub-block scale and min (get_scale_min_k4, cpp/src/dequant.cpp:258-266).
 // s0/s1/s2 are scale bytes 0-3, 4-7, 8-11 as little-endian words.
 __device__ __forceinline__ void q4k_scale_min(int j, uint32_t s0, uint32_t s1, uint32_t s2,

@@ -429,7 +429,7 @@ __device__ __forceinline__ void store_all(const Producer<QT>& pr, uint8_t* bt, c
 template <int QT, bool BF16_OUT, bool GROUPED>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
-            void* __restrict__ c, int M, int K, int N, const int* __restrict__ seg, int n_seg) {
+            void* c, int M, int K, int N, const int* __restrict__ seg, int n_seg, GemmEpi ep) {
   using L = Smem<QT>;
   using R = Raw<QT>;
   extern __shared__ uint8_t smem_raw[];
@@ -663,6 +663,43 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
               for (int qq = 0; qq < 8; ++qq) o[8 * g + qq] = r[8 * g + ((qq + 4 * h + g) & 7)];
             if (row < row_end) {
               const int64_t off64 = (int64_t)row * N + (int64_t)n_tile * BN + cb + 32 * h;
+              if (ep.bias) {  // bias of these 32 columns (the same for every row)
+                const float4* bp = reinterpret_cast<const float4*>(ep.bias + (int64_t)n_tile * BN + cb + 32 * h);
+#pragma unroll
+                for (int x = 0; x < 8; ++x) {
+                  const float4 t = __ldg(bp + x);
+                  o[4 * x] = __float_as_uint(__uint_as_float(o[4 * x]) + t.x);
+                  o[4 * x + 1] = __float_as_uint(__uint_as_float(o[4 * x + 1]) + t.y);
+                  o[4 * x + 2] = __float_as_uint(__uint_as_float(o[4 * x + 2]) + t.z);
+                  o[4 * x + 3] = __float_as_uint(__uint_as_float(o[4 * x + 3]) + t.w);
+                }
+              }
+              if (ep.res) {  // residual of the row's 32 columns, read before the store below
+                if constexpr (BF16_OUT) {
+                  const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(ep.res) + off64);
+#pragma unroll
+                  for (int x = 0; x < 4; ++x) {
+                    const uint4 t = rp[x];
+                    const uint32_t wv[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                      o[8 * x + 2 * q] = __float_as_uint(__uint_as_float(o[8 * x + 2 * q]) + __uint_as_float(wv[q] << 16));
+                      o[8 * x + 2 * q + 1] =
+                          __float_as_uint(__uint_as_float(o[8 * x + 2 * q + 1]) + __uint_as_float(wv[q] & 0xffff0000u));
+                    }
+                  }
+                } else {
+                  const float4* rp = reinterpret_cast<const float4*>(static_cast<const float*>(ep.res) + off64);
+#pragma unroll
+                  for (int x = 0; x < 8; ++x) {
+                    const float4 t = rp[x];
+                    o[4 * x] = __float_as_uint(__uint_as_float(o[4 * x]) + t.x);
+                    o[4 * x + 1] = __float_as_uint(__uint_as_float(o[4 * x + 1]) + t.y);
+                    o[4 * x + 2] = __float_as_uint(__uint_as_float(o[4 * x + 2]) + t.z);
+                    o[4 * x + 3] = __float_as_uint(__uint_as_float(o[4 * x + 3]) + t.w);
+                  }
+                }
+              }
               if constexpr (BF16_OUT) {
                 uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(c) + off64);
 #pragma unroll
@@ -731,7 +768,7 @@ static EncodeTiledFn encode_fn() {
 template <int QT, bool BF16_OUT, bool GROUPED>
 static cudaError_t launch_gemm_t(const void* a, const void* w, void* c, int64_t rows, int64_t K,
                                  int64_t N, int64_t RB, int64_t slab_bytes, const int* seg,
-                                 int n_seg, cudaStream_t st) {
+                                 int n_seg, cudaStream_t st, GemmEpi ep) {
   using namespace gemm;
   using L = Smem<QT>;
   using R = Raw<QT>;
@@ -772,21 +809,22 @@ static cudaError_t launch_gemm_t(const void* a, const void* w, void* c, int64_t 
   // segments' tile count (each segment adds at most one partial tile)
   const int64_t items = GROUPED ? (rows + BMP - 1) / BMP + n_seg : (rows + BMP - 1) / BMP;
   const dim3 grid((unsigned)(2 * (N / BN)), (unsigned)items, 1);
-  kern<<<grid, kThreads, L::kAlloc, st>>>(ma, mw, c, (int)rows, (int)K, (int)N, seg, n_seg);
+  kern<<<grid, kThreads, L::kAlloc, st>>>(ma, mw, c, (int)rows, (int)K, (int)N, seg, n_seg, ep);
   return cudaGetLastError();
 }
 
 template <bool GROUPED>
 static cudaError_t dispatch_gemm(int qtype, const void* a, const void* w, void* c, int64_t rows,
                                  int64_t K, int64_t N, int64_t row_bytes, int c_dtype,
-                                 int64_t slab_bytes, const int* seg, int n_seg, cudaStream_t st) {
+                                 int64_t slab_bytes, const int* seg, int n_seg, cudaStream_t st,
+                                 const GemmEpi& ep) {
   const bool bf = c_dtype == 1;
 #define VBQ_GEMM_CASE(QT)                                                                       \
   case QT:                                                                                      \
     return bf ? launch_gemm_t<QT, true, GROUPED>(a, w, c, rows, K, N, row_bytes, slab_bytes, seg, \
-                                                 n_seg, st)                                     \
+                                                 n_seg, st, ep)                                 \
               : launch_gemm_t<QT, false, GROUPED>(a, w, c, rows, K, N, row_bytes, slab_bytes,    \
-                                                  seg, n_seg, st);
+                                                  seg, n_seg, st, ep);
   switch (qtype) {
     VBQ_GEMM_CASE(kQ4_K)
     VBQ_GEMM_CASE(kQ6_K)
@@ -797,15 +835,15 @@ static cudaError_t dispatch_gemm(int qtype, const void* a, const void* w, void* 
 }
 
 cudaError_t launch_gemm(int qtype, const void* a, const void* w, void* c, int64_t M, int64_t K,
-                        int64_t N, int64_t row_bytes, int c_dtype, cudaStream_t st) {
-  return dispatch_gemm<false>(qtype, a, w, c, M, K, N, row_bytes, c_dtype, 0, nullptr, 0, st);
+                        int64_t N, int64_t row_bytes, int c_dtype, cudaStream_t st, const GemmEpi& ep) {
+  return dispatch_gemm<false>(qtype, a, w, c, M, K, N, row_bytes, c_dtype, 0, nullptr, 0, st, ep);
 }
 
 cudaError_t launch_gemm_grouped(int qtype, const void* a, const void* w, void* c, int64_t rows,
                                 int64_t K, int64_t N, int64_t row_bytes, int c_dtype,
                                 int64_t slab_bytes, const int* seg, int n_seg, cudaStream_t st) {
   return dispatch_gemm<true>(qtype, a, w, c, rows, K, N, row_bytes, c_dtype, slab_bytes, seg,
-                             n_seg, st);
+                             n_seg, st, GemmEpi{});
 }
 
 cudaError_t gemm_status(unsigned* out, bool clear) {

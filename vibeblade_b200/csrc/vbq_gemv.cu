@@ -347,13 +347,13 @@ struct RowMath<kQ8_0, B, VPT> {
 
 // ---------------------------------------------------------------------------------
 
-template <int QT, int B, int VPT>
+template <int QT, int B, int VPT, bool SWIGLU>
 __global__ void __launch_bounds__(256, GemvCfg<QT, B, VPT>::kMinBlocks) gemv_kernel(const float* __restrict__ x,
                                                    const uint8_t* __restrict__ w,
-                                                   float* __restrict__ y, int64_t K, int64_t N,
+                                                   float* y, int64_t K, int64_t N,
                                                    int64_t RB, int64_t kslice, int batch,
                                                    float* __restrict__ partials,
-                                                   unsigned* __restrict__ counters) {
+                                                   unsigned* __restrict__ counters, Epi epi) {
   using C = GemvCfg<QT, B, VPT>;
   using M = RowMath<QT, B, VPT>;
   using Frag = typename M::Frag;
@@ -397,7 +397,7 @@ __global__ void __launch_bounds__(256, GemvCfg<QT, B, VPT>::kMinBlocks) gemv_ker
 
   const uint8_t* wrow = w + (k0 + rl) * RB + tile * C::kTileBytes;  // this thread's first row
   const int64_t wstep = (int64_t)C::kRowLanes * RB;
-  const float* xrow = x + k0 + rl;
+  const int64_t kx0 = k0 + rl;  // this thread's first row (the x index)
 
   // Programmatic dependent launch: let the next kernel in the stream start filling SMs as
   // this grid drains, and stream the first weight units before waiting for the previous
@@ -416,7 +416,7 @@ __global__ void __launch_bounds__(256, GemvCfg<QT, B, VPT>::kMinBlocks) gemv_ker
     if (u < nrows) {
 #pragma unroll
       for (int b = 0; b < B; ++b)
-        xs[u][b] = (b < batch) ? __ldg(xrow + (int64_t)b * K + u * C::kRowLanes) : 0.f;
+        xs[u][b] = (b < batch) ? gemv_x<SWIGLU>(x, b, K, kx0 + u * C::kRowLanes) : 0.f;
     }
   }
   int since_flush = 0;
@@ -433,7 +433,7 @@ __global__ void __launch_bounds__(256, GemvCfg<QT, B, VPT>::kMinBlocks) gemv_ker
           M::load(f[u], wrow + nx * wstep, c);
 #pragma unroll
           for (int b = 0; b < B; ++b)
-            xs[u][b] = (b < batch) ? __ldg(xrow + (int64_t)b * K + (int64_t)nx * C::kRowLanes) : 0.f;
+            xs[u][b] = (b < batch) ? gemv_x<SWIGLU>(x, b, K, kx0 + (int64_t)nx * C::kRowLanes) : 0.f;
         }
         M::run(cur, xv, c, acc, corr);
       }
@@ -481,7 +481,7 @@ __global__ void __launch_bounds__(256, GemvCfg<QT, B, VPT>::kMinBlocks) gemv_ker
   const int E = batch * 256;
   if (S == 1) {
     for (int e = tid; e < E; e += C::kThreads)
-      y[(int64_t)(e >> 8) * N + tile * 256 + (e & 255)] = outbuf[e];
+      y[(int64_t)(e >> 8) * N + tile * 256 + (e & 255)] = epi_apply(epi, outbuf[e], e >> 8, N, tile * 256 + (e & 255));
     return;
   }
 
@@ -499,7 +499,7 @@ __global__ void __launch_bounds__(256, GemvCfg<QT, B, VPT>::kMinBlocks) gemv_ker
     float sum = 0.f;
     for (int sp = 0; sp < S; ++sp)
       sum += __ldcg(partials + ((int64_t)sp * batch + b) * N + tile * 256 + n);
-    y[(int64_t)b * N + tile * 256 + n] = sum;
+    y[(int64_t)b * N + tile * 256 + n] = epi_apply(epi, sum, b, N, tile * 256 + n);
   }
   if (tid == 0) counters[tile] = 0u;  // leave the scratch ready for the next call
 }
@@ -570,12 +570,12 @@ GemvPlan plan_gemv(int64_t K, int64_t N, int batch, int qtype) {
   return p;
 }
 
-template <int QT, int B, int VPT>
+template <int QT, int B, int VPT, bool SW>
 static cudaError_t launch_gemv_t(const float* x, const void* w, float* y, int64_t K, int64_t N,
                                  int64_t RB, int batch, const GemvPlan& plan, void* scratch,
-                                 cudaStream_t st) {
+                                 cudaStream_t st, Epi epi) {
   using C = GemvCfg<QT, B, VPT>;
-  auto kern = gemv_kernel<QT, B, VPT>;
+  auto kern = gemv_kernel<QT, B, VPT, SW>;
   static DeviceOnce configured;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -603,37 +603,46 @@ static cudaError_t launch_gemv_t(const float* x, const void* w, float* y, int64_
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, x, static_cast<const uint8_t*>(w), y, K, N, RB,
-                            plan.kslice, batch, partials, counters);
+                            plan.kslice, batch, partials, counters, epi);
+}
+
+template <int QT, bool SW>
+static cudaError_t launch_gemv_q(const float* x, const void* w, float* y, int64_t K, int64_t N,
+                                 int64_t RB, int batch, const GemvPlan& p, void* scratch,
+                                 cudaStream_t st, Epi e) {
+  if (batch <= 1) {
+    if constexpr (QT == kQ8_0) return launch_gemv_t<QT, 1, 32, SW>(x, w, y, K, N, RB, batch, p, scratch, st, e);
+    else return launch_gemv_t<QT, 1, 64, SW>(x, w, y, K, N, RB, batch, p, scratch, st, e);
+  }
+  if (batch <= 2) return launch_gemv_t<QT, 2, 32, SW>(x, w, y, K, N, RB, batch, p, scratch, st, e);
+  if (batch <= 4) return launch_gemv_t<QT, 4, 16, SW>(x, w, y, K, N, RB, batch, p, scratch, st, e);
+  if (batch <= 8) return launch_gemv_t<QT, 8, 8, SW>(x, w, y, K, N, RB, batch, p, scratch, st, e);
+  return launch_gemv_t<QT, 16, 8, SW>(x, w, y, K, N, RB, batch, p, scratch, st, e);
 }
 
 template <int QT>
-static cudaError_t launch_gemv_q(const float* x, const void* w, float* y, int64_t K, int64_t N,
+static cudaError_t launch_gemv_f(const float* x, const void* w, float* y, int64_t K, int64_t N,
                                  int64_t RB, int batch, const GemvPlan& p, void* scratch,
-                                 cudaStream_t st) {
-  if (batch <= 1) {
-    if constexpr (QT == kQ8_0) return launch_gemv_t<QT, 1, 32>(x, w, y, K, N, RB, batch, p, scratch, st);
-    else return launch_gemv_t<QT, 1, 64>(x, w, y, K, N, RB, batch, p, scratch, st);
-  }
-  if (batch <= 2) return launch_gemv_t<QT, 2, 32>(x, w, y, K, N, RB, batch, p, scratch, st);
-  if (batch <= 4) return launch_gemv_t<QT, 4, 16>(x, w, y, K, N, RB, batch, p, scratch, st);
-  if (batch <= 8) return launch_gemv_t<QT, 8, 8>(x, w, y, K, N, RB, batch, p, scratch, st);
-  return launch_gemv_t<QT, 16, 8>(x, w, y, K, N, RB, batch, p, scratch, st);
+                                 cudaStream_t st, const GemvFuse& f) {
+  const Epi e{f.bias, f.res};
+  return f.swiglu_x ? launch_gemv_q<QT, true>(x, w, y, K, N, RB, batch, p, scratch, st, e)
+                    : launch_gemv_q<QT, false>(x, w, y, K, N, RB, batch, p, scratch, st, e);
 }
 
 cudaError_t launch_gemv(int qtype, const float* x, const void* w, float* y, int64_t K, int64_t N,
                         int64_t row_bytes, int batch, const GemvPlan& plan, void* scratch,
-                        cudaStream_t st) {
+                        cudaStream_t st, const GemvFuse& f) {
   if (N % 256 != 0 || batch < 1 || batch > 16) return cudaErrorNotSupported;
   switch (qtype) {
     case kQ4_K:
       if (!scalar_override() && gemv_mma_fits(K, N, batch))
-        return launch_gemv_mma_q4k(x, w, y, K, N, row_bytes, batch, st);
-      return launch_gemv_q<kQ4_K>(x, w, y, K, N, row_bytes, batch, plan, scratch, st);
-    case kQ6_K: return launch_gemv_q<kQ6_K>(x, w, y, K, N, row_bytes, batch, plan, scratch, st);
+        return launch_gemv_mma_q4k(x, w, y, K, N, row_bytes, batch, st, f);
+      return launch_gemv_f<kQ4_K>(x, w, y, K, N, row_bytes, batch, plan, scratch, st, f);
+    case kQ6_K: return launch_gemv_f<kQ6_K>(x, w, y, K, N, row_bytes, batch, plan, scratch, st, f);
     case kQ8_0:
       if (!scalar_override() && gemv_q8_fits(K, N, batch))
-        return launch_gemv_q8_mma(x, w, y, K, N, row_bytes, batch, st);
-      return launch_gemv_q<kQ8_0>(x, w, y, K, N, row_bytes, batch, plan, scratch, st);
+        return launch_gemv_q8_mma(x, w, y, K, N, row_bytes, batch, st, f);
+      return launch_gemv_f<kQ8_0>(x, w, y, K, N, row_bytes, batch, plan, scratch, st, f);
     default: return cudaErrorInvalidValue;
   }
 }

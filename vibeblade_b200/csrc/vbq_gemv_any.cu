@@ -4,6 +4,8 @@
 //
 //   y[b, n] = sum_k x[b, k] * deq(W)[k, n]  (+ bias[n]) (+ res[b, n])
 //
+// (with the fused-input option, x[b, k] = silu(gate) * up of a packed [batch, 2K] buffer)
+//
 // (cpp/src/dequant.cpp:739-780, every type its switch at :748-763 lists that this library
 // reads).  The tiled kernels cover N % 256 == 0 in the quantized types; this one takes what
 // they do not: the MoE router (cpp/src/fast_model.cpp:861: N = n_experts, usually an F32 or
@@ -34,20 +36,19 @@ constexpr int kMaxBatch = 4;   // batch rows per CTA
 constexpr int kMaxSplit = 8;   // portable cluster size
 constexpr int kRowUnroll = 4;  // rows in flight per warp
 
-template <int QT, int B>
+template <int QT, int B, bool SWIGLU>
 __global__ void __launch_bounds__(kThreads)
-gemv_any_kernel(const float* __restrict__ x, const uint8_t* __restrict__ w, float* __restrict__ y,
-                const float* __restrict__ bias, const float* __restrict__ res, int K, int N,
-                int64_t RB, int batch, int kslice) {
+gemv_any_kernel(const float* __restrict__ x, const uint8_t* __restrict__ w, float* y, Epi epi,
+                int K, int N, int64_t RB, int batch, int kslice) {
   // [warp][b][256] partial sums, then [b][256] CTA sums (read by the cluster leader)
   __shared__ __align__(16) float red[kWarps * B * 256];
   __shared__ __align__(16) float cta_sum[B * 256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int seg = blockIdx.x, split = blockIdx.y, S = gridDim.y;
   // this CTA's group of batch rows
-  x += (int64_t)blockIdx.z * B * K;
+  x += (int64_t)blockIdx.z * B * (SWIGLU ? 2 * (int64_t)K : (int64_t)K);
   y += (int64_t)blockIdx.z * B * N;
-  if (res) res += (int64_t)blockIdx.z * B * N;
+  if (epi.res) epi.res += (int64_t)blockIdx.z * B * N;
   batch = batch - (int)blockIdx.z * B < B ? batch - (int)blockIdx.z * B : B;
   const int64_t v0 = (int64_t)seg * 256 + 8 * lane;  // first column of this lane
   const bool active = v0 < N;
@@ -80,7 +81,7 @@ gemv_any_kernel(const float* __restrict__ x, const uint8_t* __restrict__ w, floa
             decode8<QT>(unit, lane, v[u]);
           }
 #pragma unroll
-          for (int b = 0; b < B; ++b) xv[u][b] = (b < batch) ? __ldg(x + (int64_t)b * K + kk) : 0.f;
+          for (int b = 0; b < B; ++b) xv[u][b] = (b < batch) ? gemv_x<SWIGLU>(x, b, K, kk) : 0.f;
         } else {
 #pragma unroll
           for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
@@ -129,9 +130,7 @@ gemv_any_kernel(const float* __restrict__ x, const uint8_t* __restrict__ w, floa
           asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(o) : "r"(ra) : "memory");
           s += o;
         }
-        if (bias) s += __ldg(bias + n);
-        if (res) s += __ldg(res + (int64_t)b * N + n);
-        y[(int64_t)b * N + n] = s;
+        y[(int64_t)b * N + n] = epi_apply(epi, s, b, N, n);
       }
     }
   }
@@ -139,10 +138,9 @@ gemv_any_kernel(const float* __restrict__ x, const uint8_t* __restrict__ w, floa
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-template <int QT, int B>
-static cudaError_t launch_any_t(const float* x, const void* w, float* y, const float* bias,
-                                const float* res, int64_t K, int64_t N, int64_t RB, int batch,
-                                cudaStream_t st) {
+template <int QT, int B, bool SW>
+static cudaError_t launch_any_t(const float* x, const void* w, float* y, Epi epi, int64_t K,
+                                int64_t N, int64_t RB, int batch, cudaStream_t st) {
   const int segs = (int)((N + 255) / 256);
   // splits: enough CTAs for ~4 per SM, each slice at least 64 rows
   int S = (4 * sm_count() + segs - 1) / segs;
@@ -168,33 +166,40 @@ static cudaError_t launch_any_t(const float* x, const void* w, float* y, const f
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = S > 1 ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, gemv_any_kernel<QT, B>, x, static_cast<const uint8_t*>(w), y,
-                            bias, res, (int)K, (int)N, RB, batch, (int)kslice);
+  return cudaLaunchKernelEx(&cfg, gemv_any_kernel<QT, B, SW>, x, static_cast<const uint8_t*>(w), y,
+                            epi, (int)K, (int)N, RB, batch, (int)kslice);
+}
+
+template <int QT, bool SW>
+static cudaError_t launch_any_b(const float* x, const void* w, float* y, Epi epi, int64_t K,
+                                int64_t N, int64_t RB, int batch, cudaStream_t st) {
+  if (batch <= 1) return launch_any_t<QT, 1, SW>(x, w, y, epi, K, N, RB, batch, st);
+  if (batch <= 2) return launch_any_t<QT, 2, SW>(x, w, y, epi, K, N, RB, batch, st);
+  return launch_any_t<QT, 4, SW>(x, w, y, epi, K, N, RB, batch, st);
 }
 
 template <int QT>
-static cudaError_t launch_any_q(const float* x, const void* w, float* y, const float* bias,
-                                const float* res, int64_t K, int64_t N, int64_t RB, int batch,
-                                cudaStream_t st) {
-  if (batch <= 1) return launch_any_t<QT, 1>(x, w, y, bias, res, K, N, RB, batch, st);
-  if (batch <= 2) return launch_any_t<QT, 2>(x, w, y, bias, res, K, N, RB, batch, st);
-  return launch_any_t<QT, 4>(x, w, y, bias, res, K, N, RB, batch, st);
+static cudaError_t launch_any_q(const float* x, const void* w, float* y, int64_t K, int64_t N,
+                                int64_t RB, int batch, cudaStream_t st, const GemvFuse& f) {
+  const Epi epi{f.bias, f.res};
+  return f.swiglu_x ? launch_any_b<QT, true>(x, w, y, epi, K, N, RB, batch, st)
+                    : launch_any_b<QT, false>(x, w, y, epi, K, N, RB, batch, st);
 }
 
 }  // namespace gany
 
-cudaError_t launch_gemv_any(int qtype, const float* x, const void* w, float* y, const float* bias,
-                            const float* res, int64_t K, int64_t N, int64_t row_bytes, int batch,
-                            cudaStream_t st) {
+cudaError_t launch_gemv_any(int qtype, const float* x, const void* w, float* y, int64_t K,
+                            int64_t N, int64_t row_bytes, int batch, cudaStream_t st,
+                            const GemvFuse& f) {
   if (batch < 1 || K < 1 || N < 1 || K > INT32_MAX || N > INT32_MAX) return cudaErrorInvalidValue;
   if ((batch + gany::kMaxBatch - 1) / gany::kMaxBatch > 65535) return cudaErrorInvalidValue;
   switch (qtype) {
-    case kF32: return gany::launch_any_q<kF32>(x, w, y, bias, res, K, N, row_bytes, batch, st);
-    case kF16: return gany::launch_any_q<kF16>(x, w, y, bias, res, K, N, row_bytes, batch, st);
-    case kBF16: return gany::launch_any_q<kBF16>(x, w, y, bias, res, K, N, row_bytes, batch, st);
-    case kQ8_0: return gany::launch_any_q<kQ8_0>(x, w, y, bias, res, K, N, row_bytes, batch, st);
-    case kQ4_K: return gany::launch_any_q<kQ4_K>(x, w, y, bias, res, K, N, row_bytes, batch, st);
-    case kQ6_K: return gany::launch_any_q<kQ6_K>(x, w, y, bias, res, K, N, row_bytes, batch, st);
+    case kF32: return gany::launch_any_q<kF32>(x, w, y, K, N, row_bytes, batch, st, f);
+    case kF16: return gany::launch_any_q<kF16>(x, w, y, K, N, row_bytes, batch, st, f);
+    case kBF16: return gany::launch_any_q<kBF16>(x, w, y, K, N, row_bytes, batch, st, f);
+    case kQ8_0: return gany::launch_any_q<kQ8_0>(x, w, y, K, N, row_bytes, batch, st, f);
+    case kQ4_K: return gany::launch_any_q<kQ4_K>(x, w, y, K, N, row_bytes, batch, st, f);
+    case kQ6_K: return gany::launch_any_q<kQ6_K>(x, w, y, K, N, row_bytes, batch, st, f);
     default: return cudaErrorInvalidValue;
   }
 }

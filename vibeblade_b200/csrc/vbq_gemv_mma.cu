@@ -88,10 +88,10 @@ template <int NSET> struct Lay {
 };
 constexpr int kMaxSplit = 16;  // cluster size limit (non-portable above 8)
 
-template <int BATCH>
+template <int BATCH, bool SWIGLU>
 __global__ void __launch_bounds__(kThreads, BATCH <= 2 ? 2 : 1)
 gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restrict__ x,
-                float* __restrict__ y, int K, int N, int batch) {
+                float* y, int K, int N, int batch, Epi epi) {
   constexpr int NSET = BATCH <= 2 ? 1 : 2;  // B column sets: two batch rows per set
   extern __shared__ uint8_t smem_raw[];
   // 128-byte aligned: TMA destinations and ldmatrix rows
@@ -248,9 +248,8 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
       auto load_x = [&](int k, float2 (&xv)[BATCH]) {
 #pragma unroll
         for (int b = 0; b < BATCH; ++b) {
-          const float* xb = x + (int64_t)b * K;
-          xv[b].x = (b < batch && k < K) ? __ldg(xb + k) : 0.f;
-          xv[b].y = (b < batch && k + 1 < K) ? __ldg(xb + k + 1) : 0.f;
+          xv[b].x = (b < batch && k < K) ? gemv_x<SWIGLU>(x, b, K, k) : 0.f;
+          xv[b].y = (b < batch && k + 1 < K) ? gemv_x<SWIGLU>(x, b, K, k + 1) : 0.f;
         }
       };
       load_x(kx, xn);
@@ -452,7 +451,7 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
 
   if (S == 1) {
     for (int e = threadIdx.x; e < E; e += kThreads)
-      y[(int64_t)(e >> 8) * N + tile * 256 + (e & 255)] = outbuf[e];
+      y[(int64_t)(e >> 8) * N + tile * 256 + (e & 255)] = epi_apply(epi, outbuf[e], e >> 8, N, tile * 256 + (e & 255));
     return;
   }
   // ---- split-K inside the cluster: splits 1 .. S-1 push their partials into the leader's
@@ -472,7 +471,7 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
   for (int e = threadIdx.x; e < E; e += kThreads) {
     float sum = outbuf[e];
     for (int sp = 1; sp < S; ++sp) sum += recv[(sp - 1) * E + e];
-    y[(int64_t)(e >> 8) * N + tile * 256 + (e & 255)] = sum;
+    y[(int64_t)(e >> 8) * N + tile * 256 + (e & 255)] = epi_apply(epi, sum, e >> 8, N, tile * 256 + (e & 255));
   }
 }
 
@@ -502,7 +501,7 @@ static EncodeTiledFnG encode_fn_g() {
 // tile's cluster at once with 25 % to spare (cudaOccupancyMaxActiveClusters, cached per
 // shape).  Measured on B200 (us per launch, batch 1): 4096 x 14336 S = 4: 11.6, S = 5
 // (56 clusters in 56-59 places): 16.3; 4096 x 6144 S = 8: 8.3, S = 12: 11.7.
-template <int BATCH>
+template <int BATCH, bool SW>
 static int choose_splits(int64_t K, int64_t N, int batch, int smem_base) {
   using namespace gmma;
   const int tiles = (int)(N / 256);
@@ -541,7 +540,7 @@ static int choose_splits(int64_t K, int64_t N, int batch, int smem_base) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int active = 0;
-    if (cudaOccupancyMaxActiveClusters(&active, gmma::gemv_mma_kernel<BATCH>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&active, gmma::gemv_mma_kernel<BATCH, SW>, &cfg) != cudaSuccess) {
       cudaGetLastError();
       active = 0;
     }
@@ -554,9 +553,9 @@ static int choose_splits(int64_t K, int64_t N, int batch, int smem_base) {
   return S;
 }
 
-template <int BATCH>
+template <int BATCH, bool SWIGLU>
 static cudaError_t launch_t(const float* x, const void* w, float* y, int64_t K, int64_t N,
-                            int64_t RB, int batch, cudaStream_t st) {
+                            int64_t RB, int batch, cudaStream_t st, Epi epi) {
   using namespace gmma;
   auto enc = encode_fn_g();
   if (!enc) return cudaErrorNotSupported;
@@ -569,7 +568,7 @@ static cudaError_t launch_t(const float* x, const void* w, float* y, int64_t K, 
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
-  auto kern = gemv_mma_kernel<BATCH>;
+  auto kern = gemv_mma_kernel<BATCH, SWIGLU>;
   constexpr int kBase = Lay<(BATCH <= 2 ? 1 : 2)>::kSmem;
   static DeviceOnce configured;
   int dev = 0;
@@ -582,7 +581,7 @@ static cudaError_t launch_t(const float* x, const void* w, float* y, int64_t K, 
     if (e != cudaSuccess) return e;
     configured.mark(dev);
   }
-  const int S = choose_splits<BATCH>(K, N, batch, kBase);
+  const int S = choose_splits<BATCH, SWIGLU>(K, N, batch, kBase);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(N / 256), (unsigned)S, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -597,7 +596,7 @@ static cudaError_t launch_t(const float* x, const void* w, float* y, int64_t K, 
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = S > 1 ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, kern, mw, x, y, (int)K, (int)N, batch);
+  return cudaLaunchKernelEx(&cfg, kern, mw, x, y, (int)K, (int)N, batch, epi);
 }
 
 // Whether the tensor-core kernel takes this call (batch 1..16).  The s32 sums run over up
@@ -613,18 +612,28 @@ bool gemv_mma_fits(int64_t K, int64_t N, int batch) {
 // consecutive launches over groups of 4 batch rows (each streams the weights again).
 // Measured on B200, 4096 x 14336: batch 8 grouped 33.2 us / wide 31.3 us; batch 16
 // grouped 64.5 us / wide 51.9 us.
+template <bool SW>
+static cudaError_t launch_group(const float* x, const void* w, float* y, int64_t K, int64_t N,
+                                int64_t row_bytes, int nb, cudaStream_t st, Epi epi) {
+  return nb == 1   ? launch_t<1, SW>(x, w, y, K, N, row_bytes, nb, st, epi)
+         : nb == 2 ? launch_t<2, SW>(x, w, y, K, N, row_bytes, nb, st, epi)
+                   : launch_t<4, SW>(x, w, y, K, N, row_bytes, nb, st, epi);
+}
+
 cudaError_t launch_gemv_mma_q4k(const float* x, const void* w, float* y, int64_t K, int64_t N,
-                                int64_t row_bytes, int batch, cudaStream_t st) {
+                                int64_t row_bytes, int batch, cudaStream_t st, const GemvFuse& f) {
   if (!gemv_mma_fits(K, N, batch) || row_bytes % 16 != 0) return cudaErrorNotSupported;
-  if (batch > 4 && gemv_wide_fits(x, K, N, batch))
-    return launch_gemv_wide_q4k(x, w, y, K, N, row_bytes, batch, st);
+  // the wide kernel reads x by TMA, so a SwiGLU input runs in groups of 4 here
+  if (batch > 4 && !f.swiglu_x && gemv_wide_fits(x, K, N, batch))
+    return launch_gemv_wide_q4k(x, w, y, K, N, row_bytes, batch, st, f);
+  const int64_t xrow = f.swiglu_x ? 2 * K : K;
   for (int b0 = 0; b0 < batch; b0 += 4) {
     const int nb = batch - b0 < 4 ? batch - b0 : 4;
-    const float* xg = x + (int64_t)b0 * K;
+    const float* xg = x + (int64_t)b0 * xrow;
     float* yg = y + (int64_t)b0 * N;
-    cudaError_t e = nb == 1   ? launch_t<1>(xg, w, yg, K, N, row_bytes, nb, st)
-                    : nb == 2 ? launch_t<2>(xg, w, yg, K, N, row_bytes, nb, st)
-                              : launch_t<4>(xg, w, yg, K, N, row_bytes, nb, st);
+    const Epi epi{f.bias, f.res ? f.res + (int64_t)b0 * N : nullptr};
+    cudaError_t e = f.swiglu_x ? launch_group<true>(xg, w, yg, K, N, row_bytes, nb, st, epi)
+                               : launch_group<false>(xg, w, yg, K, N, row_bytes, nb, st, epi);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;

@@ -72,10 +72,10 @@ __device__ __forceinline__ uint32_t lds_u16(uint32_t saddr) {
   return (uint32_t)v;
 }
 
-template <int BATCH>
+template <int BATCH, bool SWIGLU>
 __global__ void __launch_bounds__(kThreads, 2)
 gemv_q8_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restrict__ x,
-               float* __restrict__ y, int K, int N, int batch) {
+               float* y, int K, int N, int batch, Epi epi) {
   constexpr int NSET = BATCH <= 2 ? 1 : 2;  // B column sets: two batch rows per set
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
@@ -194,9 +194,8 @@ gemv_q8_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restri
     auto load_x = [&](int k, float2 (&xv)[BATCH]) {
 #pragma unroll
       for (int b = 0; b < BATCH; ++b) {
-        const float* xb = x + (int64_t)b * K;
-        xv[b].x = (b < batch && k < K) ? __ldg(xb + k) : 0.f;
-        xv[b].y = (b < batch && k + 1 < K) ? __ldg(xb + k + 1) : 0.f;
+        xv[b].x = (b < batch && k < K) ? gemv_x<SWIGLU>(x, b, K, k) : 0.f;
+        xv[b].y = (b < batch && k + 1 < K) ? gemv_x<SWIGLU>(x, b, K, k + 1) : 0.f;
       }
     };
     float2 xn[BATCH], xnn[BATCH];
@@ -316,7 +315,7 @@ gemv_q8_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restri
   __syncthreads();
   if (S == 1) {
     for (int e = threadIdx.x; e < E; e += kThreads)
-      y[(int64_t)(e >> 8) * N + tile * 256 + (e & 255)] = outbuf[e];
+      y[(int64_t)(e >> 8) * N + tile * 256 + (e & 255)] = epi_apply(epi, outbuf[e], e >> 8, N, tile * 256 + (e & 255));
     return;
   }
   // ---- split-K inside the cluster (as vbq_gemv_mma.cu) ----
@@ -335,7 +334,7 @@ gemv_q8_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restri
   for (int e = threadIdx.x; e < E; e += kThreads) {
     float sum = outbuf[e];
     for (int sp = 1; sp < S; ++sp) sum += recv[(sp - 1) * E + e];
-    y[(int64_t)(e >> 8) * N + tile * 256 + (e & 255)] = sum;
+    y[(int64_t)(e >> 8) * N + tile * 256 + (e & 255)] = epi_apply(epi, sum, e >> 8, N, tile * 256 + (e & 255));
   }
 }
 
@@ -362,7 +361,7 @@ static EncodeTiledFnQ encode_fn_q() {
 
 // Splits per tile as for the Q4_K kernel: one wave of two CTAs per SM, at most 16, the
 // leader's receive slots inside the shared memory budget, 25 % spare cluster places.
-template <int BATCH>
+template <int BATCH, bool SW>
 static int choose_splits_q8(int64_t K, int64_t N, int batch, int smem_base) {
   using namespace gq8;
   const int tiles = (int)(N / 256);
@@ -400,7 +399,7 @@ static int choose_splits_q8(int64_t K, int64_t N, int batch, int smem_base) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int active = 0;
-    if (cudaOccupancyMaxActiveClusters(&active, gemv_q8_kernel<BATCH>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&active, gemv_q8_kernel<BATCH, SW>, &cfg) != cudaSuccess) {
       cudaGetLastError();
       active = 0;
     }
@@ -410,9 +409,9 @@ static int choose_splits_q8(int64_t K, int64_t N, int batch, int smem_base) {
   return S;
 }
 
-template <int BATCH>
+template <int BATCH, bool SWIGLU>
 static cudaError_t launch_q8_t(const float* x, const void* w, float* y, int64_t K, int64_t N,
-                               int64_t RB, int batch, cudaStream_t st) {
+                               int64_t RB, int batch, cudaStream_t st, Epi epi) {
   using namespace gq8;
   auto enc = encode_fn_q();
   if (!enc) return cudaErrorNotSupported;
@@ -425,7 +424,7 @@ static cudaError_t launch_q8_t(const float* x, const void* w, float* y, int64_t 
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
-  auto kern = gemv_q8_kernel<BATCH>;
+  auto kern = gemv_q8_kernel<BATCH, SWIGLU>;
   constexpr int kBase = Lay<(BATCH <= 2 ? 1 : 2)>::kSmem;
   static DeviceOnce configured;
   int dev = 0;
@@ -438,7 +437,7 @@ static cudaError_t launch_q8_t(const float* x, const void* w, float* y, int64_t 
     if (e != cudaSuccess) return e;
     configured.mark(dev);
   }
-  const int S = choose_splits_q8<BATCH>(K, N, batch, kBase);
+  const int S = choose_splits_q8<BATCH, SWIGLU>(K, N, batch, kBase);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(N / 256), (unsigned)S, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -453,7 +452,7 @@ static cudaError_t launch_q8_t(const float* x, const void* w, float* y, int64_t 
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = S > 1 ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, kern, mw, x, y, (int)K, (int)N, batch);
+  return cudaLaunchKernelEx(&cfg, kern, mw, x, y, (int)K, (int)N, batch, epi);
 }
 
 // The s32 sums run over up to K / 2 rows per accumulator with terms of at most 128 * 128
@@ -463,16 +462,25 @@ bool gemv_q8_fits(int64_t K, int64_t N, int batch) {
 }
 
 // Tensor-core Q8_0 GEMV; batches above 4 run as launches over groups of 4 batch rows.
+template <bool SW>
+static cudaError_t launch_q8_group(const float* x, const void* w, float* y, int64_t K, int64_t N,
+                                   int64_t row_bytes, int nb, cudaStream_t st, Epi epi) {
+  return nb == 1   ? launch_q8_t<1, SW>(x, w, y, K, N, row_bytes, nb, st, epi)
+         : nb == 2 ? launch_q8_t<2, SW>(x, w, y, K, N, row_bytes, nb, st, epi)
+                   : launch_q8_t<4, SW>(x, w, y, K, N, row_bytes, nb, st, epi);
+}
+
 cudaError_t launch_gemv_q8_mma(const float* x, const void* w, float* y, int64_t K, int64_t N,
-                               int64_t row_bytes, int batch, cudaStream_t st) {
+                               int64_t row_bytes, int batch, cudaStream_t st, const GemvFuse& f) {
   if (!gemv_q8_fits(K, N, batch) || row_bytes % 16 != 0) return cudaErrorNotSupported;
+  const int64_t xrow = f.swiglu_x ? 2 * K : K;
   for (int b0 = 0; b0 < batch; b0 += 4) {
     const int nb = batch - b0 < 4 ? batch - b0 : 4;
-    const float* xg = x + (int64_t)b0 * K;
+    const float* xg = x + (int64_t)b0 * xrow;
     float* yg = y + (int64_t)b0 * N;
-    cudaError_t e = nb == 1   ? launch_q8_t<1>(xg, w, yg, K, N, row_bytes, nb, st)
-                    : nb == 2 ? launch_q8_t<2>(xg, w, yg, K, N, row_bytes, nb, st)
-                              : launch_q8_t<4>(xg, w, yg, K, N, row_bytes, nb, st);
+    const Epi epi{f.bias, f.res ? f.res + (int64_t)b0 * N : nullptr};
+    cudaError_t e = f.swiglu_x ? launch_q8_group<true>(xg, w, yg, K, N, row_bytes, nb, st, epi)
+                               : launch_q8_group<false>(xg, w, yg, K, N, row_bytes, nb, st, epi);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;

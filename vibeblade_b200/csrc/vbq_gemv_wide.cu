@@ -80,7 +80,7 @@ struct Bars {
 template <int BATCH>
 __global__ void __launch_bounds__(kThreads, BATCH <= 8 ? 2 : 1)
 gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
-                 float* __restrict__ y, int K, int N, int batch) {
+                 float* y, int K, int N, int batch, Epi epi) {
   using C = Cfg<BATCH>;
   constexpr int NSET = C::kSets;
   extern __shared__ uint8_t smem_raw[];
@@ -396,7 +396,7 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
 
   if (S == 1) {
     for (int e = threadIdx.x; e < batch * 256; e += kThreads)
-      y[(int64_t)(e >> 8) * N + tile * 256 + (e & 255)] = outp[e];
+      y[(int64_t)(e >> 8) * N + tile * 256 + (e & 255)] = epi_apply(epi, outp[e], e >> 8, N, tile * 256 + (e & 255));
     return;
   }
   // ---- split-K across the cluster: CTA r adds columns n0 .. n1 - 1 of every split's
@@ -411,7 +411,7 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
     const uint32_t off = (uint32_t)((b * 256 + n) * 4);
     float sum = 0.f;
     for (int sp = 0; sp < S; ++sp) sum += ld_cluster_f32(mapa_u32(base + off, (uint32_t)sp));
-    y[(int64_t)b * N + tile * 256 + n] = sum;
+    y[(int64_t)b * N + tile * 256 + n] = epi_apply(epi, sum, b, N, tile * 256 + n);
   }
   cluster_sync_all();
 }
@@ -486,7 +486,7 @@ static int choose_splits_wide(int64_t K, int64_t N) {
 
 template <int BATCH>
 static cudaError_t launch_wide_t(const float* x, const void* w, float* y, int64_t K, int64_t N,
-                                 int64_t RB, int batch, cudaStream_t st) {
+                                 int64_t RB, int batch, cudaStream_t st, Epi epi) {
   using namespace gwide;
   using C = Cfg<BATCH>;
   auto enc = encode_fn_w();
@@ -539,7 +539,7 @@ static cudaError_t launch_wide_t(const float* x, const void* w, float* y, int64_
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = S > 1 ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, kern, mw, mx, y, (int)K, (int)N, batch);
+  return cudaLaunchKernelEx(&cfg, kern, mw, mx, y, (int)K, (int)N, batch, epi);
 }
 
 // The wide kernel reads x through a TMA tensor map: rows of x 16-byte aligned.
@@ -551,10 +551,12 @@ bool gemv_wide_fits(const float* x, int64_t K, int64_t N, int batch) {
 }
 
 cudaError_t launch_gemv_wide_q4k(const float* x, const void* w, float* y, int64_t K, int64_t N,
-                                 int64_t row_bytes, int batch, cudaStream_t st) {
-  if (!gemv_wide_fits(x, K, N, batch) || row_bytes % 16 != 0) return cudaErrorNotSupported;
-  if (batch <= 8) return launch_wide_t<8>(x, w, y, K, N, row_bytes, batch, st);
-  return launch_wide_t<16>(x, w, y, K, N, row_bytes, batch, st);
+                                 int64_t row_bytes, int batch, cudaStream_t st, const GemvFuse& f) {
+  // x arrives by TMA as it is stored: no SwiGLU input here (the caller routes that away)
+  if (!gemv_wide_fits(x, K, N, batch) || row_bytes % 16 != 0 || f.swiglu_x) return cudaErrorNotSupported;
+  const Epi epi{f.bias, f.res};
+  if (batch <= 8) return launch_wide_t<8>(x, w, y, K, N, row_bytes, batch, st, epi);
+  return launch_wide_t<16>(x, w, y, K, N, row_bytes, batch, st, epi);
 }
 
 cudaError_t gemv_wide_status(unsigned* out, bool clear) {

@@ -475,7 +475,6 @@ int vbq_gguf_upload(vbq_gguf* g, int64_t i, int64_t row0, int64_t row1, int64_t 
                     void* dst, int64_t dst_row_bytes, void* stream) {
   const Tensor* t = tensor_at(g, i);
   if (!t) return fail(VBQ_ERR_SHAPE, "vbq_gguf_upload: no tensor " + std::to_string(i));
-  if (!dst) return fail(VBQ_ERR_NULL, "vbq_gguf_upload: dst is NULL");
   // the tensor as K rows of N values (dims[0] = N, the rest = K), the layout gemv_dequant reads
   const int64_t N = t->dims[0];
   int64_t K = 1;
@@ -489,6 +488,7 @@ int vbq_gguf_upload(vbq_gguf* g, int64_t i, int64_t row0, int64_t row1, int64_t 
                                    ") is outside '" + t->name + "' or not block-aligned");
   const uint8_t* src = nullptr;
   if (int rc = tensor_bytes(g, *t, &src)) return rc;
+  if (!dst && row1 > row0 && col1 > col0) return fail(VBQ_ERR_NULL, "vbq_gguf_upload: dst is NULL");
   const int64_t rb = (N / bv) * bb;
   const int64_t wb = ((col1 - col0) / bv) * bb;  // bytes of a shard row
   if (dst_row_bytes < wb) return fail(VBQ_ERR_SHAPE, "vbq_gguf_upload: dst_row_bytes below the shard's row bytes");

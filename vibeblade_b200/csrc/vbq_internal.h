@@ -25,6 +25,15 @@ struct DeviceOnce {
 cudaError_t launch_dequant(int qtype, const void* w, void* out, int64_t rows, int64_t n,
                            int64_t row_bytes, int out_dtype, cudaStream_t st);
 
+// Optional fusions of a GEMV call (vbq_gemv_ex): the input as SwiGLU of a packed gate | up
+// buffer [batch, 2K] (x then points there), and a bias [N] and a residual [batch, N] added
+// to the output (the residual may be y itself).
+struct GemvFuse {
+  bool swiglu_x = false;
+  const float* bias = nullptr;
+  const float* res = nullptr;
+};
+
 // Split-K plan of the fused dequant-GEMV for the current device.
 struct GemvPlan {
   int splits;            // CTAs per 256-column tile along K
@@ -43,14 +52,14 @@ int gemv_split_override();  // VBQ_GEMV_SPLIT (tuning), 0 when unset
 // shapes the kernels do not cover (the C-ABI layer checks shapes first).
 cudaError_t launch_gemv(int qtype, const float* x, const void* w, float* y, int64_t K,
                         int64_t N, int64_t row_bytes, int batch, const GemvPlan& plan,
-                        void* scratch, cudaStream_t st);
+                        void* scratch, cudaStream_t st, const GemvFuse& f = GemvFuse{});
 
 // Generic GEMV (vbq_gemv_any.cu): any type (F32, F16, BF16, Q8_0, Q4_K, Q6_K), any N that
 // is a multiple of the block, any batch (groups of 4 rows on the grid), optional bias [N]
 // and residual [batch, N] added to the output; no scratch.
-cudaError_t launch_gemv_any(int qtype, const float* x, const void* w, float* y, const float* bias,
-                            const float* res, int64_t K, int64_t N, int64_t row_bytes, int batch,
-                            cudaStream_t st);
+cudaError_t launch_gemv_any(int qtype, const float* x, const void* w, float* y, int64_t K,
+                            int64_t N, int64_t row_bytes, int batch, cudaStream_t st,
+                            const GemvFuse& f = GemvFuse{});
 
 // Tensor-core (integer mma.sync) Q4_K GEMV, batch 1..16, when gemv_mma_fits(); the K-splits
 // of a tile form one thread-block cluster and add up in the leader's shared memory.
@@ -58,19 +67,30 @@ bool gemv_mma_fits(int64_t K, int64_t N, int batch);
 // Tensor-core Q8_0 GEMV (vbq_gemv_q8.cu), batch 1..16 (groups of 4 above 4), no scratch.
 bool gemv_q8_fits(int64_t K, int64_t N, int batch);
 cudaError_t launch_gemv_q8_mma(const float* x, const void* w, float* y, int64_t K, int64_t N,
-                               int64_t row_bytes, int batch, cudaStream_t st);
+                               int64_t row_bytes, int batch, cudaStream_t st,
+                               const GemvFuse& f = GemvFuse{});
 cudaError_t gemv_q8_status(unsigned* out, bool clear);
 // Batch 5..16 kernel (vbq_gemv_wide.cu): x read by TMA, so rows of x 16-byte aligned.
 bool gemv_wide_fits(const float* x, int64_t K, int64_t N, int batch);
 cudaError_t launch_gemv_wide_q4k(const float* x, const void* w, float* y, int64_t K, int64_t N,
-                                 int64_t row_bytes, int batch, cudaStream_t st);
+                                 int64_t row_bytes, int batch, cudaStream_t st,
+                                 const GemvFuse& f = GemvFuse{});
 cudaError_t gemv_wide_status(unsigned* out, bool clear);
 cudaError_t launch_gemv_mma_q4k(const float* x, const void* w, float* y, int64_t K, int64_t N,
-                                int64_t row_bytes, int batch, cudaStream_t st);
+                                int64_t row_bytes, int batch, cudaStream_t st,
+                                const GemvFuse& f = GemvFuse{});
+
+// Optional epilogue of the GEMM: bias fp32 [N] and a residual [M, N] of c's element type
+// (it may be c itself) added to the fp32 accumulator before the store.
+struct GemmEpi {
+  const float* bias = nullptr;
+  const void* res = nullptr;
+};
 
 // tcgen05 dequant-GEMM: a bf16 [M,K], W K x N blocks, c fp32 (c_dtype 0) / bf16 (1) [M,N].
 cudaError_t launch_gemm(int qtype, const void* a, const void* w, void* c, int64_t M, int64_t K,
-                        int64_t N, int64_t row_bytes, int c_dtype, cudaStream_t st);
+                        int64_t N, int64_t row_bytes, int c_dtype, cudaStream_t st,
+                        const GemmEpi& ep = GemmEpi{});
 // Grouped form: rows of A / C split by the device array seg[0..n_seg] into segments,
 // segment s multiplied by the K x N slab at w + s * slab_bytes.
 cudaError_t launch_gemm_grouped(int qtype, const void* a, const void* w, void* c, int64_t rows,

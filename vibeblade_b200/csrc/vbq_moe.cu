@@ -17,6 +17,7 @@
 
 #include <type_traits>
 
+#include "vbq_common.cuh"
 #include "vbq_internal.h"
 
 namespace vbq {
@@ -190,17 +191,7 @@ __global__ void gather_kernel(const float* __restrict__ x, const int32_t* __rest
   }
 }
 
-// nan -> 0, +-inf -> +-65504, then clip to +-65504 (vibeblade/moe.py:472-473)
-__device__ __forceinline__ float sanitize(float v) {
-  if (v != v) return 0.0f;
-  return fminf(fmaxf(v, -65504.0f), 65504.0f);
-}
-// x * sigmoid(x) = x / (1 + e^-x), the reference's two-sided form (vibeblade/moe.py:36-50)
-// written without its branch: for the sanitised inputs (|x| <= 65504) e^-x is +inf only
-// where x < -88, and the quotient is then -0, as in the two-sided form.  expf is the full-
-// precision exponential; __fdividef is within 2 ulp for every denominator here (>= 1).
-// Branch-free, so a warp whose inputs have both signs does not run both halves.
-__device__ __forceinline__ float silu_ref(float x) { return __fdividef(x, 1.0f + expf(-x)); }
+// sanitize() and silu_ref() are in vbq_common.cuh (shared with the fused GEMV input).
 
 // silu(g) * u on 8 bf16 / 4 fp32 values (one 16-byte vector of each), inputs sanitised
 __device__ __forceinline__ uint4 swiglu_vec(uint4 gv, uint4 uv, std::true_type /*bf16*/) {

@@ -176,3 +176,50 @@ def gemv_dequant_mt(x: torch.Tensor, weights: torch.Tensor, out: torch.Tensor | 
     """``gemv_dequant_mt`` (cpp/include/dequant.h:39-48).  The reference ignores
     n_threads; here the whole GPU runs the call, so it is ignored as well."""
     return gemv_dequant(x, weights, out, K, N, wtype, scratch)
+
+
+def gemv_fused(x: torch.Tensor, weights: torch.Tensor, out: torch.Tensor | None, K: int, N: int,
+               wtype, bias: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+               swiglu_input: bool = False, scratch: torch.Tensor | None = None) -> torch.Tensor:
+    """``gemv_dequant`` with the element-wise steps around it fused in (vbq_gemv_ex):
+
+    * ``swiglu_input``: ``x`` is [B, 2K], the output of a gate | up matmul, and the GEMV's
+      input is silu(gate) * up (cpp/src/fast_model.cpp:946-953) -- the down projection
+      without a SwiGLU pass;
+    * ``bias`` fp32 [N] is added to every row (Q/K/V biases, :659-668);
+    * ``residual`` fp32 [B, N] is added as well (the residual adds after o and down); it may
+      be ``out`` itself for an in-place update.
+    """
+    t = F.parse_type(wtype)
+    _require_cuda("gemv_fused", x, weights)
+    if x.dtype != torch.float32:
+        raise RuntimeError("gemv_fused: x must be float32")
+    kx = 2 * K if swiglu_input else K
+    if K <= 0 or x.numel() % kx != 0:
+        raise RuntimeError(f"gemv_fused: x has {x.numel()} values, not a multiple of {kx}")
+    batch = x.numel() // kx
+    w = _weights_u8(weights)
+    if w.numel() < F.row_bytes(t, N) * K:
+        raise RuntimeError(f"gemv_fused: weights hold {w.numel()} bytes, need {F.row_bytes(t, N) * K}")
+    for name, v, n in (("bias", bias, N), ("residual", residual, batch * N)):
+        if v is not None:
+            _require_cuda("gemv_fused", v)
+            if v.dtype != torch.float32 or v.numel() != n:
+                raise RuntimeError(f"gemv_fused: {name} must be float32 with {n} values")
+    if out is None:
+        out = torch.empty((batch, N), dtype=torch.float32, device=x.device)
+    else:
+        _require_cuda("gemv_fused", out)
+        if out.dtype != torch.float32 or out.numel() != batch * N:
+            raise RuntimeError("gemv_fused: out must be float32 with batch*N values")
+    lib = _lib.load()
+    sp = _stream_ptr(x)
+    need = gemv_scratch_bytes(K, N, t, batch)
+    scr = (_stream_scratch(x.device, sp, need) if need else None) if scratch is None else scratch
+    _lib.check(lib.vbq_gemv_ex(x.data_ptr(), w.data_ptr(), out.data_ptr(), K, N, t, batch,
+                               1 if swiglu_input else 0,
+                               bias.data_ptr() if bias is not None else None,
+                               residual.data_ptr() if residual is not None else None,
+                               scr.data_ptr() if scr is not None else None,
+                               scr.numel() * scr.element_size() if scr is not None else 0, sp), lib)
+    return out

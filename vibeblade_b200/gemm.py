@@ -14,9 +14,12 @@ from .dequant import _require_cuda, _stream_ptr, _weights_u8
 
 
 def gemm_dequant(a: torch.Tensor, weights: torch.Tensor, out: torch.Tensor | None, M: int,
-                 K: int, N: int, wtype, out_dtype=torch.float32) -> torch.Tensor:
+                 K: int, N: int, wtype, out_dtype=torch.float32, bias: torch.Tensor | None = None,
+                 residual: torch.Tensor | None = None) -> torch.Tensor:
     """a: bf16 [M, K] CUDA tensor; weights: the K x N block bytes; returns [M, N] in
-    out_dtype (torch.float32 or torch.bfloat16)."""
+    out_dtype (torch.float32 or torch.bfloat16).  Optional epilogue (vbq_gemm_ex): ``bias``
+    fp32 [N] and ``residual`` [M, N] of out_dtype (may be ``out`` itself) are added to the
+    fp32 accumulator before the one rounding to out_dtype."""
     t = F.parse_type(wtype)
     _require_cuda("gemm_dequant", a, weights)
     if a.dtype != torch.bfloat16:
@@ -37,8 +40,22 @@ def gemm_dequant(a: torch.Tensor, weights: torch.Tensor, out: torch.Tensor | Non
             raise RuntimeError("gemm_dequant: out has the wrong dtype or size")
     lib = _lib.load()
     cd = _lib.DTYPE_F32 if out_dtype == torch.float32 else _lib.DTYPE_BF16
-    _lib.check(lib.vbq_gemm(a.data_ptr(), w.data_ptr(), out.data_ptr(), M, K, N, t, cd,
-                            _stream_ptr(a)), lib)
+    if bias is None and residual is None:
+        _lib.check(lib.vbq_gemm(a.data_ptr(), w.data_ptr(), out.data_ptr(), M, K, N, t, cd,
+                                _stream_ptr(a)), lib)
+        return out
+    if bias is not None:
+        _require_cuda("gemm_dequant", bias)
+        if bias.dtype != torch.float32 or bias.numel() != N:
+            raise RuntimeError("gemm_dequant: bias must be float32 [N]")
+    if residual is not None:
+        _require_cuda("gemm_dequant", residual)
+        if residual.dtype != out_dtype or residual.numel() != M * N:
+            raise RuntimeError("gemm_dequant: residual must be [M, N] of out_dtype")
+    _lib.check(lib.vbq_gemm_ex(a.data_ptr(), w.data_ptr(), out.data_ptr(), M, K, N, t, cd,
+                               bias.data_ptr() if bias is not None else None,
+                               residual.data_ptr() if residual is not None else None,
+                               _stream_ptr(a)), lib)
     return out
 
 
