@@ -2,7 +2,9 @@
 
 Default workload: one Llama-8B decode layer in Q4_K at batch 1 --
 the five projections QKV 4096x6144, o 4096x4096, gate and up 4096x14336, down 14336x4096 --
-as fused dequant-GEMVs.  A step is one pass over the layer.  Weights are synthetic
+as fused dequant-GEMVs, in the engine's layout (vibeblade_b200.engine: gate and up packed
+into one 4096x28672 matrix, so four launches; the same bytes).  A step is one pass over the
+layer.  Weights are synthetic
 (N(0, 0.02), seed 0, quantized by vibeblade_b200.quantize); six distinct copies of the
 layer rotate so every step streams weights that are not in the 126 MB L2.
 
@@ -61,10 +63,23 @@ def make_inputs(dev, batch: int, n_copies: int, rank: int):
     return layers, xs
 
 
+def pack_gate_up(layer):
+    """The engine layout of one layer copy (vibeblade_b200.engine.DeviceLayer): gate and up
+    side by side in one K x 2N block matrix (each row: gate's blocks, then up's), one launch
+    for both; the same bytes as the two matrices."""
+    import torch
+    (kq, nq, wq), (ko, no, wo), (kg, ng, wg), (_, nu, wu), down = layer
+    gu = torch.cat([wg.view(kg, -1), wu.view(kg, -1)], dim=1).contiguous()
+    return [(kq, nq, wq), (ko, no, wo), (kg, ng + nu, gu), down]
+
+
 def bench_config(batch: int, n_copies: int, world: int) -> dict:
     """The workload description both arms print (the same dict in both)."""
     return {"workload": "llama8b_decode_layer_q4k", "batch": batch,
             "matrices": [f"{n} {k}x{m}" for n, k, m in LAYER_8B],
+            "gate_up": "the GPU arm runs gate and up as one packed 4096x28672 matrix (the engine "
+                       "layout, vibeblade_b200.engine), the reference arm as two gemv_dequant "
+                       "calls; the same weight bytes and the same algorithmic bytes per step",
             "weights": "N(0,0.02) quantized Q4_K, seed 1000*rank + 10*copy + matrix; x N(0,1) seed 1",
             "layer_copies_rotated": n_copies,
             "l2": f"inputs larger than L2: {n_copies} distinct layer copies "
@@ -463,11 +478,17 @@ def run_gpu(args) -> None:
     n_copies = args.copies
     # weights: n_copies distinct layers (distinct seeds per rank and copy)
     layers, xs = make_inputs(dev, B, n_copies, rank)
+    # the CPU baseline reads rank 0's five matrices before they are packed
+    layers_np = [[(K, N, w.cpu().numpy()) for K, N, w in layer] for layer in layers] \
+        if rank == 0 and not args.no_cpu_baseline else None
+    layers = [pack_gate_up(layer) for layer in layers]  # the engine layout: 4 launches per step
+    launch_shapes = [(K, N) for K, N, _ in layers[0]]
+    torch.cuda.empty_cache()
     g = torch.Generator(device=dev).manual_seed(101)  # other batch sizes' activations
-    ys = [torch.empty(B, N, device=dev) for _, _, N in LAYER_8B]
+    ys = [torch.empty(B, N, device=dev) for _, N in launch_shapes]
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
-    need = max(vb.gemv_scratch_bytes(K, N, QTYPE, B) for _, K, N in LAYER_8B)
+    need = max(vb.gemv_scratch_bytes(K, N, QTYPE, B) for K, N in launch_shapes)
     scratch = torch.zeros(max(need, 16), dtype=torch.uint8, device=dev)
     sptr, sbytes = scratch.data_ptr(), scratch.numel()
 
@@ -482,7 +503,7 @@ def run_gpu(args) -> None:
         launch_layer(s % n_copies, sp)
     torch.cuda.synchronize()
     # Decode steps are replayed from a CUDA graph, as a decode engine runs them: one graph
-    # holds a full rotation of the layer copies (n_copies steps, their GEMV launches chained
+    # holds a full rotation of the layer copies (n_copies steps, their 4 GEMV launches chained
     # with programmatic dependent launch, which a graph keeps), and a count of steps that is
     # not a multiple of n_copies ends with eager steps.  --no-graph launches eagerly.
     graph = None
@@ -533,24 +554,31 @@ def run_gpu(args) -> None:
     # Every launch in the timed region is the GEMV kernel, queued back to back with
     # programmatic dependent launch, so the average launch duration is the timed region
     # divided by the launches and `achieved` equals `value`.  (Per-launch events would
-    # serialise the launches and hide the overlap.)  The dominant shape, gate/up
-    # 4096x14336 (48% of kernel time in the ncu launch list), is also timed on its own.
+    # serialise the launches and hide the overlap.)  The dominant shape, the packed gate|up
+    # 4096x28672, and config 2's 4096x14336 alone are also timed on their own.
     achieved = value / world
-    big_mats = [w for layer in layers for (K, N, w) in layer if (K, N) == (4096, 14336)]
-    big_y = torch.empty(B, 14336, device=dev)
-    nbig = max(1, args.steps)
-    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for i in range(3):
-        lib.vbq_gemv(xs[4096].data_ptr(), big_mats[i % len(big_mats)].data_ptr(), big_y.data_ptr(),
-                     4096, 14336, QTYPE, B, sptr, sbytes, sp)
-    e2.record(stream)
-    for i in range(nbig):
-        lib.vbq_gemv(xs[4096].data_ptr(), big_mats[i % len(big_mats)].data_ptr(), big_y.data_ptr(),
-                     4096, 14336, QTYPE, B, sptr, sbytes, sp)
-    e3.record(stream)
-    torch.cuda.synchronize()
-    big_bytes = int(4096 * 14336 * BPW) + B * (4096 + 14336) * 4
-    big_gbs = big_bytes * nbig / (e2.elapsed_time(e3) * 1e-3) / 1e9
+
+    def time_shape(mats, K, N):
+        yy = torch.empty(B, N, device=dev)
+        for i in range(3):
+            lib.vbq_gemv(xs[K].data_ptr(), mats[i % len(mats)].data_ptr(), yy.data_ptr(), K, N, QTYPE, B,
+                         sptr, sbytes, sp)
+        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        nrep = max(1, args.steps)
+        e2.record(stream)
+        for i in range(nrep):
+            lib.vbq_gemv(xs[K].data_ptr(), mats[i % len(mats)].data_ptr(), yy.data_ptr(), K, N, QTYPE, B,
+                         sptr, sbytes, sp)
+        e3.record(stream)
+        torch.cuda.synchronize()
+        nbytes = int(K * N * BPW) + B * (K + N) * 4
+        return nbytes * nrep / (e2.elapsed_time(e3) * 1e-3) / 1e9
+
+    gu_gbs = time_shape([layer[2][2] for layer in layers], 4096, 28672)
+    from vibeblade_b200.quantize import synthetic_weights
+    sep = [synthetic_weights(4096, 14336, QTYPE, seed=900 + i, device=dev) for i in range(4)]
+    big_gbs = time_shape(sep, 4096, 14336)
+    del sep
     traffic = None
     tp = ROOT / "profiles" / "gemv_q4k_4096x14336_b1.txt"
     if tp.exists():  # dram bytes per launch from the committed ncu capture of this shape
@@ -565,13 +593,13 @@ def run_gpu(args) -> None:
     # device-to-host copy.
     in_ks = sorted(xs)
     x_sizes = [B * K for K in in_ks]
-    y_sizes = [B * N for _, _, N in LAYER_8B]
+    y_sizes = [B * N for _, N in launch_shapes]
     xh_all = torch.cat([xs[K].reshape(-1).cpu() for K in in_ks]).pin_memory()
     yh_all = torch.empty(sum(y_sizes), pin_memory=True)
     xd_all = torch.empty(sum(x_sizes), device=dev)
     yd_all = torch.empty(sum(y_sizes), device=dev)
     xd = {K: v.view(B, K) for K, v in zip(in_ks, torch.split(xd_all, x_sizes))}
-    yd = [v.view(B, N) for (_, _, N), v in zip(LAYER_8B, torch.split(yd_all, y_sizes))]
+    yd = [v.view(B, N) for (_, N), v in zip(launch_shapes, torch.split(yd_all, y_sizes))]
     h2d = xh_all.numel() * 4
     d2h = yh_all.numel() * 4
 
@@ -631,8 +659,8 @@ def run_gpu(args) -> None:
     if B == 1 and not args.no_extras:
         for bx in (4, 16):
             xb = {K: torch.randn(bx, K, generator=g, device=dev) for _, K, _ in LAYER_8B}
-            yb = [torch.empty(bx, N, device=dev) for _, _, N in LAYER_8B]
-            need_b = max(vb.gemv_scratch_bytes(K, N, QTYPE, bx) for _, K, N in LAYER_8B)
+            yb = [torch.empty(bx, N, device=dev) for _, N in launch_shapes]
+            need_b = max(vb.gemv_scratch_bytes(K, N, QTYPE, bx) for K, N in launch_shapes)
             scr_b = torch.zeros(max(need_b, 16), dtype=torch.uint8, device=dev)
 
             def layer_b(c: int, stream_ptr: int):
@@ -692,7 +720,7 @@ def run_gpu(args) -> None:
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (N(0,0.02) weights quantized Q4_K; x N(0,1))",
             "config": bench_config(B, n_copies, world),
-            "launch": (f"CUDA graph of {n_copies} steps ({5 * n_copies} GEMV kernels chained by "
+            "launch": (f"CUDA graph of {n_copies} steps ({4 * n_copies} GEMV kernels chained by "
                        "programmatic dependent launch), replayed; remainder eager"
                        if graph is not None else "eager, one C-ABI call per GEMV"),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
@@ -704,12 +732,14 @@ def run_gpu(args) -> None:
                                     else f"vbq::gwide::gemv_wide_kernel<{8 if B <= 8 else 16}> "
                                     "(u8 x s8 mma.sync, B table shared by warp pairs)"),
                          "gemv_4096x14336_gbs": round(big_gbs, 1),
-                         "gemv_4096x14336_frac": round(big_gbs / pk["hbm_gbs"], 4)},
+                         "gemv_4096x14336_frac": round(big_gbs / pk["hbm_gbs"], 4),
+                         "gemv_gate_up_4096x28672_gbs": round(gu_gbs, 1),
+                         "gemv_gate_up_4096x28672_frac": round(gu_gbs / pk["hbm_gbs"], 4)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "vibeblade_b200.gemv_dequant",
                     "graph_replayed_value": (round(e2e_graph_value, 2)
                                              if e2e_graph_value is not None else None)},
-            "gpu_launches": args.steps * len(LAYER_8B),
+            "gpu_launches": args.steps * len(launch_shapes),
             "clocks": clk.summary(),
         }
         if decode_batches:  # outside the timed region above; same layers, graph-replayed
@@ -720,8 +750,7 @@ def run_gpu(args) -> None:
         dist.destroy_process_group()
     if rank == 0:
         if not args.no_cpu_baseline:
-            # the same bytes the GPU streamed (rank 0's copies), rotated the same way
-            layers_np = [[(K, N, w.cpu().numpy()) for K, N, w in layer] for layer in layers]
+            # the same bytes the GPU streamed (rank 0's copies, as five matrices), rotated alike
             xs_np = {K: x.cpu().numpy() for K, x in xs.items()}
             gbs, kind, cores, sample, _, _ = cpu_reference_gbs(layers_np, xs_np, B, args.cpu_seconds,
                                                                os.cpu_count() or 1)

@@ -93,6 +93,7 @@ __global__ void __launch_bounds__(kThreads, BATCH <= 2 ? 2 : 1)
 gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restrict__ x,
                 float* y, int K, int N, int batch, Epi epi) {
   constexpr int NSET = BATCH <= 2 ? 1 : 2;  // B column sets: two batch rows per set
+  constexpr int kDownEvery = BATCH <= 2 ? 1 : 2;  // stages between shrink tests (a power of two)
   extern __shared__ uint8_t smem_raw[];
   // 128-byte aligned: TMA destinations and ldmatrix rows
   uint8_t* smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
@@ -310,7 +311,7 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
           // float keeps the exponent of 2^23 (|n| < 2^22); NaN, inf and overflow leave it
           float2 v[BATCH][2];
           uint32_t w[BATCH][2][2];
-          uint32_t out = 0u, small = 0u;
+          uint32_t out = 0u;
 #pragma unroll
           for (int b = 0; b < BATCH; ++b) {
             v[b][0] = __fmul2_rn(xv[b], dl0);
@@ -323,14 +324,20 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
               w[b][h][1] = __float_as_uint(fmaf(v[b][h].y, scale[b], kMagic));
               out |= (w[b][h][0] ^ 0x4b000000u) | (w[b][h][1] ^ 0x4b000000u);
             }
-            // one of the lane's four values is the sample (the test only decides whether to
-            // rescale; the rescale itself takes the full maximum): |n| < 2^16
-            // (the word holds 1.5 * 2^23 + n when in range: |n| < 2^16 <=> w - (1.5 * 2^23 - 2^16)
-            // below 2^17; an out-of-range word fails it and rescales through `out` anyway)
-            small |= (w[b][0][0] - 0x4b3f0000u < 0x20000u) ? (1u << b) : 0u;
           }
-          if (__any_sync(0xffffffffu, out >= (1u << 23)) ||
-              __reduce_and_sync(0xffffffffu, small & down_ok) != 0u || it == 0) {
+          // the shrink test (every stage up to batch 2, every second one above, where it costs
+          // more): one of the lane's four values per batch row is the sample (the test only
+          // decides whether to rescale; the rescale itself takes the full maximum).  The word
+          // holds 1.5 * 2^23 + n when in range, so |n| < 2^16 <=> w - (1.5 * 2^23 - 2^16) is below
+          // 2^17; an out-of-range word fails it and rescales through `out` anyway.
+          bool shrink = false;
+          if ((it & (kDownEvery - 1)) == 0) {
+            uint32_t small = 0u;
+#pragma unroll
+            for (int b = 0; b < BATCH; ++b) small |= (w[b][0][0] - 0x4b3f0000u < 0x20000u) ? (1u << b) : 0u;
+            shrink = __reduce_and_sync(0xffffffffu, small & down_ok) != 0u;
+          }
+          if (__any_sync(0xffffffffu, out >= (1u << 23)) || shrink || it == 0) {
             // rare (and the first stage): flag non-finite values, move the sums to fp32, then
             // scale each batch row to 2-4x its largest finite |v| and encode again.  The
             // max ignores NaN and is capped so that huge values do not rescale every stage.

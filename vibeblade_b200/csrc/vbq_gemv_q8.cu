@@ -224,17 +224,23 @@ gemv_q8_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restri
                                    f16_ieee(*reinterpret_cast<const uint16_t*>(st + (row0 + 1) * kPitch + 34 * blk)));
       float2 v[BATCH];
       uint32_t w[BATCH][2];
-      uint32_t out = 0u, small = 0u;
+      uint32_t out = 0u;
 #pragma unroll
       for (int b = 0; b < BATCH; ++b) {
         v[b] = __fmul2_rn(xv[b], d);
         w[b][0] = __float_as_uint(fmaf(v[b].x, scale[b], kMagic));
         w[b][1] = __float_as_uint(fmaf(v[b].y, scale[b], kMagic));
         out |= (w[b][0] ^ 0x4b000000u) | (w[b][1] ^ 0x4b000000u);
-        small |= (fabsf(v[b].x) * scale[b] < 65536.f) ? (1u << b) : 0u;  // a sample, as there
       }
-      if (__any_sync(0xffffffffu, out >= (1u << 23)) ||
-          __reduce_and_sync(0xffffffffu, small & down_ok) != 0u || it == 0) {
+      // the sampled shrink test, as in vbq_gemv_mma.cu (every second stage at batch 4)
+      bool shrink = false;
+      if ((it & ((BATCH <= 2 ? 1 : 2) - 1)) == 0) {
+        uint32_t small = 0u;
+#pragma unroll
+        for (int b = 0; b < BATCH; ++b) small |= (fabsf(v[b].x) * scale[b] < 65536.f) ? (1u << b) : 0u;
+        shrink = __reduce_and_sync(0xffffffffu, small & down_ok) != 0u;
+      }
+      if (__any_sync(0xffffffffu, out >= (1u << 23)) || shrink || it == 0) {
         // rare (and the first stage): see vbq_gemv_mma.cu
         if (it > 0) flush();
 #pragma unroll

@@ -252,10 +252,7 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
       const float* xs = reinterpret_cast<const float*>(st + kWBytes);  // [BATCH][32]
       float2 v[QB][2];
       uint32_t w[QB][2][2];
-      // small: bit b = batch row b's sample is 16x or more below its scale.  Each lane
-      // half owns one quarter of the rows; the bits of the other half's quarter start at 1,
-      // so the warp-wide AND below is each row's AND over the lanes that own it.
-      uint32_t out = 0u, small = 0u;
+      uint32_t out = 0u;
 #pragma unroll
       for (int j = 0; j < QB; ++j) {
         const int b = qd * QB + j;
@@ -270,10 +267,19 @@ gemv_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
           w[j][h][1] = __float_as_uint(fmaf(v[j][h].y, scale[j], kMagic));
           out |= (w[j][h][0] ^ 0x4b000000u) | (w[j][h][1] ^ 0x4b000000u);
         }
-        // one sampled value per lane (see vbq_gemv_mma.cu): |n| < 2^16
-        small |= (fabsf(v[j][0].x) * scale[j] < 65536.f) ? (1u << b) : 0u;
       }
-      small = (small & down_ok) | (((1u << QB) - 1u) << ((qd ^ 1) * QB));
+      // the sampled shrink test (see vbq_gemv_mma.cu), every second 32-row stage: bit b of
+      // `small` = batch row b's sample (one value per lane) is 16x or more below its scale,
+      // |n| < 2^16.  Each lane half owns one quarter of the rows; the bits of the other
+      // half's quarter are set, so the warp-wide AND below is each row's AND over the lanes
+      // that own it.
+      uint32_t small = 0u;
+      if ((it & 1) == 0) {
+#pragma unroll
+        for (int j = 0; j < QB; ++j)
+          small |= (fabsf(v[j][0].x) * scale[j] < 65536.f) ? (1u << (qd * QB + j)) : 0u;
+        small = (small & down_ok) | (((1u << QB) - 1u) << ((qd ^ 1) * QB));
+      }
       // the pair's decisions: either warp's wait gave up -> both leave; either warp's
       // digits left their range, or some batch row of the warp sits 16x or more below its
       // scale in every lane (or the first stage) -> both flush, then rescale
