@@ -29,7 +29,7 @@ import torch
 
 from . import _lib
 from . import formats as F
-from .dequant import _require_cuda, _stream_ptr, _weights_u8, gemv_dequant
+from .dequant import _require_cuda, _stream_ptr, _weights_u8, gemv_dequant, gemv_fused
 from .gemm import gemm_dequant
 
 # GEMM tiles are 256 columns wide; a column shard must keep whole tiles
@@ -154,24 +154,30 @@ def reduce_partial(y: torch.Tensor, world: int, group=None, async_op: bool = Fal
 _PAIR_TILE_ROWS = 512
 
 
-def row_split_prefill_reduced(lin: "TPLinear", a: torch.Tensor, group=None) -> torch.Tensor:
+def row_split_prefill_reduced(lin: "TPLinear", a: torch.Tensor, group=None,
+                              reduce_dtype=torch.bfloat16) -> torch.Tensor:
     """fp32 [M, N] = all-reduce over the ranks of lin.prefill(a) for a row-split layer.
 
-    The GEMM runs in two row halves (split at whole 512-row pair tiles); the first half's
-    all-reduce is issued as soon as its GEMM is enqueued and runs on NCCL's stream while
-    the second half computes.  Every rank takes the same collective steps for the same M."""
+    Over W > 1 ranks the GEMM writes its partial sums in `reduce_dtype` (bf16 by default:
+    half the bytes to write and to move over NVLink, within the prefill's bf16 bar) and the
+    all-reduce sums them in that type; the result is returned in fp32.  The GEMM runs in
+    two row halves (split at whole 512-row pair tiles); the first half's all-reduce is
+    issued as soon as its GEMM is enqueued and runs on NCCL's stream while the second half
+    computes.  Every rank takes the same collective steps for the same M."""
     M, W = a.shape[0], lin.world
-    y = torch.empty((M, lin.n_loc), dtype=torch.float32, device=a.device)
+    dt = torch.float32 if W == 1 else reduce_dtype
+    y = torch.empty((M, lin.n_loc), dtype=dt, device=a.device)
     split = ((M // 2 + _PAIR_TILE_ROWS - 1) // _PAIR_TILE_ROWS) * _PAIR_TILE_ROWS
     if W == 1 or split >= M:
-        lin.prefill(a, torch.float32, out=y)
-        return reduce_partial(y, W, group)
-    lin.prefill(a[:split], torch.float32, out=y[:split])
+        lin.prefill(a, dt, out=y)
+        reduce_partial(y, W, group)
+        return y if dt == torch.float32 else y.float()
+    lin.prefill(a[:split], dt, out=y[:split])
     work = reduce_partial(y[:split], W, group, async_op=True)
-    lin.prefill(a[split:], torch.float32, out=y[split:])
+    lin.prefill(a[split:], dt, out=y[split:])
     reduce_partial(y[split:], W, group)
     work.wait()
-    return y
+    return y if dt == torch.float32 else y.float()
 
 
 class TPFFN:
@@ -203,9 +209,11 @@ class TPFFN:
         return row_split_prefill_reduced(self.down, h, self.group)
 
     def decode(self, x: torch.Tensor, reduce: bool = True) -> torch.Tensor:
-        """x: fp32 [B, H] -> fp32 [B, H] (reduce as for prefill)."""
-        h = swiglu_rows(self.gate_up.decode(x), self.i_loc)
-        y = self.down.decode(h)
+        """x: fp32 [B, H] -> fp32 [B, H] (reduce as for prefill).  The down projection reads
+        silu(gate) * up straight from the gate | up output (vbq_gemv_ex): no SwiGLU pass."""
+        gu = self.gate_up.decode(x)
+        y = gemv_fused(gu, self.down.w, None, self.down.k_loc, self.down.n_loc, self.down.t,
+                       swiglu_input=True)
         return reduce_partial(y, self.down.world, self.group) if reduce else y
 
 
