@@ -192,29 +192,26 @@ def _soft(fn, *args, **kw) -> dict:
         return {"error": f"{type(e).__name__}: {e}"[:300]}
 
 
-def bench_prefill(dev, steps: int) -> dict:
-    """the 8B layer's five matrices in Q6_K times bf16 activations of
-    M = 2048 tokens (tcgen05 GEMM, bf16 out).  Whole layer per step."""
+def _prefill_layer(dev, steps: int, qtype: int, M: int, seed0: int) -> tuple[float, float]:
+    """TFLOP/s and ms of the 8B layer's five matrices at M tokens (tcgen05 GEMM, bf16 out):
+    qkv, o, then gate and up side by side on two streams (independent GEMMs over the same
+    activations, as an engine's FFN and vibeblade_b200.tp run them: 2 x 224 pair tiles at
+    M = 2048 fill 7 waves of the 74 SM pairs instead of 2 x 4), then down."""
     import torch
     import vibeblade_b200 as vb
     from vibeblade_b200.quantize import synthetic_weights
-    M = 2048
-    mats = [(K, N, synthetic_weights(K, N, 14, seed=200 + i, device=dev)) for i, (_, K, N) in enumerate(LAYER_8B)]
+    mats = [(K, N, synthetic_weights(K, N, qtype, seed=seed0 + i, device=dev)) for i, (_, K, N) in enumerate(LAYER_8B)]
     g = torch.Generator(device=dev).manual_seed(2)
     acts = {K: torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16) for _, K, _ in LAYER_8B}
     outs = [torch.empty(M, N, device=dev, dtype=torch.bfloat16) for _, _, N in LAYER_8B]
-
     cur = torch.cuda.current_stream(dev)
     side = torch.cuda.Stream(dev)
 
     def gemm(i):
         K, N, w = mats[i]
-        vb.gemm_dequant(acts[K], w, outs[i], M, K, N, 14, out_dtype=torch.bfloat16)
+        vb.gemm_dequant(acts[K], w, outs[i], M, K, N, qtype, out_dtype=torch.bfloat16)
 
     def step(_):
-        # qkv, o; then gate and up side by side (independent GEMMs over the same activations,
-        # as the engine's FFN and vibeblade_b200.tp run them: 2 x 224 pair tiles fill 7 waves
-        # of the 74 SM pairs instead of 2 x 4); down after both
         gemm(0)
         gemm(1)
         side.wait_stream(cur)
@@ -226,11 +223,27 @@ def bench_prefill(dev, steps: int) -> dict:
 
     ms = _time_steps(step, steps, 3, cur, 1)
     flops = sum(2 * M * K * N for _, K, N in LAYER_8B)
-    tf = flops * steps / (ms * 1e-3) / 1e12
-    return {"metric": "Q6_K prefill GEMM TFLOP/s (8B layer, M=2048, bf16 out)", "value": round(tf, 1),
-            "unit": "TFLOP/s", "ms_per_layer": round(ms / steps, 4), "steps": steps,
-            "frac_of_bf16_peak": round(tf / peaks()["bf16_tflops"], 4),
-            "kernel": "vbq::gemm::gemm_kernel (2-SM tcgen05, cta_group::2)"}
+    del mats, acts, outs
+    torch.cuda.empty_cache()
+    return flops * steps / (ms * 1e-3) / 1e12, ms / steps
+
+
+def bench_prefill(dev, steps: int) -> dict:
+    """the 8B layer's five matrices in Q6_K times bf16 activations at
+    M = 2048 (the value), 512 and 8192; and the same layer in Q4_K at M = 2048 and 8192 (the
+    north star's own GEMM target: Q4_K prefill at >= 55 % of the bf16 peak)."""
+    pk = peaks()["bf16_tflops"]
+    tf, ms = _prefill_layer(dev, steps, 14, 2048, 200)
+    out = {"metric": "Q6_K prefill GEMM TFLOP/s (8B layer, M=2048, bf16 out)", "value": round(tf, 1),
+           "unit": "TFLOP/s", "ms_per_layer": round(ms, 4), "steps": steps,
+           "frac_of_bf16_peak": round(tf / pk, 4),
+           "kernel": "vbq::gemm::gemm_kernel (2-SM tcgen05, cta_group::2)"}
+    for qt, name, Ms in ((14, "q6_k", (512, 8192)), (12, "q4_k", (2048, 8192))):
+        for M in Ms:
+            t, m = _prefill_layer(dev, max(3, steps // (4 if M == 8192 else 1)), qt, M, 400)
+            out[f"{name}_m{M}"] = {"value": round(t, 1), "unit": "TFLOP/s", "ms_per_layer": round(m, 4),
+                                   "frac_of_bf16_peak": round(t / pk, 4)}
+    return out
 
 
 def bench_lm_head(dev, steps: int) -> dict:
@@ -450,6 +463,27 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def bench_decode_only(dev, args) -> dict:
+    """The headline decode steps alone, launched eagerly through the C ABI (one kernel per
+    matrix in stream order): the target of the ncu launch list and captures."""
+    import torch
+    from vibeblade_b200 import _lib
+    lib = _lib.load()
+    layers, xs = make_inputs(dev, args.batch, args.copies, 0)
+    layers = [pack_gate_up(layer) for layer in layers]
+    ys = [torch.empty(args.batch, N, device=dev) for _, N, _ in layers[0]]
+    sp = torch.cuda.current_stream(dev).cuda_stream
+
+    def step(s):
+        for (K, N, w), y in zip(layers[s % len(layers)], ys):
+            _lib.check(lib.vbq_gemv(xs[K].data_ptr(), w.data_ptr(), y.data_ptr(), K, N, QTYPE, args.batch,
+                                    None, 0, sp), lib)
+
+    ms = _time_steps(step, args.steps, args.warmup, torch.cuda.current_stream(dev), 1)
+    return {"metric": METRIC, "value": round(layer_bytes(args.batch) * args.steps / (ms * 1e-3) / 1e9, 1),
+            "unit": "GB/s", "launch": "eager", "steps": args.steps, "launches_per_step": len(ys)}
+
+
 def run_only(args) -> None:
     """One of the extra measurements on its own (a small, repeatable target for ncu)."""
     import torch
@@ -457,7 +491,9 @@ def run_only(args) -> None:
     rank, world, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if args.only == "prefill":
+    if args.only == "decode":
+        res = bench_decode_only(dev, args)
+    elif args.only == "prefill":
         res = bench_prefill(dev, args.extras_steps)
     elif args.only == "moe":
         res = bench_moe(dev, args.extras_steps)
@@ -587,7 +623,7 @@ def run_gpu(args) -> None:
     big_gbs = time_shape(sep, 4096, 14336)
     del sep
     traffic = None
-    tp = ROOT / "profiles" / "gemv_q4k_4096x14336_b1.txt"
+    tp = ROOT / "profiles" / "gemv_q4k_decode_layer_engine_b1.txt"
     if tp.exists():  # dram bytes per launch from the committed ncu capture of this shape
         for line in tp.read_text().splitlines():
             if line.startswith("traffic_bytes_per_launch:"):
@@ -595,8 +631,8 @@ def run_gpu(args) -> None:
 
     # ---- end to end through the public API with host buffers ----
     # A step's inputs (x of the 4096-row and 14336-row matrices) sit back to back in one
-    # pinned host buffer and one device buffer, its five outputs likewise: one host-to-device
-    # copy, five gemv_dequant calls writing into views of the output buffer, one
+    # pinned host buffer and one device buffer, its four outputs likewise: one host-to-device
+    # copy, four gemv_dequant calls (gate|up packed) writing into views of the output buffer, one
     # device-to-host copy.
     in_ks = sorted(xs)
     x_sizes = [B * K for K in in_ks]
@@ -633,7 +669,7 @@ def run_gpu(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_value = layer_bytes(B) * args.steps * world / (float(t.item()) * 1e-3) / 1e9
 
-    # the same step (one copy in, five gemv_dequant calls, one copy out) captured once per
+    # the same step (one copy in, four gemv_dequant calls, one copy out) captured once per
     # rotation of the layer copies in a CUDA graph and replayed, as a decode engine runs its
     # step: the copies still happen every step, the per-call host work does not
     e2e_graph_value = None
@@ -732,7 +768,7 @@ def run_gpu(args) -> None:
                        if graph is not None else "eager, one C-ABI call per GEMV"),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
                          "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
-                         "traffic": traffic, "traffic_launch": "gate/up 4096x14336 (ncu)",
+                         "traffic": traffic, "traffic_launch": "packed gate|up 4096x28672 (ncu, read + write)",
                          "peak_src": pk["src"] + " (MEASURED_PEAKS.json hbm_gbs)",
                          "kernel": (f"vbq::gmma::gemv_mma_kernel<{1 if B == 1 else 2 if B == 2 else 4}> "
                                     "(u8 x s8 mma.sync, split-K in a thread-block cluster)" if B <= 4
@@ -784,7 +820,7 @@ def main() -> None:
     ap.add_argument("--no-extras", action="store_true",
                     help="skip those; config 5 is then measured on its decode side only")
     ap.add_argument("--extras-steps", type=int, default=10)
-    ap.add_argument("--only", choices=["prefill", "moe", "tp"],
+    ap.add_argument("--only", choices=["decode", "prefill", "moe", "tp"],
                     help="run just this measurement and print its JSON object")
     args = ap.parse_args()
     if args.warmup < 3:
