@@ -83,9 +83,9 @@ def test_newer_entry_points_validate_before_any_cuda_call(lib):
 
 
 def test_scratch_size_query(lib):
-    """Split-K scratch: counters + splits * batch * N partials; none when K is tiny, and
-    none for the tensor-core Q4_K kernel (batch 1..16), whose splits add up inside a
-    thread-block cluster."""
+    """Split-K scratch: counters + splits * batch * N partials for the fp32 kernel; none
+    when K is tiny, and none for the tensor-core kernels (Q4_K / Q8_0 batch 1..16), whose
+    splits add up inside a thread-block cluster."""
     v = C.c_size_t()
     assert lib.vbq_gemv_scratch_bytes(4096, 14336, 14, 1, C.byref(v)) == 0
     assert v.value > 14336 * 4

@@ -614,11 +614,12 @@ bool gemv_mma_fits(int64_t K, int64_t N, int batch) {
   return batch >= 1 && batch <= 16 && K >= 1 && K <= kMmaMaxK && N % 256 == 0 && N > 0;
 }
 
-// Tensor-core Q4_K GEMV.  Batches 5..16 go to the wide kernel (one pass over the weights)
-// when x's rows are 16-byte aligned (and K within its cap); otherwise batches above 4 run as
-// consecutive launches over groups of 4 batch rows (each streams the weights again).
-// Measured on B200, 4096 x 14336: batch 8 grouped 33.2 us / wide 31.3 us; batch 16
-// grouped 64.5 us / wide 51.9 us.
+// Tensor-core Q4_K GEMV.  Batches 5..16 go to the fp16 kernel (vbq_gemv_half.cu: one pass
+// over the weights, activations tabled once per row) when x's rows are 16-byte aligned;
+// otherwise to the integer wide kernel (x aligned, no SwiGLU input), else as consecutive
+// launches over groups of 4 batch rows (each streams the weights again).  Measured on
+// B200, 4096 x 14336: batch 8 grouped 33.2 us / wide 31.3 us / fp16 28.7 us; batch 16
+// grouped 64.5 us / wide 51.9 us / fp16 40.4 us.
 template <bool SW>
 static cudaError_t launch_group(const float* x, const void* w, float* y, int64_t K, int64_t N,
                                 int64_t row_bytes, int nb, cudaStream_t st, Epi epi) {
@@ -630,6 +631,7 @@ static cudaError_t launch_group(const float* x, const void* w, float* y, int64_t
 cudaError_t launch_gemv_mma_q4k(const float* x, const void* w, float* y, int64_t K, int64_t N,
                                 int64_t row_bytes, int batch, cudaStream_t st, const GemvFuse& f) {
   if (!gemv_mma_fits(K, N, batch) || row_bytes % 16 != 0) return cudaErrorNotSupported;
+  if (gemv_half_fits(x, K, N, batch)) return launch_gemv_half_q4k(x, w, y, K, N, row_bytes, batch, st, f);
   // the wide kernel reads x by TMA, so a SwiGLU input runs in groups of 4 here
   if (batch > 4 && !f.swiglu_x && gemv_wide_fits(x, K, N, batch))
     return launch_gemv_wide_q4k(x, w, y, K, N, row_bytes, batch, st, f);

@@ -76,6 +76,13 @@ cudaError_t launch_gemv_wide_q4k(const float* x, const void* w, float* y, int64_
                                  int64_t row_bytes, int batch, cudaStream_t st,
                                  const GemvFuse& f = GemvFuse{});
 cudaError_t gemv_wide_status(unsigned* out, bool clear);
+// Batch 5..16 Q4_K kernel on the fp16 tensor cores (vbq_gemv_half.cu): x read by TMA (rows
+// of x 16-byte aligned, K % 4 == 0); a SwiGLU input is read as its gate | up halves.
+bool gemv_half_fits(const float* x, int64_t K, int64_t N, int batch);
+cudaError_t launch_gemv_half_q4k(const float* x, const void* w, float* y, int64_t K, int64_t N,
+                                 int64_t row_bytes, int batch, cudaStream_t st,
+                                 const GemvFuse& f = GemvFuse{});
+cudaError_t gemv_half_status(unsigned* out, bool clear);
 cudaError_t launch_gemv_mma_q4k(const float* x, const void* w, float* y, int64_t K, int64_t N,
                                 int64_t row_bytes, int batch, cudaStream_t st,
                                 const GemvFuse& f = GemvFuse{});
