@@ -91,8 +91,9 @@ def peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "src": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", 1400.0)), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
 
 
 class ClockSampler:
@@ -232,17 +233,20 @@ def bench_prefill(dev, steps: int) -> dict:
     """the 8B layer's five matrices in Q6_K times bf16 activations at
     M = 2048 (the value), 512 and 8192; and the same layer in Q4_K at M = 2048 and 8192 (the
     north star's own GEMM target: Q4_K prefill at >= 55 % of the bf16 peak)."""
-    pk = peaks()["bf16_tflops"]
+    pk, pks = peaks()["bf16_tflops"], peaks()["bf16_tflops_sustained"]
     tf, ms = _prefill_layer(dev, steps, 14, 2048, 200)
+    # the steps run back to back for tens of ms under the power cap: both the burst and the
+    # sustained cuBLAS figures are given as denominators
     out = {"metric": "Q6_K prefill GEMM TFLOP/s (8B layer, M=2048, bf16 out)", "value": round(tf, 1),
            "unit": "TFLOP/s", "ms_per_layer": round(ms, 4), "steps": steps,
-           "frac_of_bf16_peak": round(tf / pk, 4),
+           "frac_of_bf16_peak": round(tf / pk, 4), "frac_of_bf16_sustained": round(tf / pks, 4),
            "kernel": "vbq::gemm::gemm_kernel (2-SM tcgen05, cta_group::2)"}
     for qt, name, Ms in ((14, "q6_k", (512, 8192)), (12, "q4_k", (2048, 8192))):
         for M in Ms:
             t, m = _prefill_layer(dev, max(3, steps // (4 if M == 8192 else 1)), qt, M, 400)
             out[f"{name}_m{M}"] = {"value": round(t, 1), "unit": "TFLOP/s", "ms_per_layer": round(m, 4),
-                                   "frac_of_bf16_peak": round(t / pk, 4)}
+                                   "frac_of_bf16_peak": round(t / pk, 4),
+                                   "frac_of_bf16_sustained": round(t / pks, 4)}
     return out
 
 
@@ -292,7 +296,8 @@ def bench_moe(dev, steps: int) -> dict:
     tf = 2 * T * k * 3 * H * I * steps / (ms * 1e-3) / 1e12
     return {"metric": "MoE FFN TFLOP/s (8 experts top-2, 4096 tokens, Q4_K)", "value": round(tf, 1),
             "unit": "TFLOP/s", "ms_per_step": round(ms / steps, 3), "steps": steps,
-            "frac_of_bf16_peak": round(tf / peaks()["bf16_tflops"], 4)}
+            "frac_of_bf16_peak": round(tf / peaks()["bf16_tflops"], 4),
+            "frac_of_bf16_sustained": round(tf / peaks()["bf16_tflops_sustained"], 4)}
 
 
 def bench_tp(dev, rank: int, world: int, steps: int, prefill: bool = True) -> dict:
