@@ -157,7 +157,9 @@ def _nccl_rank(rank, world, port, res):
     try:
         wg, wu, wd = _weights(dev)
         g = torch.Generator(device=dev).manual_seed(2)
-        x = torch.randn(256, H, generator=g, device=dev).to(torch.bfloat16)
+        # 1024 rows: the FFN runs in two 512-row halves, the first half's all-reduce in
+        # flight under the second half's GEMMs
+        x = torch.randn(1024, H, generator=g, device=dev).to(torch.bfloat16)
         y = tp.TPFFN(wg, wu, wd, H, I, QT, rank, world, dev).prefill(x)
         ys = [torch.empty_like(y) for _ in range(world)]
         dist.all_gather(ys, y)

@@ -567,13 +567,7 @@ static cudaError_t launch_t(const float* x, const void* w, float* y, int64_t K, 
   auto enc = encode_fn_g();
   if (!enc) return cudaErrorNotSupported;
   CUtensorMap mw;
-  cuuint64_t dims[2] = {(cuuint64_t)(RB / 2), (cuuint64_t)K};
-  cuuint64_t strides[1] = {(cuuint64_t)RB};
-  cuuint32_t box[2] = {(cuuint32_t)(kPitch / 2), (cuuint32_t)kRows};
-  cuuint32_t es[2] = {1, 1};
-  if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(w), dims, strides, box, es,
-          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+  if (!weight_map(reinterpret_cast<EncodeTiledFn>(enc), w, K, RB, kPitch, kRows, &mw))
     return cudaErrorInvalidValue;
   auto kern = gemv_mma_kernel<BATCH, SWIGLU>;
   constexpr int kBase = Lay<(BATCH <= 2 ? 1 : 2)>::kSmem;

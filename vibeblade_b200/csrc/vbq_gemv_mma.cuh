@@ -100,5 +100,46 @@ __device__ __forceinline__ float pow2f(int e) { return __uint_as_float((uint32_t
 // 1 / s for a power of two s = 2^k with |k| <= 126 (exact: the exponent field is negated)
 __device__ __forceinline__ float inv_pow2(float s) { return __uint_as_float(0x7f000000u - __float_as_uint(s)); }
 
+// ---- host: the weight operand's tensor map ---------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// The GEMV kernels' weight map: the K x RB bytes as a 2-D u16 array, boxes of `pitch` bytes x
+// `rows` rows, L2 256-byte promotion.  The map depends only on these arguments, so each
+// host thread keeps the last few it encoded (encoding is a driver call of about a
+// microsecond, on every decode launch otherwise).  Returns false when encoding fails.
+inline bool weight_map(EncodeTiledFn enc, const void* w, int64_t K, int64_t RB, int pitch, int rows,
+                       CUtensorMap* out) {
+  struct Entry {
+    CUtensorMap map;
+    const void* w;
+    int64_t K, RB;
+    int pitch, rows;
+    bool valid;
+  };
+  thread_local Entry cache[8] = {};
+  const uintptr_t key = (reinterpret_cast<uintptr_t>(w) >> 8) ^ (uintptr_t)K ^ ((uintptr_t)RB << 4) ^
+                        ((uintptr_t)pitch << 12) ^ (uintptr_t)rows;
+  Entry& e = cache[(key ^ (key >> 3) ^ (key >> 6)) & 7];
+  if (e.valid && e.w == w && e.K == K && e.RB == RB && e.pitch == pitch && e.rows == rows) {
+    *out = e.map;
+    return true;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)(RB / 2), (cuuint64_t)K};
+  cuuint64_t strides[1] = {(cuuint64_t)RB};
+  cuuint32_t box[2] = {(cuuint32_t)(pitch / 2), (cuuint32_t)rows};
+  cuuint32_t es[2] = {1, 1};
+  e.valid = false;
+  if (enc(&e.map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(w), dims, strides, box, es,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  e.w = w, e.K = K, e.RB = RB, e.pitch = pitch, e.rows = rows, e.valid = true;
+  *out = e.map;
+  return true;
+}
+
 }  // namespace gmma
 }  // namespace vbq

@@ -55,6 +55,9 @@ def _cuda_available() -> bool:
 
 # scratch sizes per (device, K, N, type, batch): the plan depends on the device's SM count
 _SCRATCH_BYTES: dict[tuple[int, int, int, int, int], int] = {}
+# validated gemv_dequant calls: (type as given, K, N, x values, device index) -> (type id,
+# batch, weight bytes needed, scratch bytes)
+_GEMV_PLANS: dict[tuple, tuple[int, int, int, int]] = {}
 
 
 def gemv_scratch_bytes(K: int, N: int, wtype, batch: int = 1) -> int:
@@ -131,6 +134,24 @@ def gemv_dequant(x: torch.Tensor, weights: torch.Tensor, out: torch.Tensor | Non
     ``gemv_scratch_bytes(K, N, wtype, B)`` bytes, zero-filled before its first use (each
     call leaves it zero-filled).  When None, a per-stream buffer owned by this module is
     used."""
+    # Decode fast path: a call shaped like an earlier validated one (same type, K, N, x size
+    # and device) needs only the per-tensor checks; anything unusual takes the full path
+    # below, which raises the reference's errors.
+    plan = _GEMV_PLANS.get((wtype, K, N, x.numel(), x.device.index)) if isinstance(x, torch.Tensor) else None
+    if (plan is not None and x.is_cuda and x.dtype == torch.float32 and x.is_contiguous()
+            and isinstance(weights, torch.Tensor) and weights.is_cuda and weights.is_contiguous()
+            and isinstance(out, torch.Tensor) and out.is_cuda and out.dtype == torch.float32
+            and out.is_contiguous() and scratch is None):
+        t, batch, need_w, need_s = plan
+        w = weights if weights.dtype == torch.uint8 else weights.view(torch.uint8)
+        if w.numel() >= need_w and out.numel() == batch * N:
+            sp = _stream_ptr(x)
+            scr = _stream_scratch(x.device, sp, need_s) if need_s else None
+            lib = _lib.load()
+            _lib.check(lib.vbq_gemv(x.data_ptr(), w.data_ptr(), out.data_ptr(), K, N, t, batch,
+                                    scr.data_ptr() if scr is not None else None,
+                                    scr.numel() if scr is not None else 0, sp), lib)
+            return out
     t = F.parse_type(wtype)
     _require_cuda("gemv_dequant", x, weights)
     if x.dtype != torch.float32:
@@ -167,6 +188,8 @@ def gemv_dequant(x: torch.Tensor, weights: torch.Tensor, out: torch.Tensor | Non
     scr_bytes = scr.numel() * scr.element_size() if scr is not None else 0
     _lib.check(lib.vbq_gemv(x.data_ptr(), w.data_ptr(), out.data_ptr(), K, N, t, batch,
                             scr_ptr, scr_bytes, sp), lib)
+    if K > 0 and len(_GEMV_PLANS) < 4096:
+        _GEMV_PLANS[(wtype, K, N, x.numel(), x.device.index)] = (t, batch, F.row_bytes(t, N) * K, need)
     return out
 
 

@@ -29,7 +29,7 @@ import torch
 
 from . import _lib
 from . import formats as F
-from .dequant import _require_cuda, _stream_ptr, _weights_u8, gemv_dequant, gemv_fused
+from .dequant import _require_cuda, _stream_ptr, _weights_u8, gemv_dequant
 from .gemm import gemm_dequant
 
 # GEMM tiles are 256 columns wide; a column shard must keep whole tiles
@@ -202,18 +202,44 @@ class TPFFN:
 
     def prefill(self, x: torch.Tensor, reduce: bool = True) -> torch.Tensor:
         """x: bf16 [M, H] (replicated) -> fp32 [M, H], replicated after the all-reduce
-        (reduce=False returns this rank's partial sum and leaves the sum to the caller)."""
-        h = swiglu_rows(self.gate_up.prefill(x, torch.bfloat16), self.i_loc)
-        if not reduce:
-            return self.down.prefill(h, torch.float32)
-        return row_split_prefill_reduced(self.down, h, self.group)
+        (reduce=False returns this rank's partial sum and leaves the sum to the caller).
+
+        Over W > 1 ranks the whole FFN runs in two row halves (split at whole 512-row pair
+        tiles): the first half's bf16 all-reduce runs on NCCL's stream under the second
+        half's gate|up GEMM, SwiGLU and down GEMM, and only the second half's is exposed
+        (measured at TP = 8: 0.492 ms per M = 2048 step, against 0.615 ms when only the down
+        GEMM is split).  Rows are independent in every step, so the halves give the same
+        bits as one pass."""
+        W = self.down.world
+        M = x.shape[0]
+        split = ((M // 2 + _PAIR_TILE_ROWS - 1) // _PAIR_TILE_ROWS) * _PAIR_TILE_ROWS
+        if W == 1 or split >= M:
+            h = swiglu_rows(self.gate_up.prefill(x, torch.bfloat16), self.i_loc)
+            if not reduce:
+                return self.down.prefill(h, torch.float32)
+            return row_split_prefill_reduced(self.down, h, self.group)
+        dt = torch.bfloat16 if reduce else torch.float32
+        y = torch.empty((M, self.down.n_loc), dtype=dt, device=x.device)
+        work = None
+        for lo, hi in ((0, split), (split, M)):
+            h = swiglu_rows(self.gate_up.prefill(x[lo:hi], torch.bfloat16), self.i_loc)
+            self.down.prefill(h, dt, out=y[lo:hi])
+            if reduce:
+                if work is None:
+                    work = reduce_partial(y[lo:hi], W, self.group, async_op=True)
+                else:
+                    reduce_partial(y[lo:hi], W, self.group)
+        if work is not None:
+            work.wait()
+        return y if dt == torch.float32 else y.float()
 
     def decode(self, x: torch.Tensor, reduce: bool = True) -> torch.Tensor:
-        """x: fp32 [B, H] -> fp32 [B, H] (reduce as for prefill).  The down projection reads
-        silu(gate) * up straight from the gate | up output (vbq_gemv_ex): no SwiGLU pass."""
-        gu = self.gate_up.decode(x)
-        y = gemv_fused(gu, self.down.w, None, self.down.k_loc, self.down.n_loc, self.down.t,
-                       swiglu_input=True)
+        """x: fp32 [B, H] -> fp32 [B, H] (reduce as for prefill).  SwiGLU runs as one pass over
+        the gate | up output: read inside the down GEMV it would be recomputed by each of the
+        GEMV's 256-column tiles (measured on the 70B shard at TP = 1: 48 us plain against 77 us
+        fused at batch 1, 304 against 892 at batch 16)."""
+        h = swiglu_rows(self.gate_up.decode(x), self.i_loc)
+        y = self.down.decode(h)
         return reduce_partial(y, self.down.world, self.group) if reduce else y
 
 
