@@ -159,6 +159,20 @@ int vbq_gemm_ex(const void* a, const void* w, void* c, int64_t M, int64_t K, int
                 void* stream);
 
 /*
+ * The gate | up GEMM fused with SwiGLU (prefill):
+ *     h[m, j] = silu(sum_k A[m, k] deq(W_gate)[k, j]) * (sum_k A[m, k] deq(W_up)[k, j])
+ * (cpp/src/fast_model.cpp:906-953: gate and up projections, then silu(gate) * up).  A bf16
+ * [M, K]; W_gate and W_up K x I matrices of one type (Q4_K, Q6_K, Q8_0) whose rows are
+ * row_bytes apart (0: (I / block_values) * block_bytes; a gate | up matrix packed side by
+ * side passes its own row stride and w_up = w_gate + the gate part's bytes); h bf16 [M, I].
+ * The result has the bits of two vbq_gemm calls with bf16 output followed by
+ * vbq_swiglu, without the [M, 2I] intermediate.  I % 256 == 0, K % 8 == 0, pointers
+ * 16-byte aligned, row_bytes a multiple of 16.
+ */
+int vbq_gemm_swiglu(const void* a, const void* w_gate, const void* w_up, void* h, int64_t M, int64_t K,
+                    int64_t I, int32_t type, int64_t row_bytes, void* stream);
+
+/*
  * vbq_gemv with library-owned scratch, for callers that cannot allocate device memory --
  * for example an engine that reserves all of HBM for its own pools at start-up and allows
  * no later cudaMalloc (which may also synchronise the device), or a plugin that only gets

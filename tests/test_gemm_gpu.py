@@ -17,6 +17,7 @@ import vibeblade_b200 as vb
 from conftest import max_rel
 from vibeblade_b200 import formats as F
 from vibeblade_b200.quantize import quantize, synthetic_weights
+from vibeblade_b200.tp import swiglu
 
 pytestmark = pytest.mark.gpu
 
@@ -147,4 +148,46 @@ def test_gemm_multi_tile_bf16_out_matches_fp32_out(cuda):
     c32 = vb.gemm_dequant(a, w, None, M, K, N, qtype)
     c16 = vb.gemm_dequant(a, w, None, M, K, N, qtype, out_dtype=torch.bfloat16)
     assert torch.equal(c16, c32.to(torch.bfloat16))
+    assert vb.device_status() == 0
+
+
+# ---- gate | up GEMM fused with SwiGLU (vbq_gemm_swiglu) ----
+
+SWIGLU_CASES = [(F.GGML_TYPE_Q4_K, 2048, 4096, 14336), (F.GGML_TYPE_Q6_K, 1000, 4096, 14336),
+                (F.GGML_TYPE_Q8_0, 2048, 8192, 3584), (F.GGML_TYPE_Q4_K, 300, 512, 512),
+                (F.GGML_TYPE_Q8_0, 1536 + 37, 1024, 768)]
+
+
+@pytest.mark.parametrize("qtype,M,K,I", SWIGLU_CASES)
+def test_gemm_swiglu_matches_unfused(cuda, qtype, M, K, I):
+    """The fused call gives the bits of gate and up GEMMs with bf16 output followed by
+    vbq_swiglu (cpp/src/fast_model.cpp:906-953), for separate gate and up matrices and for
+    one gate | up matrix packed side by side; repeats are bit-identical."""
+    wg = synthetic_weights(K, I, qtype, seed=11, device=cuda)
+    wu = synthetic_weights(K, I, qtype, seed=12, device=cuda)
+    g = torch.Generator(device=cuda).manual_seed(M + K)
+    a = torch.randn(M, K, generator=g, device=cuda).to(torch.bfloat16)
+    gate = vb.gemm_dequant(a, wg, None, M, K, I, qtype, out_dtype=torch.bfloat16)
+    up = vb.gemm_dequant(a, wu, None, M, K, I, qtype, out_dtype=torch.bfloat16)
+    ref = swiglu(gate, up)
+    h = vb.gemm_swiglu(a, wg, wu, None, M, K, I, qtype)
+    torch.cuda.synchronize()
+    assert vb.device_status() == 0
+    assert torch.equal(h, ref)
+    rb = F.row_bytes(qtype, I)
+    packed = torch.cat([wg.view(K, rb), wu.view(K, rb)], dim=1).contiguous()
+    h2 = vb.gemm_swiglu(a, packed, packed.view(-1)[rb:], None, M, K, I, qtype, row_bytes=2 * rb)
+    assert torch.equal(h2, ref)
+    assert torch.equal(vb.gemm_swiglu(a, wg, wu, None, M, K, I, qtype), h)
+    # and against fp32 math on the exact dequantized weights (the prefill bar)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        af = a.float()
+        gf = af @ vb.dequantize(wg, K, I, qtype)
+        uf = af @ vb.dequantize(wu, K, I, qtype)
+        hf = torch.nn.functional.silu(gf) * uf
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    assert max_rel(h.float().cpu().numpy(), hf.cpu().numpy()) <= TOL
     assert vb.device_status() == 0

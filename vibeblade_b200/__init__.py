@@ -11,7 +11,7 @@ from .formats import (GGML_TYPE_BF16, GGML_TYPE_F16, GGML_TYPE_F32, GGML_TYPE_Q4
 from .dequant import (dequantize, dequantize_row, gemv_dequant, gemv_dequant_mt, gemv_fused,
                       gemv_scratch_bytes)
 from .gguf import GGUFFile
-from .gemm import gemm_dequant, device_status
+from .gemm import gemm_dequant, gemm_swiglu, device_status
 from .moe import gemm_grouped, moe_ffn, moe_route, moe_sort, moe_workspace_bytes
 from ._lib import VbqError
 
@@ -19,7 +19,7 @@ __all__ = [
     "formats", "GGML_TYPE_Q4_K", "GGML_TYPE_Q6_K", "GGML_TYPE_Q8_0", "GGML_TYPE_F32",
     "GGML_TYPE_F16", "GGML_TYPE_BF16", "row_bytes", "GGUFFile",
     "tensor_nbytes", "dequantize", "dequantize_row", "gemv_dequant", "gemv_dequant_mt", "gemv_fused",
-    "gemv_scratch_bytes", "gemm_dequant", "device_status", "gemm_grouped", "moe_ffn",
+    "gemv_scratch_bytes", "gemm_dequant", "gemm_swiglu", "device_status", "gemm_grouped", "moe_ffn",
     "moe_route", "moe_sort", "moe_workspace_bytes",
     "VbqError",
 ]

@@ -37,6 +37,8 @@ SIGNATURES = {
     "vbq_gemv": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int32,
                            C.c_int32, C.c_void_p, C.c_size_t, C.c_void_p]),
     "vbq_device_status": (C.c_int, [C.POINTER(C.c_int32), C.c_int32]),
+    "vbq_gemm_swiglu": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
+                                  C.c_int64, C.c_int32, C.c_int64, C.c_void_p]),
     "vbq_gemm_ex": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int64,
                               C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
     "vbq_gemv_ex": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int32,

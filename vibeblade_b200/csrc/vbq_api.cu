@@ -249,6 +249,35 @@ int vbq_gemm(const void* a, const void* w, void* c, int64_t M, int64_t K, int64_
   return gemm_impl(a, w, c, M, K, N, type, c_dtype, stream, vbq::GemmEpi{});
 }
 
+int vbq_gemm_swiglu(const void* a, const void* w_gate, const void* w_up, void* h, int64_t M, int64_t K,
+                    int64_t I, int32_t type, int64_t row_bytes, void* stream) {
+  if (!quantized(type)) return fail(VBQ_ERR_TYPE, "gemm_dequant: unsupported type " + std::to_string(type));
+  if (M < 0 || K < 0 || I < 0 || row_bytes < 0) return fail(VBQ_ERR_SHAPE, "vbq_gemm_swiglu: negative size");
+  if (I % 256 != 0) return fail(VBQ_ERR_SHAPE, "vbq_gemm_swiglu: I must be a multiple of 256");
+  if (M == 0 || I == 0) return ok();
+  if (!h) return fail(VBQ_ERR_NULL, "vbq_gemm_swiglu: NULL pointer");
+  if (K == 0) {  // gate = up = 0: silu(0) * 0
+    cudaError_t e = cudaMemsetAsync(h, 0, (size_t)M * I * 2, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "vbq_gemm_swiglu memset");
+    return ok();
+  }
+  if (!a || !w_gate || !w_up) return fail(VBQ_ERR_NULL, "vbq_gemm_swiglu: NULL pointer");
+  if (K % 8 != 0) return fail(VBQ_ERR_SHAPE, "vbq_gemm_swiglu: K must be a multiple of 8 (16-byte rows of A)");
+  if (M > (int64_t)INT32_MAX || K > (int64_t)INT32_MAX || I > (int64_t)INT32_MAX)
+    return fail(VBQ_ERR_SHAPE, "vbq_gemm_swiglu: sizes above 2^31 are not supported");
+  const int64_t rb = (I / block_values(type)) * block_bytes(type);
+  const int64_t stride = row_bytes ? row_bytes : rb;
+  if (stride < rb) return fail(VBQ_ERR_SHAPE, "vbq_gemm_swiglu: row_bytes below the rows' " + std::to_string(rb) + " bytes");
+  if (stride % 16 != 0)
+    return fail(VBQ_ERR_UNSUPPORTED, "vbq_gemm_swiglu: weight rows must be a multiple of 16 bytes apart");
+  if (!aligned(a, 16) || !aligned(w_gate, 16) || !aligned(w_up, 16) || !aligned(h, 16))
+    return fail(VBQ_ERR_ALIGN, "vbq_gemm_swiglu: a, w_gate, w_up and h must be 16-byte aligned");
+  cudaError_t e = vbq::launch_gemm_swiglu(type, a, w_gate, w_up, h, M, K, I, stride,
+                                          static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "vbq_gemm_swiglu launch");
+  return ok();
+}
+
 int vbq_gemm_ex(const void* a, const void* w, void* c, int64_t M, int64_t K, int64_t N, int32_t type,
                 int32_t c_dtype, const float* bias, const void* residual, void* stream) {
   vbq::GemmEpi ep;
@@ -535,13 +564,19 @@ int vbq_moe_ffn(const float* x, const float* logits, const void* w_gate, const v
   cudaError_t e = vbq::launch_moe_route(logits, (int)T, E, topk, idx, wt, st);
   if (e == cudaSuccess) e = vbq::launch_moe_sort(idx, (int)T, E, topk, seg, pos, tok, st);
   if (e == cudaSuccess) e = vbq::launch_moe_gather(x, tok, (int)R, (int)H, ws + l.a, st);
-  if (e == cudaSuccess)
-    e = vbq::launch_gemm_grouped(type_gate, ws + l.a, w_gate, ws + l.g, R, H, I, rb_g, VBQ_DTYPE_BF16,
-                                 H * rb_g, seg, E, st);
-  if (e == cudaSuccess)
-    e = vbq::launch_gemm_grouped(type_up, ws + l.a, w_up, ws + l.u, R, H, I, rb_u, VBQ_DTYPE_BF16,
-                                 H * rb_u, seg, E, st);
-  if (e == cudaSuccess) e = vbq::launch_swiglu(ws + l.g, ws + l.u, ws + l.g, R * I, st);
+  if (type_gate == type_up) {  // gate | up and SwiGLU in one grouped GEMM (the same bits)
+    if (e == cudaSuccess)
+      e = vbq::launch_gemm_grouped_swiglu(type_gate, ws + l.a, w_gate, w_up, ws + l.g, R, H, I, rb_g,
+                                          H * rb_g, seg, E, st);
+  } else {
+    if (e == cudaSuccess)
+      e = vbq::launch_gemm_grouped(type_gate, ws + l.a, w_gate, ws + l.g, R, H, I, rb_g, VBQ_DTYPE_BF16,
+                                   H * rb_g, seg, E, st);
+    if (e == cudaSuccess)
+      e = vbq::launch_gemm_grouped(type_up, ws + l.a, w_up, ws + l.u, R, H, I, rb_u, VBQ_DTYPE_BF16,
+                                   H * rb_u, seg, E, st);
+    if (e == cudaSuccess) e = vbq::launch_swiglu(ws + l.g, ws + l.u, ws + l.g, R * I, st);
+  }
   if (e == cudaSuccess)
     e = vbq::launch_gemm_grouped(type_down, ws + l.g, w_down, ws + l.y, R, I, H, rb_d, VBQ_DTYPE_F32,
                                  I * rb_d, seg, E, st);

@@ -426,10 +426,19 @@ __device__ __forceinline__ void store_all(const Producer<QT>& pr, uint8_t* bt, c
 // seg[s+1], device memory), segment s multiplied by weight slab s (the third coordinate of
 // tmap_w).  Work item blockIdx.y walks the segments' 512-row tiles; items past the last
 // tile exit at once (both CTAs of a pair share blockIdx.y).
-template <int QT, bool BF16_OUT, bool GROUPED>
+// SWI (SwiGLU fused, bf16 out): pair tile j makes h[rows, 128 j .. 128 j + 127] =
+// silu(x W_gate) * (x W_up) for those columns.  CTA 0 dequantizes gate columns 128 j ..
+// (half j % 2 of gate tile j / 2, tmap_w), CTA 1 the same columns of up (tmap_w2), so the
+// pair MMA's N = 256 are the gate and up values of one column range and each CTA's
+// accumulator holds both for its rows; the dequantization work per tile is unchanged.  The
+// gate and up values are rounded to bf16 before the SwiGLU, as when the GEMM writes them
+// and `vbq_swiglu_rows` reads them back, so the fused output has the same bits.
+template <int QT, bool BF16_OUT, bool GROUPED, bool SWI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
-            void* c, int M, int K, int N, const int* __restrict__ seg, int n_seg, GemmEpi ep) {
+            const __grid_constant__ CUtensorMap tmap_w2, void* c, int M, int K, int N,
+            const int* __restrict__ seg, int n_seg, GemmEpi ep) {
+  static_assert(!SWI || BF16_OUT, "the fused SwiGLU writes bf16");
   using L = Smem<QT>;
   using R = Raw<QT>;
   extern __shared__ uint8_t smem_raw[];
@@ -441,7 +450,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
-  const int n_tile = blockIdx.x >> 1;
+  const int n_tile = blockIdx.x >> 1;  // SWI: the 128-column chunk of h
+  // the weight tile this CTA reads and which 128 of its 256 columns it dequantizes
+  const int w_tile = SWI ? (n_tile >> 1) : n_tile;
+  const int w_half = SWI ? (n_tile & 1) : (int)cluster_rank();
+  const CUtensorMap* tw = (SWI && cluster_rank() == 1) ? &tmap_w2 : &tmap_w;
   int m0 = blockIdx.y * BMP, row_end = M, slab = 0;
   if constexpr (GROUPED) {
     int w = (int)blockIdx.y;
@@ -504,7 +517,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   };
 
   // Q6_K tiles start inside a 16-byte chunk; the TMA box starts at the chunk
-  int tile_x = n_tile * R::kTileBytes;
+  int tile_x = w_tile * R::kTileBytes;
   const int raw_off = (QT == kQ6_K) ? (tile_x & 15) : 0;
   tile_x &= ~15;
 
@@ -535,8 +548,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         }
         const uint32_t fb = smem_u32(&bars.full_raw[q][it & 1]);  // the consuming group's
         mbar_arrive_expect_tx(fb, R::kBytes);
-        if constexpr (GROUPED) tma_load_3d(smem_u32(raw_stage(q)), &tmap_w, tile_x / 2, it * BK, slab, fb);
-        else tma_load_2d(smem_u32(raw_stage(q)), &tmap_w, tile_x / 2, it * BK, fb);
+        if constexpr (GROUPED) tma_load_3d(smem_u32(raw_stage(q)), tw, tile_x / 2, it * BK, slab, fb);
+        else tma_load_2d(smem_u32(raw_stage(q)), tw, tile_x / 2, it * BK, fb);
       }
       // drain: every issued raw stage must land before the CTA may exit
       for (int j = (it > kRStages ? it - kRStages : 0); j < it; ++j)
@@ -591,7 +604,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     const int dw = warp - 2;
     const int grp = dw >> 3;  // group g dequantizes the K steps it = g, g + 2, ...
     const int wq = dw & 7;    // this warp's 8 K rows of each step: 8 wq .. +7
-    const Lane ln{lane >> 1, lane & 1, (int)rank};
+    const Lane ln{lane >> 1, lane & 1, w_half};
     uint8_t* tbl = smem + L::kTblOff + dw * kTableBytes;
     uint32_t off[8];  // B half-tile byte offset of value i's 8-byte half-chunk
 #pragma unroll
@@ -611,7 +624,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       }
       const uint8_t* wrows = raw_stage(q) + 8 * wq * P::kPitch + raw_off;
       if constexpr (QT != kQ8_0) {
-        P::table(wrows, lane, (int)rank, tbl);
+        P::table(wrows, lane, w_half, tbl);
         __syncwarp();
       }
       P pr;
@@ -647,7 +660,39 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       const int col0 = (dw >> 3) * (BN / 2);
       const int row = m0 + half * 256 + (int)rank * 128 + quarter * 32 + lane;
       const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * 256);
-      if (half == 0 || two_acc) {
+      if constexpr (SWI) {
+        // accumulator columns 0..127: gate, 128..255: up, of h columns 128 n_tile + 0..127;
+        // this warp takes h columns c0 .. c0 + 63 (the producer's rotation as below)
+        const int c0 = (dw >> 3) * 64;
+        if (half == 0 || two_acc) {
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {  // unrolled: the rotation indexes registers
+            uint32_t rg[32], ru[32];
+            tmem_ld32(tbase + c0 + 32 * hh, rg);
+            tmem_ld32(tbase + 128 + c0 + 32 * hh, ru);
+            if (row < row_end) {
+              uint32_t o[16];
+#pragma unroll
+              for (int g = 0; g < 4; ++g)
+#pragma unroll
+                for (int qq = 0; qq < 8; qq += 2) {
+                  const uint32_t gp = pack_bf16x2(__uint_as_float(rg[8 * g + ((qq + 4 * hh + g) & 7)]),
+                                                  __uint_as_float(rg[8 * g + ((qq + 1 + 4 * hh + g) & 7)]));
+                  const uint32_t up = pack_bf16x2(__uint_as_float(ru[8 * g + ((qq + 4 * hh + g) & 7)]),
+                                                  __uint_as_float(ru[8 * g + ((qq + 1 + 4 * hh + g) & 7)]));
+                  const float2 gf = make_float2(__uint_as_float(gp << 16), __uint_as_float(gp & 0xffff0000u));
+                  const float2 uf = make_float2(__uint_as_float(up << 16), __uint_as_float(up & 0xffff0000u));
+                  o[4 * g + qq / 2] = pack_bf16x2(silu_ref(sanitize(gf.x)) * sanitize(uf.x),
+                                                  silu_ref(sanitize(gf.y)) * sanitize(uf.y));
+                }
+              uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(c) + (int64_t)row * N +
+                                                    (int64_t)n_tile * 128 + c0 + 32 * hh);
+#pragma unroll
+              for (int x = 0; x < 4; ++x) dst[x] = make_uint4(o[4 * x], o[4 * x + 1], o[4 * x + 2], o[4 * x + 3]);
+            }
+          }
+        }
+      } else if (half == 0 || two_acc) {
         // accumulator column 8L + p holds tile column 8L + ((p - L) & 7) (the producer's
         // rotation, L & 7 = lc & 7); with 64 columns per step L & 7 is 4h + g for group g
         // of half-step h
@@ -765,16 +810,16 @@ static EncodeTiledFn encode_fn() {
 // Plain GEMM: slab_bytes == 0, seg == nullptr, rows = M.  Grouped: `n_seg` slabs of
 // `slab_bytes` each starting at w, rows of A / C split by seg[0..n_seg] (device), `rows`
 // the total row count (seg[n_seg] at most).
-template <int QT, bool BF16_OUT, bool GROUPED>
-static cudaError_t launch_gemm_t(const void* a, const void* w, void* c, int64_t rows, int64_t K,
-                                 int64_t N, int64_t RB, int64_t slab_bytes, const int* seg,
+template <int QT, bool BF16_OUT, bool GROUPED, bool SWI>
+static cudaError_t launch_gemm_t(const void* a, const void* w, const void* w2, void* c, int64_t rows,
+                                 int64_t K, int64_t N, int64_t RB, int64_t slab_bytes, const int* seg,
                                  int n_seg, cudaStream_t st, GemmEpi ep) {
   using namespace gemm;
   using L = Smem<QT>;
   using R = Raw<QT>;
   auto enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
-  CUtensorMap ma, mw;
+  CUtensorMap ma, mw, mw2;
   {  // A: [rows][K] bf16, boxes of 128 rows x 64 K, 128-byte swizzle
     cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)K * 2};
@@ -785,17 +830,24 @@ static cudaError_t launch_gemm_t(const void* a, const void* w, void* c, int64_t 
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
-  {  // W: [slab][K][RB] bytes as uint16, boxes of 64 rows x one tile's (aligned) bytes
-    cuuint64_t dims[3] = {(cuuint64_t)(RB / 2), (cuuint64_t)K, (cuuint64_t)(GROUPED ? n_seg : 1)};
+  // W (and, fused with SwiGLU, the up matrix W2): [slab][K][RB] bytes as uint16, boxes of
+  // 64 rows x one tile's (aligned) bytes.  A fused call covers I = N columns of each.
+  // The map's rows end at the matrix's own N columns (a packed gate | up row is longer than
+  // either part): a box reaching past them (the last Q6_K tile's 240 bytes) reads zeros,
+  // never the next part or memory past the buffer.
+  const int64_t row_n = (N / Fmt<QT>::kValues) * Fmt<QT>::kBytes;
+  for (int m = 0; m < (SWI ? 2 : 1); ++m) {
+    cuuint64_t dims[3] = {(cuuint64_t)(row_n / 2), (cuuint64_t)K, (cuuint64_t)(GROUPED ? n_seg : 1)};
     cuuint64_t strides[2] = {(cuuint64_t)RB, (cuuint64_t)(GROUPED ? slab_bytes : RB * K)};
     cuuint32_t box[3] = {(cuuint32_t)(R::kPitch / 2), BK, 1};
     cuuint32_t es[3] = {1, 1, 1};
-    if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT16, GROUPED ? 3 : 2, const_cast<void*>(w), dims, strides,
-            box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+    if (enc(m ? &mw2 : &mw, CU_TENSOR_MAP_DATA_TYPE_UINT16, GROUPED ? 3 : 2, const_cast<void*>(m ? w2 : w), dims,
+            strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
-  auto kern = gemm_kernel<QT, BF16_OUT, GROUPED>;
+  if (!SWI) mw2 = mw;
+  auto kern = gemm_kernel<QT, BF16_OUT, GROUPED, SWI>;
   static DeviceOnce configured;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -808,8 +860,9 @@ static cudaError_t launch_gemm_t(const void* a, const void* w, void* c, int64_t 
   // two CTAs (one cluster) per 512 x 256 tile of C; grouped: an upper bound on the
   // segments' tile count (each segment adds at most one partial tile)
   const int64_t items = GROUPED ? (rows + BMP - 1) / BMP + n_seg : (rows + BMP - 1) / BMP;
-  const dim3 grid((unsigned)(2 * (N / BN)), (unsigned)items, 1);
-  kern<<<grid, kThreads, L::kAlloc, st>>>(ma, mw, c, (int)rows, (int)K, (int)N, seg, n_seg, ep);
+  // SWI: one pair per 128 columns of h (= per 256 columns of gate | up)
+  const dim3 grid((unsigned)(2 * (SWI ? N / 128 : N / BN)), (unsigned)items, 1);
+  kern<<<grid, kThreads, L::kAlloc, st>>>(ma, mw, mw2, c, (int)rows, (int)K, (int)N, seg, n_seg, ep);
   return cudaGetLastError();
 }
 
@@ -821,10 +874,10 @@ static cudaError_t dispatch_gemm(int qtype, const void* a, const void* w, void* 
   const bool bf = c_dtype == 1;
 #define VBQ_GEMM_CASE(QT)                                                                       \
   case QT:                                                                                      \
-    return bf ? launch_gemm_t<QT, true, GROUPED>(a, w, c, rows, K, N, row_bytes, slab_bytes, seg, \
-                                                 n_seg, st, ep)                                 \
-              : launch_gemm_t<QT, false, GROUPED>(a, w, c, rows, K, N, row_bytes, slab_bytes,    \
-                                                  seg, n_seg, st, ep);
+    return bf ? launch_gemm_t<QT, true, GROUPED, false>(a, w, w, c, rows, K, N, row_bytes, slab_bytes, \
+                                                        seg, n_seg, st, ep)                      \
+              : launch_gemm_t<QT, false, GROUPED, false>(a, w, w, c, rows, K, N, row_bytes,        \
+                                                         slab_bytes, seg, n_seg, st, ep);
   switch (qtype) {
     VBQ_GEMM_CASE(kQ4_K)
     VBQ_GEMM_CASE(kQ6_K)
@@ -844,6 +897,38 @@ cudaError_t launch_gemm_grouped(int qtype, const void* a, const void* w, void* c
                                 int64_t slab_bytes, const int* seg, int n_seg, cudaStream_t st) {
   return dispatch_gemm<true>(qtype, a, w, c, rows, K, N, row_bytes, c_dtype, slab_bytes, seg,
                              n_seg, st, GemmEpi{});
+}
+
+// Fused SwiGLU: h bf16 [rows, I] = silu(a W_gate) * (a W_up), W_gate / W_up K x I with row
+// stride row_bytes (plain) or slabs as the grouped GEMM (slab_bytes > 0, seg, n_seg).
+template <bool GROUPED>
+static cudaError_t dispatch_gemm_swiglu(int qtype, const void* a, const void* wg, const void* wu, void* h,
+                                        int64_t rows, int64_t K, int64_t I, int64_t row_bytes,
+                                        int64_t slab_bytes, const int* seg, int n_seg, cudaStream_t st) {
+  switch (qtype) {
+    case kQ4_K:
+      return launch_gemm_t<kQ4_K, true, GROUPED, true>(a, wg, wu, h, rows, K, I, row_bytes, slab_bytes, seg,
+                                                       n_seg, st, GemmEpi{});
+    case kQ6_K:
+      return launch_gemm_t<kQ6_K, true, GROUPED, true>(a, wg, wu, h, rows, K, I, row_bytes, slab_bytes, seg,
+                                                       n_seg, st, GemmEpi{});
+    case kQ8_0:
+      return launch_gemm_t<kQ8_0, true, GROUPED, true>(a, wg, wu, h, rows, K, I, row_bytes, slab_bytes, seg,
+                                                       n_seg, st, GemmEpi{});
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_gemm_swiglu(int qtype, const void* a, const void* w_gate, const void* w_up, void* h,
+                               int64_t M, int64_t K, int64_t I, int64_t row_bytes, cudaStream_t st) {
+  return dispatch_gemm_swiglu<false>(qtype, a, w_gate, w_up, h, M, K, I, row_bytes, 0, nullptr, 0, st);
+}
+
+cudaError_t launch_gemm_grouped_swiglu(int qtype, const void* a, const void* w_gate, const void* w_up,
+                                       void* h, int64_t rows, int64_t K, int64_t I, int64_t row_bytes,
+                                       int64_t slab_bytes, const int* seg, int n_seg, cudaStream_t st) {
+  return dispatch_gemm_swiglu<true>(qtype, a, w_gate, w_up, h, rows, K, I, row_bytes, slab_bytes, seg,
+                                    n_seg, st);
 }
 
 cudaError_t gemm_status(unsigned* out, bool clear) {

@@ -103,6 +103,15 @@ cudaError_t launch_gemm(int qtype, const void* a, const void* w, void* c, int64_
 cudaError_t launch_gemm_grouped(int qtype, const void* a, const void* w, void* c, int64_t rows,
                                 int64_t K, int64_t N, int64_t row_bytes, int c_dtype,
                                 int64_t slab_bytes, const int* seg, int n_seg, cudaStream_t st);
+// The gate | up GEMM fused with SwiGLU: h bf16 [M, I] = silu(a W_gate) * (a W_up), both
+// weights K x I with row stride row_bytes (same type); the grouped form takes slabs as
+// launch_gemm_grouped.  The result has the bits of the two GEMMs (bf16 out) followed by
+// launch_swiglu.
+cudaError_t launch_gemm_swiglu(int qtype, const void* a, const void* w_gate, const void* w_up, void* h,
+                               int64_t M, int64_t K, int64_t I, int64_t row_bytes, cudaStream_t st);
+cudaError_t launch_gemm_grouped_swiglu(int qtype, const void* a, const void* w_gate, const void* w_up,
+                                       void* h, int64_t rows, int64_t K, int64_t I, int64_t row_bytes,
+                                       int64_t slab_bytes, const int* seg, int n_seg, cudaStream_t st);
 cudaError_t gemm_status(unsigned* out, bool clear);
 
 // MoE pieces (vbq_moe.cu).  Routing of T tokens over E experts from fp32 logits [T, E]:

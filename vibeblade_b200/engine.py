@@ -32,7 +32,7 @@ import torch
 
 from . import formats as F
 from .dequant import gemv_fused
-from .gemm import gemm_dequant
+from .gemm import gemm_dequant, gemm_swiglu
 from .gguf import GGUFFile
 from .tp import SHARD_COLUMN_ALIGN, swiglu_rows
 
@@ -157,6 +157,11 @@ class DeviceLayer:
         return types[0]
 
     # ---- matmul plumbing ----
+    @staticmethod
+    def _gemm_ok(t: int, K: int, N: int) -> bool:
+        """Whether the tcgen05 GEMM takes a K x N matrix of type t."""
+        return t in F.QUANTIZED and N % 256 == 0 and F.row_bytes(t, N) % 16 == 0 and K % 8 == 0
+
     def _mm(self, x: torch.Tensor, w: torch.Tensor, K: int, N: int, t: int, *, bias=None, residual=None,
             swiglu_input=False, prefill: bool, out_dtype=torch.float32) -> torch.Tensor:
         """x [T, K] (or [T, 2K] with swiglu_input) times W -> [T, N]: the fused GEMV (bias and
@@ -166,8 +171,7 @@ class DeviceLayer:
         inside the GEMV it would be recomputed by every 256-column tile (measured on the 70B
         down projection: 48 us plain against 77 us fused at batch 1, 304 against 892 at 16)."""
         T = x.shape[0]
-        gemm_ok = t in F.QUANTIZED and N % 256 == 0 and F.row_bytes(t, N) % 16 == 0 and K % 8 == 0
-        if prefill and gemm_ok:
+        if prefill and self._gemm_ok(t, K, N):
             a = x.to(torch.bfloat16).contiguous()
             if swiglu_input:
                 a = swiglu_rows(a, K)
@@ -216,9 +220,17 @@ class DeviceLayer:
         """residual + down(silu(h Wgate) * (h Wup)) (cpp/src/fast_model.cpp:906-998)."""
         prefill = h.shape[0] > DECODE_MAX_TOKENS if prefill is None else prefill
         c = self.cfg
+        res = residual.float().contiguous() if self.rank == 0 else None
+        gate_bytes = F.row_bytes(self.gu_type, self.ffn_loc)
+        if (prefill and self._gemm_ok(self.gu_type, c.hidden, 2 * self.ffn_loc) and self.ffn_loc % 256 == 0
+                and gate_bytes % 16 == 0):
+            # gate | up and SwiGLU in one GEMM (the [T, 2I] intermediate never written)
+            hs = gemm_swiglu(h.to(torch.bfloat16).contiguous(), self.w_gu, self.w_gu.view(-1)[gate_bytes:], None,
+                             h.shape[0], c.hidden, self.ffn_loc, self.gu_type, row_bytes=2 * gate_bytes)
+            y = self._mm(hs, self.w_down, self.ffn_loc, c.hidden, self.down_type, residual=res, prefill=True)
+            return self._reduce(y)
         gu = self._mm(h, self.w_gu, c.hidden, 2 * self.ffn_loc, self.gu_type, prefill=prefill,
                       out_dtype=torch.bfloat16 if prefill else torch.float32)
-        res = residual.float().contiguous() if self.rank == 0 else None
         y = self._mm(gu, self.w_down, self.ffn_loc, c.hidden, self.down_type, residual=res,
                      swiglu_input=True, prefill=prefill)
         return self._reduce(y)

@@ -68,3 +68,37 @@ def device_status(clear: bool = True) -> int:
     if rc not in (_lib.VBQ_OK, _lib.VBQ_ERR_TIMEOUT):
         _lib.check(rc, lib)
     return int(v.value)
+
+
+def gemm_swiglu(a: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, out: torch.Tensor | None,
+                M: int, K: int, I: int, wtype, row_bytes: int = 0) -> torch.Tensor:
+    """The gate | up GEMM fused with SwiGLU (vbq_gemm_swiglu): bf16 [M, I] =
+    silu(a W_gate) * (a W_up) (cpp/src/fast_model.cpp:906-953), the same bits as two
+    ``gemm_dequant`` calls with bf16 output and ``swiglu`` without the [M, 2I] round trip.
+
+    ``a``: bf16 [M, K]; ``w_gate`` / ``w_up``: the block bytes of two K x I matrices of one
+    type, each starting at its tensor's data pointer with rows ``row_bytes`` apart (0: the
+    packed row of I columns).  For a gate | up matrix packed side by side, pass it as
+    ``w_gate``, ``w_up`` = a view starting at the up part, and the packed row stride."""
+    t = F.parse_type(wtype)
+    _require_cuda("gemm_swiglu", a)
+    for w in (w_gate, w_up):
+        if not isinstance(w, torch.Tensor) or not w.is_cuda:
+            raise RuntimeError("gemm_swiglu: tensors must be CUDA tensors (the k-quant path runs on the GPU only)")
+    if a.dtype != torch.bfloat16 or a.numel() != M * K:
+        raise RuntimeError(f"gemm_swiglu: a must be bfloat16 with M*K = {M * K} values")
+    stride = row_bytes or F.row_bytes(t, I)
+    for name, w in (("w_gate", w_gate), ("w_up", w_up)):
+        span = w.numel() * w.element_size() if w.is_contiguous() else None
+        if span is not None and K > 0 and span < stride * (K - 1) + F.row_bytes(t, I):
+            raise RuntimeError(f"gemm_swiglu: {name} holds {span} bytes, too few for {K} rows")
+    if out is None:
+        out = torch.empty((M, I), dtype=torch.bfloat16, device=a.device)
+    else:
+        _require_cuda("gemm_swiglu", out)
+        if out.dtype != torch.bfloat16 or out.numel() != M * I:
+            raise RuntimeError("gemm_swiglu: out must be bfloat16 with M*I values")
+    lib = _lib.load()
+    _lib.check(lib.vbq_gemm_swiglu(a.data_ptr(), w_gate.data_ptr(), w_up.data_ptr(), out.data_ptr(), M, K, I,
+                                   t, row_bytes, _stream_ptr(a)), lib)
+    return out

@@ -30,7 +30,7 @@ import torch
 from . import _lib
 from . import formats as F
 from .dequant import _require_cuda, _stream_ptr, _weights_u8, gemv_dequant
-from .gemm import gemm_dequant
+from .gemm import gemm_dequant, gemm_swiglu
 
 # GEMM tiles are 256 columns wide; a column shard must keep whole tiles
 SHARD_COLUMN_ALIGN = 256
@@ -214,7 +214,7 @@ class TPFFN:
         M = x.shape[0]
         split = ((M // 2 + _PAIR_TILE_ROWS - 1) // _PAIR_TILE_ROWS) * _PAIR_TILE_ROWS
         if W == 1 or split >= M:
-            h = swiglu_rows(self.gate_up.prefill(x, torch.bfloat16), self.i_loc)
+            h = self.gate_up_swiglu(x)
             if not reduce:
                 return self.down.prefill(h, torch.float32)
             return row_split_prefill_reduced(self.down, h, self.group)
@@ -222,7 +222,7 @@ class TPFFN:
         y = torch.empty((M, self.down.n_loc), dtype=dt, device=x.device)
         work = None
         for lo, hi in ((0, split), (split, M)):
-            h = swiglu_rows(self.gate_up.prefill(x[lo:hi], torch.bfloat16), self.i_loc)
+            h = self.gate_up_swiglu(x[lo:hi])
             self.down.prefill(h, dt, out=y[lo:hi])
             if reduce:
                 if work is None:
@@ -232,6 +232,17 @@ class TPFFN:
         if work is not None:
             work.wait()
         return y if dt == torch.float32 else y.float()
+
+    def gate_up_swiglu(self, x: torch.Tensor) -> torch.Tensor:
+        """bf16 [M, H] -> bf16 h [M, I / W] = silu(x Wgate) * (x Wup) for this rank's shard: one
+        GEMM over the packed gate | up matrix with SwiGLU in its epilogue (vbq_gemm_swiglu),
+        where the up part starts on a 16-byte boundary; else the GEMM and a SwiGLU pass."""
+        g = self.gate_up
+        gate_bytes = F.row_bytes(g.t, self.i_loc)
+        if gate_bytes % 16 == 0 and self.i_loc % 256 == 0:
+            return gemm_swiglu(x, g.w, g.w.view(-1)[gate_bytes:], None, x.shape[0], g.k_loc, self.i_loc, g.t,
+                               row_bytes=2 * gate_bytes)
+        return swiglu_rows(g.prefill(x, torch.bfloat16), self.i_loc)
 
     def decode(self, x: torch.Tensor, reduce: bool = True) -> torch.Tensor:
         """x: fp32 [B, H] -> fp32 [B, H] (reduce as for prefill).  SwiGLU runs as one pass over
