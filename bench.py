@@ -503,6 +503,8 @@ def run_only(args) -> None:
         res = bench_prefill(dev, args.extras_steps)
     elif args.only == "moe":
         res = bench_moe(dev, args.extras_steps)
+    elif args.only == "lm_head":
+        res = bench_lm_head(dev, args.extras_steps)
     else:
         res = bench_tp(dev, rank, world, args.extras_steps)
     if world > 1:
@@ -880,7 +882,7 @@ def main() -> None:
     ap.add_argument("--no-extras", action="store_true",
                     help="skip those; config 5 is then measured on its decode side only")
     ap.add_argument("--extras-steps", type=int, default=10)
-    ap.add_argument("--only", choices=["decode", "prefill", "moe", "tp"],
+    ap.add_argument("--only", choices=["decode", "prefill", "moe", "lm_head", "tp"],
                     help="run just this measurement and print its JSON object")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -288,15 +288,16 @@ int vbq_gemm_ex(const void* a, const void* w, void* c, int64_t M, int64_t K, int
 
 int vbq_device_status(int32_t* status, int32_t clear) {
   if (!status) return fail(VBQ_ERR_NULL, "vbq_device_status: status is NULL");
-  unsigned g = 0, g2 = 0, g3 = 0, g4 = 0, g5 = 0, g6 = 0;
+  unsigned g = 0, g2 = 0, g3 = 0, g4 = 0, g5 = 0, g6 = 0, g7 = 0;
   cudaError_t e = vbq::gemv_status(&g, clear != 0);
   if (e == cudaSuccess) e = vbq::gemm_status(&g2, clear != 0);
   if (e == cudaSuccess) e = vbq::gemv_mma_status(&g3, clear != 0);
   if (e == cudaSuccess) e = vbq::gemv_wide_status(&g4, clear != 0);
   if (e == cudaSuccess) e = vbq::gemv_q8_status(&g5, clear != 0);
   if (e == cudaSuccess) e = vbq::gemv_half_status(&g6, clear != 0);
+  if (e == cudaSuccess) e = vbq::gemv_q6_status(&g7, clear != 0);
   if (e != cudaSuccess) return cuda_fail(e, "vbq_device_status");
-  g |= g2 | g3 | g4 | g5 | g6;
+  g |= g2 | g3 | g4 | g5 | g6 | g7;
   *status = (int32_t)g;
   if (g & 1u) return fail(VBQ_ERR_TIMEOUT, "a bounded device-side wait gave up (a copy never completed)");
   return ok();

@@ -533,7 +533,7 @@ int gemv_split_override() {
   return v;
 }
 
-// VBQ_GEMV_SCALAR=1 routes Q4_K and Q8_0 to the scalar kernel (comparison runs).
+// VBQ_GEMV_SCALAR=1 routes Q4_K, Q6_K and Q8_0 to the scalar kernel (comparison runs).
 static bool scalar_override() {
   static const bool v = [] {
     const char* env = getenv("VBQ_GEMV_SCALAR");
@@ -545,6 +545,7 @@ static bool scalar_override() {
 GemvPlan plan_gemv(int64_t K, int64_t N, int batch, int qtype) {
   GemvPlan p{};
   if (!scalar_override() && ((qtype == kQ4_K && gemv_mma_fits(K, N, batch)) ||
+                             (qtype == kQ6_K && gemv_q6_fits(K, N, batch)) ||
                              (qtype == kQ8_0 && gemv_q8_fits(K, N, batch)))) {
     p.splits = 1;  // chosen at launch; the splits reduce in a cluster, without scratch
     p.kslice = K;
@@ -638,7 +639,10 @@ cudaError_t launch_gemv(int qtype, const float* x, const void* w, float* y, int6
       if (!scalar_override() && gemv_mma_fits(K, N, batch))
         return launch_gemv_mma_q4k(x, w, y, K, N, row_bytes, batch, st, f);
       return launch_gemv_f<kQ4_K>(x, w, y, K, N, row_bytes, batch, plan, scratch, st, f);
-    case kQ6_K: return launch_gemv_f<kQ6_K>(x, w, y, K, N, row_bytes, batch, plan, scratch, st, f);
+    case kQ6_K:
+      if (!scalar_override() && gemv_q6_fits(K, N, batch))
+        return launch_gemv_q6_mma(x, w, y, K, N, row_bytes, batch, st, f);
+      return launch_gemv_f<kQ6_K>(x, w, y, K, N, row_bytes, batch, plan, scratch, st, f);
     case kQ8_0:
       if (!scalar_override() && gemv_q8_fits(K, N, batch))
         return launch_gemv_q8_mma(x, w, y, K, N, row_bytes, batch, st, f);

@@ -1,0 +1,646 @@
+// vbq_gemv_q6.cu -- Q6_K dequant-GEMV on the integer tensor cores (decode, batch 1).
+//
+//   y[n] = sum_k x[k] * deq(W)[k, n],   deq(W)[k, n] = (d[k] * sc[k, s]) * (u[k, n] - 32)
+//
+// with the reference's Q6_K block (cpp/src/dequant.cpp:359-402): 256 values in 210 bytes,
+// ql[128] @0 (value i: nibble i & 1 of byte i >> 1), qh[64] @128 (value i: 2-bit field
+// i & 3 of byte i >> 2), int8 scales[16] @192 (s = i >> 4), fp16 d @208; u = lo | hi << 4.
+// Regrouped as
+//   y[n] = sum_k u[k, n] * v[k, s]  -  32 * sum_k v[k, s],   v = x * (d * sc),
+// the first term runs on mma.sync m16n8k32 (u8 x s8 -> s32), two instructions per 1024
+// weights, the second in fp32 on the side:
+//   * A (16 columns x 32 rows): the 6-bit codes u as exact u8.  A pair p of ql bytes
+//     (2p, 2p + 1) holds values 4p .. 4p + 3 and shares qh byte p.  M-tile row g of a
+//     16-byte ql chunk is the pair's even byte, row g + 8 its odd byte; the low-nibble
+//     MMA takes values 4p and 4p + 2, the high-nibble MMA 4p + 1 and 4p + 3.  Each lane
+//     loads its fragment bytes itself (a 16-bit load of its pair per row, an 8-bit load
+//     of its qh byte per row): Q6_K blocks are only 2-byte aligned in a row, so the rows
+//     cannot go through ldmatrix without first being copied to aligned addresses.  Four
+//     PRMTs turn four rows' pairs into the even- and odd-byte registers, three PRMTs the
+//     qh bytes, and one LOP3 per register merges nibble and high bits.
+//   * B (32 rows x 8): v as a 22-bit fixed-point integer n on a power-of-two scale per
+//     warp, in three signed byte digits (the 1.5 * 2^23 magic, as in vbq_gemv_mma.cu).
+//     A chunk covers two 16-column sub-blocks (pairs 8c .. 8c + 3 and 8c + 4 .. 8c + 7),
+//     so B columns 0-2 hold the digits of the first sub-block's v and 4-6 the second's;
+//     columns 3 and 7 are all ones, so the MMA also yields sum u, and the digit offset
+//     comes off in int32.  Every B column is used.
+//   * The s32 accumulators run across the CTA's stages; a stage whose |v| outgrows the
+//     scale, or whose sampled |v| all sit 16x below it, moves the sums to fp32 and sets
+//     the scale again (warp-uniform; rare on ordinary activations).
+// Accuracy: each v is rounded to 2^-20 of the warp's largest |v| in the stage that set the
+// scale (headroom 2-4x), products and sums exact, fp32 at the end.  A non-finite v marks
+// the warp's 128 outputs NaN.
+//
+// Decomposition: a CTA owns one 256-column tile (one block per row) and every S-th 128-row
+// stage of the matrix; the S splits of a tile form one thread-block cluster and add up in
+// split 0's shared memory (st.async), as in vbq_gemv_mma.cu.
+// Staging: a row pitch RB = 210 N / 256 is only 2-byte aligned, but rows k = c + 8i of one
+// class c lie 8 RB apart, a multiple of 16 bytes.  So each class has its own 2-D tensor
+// map (base: the row-c start rounded down to 16 bytes; x in bytes), and warp 8 loads a
+// stage with eight TMA boxes of 16 rows x 224 bytes, the 16-byte-aligned window that holds
+// the tile's block in each row (the block sits at byte o = its address mod 16 of the
+// window, the same o for the whole class).  Per-row bulk copies (128 per stage) measured
+// 2.6x slower than the scalar kernel: the copy engine's cost per request dominates.  The
+// maps end at each row's last byte and at K, so the boxes zero-fill past the matrix.
+// Stage row r sits at (r mod 8) x 3584 + 224 (r / 8).  The MMA's reduction index k of a
+// warp (rows 32q .. 32q + 31) maps to stage row 32q + 8t + 4h + j for k = 16h + 4t + j, so
+// the four rows of one fragment load (t = 0..3) sit 224 bytes apart in one box: distinct
+// 32-byte bank windows, and every 16-bit fragment load is one wavefront.  Warps 0-7 each
+// take 32 rows x 128 columns of a stage: the B table for their rows, then 4 x 2 MMAs.
+// Waits are bounded.
+#include <cuda.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "vbq_common.cuh"
+#include "vbq_gemv_mma.cuh"
+#include "vbq_internal.h"
+
+namespace vbq {
+
+// Sticky error bits of this file's kernel (kStatusTimeout: a bounded wait gave up).
+__device__ unsigned g_gemv_q6_status = 0;
+
+namespace gq6 {
+
+using gmma::kMagic;
+using gmma::kExpMin;
+using gmma::kExpMax;
+using gmma::pow2f;
+using gmma::inv_pow2;
+using gmma::mma_u8s8;
+using gmma::mbar_wait_hinted;
+using gmma::cluster_arrive;
+using gmma::cluster_wait;
+using gmma::cluster_rank;
+using gmma::mapa_u32;
+using gmma::st_async_v4;
+
+constexpr int kConsumers = 8;
+constexpr int kThreads = 32 * (kConsumers + 1);
+constexpr int kRows = 16 * kConsumers;  // rows per stage
+constexpr int kBlock = 210;             // bytes of one Q6_K block
+constexpr int kWin = 224;               // loaded window per row (covers o + 210, o <= 14)
+constexpr int kBoxRows = kRows / 8;     // rows of one class in a stage
+constexpr int kBoxBytes = kBoxRows * kWin;  // 3584 = 28 x 128: boxes stay 128-byte aligned
+// stage row r: box r mod 8, row r / 8 of the box
+__host__ __device__ constexpr int line_off(int r) { return (r & 7) * kBoxBytes + kWin * (r >> 3); }
+constexpr int kStageBytes = 8 * kBoxBytes;  // 28672
+constexpr int kStages = 4;  // a power of two
+// B table per warp: [4 chunks][8 columns][32 rows] s8, rows ordered so that lane (g, t)'s
+// two fragment words are adjacent (one 8-byte load at byte 8t of column g); chunk stride
+// 288 B keeps the table stores of the four chunks on different banks.
+constexpr int kColStride = 32;
+constexpr int kChunkStride = 288;
+constexpr int kTblBytes = 4 * kChunkStride;
+constexpr int kRedBytes = kConsumers * 128 * 4 + 256 * 4;  // per-warp outputs + CTA sum
+
+// the eight class maps (a grid constant: 1 KB of kernel parameters)
+struct ClassMaps {
+  CUtensorMap m[8];
+};
+
+struct Bars {
+  uint64_t full[kStages], empty[kStages];
+  uint64_t red;  // the cluster leader's: the other splits' partial sums have landed
+  int abort;
+};
+constexpr int kTblOff = kStages * kStageBytes;
+constexpr int kBarOff = kTblOff + kConsumers * kTblBytes;
+constexpr int kRecvOff = kBarOff + 128;  // the leader's receive slots (sized at launch)
+constexpr int kSmemBase = kRecvOff + 128;  // + alignment slack
+static_assert(kRedBytes <= kStages * kStageBytes, "reduction buffer inside the ring");
+static_assert(sizeof(Bars) <= 128, "barrier block");
+constexpr int kMaxSplit = 16;
+
+template <bool SWIGLU>
+__global__ void __launch_bounds__(kThreads, 1)
+gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__ x, float* y,
+               int K, int N, int64_t RB, Epi epi) {
+  extern __shared__ uint8_t smem_raw[];
+  // 128-byte aligned: TMA box destinations
+  uint8_t* smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
+  Bars& bars = *reinterpret_cast<Bars*>(smem + kBarOff);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, split = blockIdx.y, S = gridDim.y;
+  // CTA `split` takes the 128-row stages split, split + S, split + 2S, ... of the matrix
+  const int tot_st = (K + kRows - 1) / kRows;
+  const int nst = split < tot_st ? (tot_st - split + S - 1) / S : 0;
+  // Offset of a row's block in its 16-byte window: (k RB + 210 tile) mod 16 (w is 16-byte
+  // aligned).  Stages start at multiples of 128 rows, so it depends only on the row's
+  // place r in the stage.
+  const int rb15 = (int)(RB & 15), t15 = (tile * kBlock) & 15;
+  auto off_of = [&](int r) { return (r * rb15 + t15) & 15; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&bars.full[s]), 1);
+      mbar_init(smem_u32(&bars.empty[s]), kConsumers);
+    }
+    mbar_init(smem_u32(&bars.red), 1);
+    bars.abort = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (S > 1) cluster_arrive();  // barriers initialised; waited for before any remote store
+  // Programmatic dependent launch: weights are streamed before waiting for the previous
+  // grid (they never depend on it), x, y and the cluster exchange only after.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  volatile int* abort_flag = &bars.abort;
+  auto give_up = [&]() {
+    *abort_flag = 1;
+    atomicOr(&g_gemv_q6_status, kStatusTimeout);
+  };
+
+  // flushed fp32 sums [chunk][low / high nibbles] of the lane's MMA row (g for t even,
+  // g + 8 for t odd), the sums of v for the lane's two table sub-blocks, non-finite flag
+  float fac[4][2];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) fac[c][0] = fac[c][1] = 0.f;
+  float2 sv = make_float2(0.f, 0.f);
+  unsigned nonfin = 0u;
+
+  if (warp == kConsumers) {
+    // ------------------------------ TMA producer ------------------------------
+    // class c's box: x = the window of the tile's block in map c, y = the stage's first row
+    // of the class; classes without rows (K < 8) have no map and load nothing
+    const int n_cls = K < 8 ? K : 8;
+    const int xw = ((((int)(RB & 15) * lane) & 15) + tile * kBlock) & ~15;
+    int it = 0;
+    for (; it < nst; ++it) {
+      const int s = it & (kStages - 1);
+      if (it == kStages) asm volatile("griddepcontrol.wait;" ::: "memory");
+      int ok = 1;
+      if (lane == 0)
+        ok = !*abort_flag &&
+             mbar_wait_hinted(smem_u32(&bars.empty[s]), ((it / kStages) & 1) ^ 1, kWaitBudgetCycles);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0 && !*abort_flag) give_up();
+        break;
+      }
+      const uint32_t fb = smem_u32(&bars.full[s]);
+      if (lane == 0) mbar_arrive_expect_tx(fb, (uint32_t)(n_cls * kBoxBytes));
+      __syncwarp();
+      if (lane < n_cls)
+        gmma::tma_load_2d(smem_u32(smem + s * kStageBytes + lane * kBoxBytes), &maps.m[lane], xw,
+                          (split + S * it) * kBoxRows, fb);
+    }
+    // every issued stage lands before the CTA may exit
+    if (lane == 0)
+      for (int j = (it > kStages ? it - kStages : 0); j < it; ++j)
+        mbar_wait_bounded(smem_u32(&bars.full[j & (kStages - 1)]), (j / kStages) & 1, kWaitBudgetCycles);
+    __syncwarp();
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+  } else {
+    // ------------------------------ consumers ------------------------------
+    // warp: columns 128 gp .. + 127 and rows rw .. rw + 31 of each stage
+    const int gp = warp & 1, rw = 32 * (warp >> 1);
+    const int g = lane >> 2, t = lane & 3;   // MMA fragment role
+    const int m = lane & 7, cc = lane >> 3;  // table role: rows 4m .. 4m + 3, chunk cc
+    uint8_t* tbl = smem + kTblOff + warp * kTblBytes;
+    for (int i = lane; i < 4 * 2 * 8; i += 32) {  // all-ones columns 3 and 7 of each chunk
+      const int w8 = i & 7, c2 = (i >> 3) & 1, ch = i >> 4;
+      reinterpret_cast<uint32_t*>(tbl + ch * kChunkStride + (3 + 4 * c2) * kColStride)[w8] = 0x01010101u;
+    }
+    // Fragment loads, k = 4t + j (j < 4) and 16 + 4t + (j - 4): warp rows 8t + j and
+    // 8t + 4 + (j - 4); the pair of m-tile row g in chunk c is 8c + g, its ql bytes at
+    // o + 64 gp + 2 (8c + g), its qh byte at o + 128 + 32 gp + 8c + g.  The offsets are the
+    // same in every stage.
+    int ql_off[8], qh_off[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int r = rw + 8 * t + j;
+      const int base = line_off(r) + off_of(r);
+      ql_off[j] = base + 64 * gp + 2 * g;
+      qh_off[j] = base + 128 + 32 * gp + g;
+    }
+    // table rows k = 4m + j: warp rows 8 (m & 3) + 4 (m >> 2) + j (consecutive); d at o + 208,
+    // the scale pair (sub-blocks 8 gp + 2 cc, + 1) at o + 192 + 8 gp + 2 cc
+    const int trow = rw + 8 * (m & 3) + 4 * (m >> 2);
+    int d_off[4], sc_off[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = trow + j;
+      const int base = line_off(r) + off_of(r);
+      d_off[j] = base + 208;
+      sc_off[j] = base + 192 + 8 * gp + 2 * cc;
+    }
+    // the lane's table words: chunk cc, k = 4m .. 4m + 3 (byte 8 (m & 3) + 4 (m >> 2) of a
+    // column); its B fragments: column g, k = 4t .. 4t + 3 and 16 + 4t .. 16 + 4t + 3
+    uint8_t* const tcol = tbl + cc * kChunkStride + 8 * (m & 3) + 4 * (m >> 2);
+    const uint8_t* const tfrag = tbl + g * kColStride + 8 * t;
+    __syncwarp();
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    int acc[4][2][4];  // [chunk][low / high nibbles][fragment]
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) acc[c][h][0] = acc[c][h][1] = acc[c][h][2] = acc[c][h][3] = 0;
+    float scale = 1.f;     // a power of two; the step of v is 1 / scale
+    bool down_ok = false;  // the scale may come down (it was not set from an all-zero stage)
+    // s32 sums -> fp32.  Lanes t even hold digits 0, 1 of their sub-block, lanes t odd digit
+    // 2 and the code sum S.  With the top digit centred (d2 - 64 per code) the pair's parts
+    // are (a0 + 256 a1) and (65536 (a2 - 64 S) + 32896 S): the int32 difference is exact and
+    // the fp32 terms stay within 2^-20 of the result.
+    auto flush = [&]() {
+      const int odd = t & 1;
+      const float c1 = odd ? 65536.f : 1.f, c2 = odd ? 32896.f : 256.f;
+      const int cen = odd ? 64 : 0;
+      const float sb = inv_pow2(scale);
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          int* a = acc[c][h];
+          const float p0 = fmaf(c2, (float)a[1], c1 * (float)(a[0] - cen * a[1]));
+          const float p1 = fmaf(c2, (float)a[3], c1 * (float)(a[2] - cen * a[3]));
+          // the pair's halves: lane t even keeps row g, lane t odd row g + 8
+          const float mine = odd ? p1 : p0, other = odd ? p0 : p1;
+          const float sum = mine + __shfl_xor_sync(0xffffffffu, other, 1);
+          fac[c][h] = fmaf(sum, sb, fac[c][h]);
+          a[0] = a[1] = a[2] = a[3] = 0;
+        }
+    };
+
+    // x of the lane's table rows, two stages ahead
+    int kx = split * kRows + trow;
+    const int kstep = S * kRows;
+    auto load_x = [&](int k, float (&xv)[4]) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) xv[j] = k + j < K ? gemv_x<SWIGLU>(x, 0, K, k + j) : 0.f;
+    };
+    float xn[4], xnn[4];
+    load_x(kx, xn);
+    kx += kstep;
+    load_x(kx, xnn);
+#pragma unroll 1
+    for (int it = 0; it < nst; ++it) {
+      const int u = it & (kStages - 1);
+      const uint32_t par = (uint32_t)(it / kStages) & 1u;
+      float xv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        xv[j] = xn[j];
+        xn[j] = xnn[j];
+      }
+      kx += kstep;
+      load_x(kx, xnn);  // rows of the stage after next (zero past K)
+      if (!__all_sync(0xffffffffu, mbar_wait_hinted(smem_u32(&bars.full[u]), par, kWaitBudgetCycles))) {
+        if (lane == 0) give_up();
+        break;
+      }
+      const uint8_t* st = smem + u * kStageBytes;
+      const int krow = (split + S * it) * kRows + trow;  // the lane's first table row
+      // ---- v = x * (d * sc) of rows trow + j, sub-blocks (2 cc, 2 cc + 1) of the warp ----
+      float2 v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t dh = *reinterpret_cast<const uint16_t*>(st + d_off[j]);
+        const uint32_t sp = (uint32_t)*reinterpret_cast<const uint16_t*>(st + sc_off[j]) ^ 0x8080u;
+        // the int8 scales as floats: byte ^ 0x80 into the 2^23 magic, minus 2^23 + 128 (exact)
+        const float2 sc = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(sp, 0x4b000000u, 0x7650)),
+                                                 __uint_as_float(__byte_perm(sp, 0x4b000000u, 0x7651))),
+                                     make_float2(-8388736.f, -8388736.f));
+        const float d = f16_ref(dh);
+        // d * sc is the reference's fp32 scale (exact product); rows past K are zero-filled
+        const float2 dl = __fmul2_rn(make_float2(d, d), sc);
+        v[j] = krow + j < K ? __fmul2_rn(make_float2(xv[j], xv[j]), dl) : make_float2(0.f, 0.f);
+        sv = __fadd2_rn(sv, v[j]);
+      }
+      // v on the current scale: 1.5 * 2^23 + n in the float, in range exactly when the float
+      // keeps the exponent of 2^23 (|n| < 2^22); NaN, inf and overflow leave it
+      uint32_t wd[4][2];
+      uint32_t out = 0u;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        wd[j][0] = __float_as_uint(fmaf(v[j].x, scale, kMagic));
+        wd[j][1] = __float_as_uint(fmaf(v[j].y, scale, kMagic));
+        out |= (wd[j][0] ^ 0x4b000000u) | (wd[j][1] ^ 0x4b000000u);
+      }
+      // the shrink test: one sampled value per lane, |n| < 2^16 <=> w - (1.5 * 2^23 - 2^16)
+      // below 2^17 (an out-of-range word fails it and rescales through `out` anyway)
+      const bool shrink =
+          __all_sync(0xffffffffu, down_ok && (wd[0][0] - 0x4b3f0000u < 0x20000u));
+      if (__any_sync(0xffffffffu, out >= (1u << 23)) || shrink || it == 0) {
+        // rare (and the first stage): flag non-finite values, move the sums to fp32, then
+        // scale to 2-4x the warp's largest finite |v| and encode again.  The max ignores
+        // NaN and is capped so that huge values do not rescale every stage.
+        if (it > 0) flush();
+        float sum = 0.f, mx = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          sum += fabsf(v[j].x) + fabsf(v[j].y);
+          mx = fmaxf(mx, fmaxf(fabsf(v[j].x), fabsf(v[j].y)));
+        }
+        nonfin |= (sum < 0x1p100f) ? 0u : 1u;  // NaN / inf propagate
+        mx = fminf(mx, 0x1p99f);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        int e = (int)((__float_as_uint(mx) >> 23) & 0xffu) - 127 + 1;
+        e = e < kExpMin ? kExpMin : (e > kExpMax ? kExpMax : e);
+        scale = pow2f(21 - e);
+        down_ok = e > kExpMin;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          wd[j][0] = __float_as_uint(fmaf(v[j].x, scale, kMagic));
+          wd[j][1] = __float_as_uint(fmaf(v[j].y, scale, kMagic));
+        }
+      }
+      // ---- B table: three signed digits of n, four rows per word, per sub-block ----
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t a0 = wd[0][h], a1 = wd[1][h], a2 = wd[2][h], a3 = wd[3][h];
+        const uint32_t t01 = __byte_perm(a0, a1, 0x5140), t23 = __byte_perm(a2, a3, 0x5140);
+        const uint32_t u01 = __byte_perm(a0, a1, 0x0062), u23 = __byte_perm(a2, a3, 0x0062);
+        uint8_t* col = tcol + 4 * h * kColStride;
+        *reinterpret_cast<uint32_t*>(col) = __byte_perm(t01, t23, 0x5410) ^ 0x80808080u;
+        *reinterpret_cast<uint32_t*>(col + kColStride) = __byte_perm(t01, t23, 0x7632) ^ 0x80808080u;
+        *reinterpret_cast<uint32_t*>(col + 2 * kColStride) = __byte_perm(u01, u23, 0x5410);
+      }
+      __syncwarp();
+      // ---- 4 chunks of 8 pairs x 32 rows: low- and high-nibble MMAs ----
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t ev[2], od[2], hq[2];  // [rows 4t.. / 16 + 4t..]: even bytes, odd bytes, qh
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t q[4], hb[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            q[j] = *reinterpret_cast<const uint16_t*>(st + ql_off[4 * hh + j] + 16 * c);
+            hb[j] = st[qh_off[4 * hh + j] + 8 * c];
+          }
+          const uint32_t t01 = __byte_perm(q[0], q[1], 0x5140), t23 = __byte_perm(q[2], q[3], 0x5140);
+          ev[hh] = __byte_perm(t01, t23, 0x5410);
+          od[hh] = __byte_perm(t01, t23, 0x7632);
+          hq[hh] = __byte_perm(__byte_perm(hb[0], hb[1], 0x0040), __byte_perm(hb[2], hb[3], 0x0040), 0x5410);
+        }
+        // codes u = nibble | field << 4 (u8 0..63).  f02 holds fields 0 / 2 at bits 0-1 / 4-5
+        // of each byte, f13 fields 1 / 3; the masks keep each byte's bits 6-7 zero.
+        uint32_t alo[4], ahi[4];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint32_t f02 = hq[hh] & 0x33333333u, f13 = (hq[hh] >> 2) & 0x33333333u;
+          alo[2 * hh] = (ev[hh] & 0x0f0f0f0fu) | ((f02 << 4) & 0xf0f0f0f0u);      // value 4p
+          alo[2 * hh + 1] = (od[hh] & 0x0f0f0f0fu) | (f02 & 0xf0f0f0f0u);         // value 4p + 2
+          ahi[2 * hh] = ((ev[hh] >> 4) & 0x0f0f0f0fu) | ((f13 << 4) & 0xf0f0f0f0u);  // 4p + 1
+          ahi[2 * hh + 1] = ((od[hh] >> 4) & 0x0f0f0f0fu) | (f13 & 0xf0f0f0f0u);     // 4p + 3
+        }
+        const uint2 b = *reinterpret_cast<const uint2*>(tfrag + c * kChunkStride);
+        // fragment order: a0 row g k 0-15, a1 row g + 8, a2 row g k 16-31, a3 row g + 8
+        mma_u8s8(acc[c][0], alo[0], alo[1], alo[2], alo[3], b.x, b.y);
+        mma_u8s8(acc[c][1], ahi[0], ahi[1], ahi[2], ahi[3], b.x, b.y);
+      }
+      __syncwarp();  // table and stage reads done
+      if (lane == 0) mbar_arrive(smem_u32(&bars.empty[u]));
+    }
+    flush();
+    // sums of v over the lane's group (lanes 8 cc .. 8 cc + 7); flags over the warp
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      if (o < 8) {
+        sv.x += __shfl_xor_sync(0xffffffffu, sv.x, o);
+        sv.y += __shfl_xor_sync(0xffffffffu, sv.y, o);
+      }
+      nonfin |= __shfl_xor_sync(0xffffffffu, nonfin, o);
+    }
+  }
+
+  // ---- per-warp outputs -> shared memory (the stage ring, now idle) ----
+  __syncthreads();
+  float* red = reinterpret_cast<float*>(smem);  // [warp][the warp's 128 columns]
+  if (warp < kConsumers) {
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      // sums of v of chunk c's sub-blocks sit in lanes 8c .. 8c + 7
+      const float sx = __shfl_sync(0xffffffffu, sv.x, 8 * c);
+      const float sy = __shfl_sync(0xffffffffu, sv.y, 8 * c);
+      // lanes whose MMA rows (pairs 8c + g: sub-block g >> 2) met the B columns of that
+      // sub-block (t >> 1) hold outputs: row g (t even) / g + 8 (t odd) of the chunk, i.e.
+      // values 32c + 4g + 2 (t & 1) + h
+      if ((t >> 1) == (g >> 2)) {
+        const float off = 32.f * ((g >> 2) ? sy : sx);
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          red[warp * 128 + 32 * c + 4 * g + 2 * (t & 1) + h] =
+              nonfin ? __int_as_float(0x7fc00000) : fac[c][h] - off;
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- sum the warps in order: this CTA's partial y ----
+  constexpr int E = 256;
+  float* outbuf = red + kConsumers * 128;  // after the per-warp slots, still in the ring
+  for (int e = threadIdx.x; e < E; e += kThreads) {
+    const int half = e >> 7, cl = e & 127;
+    float v = 0.f;
+    for (int w2 = half; w2 < kConsumers; w2 += 2) v += red[w2 * 128 + cl];  // warps of this half
+    outbuf[e] = v;
+  }
+  __syncthreads();
+
+  if (S == 1) {
+    for (int e = threadIdx.x; e < E; e += kThreads)
+      y[tile * 256 + e] = epi_apply(epi, outbuf[e], 0, N, tile * 256 + e);
+    return;
+  }
+  // ---- split-K inside the cluster: splits 1 .. S-1 push their partials into the leader's
+  // slots (st.async, counted on its barrier) and exit; the leader adds them in split order
+  cluster_wait();  // every CTA of the cluster has initialised its barriers
+  const uint32_t rank = cluster_rank();
+  float* recv = reinterpret_cast<float*>(smem + kRecvOff);
+  if (rank != 0) {
+    const uint32_t dst = mapa_u32(smem_u32(recv + (rank - 1) * E), 0u);
+    const uint32_t bar = mapa_u32(smem_u32(&bars.red), 0u);
+    for (int e4 = threadIdx.x; e4 < E / 4; e4 += kThreads)
+      st_async_v4(dst + 16u * (uint32_t)e4, reinterpret_cast<const float4*>(outbuf)[e4], bar);
+    return;
+  }
+  if (threadIdx.x == 0) mbar_arrive_expect_tx(smem_u32(&bars.red), (uint32_t)((S - 1) * E * 4));
+  if (!mbar_wait_bounded(smem_u32(&bars.red), 0, kWaitBudgetCycles) && threadIdx.x == 0) give_up();
+  for (int e = threadIdx.x; e < E; e += kThreads) {
+    float sum = outbuf[e];
+    for (int sp = 1; sp < S; ++sp) sum += recv[(sp - 1) * E + e];
+    y[tile * 256 + e] = epi_apply(epi, sum, 0, N, tile * 256 + e);
+  }
+}
+
+}  // namespace gq6
+
+// ---- host side -----------------------------------------------------------------------
+
+static gmma::EncodeTiledFn encode_fn_q6() {
+  static gmma::EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<gmma::EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// The eight class maps of a K x RB Q6_K matrix at w (16-byte aligned): map c covers rows
+// c, c + 8, ... as a u8 array of (RB + delta_c) bytes per row, 8 RB apart, from the row-c
+// start rounded down to 16 bytes (delta_c = c RB mod 16 bytes before it); boxes of 224 bytes
+// x 16 rows.  Each host thread keeps the last few sets it encoded.  Returns false when
+// encoding fails.
+static bool class_maps(gmma::EncodeTiledFn enc, const void* w, int64_t K, int64_t RB, gq6::ClassMaps* out) {
+  struct Entry {
+    gq6::ClassMaps maps;
+    const void* w;
+    int64_t K, RB;
+    bool valid;
+  };
+  thread_local Entry cache[4] = {};
+  const uintptr_t key = (reinterpret_cast<uintptr_t>(w) >> 8) ^ (uintptr_t)K ^ ((uintptr_t)RB << 3);
+  Entry& e = cache[(key ^ (key >> 5)) & 3];
+  if (e.valid && e.w == w && e.K == K && e.RB == RB) {
+    *out = e.maps;
+    return true;
+  }
+  e.valid = false;
+  for (int c = 0; c < 8; ++c) {
+    if (c >= K) {  // no rows in this class: never loaded
+      memset(&e.maps.m[c], 0, sizeof(CUtensorMap));
+      continue;
+    }
+    const uintptr_t start = reinterpret_cast<uintptr_t>(w) + (uintptr_t)(c * RB);
+    const uintptr_t base = start & ~uintptr_t(15);
+    cuuint64_t dims[2] = {(cuuint64_t)(RB + (int64_t)(start - base)), (cuuint64_t)((K - c + 7) / 8)};
+    cuuint64_t strides[1] = {(cuuint64_t)(8 * RB)};
+    cuuint32_t box[2] = {(cuuint32_t)gq6::kWin, (cuuint32_t)gq6::kBoxRows};
+    cuuint32_t es[2] = {1, 1};
+    if (enc(&e.maps.m[c], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, reinterpret_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+  }
+  e.w = w, e.K = K, e.RB = RB, e.valid = true;
+  *out = e.maps;
+  return true;
+}
+
+// Splits per tile: at most one wave (one CTA per SM) and 16 (one cluster), the leader's
+// receive slots inside the shared-memory budget, and room for every tile's cluster at once
+// with 25 % to spare (cudaOccupancyMaxActiveClusters, cached per shape).
+template <bool SW>
+static int choose_splits_q6(int64_t K, int64_t N) {
+  using namespace gq6;
+  const int tiles = (int)(N / 256);
+  const int64_t tot_st = (K + kRows - 1) / kRows;
+  const int slots = sm_count();
+  int S = tiles > 0 ? slots / tiles : 1;
+  if (S > kMaxSplit) S = kMaxSplit;
+  if (S > tot_st) S = (int)tot_st;
+  if (S < 1) S = 1;
+  constexpr int cap = 227 * 1024;
+  if (gemv_split_override()) {
+    S = gemv_split_override() > kMaxSplit ? kMaxSplit : gemv_split_override();
+    if (S > tot_st) S = (int)tot_st;
+    while (S > 1 && kSmemBase + (S - 1) * 1024 > cap) --S;
+    return S;
+  }
+  while (S > 1 && kSmemBase + (S - 1) * 1024 > cap) --S;
+  struct Entry { int64_t tiles; int s_in, s_out; };
+  static Entry cache[32];
+  static int n_cache = 0;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n_cache; ++i)
+    if (cache[i].tiles == tiles && cache[i].s_in == S) return cache[i].s_out;
+  const int s_in = S;
+  for (; S > 1; --S) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)tiles, (unsigned)S, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSmemBase + (S - 1) * 1024;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = (unsigned)S;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int active = 0;
+    if (cudaOccupancyMaxActiveClusters(&active, gq6::gemv_q6_kernel<SW>, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      active = 0;
+    }
+    if (active * 4 >= tiles * 5) break;
+  }
+  if (n_cache < 32) cache[n_cache++] = Entry{tiles, s_in, S};
+  return S;
+}
+
+template <bool SW>
+static cudaError_t launch_q6_t(const float* x, const void* w, float* y, int64_t K, int64_t N,
+                               int64_t RB, cudaStream_t st, Epi epi) {
+  using namespace gq6;
+  auto enc = encode_fn_q6();
+  if (!enc) return cudaErrorNotSupported;
+  ClassMaps maps;
+  if (!class_maps(enc, w, K, RB, &maps)) return cudaErrorInvalidValue;
+  auto kern = gemv_q6_kernel<SW>;
+  static DeviceOnce configured;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (!configured.done(dev)) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+    configured.mark(dev);
+  }
+  const int S = choose_splits_q6<SW>(K, N);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(N / 256), (unsigned)S, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmemBase + (S - 1) * 1024;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = (unsigned)S;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = S > 1 ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kern, maps, x, y, (int)K, (int)N, RB, epi);
+}
+
+// Whether the tensor-core Q6_K kernel takes this call: batch 1, whole 256-column tiles, and
+// K up to 2^17 (the s32 sums hold at most K / 4 x 32 terms below 64 x 128 in magnitude,
+// well inside 2^31).  The weights must be 16-byte aligned (the C ABI requires it).
+constexpr int64_t kQ6MaxK = 131072;
+bool gemv_q6_fits(int64_t K, int64_t N, int batch) {
+  return batch == 1 && K >= 1 && K <= kQ6MaxK && N % 256 == 0 && N > 0;
+}
+
+cudaError_t launch_gemv_q6_mma(const float* x, const void* w, float* y, int64_t K, int64_t N,
+                               int64_t row_bytes, int batch, cudaStream_t st, const GemvFuse& f) {
+  if (!gemv_q6_fits(K, N, batch) || (reinterpret_cast<uintptr_t>(w) & 15u) != 0 ||
+      row_bytes != (N / 256) * gq6::kBlock)
+    return cudaErrorNotSupported;
+  const Epi epi{f.bias, f.res};
+  return f.swiglu_x ? launch_q6_t<true>(x, w, y, K, N, row_bytes, st, epi)
+                    : launch_q6_t<false>(x, w, y, K, N, row_bytes, st, epi);
+}
+
+cudaError_t gemv_q6_status(unsigned* out, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_gemv_q6_status, sizeof(unsigned));
+  if (e != cudaSuccess || !clear) return e;
+  const unsigned zero = 0;
+  return cudaMemcpyToSymbol(g_gemv_q6_status, &zero, sizeof(unsigned));
+}
+
+}  // namespace vbq

@@ -70,6 +70,13 @@ cudaError_t launch_gemv_q8_mma(const float* x, const void* w, float* y, int64_t 
                                int64_t row_bytes, int batch, cudaStream_t st,
                                const GemvFuse& f = GemvFuse{});
 cudaError_t gemv_q8_status(unsigned* out, bool clear);
+// Tensor-core Q6_K GEMV (vbq_gemv_q6.cu), batch 1, no scratch; w 16-byte aligned and
+// row_bytes the natural N / 256 * 210.
+bool gemv_q6_fits(int64_t K, int64_t N, int batch);
+cudaError_t launch_gemv_q6_mma(const float* x, const void* w, float* y, int64_t K, int64_t N,
+                               int64_t row_bytes, int batch, cudaStream_t st,
+                               const GemvFuse& f = GemvFuse{});
+cudaError_t gemv_q6_status(unsigned* out, bool clear);
 // Batch 5..16 kernel (vbq_gemv_wide.cu): x read by TMA, so rows of x 16-byte aligned.
 bool gemv_wide_fits(const float* x, int64_t K, int64_t N, int batch);
 cudaError_t launch_gemv_wide_q4k(const float* x, const void* w, float* y, int64_t K, int64_t N,
