@@ -137,10 +137,11 @@ def test_q6_swiglu_input_and_epilogue(cuda):
     torch.testing.assert_close(yf, y0 + bias + res, rtol=0, atol=1e-5)
 
 
-@pytest.mark.parametrize("N", [256, 2048, 8192, 37888])
+@pytest.mark.parametrize("N", [256, 2048, 8192, 37888, 49152, 65536])
 def test_q6_split_widths(cuda, N):
-    """Tile counts from 1 (the cluster split-K at its widest) to more tiles than SMs (one
-    split, several waves); no scratch is needed at batch 1."""
+    """Tile counts from 1 (the cluster split-K at its widest) through one wave of clusters
+    to more tiles than CTA slots (two splits over several waves, or one split filling a
+    wave); no scratch is needed at batch 1."""
     K = 8192
     assert vb.gemv_scratch_bytes(K, N, Q6, 1) == 0
     w = synthetic_weights(K, N, Q6, seed=N, device=cuda)

@@ -36,18 +36,22 @@
 // split 0's shared memory (st.async), as in vbq_gemv_mma.cu.
 // Staging: a row pitch RB = 210 N / 256 is only 2-byte aligned, but rows k = c + 8i of one
 // class c lie 8 RB apart, a multiple of 16 bytes.  So each class has its own 2-D tensor
-// map (base: the row-c start rounded down to 16 bytes; x in bytes), and warp 8 loads a
-// stage with eight TMA boxes of 16 rows x 224 bytes, the 16-byte-aligned window that holds
-// the tile's block in each row (the block sits at byte o = its address mod 16 of the
-// window, the same o for the whole class).  Per-row bulk copies (128 per stage) measured
-// 2.6x slower than the scalar kernel: the copy engine's cost per request dominates.  The
-// maps end at each row's last byte and at K, so the boxes zero-fill past the matrix.
+// map (base: the row-c start rounded down to 16 bytes; x in bytes), and a stage is eight
+// TMA boxes of 16 rows x 224 bytes, the 16-byte-aligned window that holds the tile's block
+// in each row (the block sits at byte o = its address mod 16 of the window, the same o for
+// the whole class).  Per-row bulk copies (128 per stage) measured 2.6x slower than the
+// scalar kernel: the copy engine's cost per request dominates.  The maps end at each row's
+// last byte and at K, so the boxes zero-fill past the matrix.
 // Stage row r sits at (r mod 8) x 3584 + 224 (r / 8).  The MMA's reduction index k of a
 // warp (rows 32q .. 32q + 31) maps to stage row 32q + 8t + 4h + j for k = 16h + 4t + j, so
 // the four rows of one fragment load (t = 0..3) sit 224 bytes apart in one box: distinct
-// 32-byte bank windows, and every 16-bit fragment load is one wavefront.  Warps 0-7 each
-// take 32 rows x 128 columns of a stage: the B table for their rows, then 4 x 2 MMAs.
-// Waits are bounded.
+// 32-byte bank windows, and every 16-bit fragment load is one wavefront.
+// Warps: eight per CTA, two CTAs per SM (128 registers a thread), each warp 32 rows x 128
+// columns of a stage: the B table for its rows, then 4 x 2 MMAs.  There is no producer
+// warp: a 3-slot ring per CTA, the first stages issued at the start, and the last warp to
+// finish a slot (a shared counter) refills it with the stage three further on.  The ALU
+// pipe bounds the kernel (code building and byte packing; the tensor pipe is ~8 % busy), so
+// fragment rows are packed with multiply-adds on the FMA pipe.  Waits are bounded.
 #include <cuda.h>
 
 #include <cstring>
@@ -78,7 +82,7 @@ using gmma::mapa_u32;
 using gmma::st_async_v4;
 
 constexpr int kConsumers = 8;
-constexpr int kThreads = 32 * (kConsumers + 1);
+constexpr int kThreads = 32 * kConsumers;  // no producer warp: the last warp through a slot refills it
 constexpr int kRows = 16 * kConsumers;  // rows per stage
 constexpr int kBlock = 210;             // bytes of one Q6_K block
 constexpr int kWin = 224;               // loaded window per row (covers o + 210, o <= 14)
@@ -87,7 +91,7 @@ constexpr int kBoxBytes = kBoxRows * kWin;  // 3584 = 28 x 128: boxes stay 128-b
 // stage row r: box r mod 8, row r / 8 of the box
 __host__ __device__ constexpr int line_off(int r) { return (r & 7) * kBoxBytes + kWin * (r >> 3); }
 constexpr int kStageBytes = 8 * kBoxBytes;  // 28672
-constexpr int kStages = 4;  // a power of two
+constexpr int kStages = 3;  // per CTA; two CTAs per SM keep six stages in flight
 // B table per warp: [4 chunks][8 columns][32 rows] s8, rows ordered so that lane (g, t)'s
 // two fragment words are adjacent (one 8-byte load at byte 8t of column g); chunk stride
 // 288 B keeps the table stores of the four chunks on different banks.
@@ -102,9 +106,11 @@ struct ClassMaps {
 };
 
 struct Bars {
-  uint64_t full[kStages], empty[kStages];
-  uint64_t red;  // the cluster leader's: the other splits' partial sums have landed
+  uint64_t full[kStages];
+  uint64_t red;               // the cluster leader's: the other splits' partial sums have landed
+  unsigned done[kStages];     // warps through the slot's current stage
   int abort;
+  int issued;                 // stages whose boxes have been issued
 };
 constexpr int kTblOff = kStages * kStageBytes;
 constexpr int kBarOff = kTblOff + kConsumers * kTblBytes;
@@ -114,8 +120,26 @@ static_assert(kRedBytes <= kStages * kStageBytes, "reduction buffer inside the r
 static_assert(sizeof(Bars) <= 128, "barrier block");
 constexpr int kMaxSplit = 16;
 
+// 16- / 8-bit shared loads at a 32-bit shared address, zero-extended
+__device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds_u8(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+// a * m + b on the FMA pipe (packing disjoint bit fields without the ALU pipe)
+__device__ __forceinline__ uint32_t mad_u32(uint32_t a, uint32_t m, uint32_t b) {
+  uint32_t d;
+  asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(m), "r"(b));
+  return d;
+}
+
 template <bool SWIGLU>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
 gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__ x, float* y,
                int K, int N, int64_t RB, Epi epi) {
   extern __shared__ uint8_t smem_raw[];
@@ -136,10 +160,11 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(smem_u32(&bars.full[s]), 1);
-      mbar_init(smem_u32(&bars.empty[s]), kConsumers);
+      bars.done[s] = 0u;
     }
     mbar_init(smem_u32(&bars.red), 1);
     bars.abort = 0;
+    bars.issued = nst < kStages ? nst : kStages;
     mbar_fence_init();
   }
   __syncthreads();
@@ -161,40 +186,24 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
   float2 sv = make_float2(0.f, 0.f);
   unsigned nonfin = 0u;
 
-  if (warp == kConsumers) {
-    // ------------------------------ TMA producer ------------------------------
-    // class c's box: x = the window of the tile's block in map c, y = the stage's first row
-    // of the class; classes without rows (K < 8) have no map and load nothing
-    const int n_cls = K < 8 ? K : 8;
-    const int xw = ((((int)(RB & 15) * lane) & 15) + tile * kBlock) & ~15;
-    int it = 0;
-    for (; it < nst; ++it) {
-      const int s = it & (kStages - 1);
-      if (it == kStages) asm volatile("griddepcontrol.wait;" ::: "memory");
-      int ok = 1;
-      if (lane == 0)
-        ok = !*abort_flag &&
-             mbar_wait_hinted(smem_u32(&bars.empty[s]), ((it / kStages) & 1) ^ 1, kWaitBudgetCycles);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) {
-        if (lane == 0 && !*abort_flag) give_up();
-        break;
-      }
-      const uint32_t fb = smem_u32(&bars.full[s]);
-      if (lane == 0) mbar_arrive_expect_tx(fb, (uint32_t)(n_cls * kBoxBytes));
-      __syncwarp();
-      if (lane < n_cls)
-        gmma::tma_load_2d(smem_u32(smem + s * kStageBytes + lane * kBoxBytes), &maps.m[lane], xw,
-                          (split + S * it) * kBoxRows, fb);
-    }
-    // every issued stage lands before the CTA may exit
-    if (lane == 0)
-      for (int j = (it > kStages ? it - kStages : 0); j < it; ++j)
-        mbar_wait_bounded(smem_u32(&bars.full[j & (kStages - 1)]), (j / kStages) & 1, kWaitBudgetCycles);
+  // Stage loads: class c's box at x = the window of the tile's block in map c, y = the
+  // stage's first row of the class; classes without rows (K < 8) have no map and load
+  // nothing.  One warp issues a stage: lane 0 sets the byte count, lanes 0 .. 7 a box each.
+  const int n_cls = K < 8 ? K : 8;
+  const int xw = ((((int)(RB & 15) * (lane & 7)) & 15) + tile * kBlock) & ~15;
+  auto load_stage = [&](int sidx, int slot) {
+    const uint32_t fb = smem_u32(&bars.full[slot]);
+    if (lane == 0) mbar_arrive_expect_tx(fb, (uint32_t)(n_cls * kBoxBytes));
     __syncwarp();
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-  } else {
-    // ------------------------------ consumers ------------------------------
+    if (lane < n_cls)
+      gmma::tma_load_2d(smem_u32(smem + slot * kStageBytes + lane * kBoxBytes), &maps.m[lane], xw,
+                        (split + S * sidx) * kBoxRows, fb);
+  };
+  // the first stages: weights never depend on the previous grid
+  if (warp == 0)
+    for (int s = 0; s < kStages && s < nst; ++s) load_stage(s, s);
+
+  {
     // warp: columns 128 gp .. + 127 and rows rw .. rw + 31 of each stage
     const int gp = warp & 1, rw = 32 * (warp >> 1);
     const int g = lane >> 2, t = lane & 3;   // MMA fragment role
@@ -278,7 +287,7 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
     load_x(kx, xnn);
 #pragma unroll 1
     for (int it = 0; it < nst; ++it) {
-      const int u = it & (kStages - 1);
+      const int u = it % kStages;
       const uint32_t par = (uint32_t)(it / kStages) & 1u;
       float xv[4];
 #pragma unroll
@@ -362,6 +371,14 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
       }
       __syncwarp();
       // ---- 4 chunks of 8 pairs x 32 rows: low- and high-nibble MMAs ----
+      // the fragment rows' shared addresses in this stage (chunk c adds 16c / 8c)
+      uint32_t qa[8], ha[8];
+      const uint32_t stb = smem_u32(st);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        qa[j] = stb + (uint32_t)ql_off[j];
+        ha[j] = stb + (uint32_t)qh_off[j];
+      }
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t ev[2], od[2], hq[2];  // [rows 4t.. / 16 + 4t..]: even bytes, odd bytes, qh
@@ -370,23 +387,26 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
           uint32_t q[4], hb[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            q[j] = *reinterpret_cast<const uint16_t*>(st + ql_off[4 * hh + j] + 16 * c);
-            hb[j] = st[qh_off[4 * hh + j] + 8 * c];
+            q[j] = lds_u16(qa[4 * hh + j] + 16u * c);
+            hb[j] = lds_u8(ha[4 * hh + j] + 8u * c);
           }
-          const uint32_t t01 = __byte_perm(q[0], q[1], 0x5140), t23 = __byte_perm(q[2], q[3], 0x5140);
-          ev[hh] = __byte_perm(t01, t23, 0x5410);
-          od[hh] = __byte_perm(t01, t23, 0x7632);
-          hq[hh] = __byte_perm(__byte_perm(hb[0], hb[1], 0x0040), __byte_perm(hb[2], hb[3], 0x0040), 0x5410);
+          // rows j = 0..3 of the pair (even byte, odd byte) and of the qh byte, packed by
+          // multiply-adds; two PRMTs split even and odd bytes
+          const uint32_t p01 = mad_u32(q[1], 65536u, q[0]), p23 = mad_u32(q[3], 65536u, q[2]);
+          ev[hh] = __byte_perm(p01, p23, 0x6420);
+          od[hh] = __byte_perm(p01, p23, 0x7531);
+          hq[hh] = mad_u32(mad_u32(hb[3], 256u, hb[2]), 65536u, mad_u32(hb[1], 256u, hb[0]));
         }
         // codes u = nibble | field << 4 (u8 0..63).  f02 holds fields 0 / 2 at bits 0-1 / 4-5
         // of each byte, f13 fields 1 / 3; the masks keep each byte's bits 6-7 zero.
+        // (right shifts as mul.hi on the FMA pipe measured 5 % slower than these)
         uint32_t alo[4], ahi[4];
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const uint32_t f02 = hq[hh] & 0x33333333u, f13 = (hq[hh] >> 2) & 0x33333333u;
-          alo[2 * hh] = (ev[hh] & 0x0f0f0f0fu) | ((f02 << 4) & 0xf0f0f0f0u);      // value 4p
+          alo[2 * hh] = (ev[hh] & 0x0f0f0f0fu) | ((f02 * 16u) & 0xf0f0f0f0u);      // value 4p
           alo[2 * hh + 1] = (od[hh] & 0x0f0f0f0fu) | (f02 & 0xf0f0f0f0u);         // value 4p + 2
-          ahi[2 * hh] = ((ev[hh] >> 4) & 0x0f0f0f0fu) | ((f13 << 4) & 0xf0f0f0f0u);  // 4p + 1
+          ahi[2 * hh] = ((ev[hh] >> 4) & 0x0f0f0f0fu) | ((f13 * 16u) & 0xf0f0f0f0u);  // 4p + 1
           ahi[2 * hh + 1] = ((od[hh] >> 4) & 0x0f0f0f0fu) | (f13 & 0xf0f0f0f0u);     // 4p + 3
         }
         const uint2 b = *reinterpret_cast<const uint2*>(tfrag + c * kChunkStride);
@@ -395,7 +415,23 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
         mma_u8s8(acc[c][1], ahi[0], ahi[1], ahi[2], ahi[3], b.x, b.y);
       }
       __syncwarp();  // table and stage reads done
-      if (lane == 0) mbar_arrive(smem_u32(&bars.empty[u]));
+      // the last warp through slot u refills it with stage it + kStages: the warps' reads
+      // of the slot come before their count (release), the count before the refill
+      // (acquire), and the proxy fence orders them before the asynchronous copy
+      unsigned last = 0u;
+      if (lane == 0) {
+        __threadfence_block();
+        last = atomicAdd(&bars.done[u], 1u) == (unsigned)(kConsumers - 1);
+        __threadfence_block();
+      }
+      if (__shfl_sync(0xffffffffu, last, 0)) {
+        if (lane == 0) bars.done[u] = 0u;
+        if (it + kStages < nst) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          load_stage(it + kStages, u);
+          if (lane == 0) atomicMax(&bars.issued, it + kStages + 1);
+        }
+      }
     }
     flush();
     // sums of v over the lane's group (lanes 8 cc .. 8 cc + 7); flags over the warp
@@ -411,8 +447,17 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
 
   // ---- per-warp outputs -> shared memory (the stage ring, now idle) ----
   __syncthreads();
+  if (*abort_flag) {
+    // a wait gave up: boxes may still be landing in the ring; they land (bounded) first
+    if (threadIdx.x == 0) {
+      const int is = bars.issued;
+      for (int j = is > kStages ? is - kStages : 0; j < is; ++j)
+        mbar_wait_bounded(smem_u32(&bars.full[j % kStages]), (j / kStages) & 1, kWaitBudgetCycles);
+    }
+    __syncthreads();
+  }
   float* red = reinterpret_cast<float*>(smem);  // [warp][the warp's 128 columns]
-  if (warp < kConsumers) {
+  {
     const int g = lane >> 2, t = lane & 3;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
@@ -528,20 +573,27 @@ static bool class_maps(gmma::EncodeTiledFn enc, const void* w, int64_t K, int64_
   return true;
 }
 
-// Splits per tile: at most one wave (one CTA per SM) and 16 (one cluster), the leader's
-// receive slots inside the shared-memory budget, and room for every tile's cluster at once
-// with 25 % to spare (cudaOccupancyMaxActiveClusters, cached per shape).
+// Splits per tile: one wave (two CTAs per SM) when the tiles fit in it, with room for every
+// tile's cluster at once and 25 % to spare (cudaOccupancyMaxActiveClusters, cached per
+// shape); two splits past half a wave of tiles; at most 16 (one cluster) and the leader's
+// receive slots inside the shared-memory budget.
 template <bool SW>
 static int choose_splits_q6(int64_t K, int64_t N) {
   using namespace gq6;
   const int tiles = (int)(N / 256);
   const int64_t tot_st = (K + kRows - 1) / kRows;
-  const int slots = sm_count();
+  const int slots = 2 * sm_count();
   int S = tiles > 0 ? slots / tiles : 1;
+  // More tiles than half the slots: two splits, unless one already fills 85 % of a wave.
+  // Each SM runs its CTAs at a fixed rate (the ALU pipe bounds the kernel), so CTAs half as
+  // long even out the SMs' loads and shorten the last wave.  Measured (us, K = 4096, one /
+  // two splits): 192 tiles 52.2 / 44.6, 256 tiles 52.2 / 54.9, 400 tiles 83.7 / 81.8,
+  // 501 tiles 101.6 / 97.9, 593 tiles 128.9 / 120.8.
+  if (S < 2) S = (tiles <= slots && tiles * 100 >= 85 * slots) ? 1 : 2;
   if (S > kMaxSplit) S = kMaxSplit;
   if (S > tot_st) S = (int)tot_st;
   if (S < 1) S = 1;
-  constexpr int cap = 227 * 1024;
+  constexpr int cap = 113 * 1024;  // two CTAs per SM
   if (gemv_split_override()) {
     S = gemv_split_override() > kMaxSplit ? kMaxSplit : gemv_split_override();
     if (S > tot_st) S = (int)tot_st;
@@ -549,6 +601,7 @@ static int choose_splits_q6(int64_t K, int64_t N) {
     return S;
   }
   while (S > 1 && kSmemBase + (S - 1) * 1024 > cap) --S;
+  if ((int64_t)tiles * S > slots) return S;  // several waves by design: pairs place anywhere
   struct Entry { int64_t tiles; int s_in, s_out; };
   static Entry cache[32];
   static int n_cache = 0;
@@ -594,7 +647,7 @@ static cudaError_t launch_q6_t(const float* x, const void* w, float* y, int64_t 
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (!configured.done(dev)) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 113 * 1024);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
