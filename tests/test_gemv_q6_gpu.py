@@ -1,5 +1,6 @@
-"""The batch-1 Q6_K GEMV on the integer tensor cores (vbq_gemv_q6.cu) through its own paths:
-the per-warp power-of-two scale of v = x * d * sc (set from the first stage, set again
+"""The batch 1-2 Q6_K GEMV on the integer tensor cores (vbq_gemv_q6.cu) through its own
+paths: the per-warp, per-batch-row power-of-two scale of v = x * d * sc (set from the first
+stage, set again
 when a stage outgrows it or falls 16x below it, or when the first stage held only
 zeros), the -32 offset taken off through the sums of v, codes and scales at their
 extremes, rows whose 16-byte copy window reaches the end of the matrix, the cluster
@@ -38,25 +39,36 @@ def _check(y, ref, what):
 
 def _ref64(cuda, x, w, K, N):
     deq = vb.dequantize(w, K, N, Q6).double()
-    return (torch.as_tensor(x, device=cuda).double().reshape(1, K) @ deq).cpu().numpy()
+    return (torch.as_tensor(x, device=cuda).double().reshape(-1, K) @ deq).cpu().numpy()
 
 
+def _check_rows(y, ref, what):
+    for b in range(np.asarray(ref).reshape(-1, np.asarray(ref).shape[-1]).shape[0]):
+        _check(np.asarray(y).reshape(-1, np.asarray(y).shape[-1])[b],
+               np.asarray(ref).reshape(-1, np.asarray(ref).shape[-1])[b], f"{what} row {b}")
+
+
+@pytest.mark.parametrize("batch", [1, 2])
 @pytest.mark.parametrize("K,N", [(4096, 1024), (1000, 512), (14336, 4096), (4096, 12288)])
-def test_q6_scale_paths(cuda, oracle, K, N):
+def test_q6_scale_paths(cuda, oracle, K, N, batch):
     """Rows whose first stages are all zeros (scale unset, set by a later stage), rows that
     grow 10^4-fold half-way down (set again mid-matrix) and rows 10^-3 smaller (the scale
-    comes back down); each K-split of a tile meets them at its own first stage."""
+    comes back down); each K-split of a tile meets them at its own first stage.  At batch 2
+    the second row has a different profile, so the two rows' scales move independently."""
     rng = np.random.default_rng(K + N)
     w = synthetic_weights(K, N, Q6, seed=K + N, device=cuda)
-    x = rng.normal(0, 1, K).astype(np.float32)
-    x[: min(K, 700)] = 0.0
-    x[K // 2:] *= 1e4
-    x[K // 3: K // 2] *= 1e-3
+    x = rng.normal(0, 1, (batch, K)).astype(np.float32)
+    x[0, : min(K, 700)] = 0.0
+    x[0, K // 2:] *= 1e4
+    x[0, K // 3: K // 2] *= 1e-3
+    if batch > 1:
+        x[1, : K // 4] *= 1e3
+        x[1, K - min(K, 300):] = 0.0
     y = vb.gemv_dequant(torch.from_numpy(x).to(cuda), w, None, K, N, Q6).cpu().numpy()
     assert vb.device_status() == 0
-    _check(y, _ref64(cuda, x, w, K, N), "fp64")
+    _check_rows(y, _ref64(cuda, x, w, K, N), "fp64")
     if K * N <= 4096 * 4096:
-        _check(y, oracle.gemv_dequant(x[None], w.cpu().numpy(), K, N, Q6), "oracle")
+        _check_rows(y, oracle.gemv_dequant(x, w.cpu().numpy(), K, N, Q6), "oracle")
 
 
 def _blocks(K, N, rng, ql=None, qh=None, sc=None, d=None):
@@ -74,39 +86,41 @@ def _blocks(K, N, rng, ql=None, qh=None, sc=None, d=None):
     return b.reshape(K, nb * 210)
 
 
+@pytest.mark.parametrize("batch", [1, 2])
 @pytest.mark.parametrize("ql,qh,sc", [(0xff, 0xff, 127), (0x00, 0x00, -128), (0xff, 0xff, -128),
                                       (0x0f, 0xaa, -1), (None, None, None), (None, None, -128)])
-def test_q6_extreme_codes_and_scales(cuda, oracle, ql, qh, sc):
+def test_q6_extreme_codes_and_scales(cuda, oracle, ql, qh, sc, batch):
     """Codes at 63 and 0 (q = 31 and -32) and scales at +127 / -128: the u8 codes, the s8
     digits and the int32 centring at the ends of their ranges."""
     K, N = 1000, 768
     rng = np.random.default_rng(7)
     w = _blocks(K, N, rng, ql, qh, sc)
-    x = rng.normal(0, 1, K).astype(np.float32)
+    x = rng.normal(0, 1, (batch, K)).astype(np.float32)
     y = vb.gemv_dequant(torch.from_numpy(x).to(cuda), torch.from_numpy(w).to(cuda), None, K, N,
                         Q6).cpu().numpy()
     assert vb.device_status() == 0
-    _check(y, oracle.gemv_dequant(x[None], w, K, N, Q6), "oracle")
+    _check_rows(y, oracle.gemv_dequant(x, w, K, N, Q6), "oracle")
 
 
+@pytest.mark.parametrize("batch", [1, 2])
 @pytest.mark.parametrize("K", [1, 2, 3, 127, 128, 129, 255, 333])
 @pytest.mark.parametrize("N", [256, 768, 1280])
-def test_q6_matrix_end_windows(cuda, oracle, K, N):
+def test_q6_matrix_end_windows(cuda, oracle, K, N, batch):
     """Row pitches of 210, 630 and 1050 bytes: the blocks sit at every even offset of their
     16-byte windows, and the block that ends the matrix has its last bytes past the final
     16-byte boundary whenever K * pitch is not a multiple of 16."""
     rng = np.random.default_rng(K * 7 + N)
     w = quantize(rng.normal(0, 0.3, (K, N)).astype(np.float32), Q6).numpy()
-    x = rng.normal(0, 1, K).astype(np.float32)
+    x = rng.normal(0, 1, (batch, K)).astype(np.float32)
     y = vb.gemv_dequant(torch.from_numpy(x).to(cuda), torch.from_numpy(w).to(cuda), None, K, N,
                         Q6).cpu().numpy()
-    _check(y, oracle.gemv_dequant(x[None], w, K, N, Q6), "oracle")
+    _check_rows(y, oracle.gemv_dequant(x, w, K, N, Q6), "oracle")
 
 
 @pytest.mark.parametrize("bad", [float("nan"), float("inf"), float("-inf")])
-def test_q6_nonfinite_x(cuda, bad):
-    """A non-finite activation makes every output NaN (the reference's fp32 sum is NaN or
-    +-inf there)."""
+def test_q6_nonfinite_x(cuda, oracle, bad):
+    """A non-finite activation makes every output of its batch row NaN (the reference's fp32
+    sum is NaN or +-inf there); at batch 2 the other row is unaffected."""
     K, N = 2048, 1024
     w = synthetic_weights(K, N, Q6, seed=3, device=cuda)
     x = torch.randn(K, device=cuda)
@@ -114,22 +128,29 @@ def test_q6_nonfinite_x(cuda, bad):
     y = vb.gemv_dequant(x, w, None, K, N, Q6)
     assert torch.isnan(y).all()
     assert vb.device_status() == 0
+    x2 = torch.randn(2, K, device=cuda)
+    x2[1, 777] = bad
+    y2 = vb.gemv_dequant(x2, w, None, K, N, Q6)
+    assert torch.isnan(y2[1]).all()
+    assert vb.device_status() == 0
+    _check(y2[0].cpu().numpy(), _ref64(cuda, x2[0], w, K, N), "fp64 row 0")
 
 
-def test_q6_swiglu_input_and_epilogue(cuda):
-    """silu(gate) * up read from a [1, 2K] buffer; bias and residual added in the epilogue;
-    repeated calls bit-identical."""
+@pytest.mark.parametrize("batch", [1, 2])
+def test_q6_swiglu_input_and_epilogue(cuda, batch):
+    """silu(gate) * up read from a [batch, 2K] buffer; bias and residual added in the
+    epilogue; repeated calls bit-identical."""
     K, N = 14336, 4096
     w = synthetic_weights(K, N, Q6, seed=11, device=cuda)
-    gu = torch.randn(1, 2 * K, device=cuda) * 2
+    gu = torch.randn(batch, 2 * K, device=cuda) * 2
     h = torch.nn.functional.silu(gu[:, :K].double()) * gu[:, K:].double()
     y = vb.gemv_fused(gu, w, None, K, N, Q6, swiglu_input=True)
     assert vb.device_status() == 0
     ref = (h @ vb.dequantize(w, K, N, Q6).double()).cpu().numpy()
-    _check(y.cpu().numpy(), ref, "fp64")
-    x = torch.randn(1, K, device=cuda)
+    _check_rows(y.cpu().numpy(), ref, "fp64")
+    x = torch.randn(batch, K, device=cuda)
     bias = torch.randn(N, device=cuda)
-    res = torch.randn(1, N, device=cuda)
+    res = torch.randn(batch, N, device=cuda)
     y0 = vb.gemv_dequant(x, w, None, K, N, Q6)
     for _ in range(3):
         assert torch.equal(vb.gemv_dequant(x, w, None, K, N, Q6), y0)
@@ -137,15 +158,16 @@ def test_q6_swiglu_input_and_epilogue(cuda):
     torch.testing.assert_close(yf, y0 + bias + res, rtol=0, atol=1e-5)
 
 
+@pytest.mark.parametrize("batch", [1, 2])
 @pytest.mark.parametrize("N", [256, 2048, 8192, 37888, 49152, 65536])
-def test_q6_split_widths(cuda, N):
+def test_q6_split_widths(cuda, N, batch):
     """Tile counts from 1 (the cluster split-K at its widest) through one wave of clusters
     to more tiles than CTA slots (two splits over several waves, or one split filling a
-    wave); no scratch is needed at batch 1."""
+    wave); no scratch is needed at batch 1 or 2."""
     K = 8192
-    assert vb.gemv_scratch_bytes(K, N, Q6, 1) == 0
+    assert vb.gemv_scratch_bytes(K, N, Q6, batch) == 0
     w = synthetic_weights(K, N, Q6, seed=N, device=cuda)
-    x = torch.randn(1, K, device=cuda)
+    x = torch.randn(batch, K, device=cuda)
     y = vb.gemv_dequant(x, w, None, K, N, Q6)
     assert vb.device_status() == 0
-    _check(y.cpu().numpy(), _ref64(cuda, x, w, K, N), "fp64")
+    _check_rows(y.cpu().numpy(), _ref64(cuda, x, w, K, N), "fp64")

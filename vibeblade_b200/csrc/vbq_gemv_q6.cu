@@ -91,34 +91,47 @@ constexpr int kBoxBytes = kBoxRows * kWin;  // 3584 = 28 x 128: boxes stay 128-b
 // stage row r: box r mod 8, row r / 8 of the box
 __host__ __device__ constexpr int line_off(int r) { return (r & 7) * kBoxBytes + kWin * (r >> 3); }
 constexpr int kStageBytes = 8 * kBoxBytes;  // 28672
-constexpr int kStages = 3;  // per CTA; two CTAs per SM keep six stages in flight
 // B table per warp: [4 chunks][8 columns][32 rows] s8, rows ordered so that lane (g, t)'s
 // two fragment words are adjacent (one 8-byte load at byte 8t of column g); chunk stride
 // 288 B keeps the table stores of the four chunks on different banks.
 constexpr int kColStride = 32;
 constexpr int kChunkStride = 288;
 constexpr int kTblBytes = 4 * kChunkStride;
-constexpr int kRedBytes = kConsumers * 128 * 4 + 256 * 4;  // per-warp outputs + CTA sum
 
 // the eight class maps (a grid constant: 1 KB of kernel parameters)
 struct ClassMaps {
   CUtensorMap m[8];
 };
 
+constexpr int kMaxStages = 6;
 struct Bars {
-  uint64_t full[kStages];
+  uint64_t full[kMaxStages];
   uint64_t red;               // the cluster leader's: the other splits' partial sums have landed
-  unsigned done[kStages];     // warps through the slot's current stage
+  unsigned done[kMaxStages];  // warps through the slot's current stage
   int abort;
   int issued;                 // stages whose boxes have been issued
 };
-constexpr int kTblOff = kStages * kStageBytes;
-constexpr int kBarOff = kTblOff + kConsumers * kTblBytes;
-constexpr int kRecvOff = kBarOff + 128;  // the leader's receive slots (sized at launch)
-constexpr int kSmemBase = kRecvOff + 128;  // + alignment slack
-static_assert(kRedBytes <= kStages * kStageBytes, "reduction buffer inside the ring");
 static_assert(sizeof(Bars) <= 128, "barrier block");
 constexpr int kMaxSplit = 16;
+
+// Per batch size.  Batch 1: two CTAs per SM (125 registers) with a 3-slot ring each.
+// Batch 2: a second set of accumulators and tables needs more registers, so one CTA per SM
+// with a 6-slot ring.  Shared memory: the ring, one B table per warp and batch row, the
+// barriers, and the cluster leader's receive slots (sized at launch).
+template <int BATCH>
+struct Cfg {
+  static constexpr int kStages = BATCH == 1 ? 3 : 6;
+  static constexpr int kMinBlocks = BATCH == 1 ? 2 : 1;
+  static constexpr int kSmemCap = (BATCH == 1 ? 113 : 227) * 1024;
+  static constexpr int kTblOff = kStages * kStageBytes;
+  static constexpr int kBarOff = kTblOff + kConsumers * BATCH * kTblBytes;
+  static constexpr int kRecvOff = kBarOff + 128;
+  static constexpr int kSmemBase = kRecvOff + 128;  // + alignment slack
+  static_assert(kStages <= kMaxStages, "barrier block");
+  // per-warp outputs and the CTA's sum reuse the ring after the main loop
+  static_assert(kConsumers * BATCH * 128 * 4 + BATCH * 256 * 4 <= kStages * kStageBytes,
+                "reduction buffer inside the ring");
+};
 
 // 16- / 8-bit shared loads at a 32-bit shared address, zero-extended
 __device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
@@ -138,14 +151,17 @@ __device__ __forceinline__ uint32_t mad_u32(uint32_t a, uint32_t m, uint32_t b) 
   return d;
 }
 
-template <bool SWIGLU>
-__global__ void __launch_bounds__(kThreads, 2)
+// batch: rows of x and y present (1 .. BATCH)
+template <int BATCH, bool SWIGLU>
+__global__ void __launch_bounds__(kThreads, Cfg<BATCH>::kMinBlocks)
 gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__ x, float* y,
-               int K, int N, int64_t RB, Epi epi) {
+               int K, int N, int64_t RB, int batch, Epi epi) {
+  using C = Cfg<BATCH>;
+  constexpr int kStages = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   // 128-byte aligned: TMA box destinations
   uint8_t* smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
-  Bars& bars = *reinterpret_cast<Bars*>(smem + kBarOff);
+  Bars& bars = *reinterpret_cast<Bars*>(smem + C::kBarOff);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y, S = gridDim.y;
   // CTA `split` takes the 128-row stages split, split + S, split + 2S, ... of the matrix
@@ -178,12 +194,17 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
     atomicOr(&g_gemv_q6_status, kStatusTimeout);
   };
 
-  // flushed fp32 sums [chunk][low / high nibbles] of the lane's MMA row (g for t even,
-  // g + 8 for t odd), the sums of v for the lane's two table sub-blocks, non-finite flag
-  float fac[4][2];
+  // flushed fp32 sums [batch row][chunk][low / high nibbles] of the lane's MMA row (g for
+  // t even, g + 8 for t odd), the sums of v for the lane's two table sub-blocks per batch
+  // row, non-finite flags (bit b)
+  float fac[BATCH][4][2];
+  float2 sv[BATCH];
 #pragma unroll
-  for (int c = 0; c < 4; ++c) fac[c][0] = fac[c][1] = 0.f;
-  float2 sv = make_float2(0.f, 0.f);
+  for (int b = 0; b < BATCH; ++b) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) fac[b][c][0] = fac[b][c][1] = 0.f;
+    sv[b] = make_float2(0.f, 0.f);
+  }
   unsigned nonfin = 0u;
 
   // Stage loads: class c's box at x = the window of the tile's block in map c, y = the
@@ -208,10 +229,12 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
     const int gp = warp & 1, rw = 32 * (warp >> 1);
     const int g = lane >> 2, t = lane & 3;   // MMA fragment role
     const int m = lane & 7, cc = lane >> 3;  // table role: rows 4m .. 4m + 3, chunk cc
-    uint8_t* tbl = smem + kTblOff + warp * kTblBytes;
-    for (int i = lane; i < 4 * 2 * 8; i += 32) {  // all-ones columns 3 and 7 of each chunk
-      const int w8 = i & 7, c2 = (i >> 3) & 1, ch = i >> 4;
-      reinterpret_cast<uint32_t*>(tbl + ch * kChunkStride + (3 + 4 * c2) * kColStride)[w8] = 0x01010101u;
+    // the warp's B tables, one per batch row
+    uint8_t* tbl = smem + C::kTblOff + warp * BATCH * kTblBytes;
+    for (int i = lane; i < BATCH * 4 * 2 * 8; i += 32) {  // all-ones columns 3 and 7 of each chunk
+      const int w8 = i & 7, c2 = (i >> 3) & 1, ch = (i >> 4) & 3, tb = i >> 6;
+      reinterpret_cast<uint32_t*>(tbl + tb * kTblBytes + ch * kChunkStride + (3 + 4 * c2) * kColStride)[w8] =
+          0x01010101u;
     }
     // Fragment loads, k = 4t + j (j < 4) and 16 + 4t + (j - 4): warp rows 8t + j and
     // 8t + 4 + (j - 4); the pair of m-tile row g in chunk c is 8c + g, its ql bytes at
@@ -243,13 +266,19 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
     __syncwarp();
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
-    int acc[4][2][4];  // [chunk][low / high nibbles][fragment]
+    int acc[BATCH][4][2][4];  // [batch row][chunk][low / high nibbles][fragment]
+    float scale[BATCH];       // powers of two; the step of v is 1 / scale
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
+    for (int b = 0; b < BATCH; ++b) {
+      scale[b] = 1.f;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) acc[c][h][0] = acc[c][h][1] = acc[c][h][2] = acc[c][h][3] = 0;
-    float scale = 1.f;     // a power of two; the step of v is 1 / scale
-    bool down_ok = false;  // the scale may come down (it was not set from an all-zero stage)
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) acc[b][c][h][0] = acc[b][c][h][1] = acc[b][c][h][2] = acc[b][c][h][3] = 0;
+    }
+    // bit b: batch row b's scale may come down (a present row whose scale was not set from
+    // an all-zero stage)
+    uint32_t down_ok = 0u;
     // s32 sums -> fp32.  Lanes t even hold digits 0, 1 of their sub-block, lanes t odd digit
     // 2 and the code sum S.  With the top digit centred (d2 - 64 per code) the pair's parts
     // are (a0 + 256 a1) and (65536 (a2 - 64 S) + 32896 S): the int32 difference is exact and
@@ -258,30 +287,35 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
       const int odd = t & 1;
       const float c1 = odd ? 65536.f : 1.f, c2 = odd ? 32896.f : 256.f;
       const int cen = odd ? 64 : 0;
-      const float sb = inv_pow2(scale);
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int b = 0; b < BATCH; ++b) {
+        const float sb = inv_pow2(scale[b]);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          int* a = acc[c][h];
-          const float p0 = fmaf(c2, (float)a[1], c1 * (float)(a[0] - cen * a[1]));
-          const float p1 = fmaf(c2, (float)a[3], c1 * (float)(a[2] - cen * a[3]));
-          // the pair's halves: lane t even keeps row g, lane t odd row g + 8
-          const float mine = odd ? p1 : p0, other = odd ? p0 : p1;
-          const float sum = mine + __shfl_xor_sync(0xffffffffu, other, 1);
-          fac[c][h] = fmaf(sum, sb, fac[c][h]);
-          a[0] = a[1] = a[2] = a[3] = 0;
-        }
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            int* a = acc[b][c][h];
+            const float p0 = fmaf(c2, (float)a[1], c1 * (float)(a[0] - cen * a[1]));
+            const float p1 = fmaf(c2, (float)a[3], c1 * (float)(a[2] - cen * a[3]));
+            // the pair's halves: lane t even keeps row g, lane t odd row g + 8
+            const float mine = odd ? p1 : p0, other = odd ? p0 : p1;
+            const float sum = mine + __shfl_xor_sync(0xffffffffu, other, 1);
+            fac[b][c][h] = fmaf(sum, sb, fac[b][c][h]);
+            a[0] = a[1] = a[2] = a[3] = 0;
+          }
+      }
     };
 
     // x of the lane's table rows, two stages ahead
     int kx = split * kRows + trow;
     const int kstep = S * kRows;
-    auto load_x = [&](int k, float (&xv)[4]) {
+    auto load_x = [&](int k, float (&xv)[BATCH][4]) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) xv[j] = k + j < K ? gemv_x<SWIGLU>(x, 0, K, k + j) : 0.f;
+      for (int b = 0; b < BATCH; ++b)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) xv[b][j] = (b < batch && k + j < K) ? gemv_x<SWIGLU>(x, b, K, k + j) : 0.f;
     };
-    float xn[4], xnn[4];
+    float xn[BATCH][4], xnn[BATCH][4];
     load_x(kx, xn);
     kx += kstep;
     load_x(kx, xnn);
@@ -289,12 +323,14 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
     for (int it = 0; it < nst; ++it) {
       const int u = it % kStages;
       const uint32_t par = (uint32_t)(it / kStages) & 1u;
-      float xv[4];
+      float xv[BATCH][4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        xv[j] = xn[j];
-        xn[j] = xnn[j];
-      }
+      for (int b = 0; b < BATCH; ++b)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          xv[b][j] = xn[b][j];
+          xn[b][j] = xnn[b][j];
+        }
       kx += kstep;
       load_x(kx, xnn);  // rows of the stage after next (zero past K)
       if (!__all_sync(0xffffffffu, mbar_wait_hinted(smem_u32(&bars.full[u]), par, kWaitBudgetCycles))) {
@@ -304,7 +340,7 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
       const uint8_t* st = smem + u * kStageBytes;
       const int krow = (split + S * it) * kRows + trow;  // the lane's first table row
       // ---- v = x * (d * sc) of rows trow + j, sub-blocks (2 cc, 2 cc + 1) of the warp ----
-      float2 v[4];
+      float2 v[BATCH][4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint32_t dh = *reinterpret_cast<const uint16_t*>(st + d_off[j]);
@@ -316,59 +352,72 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
         const float d = f16_ref(dh);
         // d * sc is the reference's fp32 scale (exact product); rows past K are zero-filled
         const float2 dl = __fmul2_rn(make_float2(d, d), sc);
-        v[j] = krow + j < K ? __fmul2_rn(make_float2(xv[j], xv[j]), dl) : make_float2(0.f, 0.f);
-        sv = __fadd2_rn(sv, v[j]);
+        const bool live = krow + j < K;
+#pragma unroll
+        for (int b = 0; b < BATCH; ++b) {
+          v[b][j] = live ? __fmul2_rn(make_float2(xv[b][j], xv[b][j]), dl) : make_float2(0.f, 0.f);
+          sv[b] = __fadd2_rn(sv[b], v[b][j]);
+        }
       }
       // v on the current scale: 1.5 * 2^23 + n in the float, in range exactly when the float
       // keeps the exponent of 2^23 (|n| < 2^22); NaN, inf and overflow leave it
-      uint32_t wd[4][2];
-      uint32_t out = 0u;
+      uint32_t wd[BATCH][4][2];
+      uint32_t out = 0u, small = 0u;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        wd[j][0] = __float_as_uint(fmaf(v[j].x, scale, kMagic));
-        wd[j][1] = __float_as_uint(fmaf(v[j].y, scale, kMagic));
-        out |= (wd[j][0] ^ 0x4b000000u) | (wd[j][1] ^ 0x4b000000u);
+      for (int b = 0; b < BATCH; ++b) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          wd[b][j][0] = __float_as_uint(fmaf(v[b][j].x, scale[b], kMagic));
+          wd[b][j][1] = __float_as_uint(fmaf(v[b][j].y, scale[b], kMagic));
+          out |= (wd[b][j][0] ^ 0x4b000000u) | (wd[b][j][1] ^ 0x4b000000u);
+        }
+        // the shrink test: one sampled value per lane and batch row, |n| < 2^16 <=>
+        // w - (1.5 * 2^23 - 2^16) below 2^17 (an out-of-range word fails it and rescales
+        // through `out` anyway)
+        small |= (wd[b][0][0] - 0x4b3f0000u < 0x20000u) ? (1u << b) : 0u;
       }
-      // the shrink test: one sampled value per lane, |n| < 2^16 <=> w - (1.5 * 2^23 - 2^16)
-      // below 2^17 (an out-of-range word fails it and rescales through `out` anyway)
-      const bool shrink =
-          __all_sync(0xffffffffu, down_ok && (wd[0][0] - 0x4b3f0000u < 0x20000u));
+      const bool shrink = __reduce_and_sync(0xffffffffu, small & down_ok) != 0u;
       if (__any_sync(0xffffffffu, out >= (1u << 23)) || shrink || it == 0) {
         // rare (and the first stage): flag non-finite values, move the sums to fp32, then
-        // scale to 2-4x the warp's largest finite |v| and encode again.  The max ignores
-        // NaN and is capped so that huge values do not rescale every stage.
+        // scale each batch row to 2-4x the warp's largest finite |v| and encode again.  The
+        // max ignores NaN and is capped so that huge values do not rescale every stage.
         if (it > 0) flush();
-        float sum = 0.f, mx = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          sum += fabsf(v[j].x) + fabsf(v[j].y);
-          mx = fmaxf(mx, fmaxf(fabsf(v[j].x), fabsf(v[j].y)));
-        }
-        nonfin |= (sum < 0x1p100f) ? 0u : 1u;  // NaN / inf propagate
-        mx = fminf(mx, 0x1p99f);
+        for (int b = 0; b < BATCH; ++b) {
+          float sum = 0.f, mx = 0.f;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        int e = (int)((__float_as_uint(mx) >> 23) & 0xffu) - 127 + 1;
-        e = e < kExpMin ? kExpMin : (e > kExpMax ? kExpMax : e);
-        scale = pow2f(21 - e);
-        down_ok = e > kExpMin;
+          for (int j = 0; j < 4; ++j) {
+            sum += fabsf(v[b][j].x) + fabsf(v[b][j].y);
+            mx = fmaxf(mx, fmaxf(fabsf(v[b][j].x), fabsf(v[b][j].y)));
+          }
+          nonfin |= (sum < 0x1p100f) ? 0u : (1u << b);  // NaN / inf propagate
+          mx = fminf(mx, 0x1p99f);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          wd[j][0] = __float_as_uint(fmaf(v[j].x, scale, kMagic));
-          wd[j][1] = __float_as_uint(fmaf(v[j].y, scale, kMagic));
+          for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+          int e = (int)((__float_as_uint(mx) >> 23) & 0xffu) - 127 + 1;
+          e = e < kExpMin ? kExpMin : (e > kExpMax ? kExpMax : e);
+          scale[b] = pow2f(21 - e);
+          down_ok = (b < batch && e > kExpMin) ? (down_ok | (1u << b)) : (down_ok & ~(1u << b));
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            wd[b][j][0] = __float_as_uint(fmaf(v[b][j].x, scale[b], kMagic));
+            wd[b][j][1] = __float_as_uint(fmaf(v[b][j].y, scale[b], kMagic));
+          }
         }
       }
-      // ---- B table: three signed digits of n, four rows per word, per sub-block ----
+      // ---- B tables: three signed digits of n, four rows per word, per sub-block ----
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t a0 = wd[0][h], a1 = wd[1][h], a2 = wd[2][h], a3 = wd[3][h];
-        const uint32_t t01 = __byte_perm(a0, a1, 0x5140), t23 = __byte_perm(a2, a3, 0x5140);
-        const uint32_t u01 = __byte_perm(a0, a1, 0x0062), u23 = __byte_perm(a2, a3, 0x0062);
-        uint8_t* col = tcol + 4 * h * kColStride;
-        *reinterpret_cast<uint32_t*>(col) = __byte_perm(t01, t23, 0x5410) ^ 0x80808080u;
-        *reinterpret_cast<uint32_t*>(col + kColStride) = __byte_perm(t01, t23, 0x7632) ^ 0x80808080u;
-        *reinterpret_cast<uint32_t*>(col + 2 * kColStride) = __byte_perm(u01, u23, 0x5410);
-      }
+      for (int b = 0; b < BATCH; ++b)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t a0 = wd[b][0][h], a1 = wd[b][1][h], a2 = wd[b][2][h], a3 = wd[b][3][h];
+          const uint32_t t01 = __byte_perm(a0, a1, 0x5140), t23 = __byte_perm(a2, a3, 0x5140);
+          const uint32_t u01 = __byte_perm(a0, a1, 0x0062), u23 = __byte_perm(a2, a3, 0x0062);
+          uint8_t* col = tcol + b * kTblBytes + 4 * h * kColStride;
+          *reinterpret_cast<uint32_t*>(col) = __byte_perm(t01, t23, 0x5410) ^ 0x80808080u;
+          *reinterpret_cast<uint32_t*>(col + kColStride) = __byte_perm(t01, t23, 0x7632) ^ 0x80808080u;
+          *reinterpret_cast<uint32_t*>(col + 2 * kColStride) = __byte_perm(u01, u23, 0x5410);
+        }
       __syncwarp();
       // ---- 4 chunks of 8 pairs x 32 rows: low- and high-nibble MMAs ----
       // the fragment rows' shared addresses in this stage (chunk c adds 16c / 8c)
@@ -409,10 +458,14 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
           ahi[2 * hh] = ((ev[hh] >> 4) & 0x0f0f0f0fu) | ((f13 * 16u) & 0xf0f0f0f0u);  // 4p + 1
           ahi[2 * hh + 1] = ((od[hh] >> 4) & 0x0f0f0f0fu) | (f13 & 0xf0f0f0f0u);     // 4p + 3
         }
-        const uint2 b = *reinterpret_cast<const uint2*>(tfrag + c * kChunkStride);
-        // fragment order: a0 row g k 0-15, a1 row g + 8, a2 row g k 16-31, a3 row g + 8
-        mma_u8s8(acc[c][0], alo[0], alo[1], alo[2], alo[3], b.x, b.y);
-        mma_u8s8(acc[c][1], ahi[0], ahi[1], ahi[2], ahi[3], b.x, b.y);
+        // fragment order: a0 row g k 0-15, a1 row g + 8, a2 row g k 16-31, a3 row g + 8;
+        // one A for every batch row
+#pragma unroll
+        for (int b = 0; b < BATCH; ++b) {
+          const uint2 bf = *reinterpret_cast<const uint2*>(tfrag + b * kTblBytes + c * kChunkStride);
+          mma_u8s8(acc[b][c][0], alo[0], alo[1], alo[2], alo[3], bf.x, bf.y);
+          mma_u8s8(acc[b][c][1], ahi[0], ahi[1], ahi[2], ahi[3], bf.x, bf.y);
+        }
       }
       __syncwarp();  // table and stage reads done
       // the last warp through slot u refills it with stage it + kStages: the warps' reads
@@ -438,8 +491,11 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       if (o < 8) {
-        sv.x += __shfl_xor_sync(0xffffffffu, sv.x, o);
-        sv.y += __shfl_xor_sync(0xffffffffu, sv.y, o);
+#pragma unroll
+        for (int b = 0; b < BATCH; ++b) {
+          sv[b].x += __shfl_xor_sync(0xffffffffu, sv[b].x, o);
+          sv[b].y += __shfl_xor_sync(0xffffffffu, sv[b].y, o);
+        }
       }
       nonfin |= __shfl_xor_sync(0xffffffffu, nonfin, o);
     }
@@ -456,49 +512,53 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
     }
     __syncthreads();
   }
-  float* red = reinterpret_cast<float*>(smem);  // [warp][the warp's 128 columns]
+  float* red = reinterpret_cast<float*>(smem);  // [warp][batch row][the warp's 128 columns]
   {
     const int g = lane >> 2, t = lane & 3;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      // sums of v of chunk c's sub-blocks sit in lanes 8c .. 8c + 7
-      const float sx = __shfl_sync(0xffffffffu, sv.x, 8 * c);
-      const float sy = __shfl_sync(0xffffffffu, sv.y, 8 * c);
-      // lanes whose MMA rows (pairs 8c + g: sub-block g >> 2) met the B columns of that
-      // sub-block (t >> 1) hold outputs: row g (t even) / g + 8 (t odd) of the chunk, i.e.
-      // values 32c + 4g + 2 (t & 1) + h
-      if ((t >> 1) == (g >> 2)) {
-        const float off = 32.f * ((g >> 2) ? sy : sx);
+    for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
-          red[warp * 128 + 32 * c + 4 * g + 2 * (t & 1) + h] =
-              nonfin ? __int_as_float(0x7fc00000) : fac[c][h] - off;
+      for (int b = 0; b < BATCH; ++b) {
+        // sums of v of chunk c's sub-blocks sit in lanes 8c .. 8c + 7
+        const float sx = __shfl_sync(0xffffffffu, sv[b].x, 8 * c);
+        const float sy = __shfl_sync(0xffffffffu, sv[b].y, 8 * c);
+        // lanes whose MMA rows (pairs 8c + g: sub-block g >> 2) met the B columns of that
+        // sub-block (t >> 1) hold outputs: row g (t even) / g + 8 (t odd) of the chunk,
+        // i.e. values 32c + 4g + 2 (t & 1) + h
+        if ((t >> 1) == (g >> 2) && b < batch) {
+          const float off = 32.f * ((g >> 2) ? sy : sx);
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            red[(warp * BATCH + b) * 128 + 32 * c + 4 * g + 2 * (t & 1) + h] =
+                ((nonfin >> b) & 1u) ? __int_as_float(0x7fc00000) : fac[b][c][h] - off;
+        }
       }
-    }
   }
   __syncthreads();
 
-  // ---- sum the warps in order: this CTA's partial y ----
-  constexpr int E = 256;
-  float* outbuf = red + kConsumers * 128;  // after the per-warp slots, still in the ring
+  // ---- sum the warps in order: this CTA's partial y, [batch row][256] ----
+  const int E = batch * 256;
+  float* outbuf = red + kConsumers * BATCH * 128;  // after the per-warp slots, still in the ring
   for (int e = threadIdx.x; e < E; e += kThreads) {
-    const int half = e >> 7, cl = e & 127;
+    const int b = e >> 8, half = (e >> 7) & 1, cl = e & 127;
     float v = 0.f;
-    for (int w2 = half; w2 < kConsumers; w2 += 2) v += red[w2 * 128 + cl];  // warps of this half
+    for (int w2 = half; w2 < kConsumers; w2 += 2) v += red[(w2 * BATCH + b) * 128 + cl];  // this half's warps
     outbuf[e] = v;
   }
   __syncthreads();
 
   if (S == 1) {
-    for (int e = threadIdx.x; e < E; e += kThreads)
-      y[tile * 256 + e] = epi_apply(epi, outbuf[e], 0, N, tile * 256 + e);
+    for (int e = threadIdx.x; e < E; e += kThreads) {
+      const int b = e >> 8, n = tile * 256 + (e & 255);
+      y[(int64_t)b * N + n] = epi_apply(epi, outbuf[e], b, N, n);
+    }
     return;
   }
   // ---- split-K inside the cluster: splits 1 .. S-1 push their partials into the leader's
   // slots (st.async, counted on its barrier) and exit; the leader adds them in split order
   cluster_wait();  // every CTA of the cluster has initialised its barriers
   const uint32_t rank = cluster_rank();
-  float* recv = reinterpret_cast<float*>(smem + kRecvOff);
+  float* recv = reinterpret_cast<float*>(smem + C::kRecvOff);
   if (rank != 0) {
     const uint32_t dst = mapa_u32(smem_u32(recv + (rank - 1) * E), 0u);
     const uint32_t bar = mapa_u32(smem_u32(&bars.red), 0u);
@@ -511,7 +571,8 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
   for (int e = threadIdx.x; e < E; e += kThreads) {
     float sum = outbuf[e];
     for (int sp = 1; sp < S; ++sp) sum += recv[(sp - 1) * E + e];
-    y[tile * 256 + e] = epi_apply(epi, sum, 0, N, tile * 256 + e);
+    const int b = e >> 8, n = tile * 256 + (e & 255);
+    y[(int64_t)b * N + n] = epi_apply(epi, sum, b, N, n);
   }
 }
 
@@ -573,16 +634,17 @@ static bool class_maps(gmma::EncodeTiledFn enc, const void* w, int64_t K, int64_
   return true;
 }
 
-// Splits per tile: one wave (two CTAs per SM) when the tiles fit in it, with room for every
-// tile's cluster at once and 25 % to spare (cudaOccupancyMaxActiveClusters, cached per
-// shape); two splits past half a wave of tiles; at most 16 (one cluster) and the leader's
-// receive slots inside the shared-memory budget.
-template <bool SW>
-static int choose_splits_q6(int64_t K, int64_t N) {
+// Splits per tile: one wave (Cfg::kMinBlocks CTAs per SM) when the tiles fit in it, with
+// room for every tile's cluster at once and 25 % to spare (cudaOccupancyMaxActiveClusters,
+// cached per shape); two splits past half a wave of tiles; at most 16 (one cluster) and
+// the leader's receive slots (batch KB per split) inside the shared-memory budget.
+template <int BATCH, bool SW>
+static int choose_splits_q6(int64_t K, int64_t N, int batch) {
   using namespace gq6;
+  using C = Cfg<BATCH>;
   const int tiles = (int)(N / 256);
   const int64_t tot_st = (K + kRows - 1) / kRows;
-  const int slots = 2 * sm_count();
+  const int slots = C::kMinBlocks * sm_count();
   int S = tiles > 0 ? slots / tiles : 1;
   // More tiles than half the slots: two splits, unless one already fills 85 % of a wave.
   // Each SM runs its CTAs at a fixed rate (the ALU pipe bounds the kernel), so CTAs half as
@@ -593,28 +655,28 @@ static int choose_splits_q6(int64_t K, int64_t N) {
   if (S > kMaxSplit) S = kMaxSplit;
   if (S > tot_st) S = (int)tot_st;
   if (S < 1) S = 1;
-  constexpr int cap = 113 * 1024;  // two CTAs per SM
+  const int slot_bytes = batch * 1024;
   if (gemv_split_override()) {
     S = gemv_split_override() > kMaxSplit ? kMaxSplit : gemv_split_override();
     if (S > tot_st) S = (int)tot_st;
-    while (S > 1 && kSmemBase + (S - 1) * 1024 > cap) --S;
+    while (S > 1 && C::kSmemBase + (S - 1) * slot_bytes > C::kSmemCap) --S;
     return S;
   }
-  while (S > 1 && kSmemBase + (S - 1) * 1024 > cap) --S;
+  while (S > 1 && C::kSmemBase + (S - 1) * slot_bytes > C::kSmemCap) --S;
   if ((int64_t)tiles * S > slots) return S;  // several waves by design: pairs place anywhere
-  struct Entry { int64_t tiles; int s_in, s_out; };
+  struct Entry { int64_t tiles; int batch, s_in, s_out; };
   static Entry cache[32];
   static int n_cache = 0;
   static std::mutex mu;
   std::lock_guard<std::mutex> lock(mu);
   for (int i = 0; i < n_cache; ++i)
-    if (cache[i].tiles == tiles && cache[i].s_in == S) return cache[i].s_out;
+    if (cache[i].tiles == tiles && cache[i].batch == batch && cache[i].s_in == S) return cache[i].s_out;
   const int s_in = S;
   for (; S > 1; --S) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)tiles, (unsigned)S, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = kSmemBase + (S - 1) * 1024;
+    cfg.dynamicSmemBytes = C::kSmemBase + (S - 1) * slot_bytes;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
@@ -623,41 +685,42 @@ static int choose_splits_q6(int64_t K, int64_t N) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int active = 0;
-    if (cudaOccupancyMaxActiveClusters(&active, gq6::gemv_q6_kernel<SW>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&active, gq6::gemv_q6_kernel<BATCH, SW>, &cfg) != cudaSuccess) {
       cudaGetLastError();
       active = 0;
     }
     if (active * 4 >= tiles * 5) break;
   }
-  if (n_cache < 32) cache[n_cache++] = Entry{tiles, s_in, S};
+  if (n_cache < 32) cache[n_cache++] = Entry{tiles, batch, s_in, S};
   return S;
 }
 
-template <bool SW>
+template <int BATCH, bool SW>
 static cudaError_t launch_q6_t(const float* x, const void* w, float* y, int64_t K, int64_t N,
-                               int64_t RB, cudaStream_t st, Epi epi) {
+                               int64_t RB, int batch, cudaStream_t st, Epi epi) {
   using namespace gq6;
+  using C = Cfg<BATCH>;
   auto enc = encode_fn_q6();
   if (!enc) return cudaErrorNotSupported;
   ClassMaps maps;
   if (!class_maps(enc, w, K, RB, &maps)) return cudaErrorInvalidValue;
-  auto kern = gemv_q6_kernel<SW>;
+  auto kern = gemv_q6_kernel<BATCH, SW>;
   static DeviceOnce configured;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (!configured.done(dev)) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 113 * 1024);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemCap);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
     configured.mark(dev);
   }
-  const int S = choose_splits_q6<SW>(K, N);
+  const int S = choose_splits_q6<BATCH, SW>(K, N, batch);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(N / 256), (unsigned)S, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSmemBase + (S - 1) * 1024;
+  cfg.dynamicSmemBytes = C::kSmemBase + (S - 1) * batch * 1024;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -668,15 +731,15 @@ static cudaError_t launch_q6_t(const float* x, const void* w, float* y, int64_t 
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = S > 1 ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, kern, maps, x, y, (int)K, (int)N, RB, epi);
+  return cudaLaunchKernelEx(&cfg, kern, maps, x, y, (int)K, (int)N, RB, batch, epi);
 }
 
-// Whether the tensor-core Q6_K kernel takes this call: batch 1, whole 256-column tiles, and
-// K up to 2^17 (the s32 sums hold at most K / 4 x 32 terms below 64 x 128 in magnitude,
-// well inside 2^31).  The weights must be 16-byte aligned (the C ABI requires it).
+// Whether the tensor-core Q6_K kernel takes this call: batch 1 or 2, whole 256-column
+// tiles, and K up to 2^17 (the s32 sums hold at most K / 4 x 32 terms below 64 x 128 in
+// magnitude, well inside 2^31).  The weights must be 16-byte aligned (the C ABI requires it).
 constexpr int64_t kQ6MaxK = 131072;
 bool gemv_q6_fits(int64_t K, int64_t N, int batch) {
-  return batch == 1 && K >= 1 && K <= kQ6MaxK && N % 256 == 0 && N > 0;
+  return batch >= 1 && batch <= 2 && K >= 1 && K <= kQ6MaxK && N % 256 == 0 && N > 0;
 }
 
 cudaError_t launch_gemv_q6_mma(const float* x, const void* w, float* y, int64_t K, int64_t N,
@@ -685,8 +748,11 @@ cudaError_t launch_gemv_q6_mma(const float* x, const void* w, float* y, int64_t 
       row_bytes != (N / 256) * gq6::kBlock)
     return cudaErrorNotSupported;
   const Epi epi{f.bias, f.res};
-  return f.swiglu_x ? launch_q6_t<true>(x, w, y, K, N, row_bytes, st, epi)
-                    : launch_q6_t<false>(x, w, y, K, N, row_bytes, st, epi);
+  if (batch == 1)
+    return f.swiglu_x ? launch_q6_t<1, true>(x, w, y, K, N, row_bytes, 1, st, epi)
+                      : launch_q6_t<1, false>(x, w, y, K, N, row_bytes, 1, st, epi);
+  return f.swiglu_x ? launch_q6_t<2, true>(x, w, y, K, N, row_bytes, batch, st, epi)
+                    : launch_q6_t<2, false>(x, w, y, K, N, row_bytes, batch, st, epi);
 }
 
 cudaError_t gemv_q6_status(unsigned* out, bool clear) {
