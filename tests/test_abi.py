@@ -85,12 +85,12 @@ def test_newer_entry_points_validate_before_any_cuda_call(lib):
 def test_scratch_size_query(lib):
     """Split-K scratch: counters + splits * batch * N partials for the fp32 kernel; none
     when K is tiny, and none for the tensor-core kernels (Q4_K / Q8_0 batch 1..16, Q6_K
-    batch 1-2), whose splits add up inside a thread-block cluster."""
+    batch 1-4), whose splits add up inside a thread-block cluster."""
     v = C.c_size_t()
-    for batch in (1, 2):
+    for batch in (1, 2, 3, 4):
         assert lib.vbq_gemv_scratch_bytes(4096, 14336, 14, batch, C.byref(v)) == 0 and v.value == 0
-    assert lib.vbq_gemv_scratch_bytes(4096, 14336, 14, 3, C.byref(v)) == 0
-    assert v.value > 3 * 14336 * 4
+    assert lib.vbq_gemv_scratch_bytes(4096, 14336, 14, 5, C.byref(v)) == 0
+    assert v.value > 5 * 14336 * 4
     big = v.value
     assert lib.vbq_gemv_scratch_bytes(4096, 14336, 14, 16, C.byref(v)) == 0
     assert v.value > big

@@ -1,4 +1,4 @@
-"""The batch 1-2 Q6_K GEMV on the integer tensor cores (vbq_gemv_q6.cu) through its own
+"""The batch 1-4 Q6_K GEMV on the integer tensor cores (vbq_gemv_q6.cu) through its own
 paths: the per-warp, per-batch-row power-of-two scale of v = x * d * sc (set from the first
 stage, set again
 when a stage outgrows it or falls 16x below it, or when the first stage held only
@@ -43,12 +43,19 @@ def _ref64(cuda, x, w, K, N):
 
 
 def _check_rows(y, ref, what):
-    for b in range(np.asarray(ref).reshape(-1, np.asarray(ref).shape[-1]).shape[0]):
-        _check(np.asarray(y).reshape(-1, np.asarray(y).shape[-1])[b],
-               np.asarray(ref).reshape(-1, np.asarray(ref).shape[-1])[b], f"{what} row {b}")
+    """_check per batch row; a row whose reference is all zeros (x row of zeros) must come
+    out exactly zero."""
+    ref = np.asarray(ref, np.float64)
+    ref = ref.reshape(-1, ref.shape[-1])
+    y = np.asarray(y, np.float64).reshape(ref.shape)
+    for b in range(ref.shape[0]):
+        if not np.abs(ref[b]).max() > 0:
+            assert np.array_equal(y[b], np.zeros_like(y[b])), f"{what} row {b}: not all zeros"
+        else:
+            _check(y[b], ref[b], f"{what} row {b}")
 
 
-@pytest.mark.parametrize("batch", [1, 2])
+@pytest.mark.parametrize("batch", [1, 2, 3, 4])
 @pytest.mark.parametrize("K,N", [(4096, 1024), (1000, 512), (14336, 4096), (4096, 12288)])
 def test_q6_scale_paths(cuda, oracle, K, N, batch):
     """Rows whose first stages are all zeros (scale unset, set by a later stage), rows that
@@ -64,6 +71,8 @@ def test_q6_scale_paths(cuda, oracle, K, N, batch):
     if batch > 1:
         x[1, : K // 4] *= 1e3
         x[1, K - min(K, 300):] = 0.0
+    if batch > 3:
+        x[3] = 0.0  # a batch row of zeros never sets its scale
     y = vb.gemv_dequant(torch.from_numpy(x).to(cuda), w, None, K, N, Q6).cpu().numpy()
     assert vb.device_status() == 0
     _check_rows(y, _ref64(cuda, x, w, K, N), "fp64")
@@ -86,7 +95,7 @@ def _blocks(K, N, rng, ql=None, qh=None, sc=None, d=None):
     return b.reshape(K, nb * 210)
 
 
-@pytest.mark.parametrize("batch", [1, 2])
+@pytest.mark.parametrize("batch", [1, 2, 3, 4])
 @pytest.mark.parametrize("ql,qh,sc", [(0xff, 0xff, 127), (0x00, 0x00, -128), (0xff, 0xff, -128),
                                       (0x0f, 0xaa, -1), (None, None, None), (None, None, -128)])
 def test_q6_extreme_codes_and_scales(cuda, oracle, ql, qh, sc, batch):
@@ -102,7 +111,7 @@ def test_q6_extreme_codes_and_scales(cuda, oracle, ql, qh, sc, batch):
     _check_rows(y, oracle.gemv_dequant(x, w, K, N, Q6), "oracle")
 
 
-@pytest.mark.parametrize("batch", [1, 2])
+@pytest.mark.parametrize("batch", [1, 2, 3, 4])
 @pytest.mark.parametrize("K", [1, 2, 3, 127, 128, 129, 255, 333])
 @pytest.mark.parametrize("N", [256, 768, 1280])
 def test_q6_matrix_end_windows(cuda, oracle, K, N, batch):
@@ -120,7 +129,7 @@ def test_q6_matrix_end_windows(cuda, oracle, K, N, batch):
 @pytest.mark.parametrize("bad", [float("nan"), float("inf"), float("-inf")])
 def test_q6_nonfinite_x(cuda, oracle, bad):
     """A non-finite activation makes every output of its batch row NaN (the reference's fp32
-    sum is NaN or +-inf there); at batch 2 the other row is unaffected."""
+    sum is NaN or +-inf there); at batch 2 and 4 the other rows are unaffected."""
     K, N = 2048, 1024
     w = synthetic_weights(K, N, Q6, seed=3, device=cuda)
     x = torch.randn(K, device=cuda)
@@ -128,15 +137,17 @@ def test_q6_nonfinite_x(cuda, oracle, bad):
     y = vb.gemv_dequant(x, w, None, K, N, Q6)
     assert torch.isnan(y).all()
     assert vb.device_status() == 0
-    x2 = torch.randn(2, K, device=cuda)
-    x2[1, 777] = bad
-    y2 = vb.gemv_dequant(x2, w, None, K, N, Q6)
-    assert torch.isnan(y2[1]).all()
-    assert vb.device_status() == 0
-    _check(y2[0].cpu().numpy(), _ref64(cuda, x2[0], w, K, N), "fp64 row 0")
+    for batch, row in ((2, 1), (4, 2)):
+        x2 = torch.randn(batch, K, device=cuda)
+        x2[row, 777] = bad
+        y2 = vb.gemv_dequant(x2, w, None, K, N, Q6)
+        assert torch.isnan(y2[row]).all()
+        assert vb.device_status() == 0
+        ok = [b for b in range(batch) if b != row]
+        _check_rows(y2[ok].cpu().numpy(), _ref64(cuda, x2[ok], w, K, N), "fp64")
 
 
-@pytest.mark.parametrize("batch", [1, 2])
+@pytest.mark.parametrize("batch", [1, 2, 3, 4])
 def test_q6_swiglu_input_and_epilogue(cuda, batch):
     """silu(gate) * up read from a [batch, 2K] buffer; bias and residual added in the
     epilogue; repeated calls bit-identical."""
@@ -158,12 +169,12 @@ def test_q6_swiglu_input_and_epilogue(cuda, batch):
     torch.testing.assert_close(yf, y0 + bias + res, rtol=0, atol=1e-5)
 
 
-@pytest.mark.parametrize("batch", [1, 2])
+@pytest.mark.parametrize("batch", [1, 2, 3, 4])
 @pytest.mark.parametrize("N", [256, 2048, 8192, 37888, 49152, 65536])
 def test_q6_split_widths(cuda, N, batch):
     """Tile counts from 1 (the cluster split-K at its widest) through one wave of clusters
     to more tiles than CTA slots (two splits over several waves, or one split filling a
-    wave); no scratch is needed at batch 1 or 2."""
+    wave); no scratch is needed at batch 1-4."""
     K = 8192
     assert vb.gemv_scratch_bytes(K, N, Q6, batch) == 0
     w = synthetic_weights(K, N, Q6, seed=N, device=cuda)

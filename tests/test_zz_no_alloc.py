@@ -25,7 +25,7 @@ TOL = 1e-3  # max-norm relative error, as in the other GEMV tests
 SHAPES = [
     (12, 4096, 14336, 1),   # Q4_K gate/up of the decode layer
     (12, 14336, 4096, 4),   # Q4_K down, batch 4
-    (14, 4096, 4096, 3),    # Q6_K batch 3 (batch 1-2 take the tensor-core kernel, no scratch)
+    (14, 4096, 4096, 6),    # Q6_K batch 6 (batch 1-4 take the tensor-core kernel, no scratch)
     (8, 8192, 10240, 16),   # Q8_0 70B-shape QKV, batch 16
     (12, 300, 1024, 3),     # ragged K: a single split, no scratch at all
     (14, 4096, 4096, 24),   # Q6_K batch 24: two launches (16 + 8 rows) over the array

@@ -114,13 +114,13 @@ struct Bars {
 static_assert(sizeof(Bars) <= 128, "barrier block");
 constexpr int kMaxSplit = 16;
 
-// Per batch size.  Batch 1: two CTAs per SM (125 registers) with a 3-slot ring each.
-// Batch 2: a second set of accumulators and tables needs more registers, so one CTA per SM
-// with a 6-slot ring.  Shared memory: the ring, one B table per warp and batch row, the
+// Per batch size.  Batch 1: two CTAs per SM (126 registers) with a 3-slot ring each.
+// Batch 2 and 4: more sets of accumulators and tables need more registers, so one CTA per
+// SM with a 6- / 5-slot ring (batch 4 at 255 registers spills ~130 bytes).  Shared memory: the ring, one B table per warp and batch row, the
 // barriers, and the cluster leader's receive slots (sized at launch).
 template <int BATCH>
 struct Cfg {
-  static constexpr int kStages = BATCH == 1 ? 3 : 6;
+  static constexpr int kStages = BATCH == 1 ? 3 : (BATCH == 2 ? 6 : 5);
   static constexpr int kMinBlocks = BATCH == 1 ? 2 : 1;
   static constexpr int kSmemCap = (BATCH == 1 ? 113 : 227) * 1024;
   static constexpr int kTblOff = kStages * kStageBytes;
@@ -239,25 +239,27 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
     // Fragment loads, k = 4t + j (j < 4) and 16 + 4t + (j - 4): warp rows 8t + j and
     // 8t + 4 + (j - 4); the pair of m-tile row g in chunk c is 8c + g, its ql bytes at
     // o + 64 gp + 2 (8c + g), its qh byte at o + 128 + 32 gp + 8c + g.  The offsets are the
-    // same in every stage.
+    // same in every stage; a row's qh byte sits qh_d bytes after its ql pair.  Above batch
+    // 2, where registers are short, the qh (and scale) addresses are formed from that
+    // distance; below, they are kept (measured 2 % faster at batch 1).
     int ql_off[8], qh_off[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int r = rw + 8 * t + j;
-      const int base = line_off(r) + off_of(r);
-      ql_off[j] = base + 64 * gp + 2 * g;
-      qh_off[j] = base + 128 + 32 * gp + g;
+      ql_off[j] = line_off(r) + off_of(r) + 64 * gp + 2 * g;
+      qh_off[j] = ql_off[j] + 128 - 32 * gp - g;
     }
+    const uint32_t qh_d = (uint32_t)(128 - 32 * gp - g);
     // table rows k = 4m + j: warp rows 8 (m & 3) + 4 (m >> 2) + j (consecutive); d at o + 208,
     // the scale pair (sub-blocks 8 gp + 2 cc, + 1) at o + 192 + 8 gp + 2 cc
     const int trow = rw + 8 * (m & 3) + 4 * (m >> 2);
     int d_off[4], sc_off[4];
+    const int sc_d = 8 * gp + 2 * cc - 16;  // the scale pair, relative to d
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int r = trow + j;
-      const int base = line_off(r) + off_of(r);
-      d_off[j] = base + 208;
-      sc_off[j] = base + 192 + 8 * gp + 2 * cc;
+      d_off[j] = line_off(r) + off_of(r) + 208;
+      sc_off[j] = d_off[j] + sc_d;
     }
     // the lane's table words: chunk cc, k = 4m .. 4m + 3 (byte 8 (m & 3) + 4 (m >> 2) of a
     // column); its B fragments: column g, k = 4t .. 4t + 3 and 16 + 4t .. 16 + 4t + 3
@@ -306,7 +308,9 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
       }
     };
 
-    // x of the lane's table rows, two stages ahead
+    // x of the lane's table rows, two stages ahead (one above batch 2, where registers
+    // are short)
+    constexpr int kAhead = BATCH > 2 ? 1 : 2;
     int kx = split * kRows + trow;
     const int kstep = S * kRows;
     auto load_x = [&](int k, float (&xv)[BATCH][4]) {
@@ -317,8 +321,10 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
     };
     float xn[BATCH][4], xnn[BATCH][4];
     load_x(kx, xn);
-    kx += kstep;
-    load_x(kx, xnn);
+    if constexpr (kAhead == 2) {
+      kx += kstep;
+      load_x(kx, xnn);
+    }
 #pragma unroll 1
     for (int it = 0; it < nst; ++it) {
       const int u = it % kStages;
@@ -329,10 +335,11 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           xv[b][j] = xn[b][j];
-          xn[b][j] = xnn[b][j];
+          if constexpr (kAhead == 2) xn[b][j] = xnn[b][j];
         }
       kx += kstep;
-      load_x(kx, xnn);  // rows of the stage after next (zero past K)
+      if constexpr (kAhead == 2) load_x(kx, xnn);  // rows of the stage after next (zero past K)
+      else load_x(kx, xn);                         // rows of the next stage
       if (!__all_sync(0xffffffffu, mbar_wait_hinted(smem_u32(&bars.full[u]), par, kWaitBudgetCycles))) {
         if (lane == 0) give_up();
         break;
@@ -344,7 +351,8 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint32_t dh = *reinterpret_cast<const uint16_t*>(st + d_off[j]);
-        const uint32_t sp = (uint32_t)*reinterpret_cast<const uint16_t*>(st + sc_off[j]) ^ 0x8080u;
+        const int so = BATCH > 2 ? d_off[j] + sc_d : sc_off[j];
+        const uint32_t sp = (uint32_t)*reinterpret_cast<const uint16_t*>(st + so) ^ 0x8080u;
         // the int8 scales as floats: byte ^ 0x80 into the 2^23 magic, minus 2^23 + 128 (exact)
         const float2 sc = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(sp, 0x4b000000u, 0x7650)),
                                                  __uint_as_float(__byte_perm(sp, 0x4b000000u, 0x7651))),
@@ -426,7 +434,7 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         qa[j] = stb + (uint32_t)ql_off[j];
-        ha[j] = stb + (uint32_t)qh_off[j];
+        ha[j] = BATCH > 2 ? qa[j] + qh_d : stb + (uint32_t)qh_off[j];
       }
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -734,12 +742,12 @@ static cudaError_t launch_q6_t(const float* x, const void* w, float* y, int64_t 
   return cudaLaunchKernelEx(&cfg, kern, maps, x, y, (int)K, (int)N, RB, batch, epi);
 }
 
-// Whether the tensor-core Q6_K kernel takes this call: batch 1 or 2, whole 256-column
+// Whether the tensor-core Q6_K kernel takes this call: batch 1 to 4, whole 256-column
 // tiles, and K up to 2^17 (the s32 sums hold at most K / 4 x 32 terms below 64 x 128 in
 // magnitude, well inside 2^31).  The weights must be 16-byte aligned (the C ABI requires it).
 constexpr int64_t kQ6MaxK = 131072;
 bool gemv_q6_fits(int64_t K, int64_t N, int batch) {
-  return batch >= 1 && batch <= 2 && K >= 1 && K <= kQ6MaxK && N % 256 == 0 && N > 0;
+  return batch >= 1 && batch <= 4 && K >= 1 && K <= kQ6MaxK && N % 256 == 0 && N > 0;
 }
 
 cudaError_t launch_gemv_q6_mma(const float* x, const void* w, float* y, int64_t K, int64_t N,
@@ -751,6 +759,11 @@ cudaError_t launch_gemv_q6_mma(const float* x, const void* w, float* y, int64_t 
   if (batch == 1)
     return f.swiglu_x ? launch_q6_t<1, true>(x, w, y, K, N, row_bytes, 1, st, epi)
                       : launch_q6_t<1, false>(x, w, y, K, N, row_bytes, 1, st, epi);
+  // batch 3-4 on the 4-row form: measured against two 2-row launches (the weights streamed
+  // twice) at batch 4, 4096 x 128256 239 vs 323 us, 14336 x 4096 39.7 vs 52.5 us
+  if (batch > 2)
+    return f.swiglu_x ? launch_q6_t<4, true>(x, w, y, K, N, row_bytes, batch, st, epi)
+                      : launch_q6_t<4, false>(x, w, y, K, N, row_bytes, batch, st, epi);
   return f.swiglu_x ? launch_q6_t<2, true>(x, w, y, K, N, row_bytes, batch, st, epi)
                     : launch_q6_t<2, false>(x, w, y, K, N, row_bytes, batch, st, epi);
 }
