@@ -23,13 +23,14 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-3  # max-norm relative error, as in the other GEMV tests
 
 SHAPES = [
-    (12, 4096, 14336, 1),   # Q4_K gate/up of the decode layer
-    (12, 14336, 4096, 4),   # Q4_K down, batch 4
-    (14, 4096, 4096, 6),    # Q6_K batch 6 (batch 1-4 take the tensor-core kernel, no scratch)
-    (8, 8192, 10240, 16),   # Q8_0 70B-shape QKV, batch 16
-    (12, 300, 1024, 3),     # ragged K: a single split, no scratch at all
-    (14, 4096, 4096, 24),   # Q6_K batch 24: two launches (16 + 8 rows) over the array
-    (14, 14336, 4096, 5),   # Q6_K down projection, batch 5
+    (12, 4096, 14336, 1),    # Q4_K gate/up of the decode layer (cluster split-K, no scratch)
+    (12, 14336, 4096, 4),    # Q4_K down, batch 4
+    (8, 8192, 10240, 16),    # Q8_0 70B-shape QKV, batch 16
+    (12, 300, 1024, 3),      # ragged K: a single split, no scratch at all
+    (14, 4096, 4096, 24),    # Q6_K batch 24: groups of 4 rows on the tensor-core kernel
+    # K past the tensor-core kernels' caps: the fp32 kernel, its split-K scratch in the array
+    (14, 131328, 1024, 2),   # Q6_K (cap 2^17)
+    (12, 196864, 512, 3),    # Q4_K (cap 3 x 2^16)
 ]
 
 
@@ -66,7 +67,7 @@ import ctypes as C, sys, torch
 sys.path.insert(0, sys.argv[1])
 from vibeblade_b200 import _lib
 lib = _lib.load()
-K, N, t, B = 4096, 14336, 14, 16  # Q6_K: the split-K kernel with scratch
+K, N, t, B = 4096, 14336, 14, 16  # Q6_K on the fp32 split-K kernel (VBQ_GEMV_SCALAR=1)
 v = C.c_size_t()
 assert lib.vbq_gemv_scratch_bytes(K, N, t, B, C.byref(v)) == 0
 assert v.value > (8 << 20), v.value
@@ -84,13 +85,14 @@ print("rejected")
 def test_static_scratch_rejects_shapes_beyond_its_size(cuda):
     """The split planner keeps scratch to a few MB, inside the fixed array; a tuning
     override of the split factor (VBQ_GEMV_SPLIT, read once per process, hence the child
-    process) makes a shape need more, and the call must refuse it without launching."""
+    process; VBQ_GEMV_SCALAR=1 keeps the shape on the fp32 kernel, the one that uses
+    scratch) makes a shape need more, and the call must refuse it without launching."""
     import os
     import subprocess
     import sys
     from pathlib import Path
     root = str(Path(__file__).resolve().parents[1])
-    env = dict(os.environ, VBQ_GEMV_SPLIT="64")
+    env = dict(os.environ, VBQ_GEMV_SPLIT="64", VBQ_GEMV_SCALAR="1")
     r = subprocess.run([sys.executable, "-c", _REJECT_SCRIPT, root], env=env,
                        capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "rejected" in r.stdout, r.stdout + r.stderr

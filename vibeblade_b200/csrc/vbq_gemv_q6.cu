@@ -742,30 +742,44 @@ static cudaError_t launch_q6_t(const float* x, const void* w, float* y, int64_t 
   return cudaLaunchKernelEx(&cfg, kern, maps, x, y, (int)K, (int)N, RB, batch, epi);
 }
 
-// Whether the tensor-core Q6_K kernel takes this call: batch 1 to 4, whole 256-column
-// tiles, and K up to 2^17 (the s32 sums hold at most K / 4 x 32 terms below 64 x 128 in
+// Whether the tensor-core Q6_K kernel takes this call: batch 1 to 16 (groups of 4 above 4),
+// whole 256-column tiles, and K up to 2^17 (the s32 sums hold at most K / 4 x 32 terms below 64 x 128 in
 // magnitude, well inside 2^31).  The weights must be 16-byte aligned (the C ABI requires it).
 constexpr int64_t kQ6MaxK = 131072;
 bool gemv_q6_fits(int64_t K, int64_t N, int batch) {
-  return batch >= 1 && batch <= 4 && K >= 1 && K <= kQ6MaxK && N % 256 == 0 && N > 0;
+  return batch >= 1 && batch <= 16 && K >= 1 && K <= kQ6MaxK && N % 256 == 0 && N > 0;
 }
 
+// Up to 4 batch rows in one launch.
+static cudaError_t launch_q6_rows(const float* x, const void* w, float* y, int64_t K, int64_t N,
+                                  int64_t row_bytes, int batch, cudaStream_t st, bool sw, Epi epi) {
+  if (batch == 1)
+    return sw ? launch_q6_t<1, true>(x, w, y, K, N, row_bytes, 1, st, epi)
+              : launch_q6_t<1, false>(x, w, y, K, N, row_bytes, 1, st, epi);
+  // batch 3-4 on the 4-row form: measured against two 2-row launches (the weights streamed
+  // twice) at batch 4, 4096 x 128256 239 vs 323 us, 14336 x 4096 39.7 vs 52.5 us
+  if (batch > 2)
+    return sw ? launch_q6_t<4, true>(x, w, y, K, N, row_bytes, batch, st, epi)
+              : launch_q6_t<4, false>(x, w, y, K, N, row_bytes, batch, st, epi);
+  return sw ? launch_q6_t<2, true>(x, w, y, K, N, row_bytes, batch, st, epi)
+            : launch_q6_t<2, false>(x, w, y, K, N, row_bytes, batch, st, epi);
+}
+
+// Batch 5-16 as consecutive launches over groups of 4 rows (each streams the weights again).
 cudaError_t launch_gemv_q6_mma(const float* x, const void* w, float* y, int64_t K, int64_t N,
                                int64_t row_bytes, int batch, cudaStream_t st, const GemvFuse& f) {
   if (!gemv_q6_fits(K, N, batch) || (reinterpret_cast<uintptr_t>(w) & 15u) != 0 ||
       row_bytes != (N / 256) * gq6::kBlock)
     return cudaErrorNotSupported;
-  const Epi epi{f.bias, f.res};
-  if (batch == 1)
-    return f.swiglu_x ? launch_q6_t<1, true>(x, w, y, K, N, row_bytes, 1, st, epi)
-                      : launch_q6_t<1, false>(x, w, y, K, N, row_bytes, 1, st, epi);
-  // batch 3-4 on the 4-row form: measured against two 2-row launches (the weights streamed
-  // twice) at batch 4, 4096 x 128256 239 vs 323 us, 14336 x 4096 39.7 vs 52.5 us
-  if (batch > 2)
-    return f.swiglu_x ? launch_q6_t<4, true>(x, w, y, K, N, row_bytes, batch, st, epi)
-                      : launch_q6_t<4, false>(x, w, y, K, N, row_bytes, batch, st, epi);
-  return f.swiglu_x ? launch_q6_t<2, true>(x, w, y, K, N, row_bytes, batch, st, epi)
-                    : launch_q6_t<2, false>(x, w, y, K, N, row_bytes, batch, st, epi);
+  const int64_t xrow = f.swiglu_x ? 2 * K : K;
+  for (int b0 = 0; b0 < batch; b0 += 4) {
+    const int nb = batch - b0 < 4 ? batch - b0 : 4;
+    const Epi epi{f.bias, f.res ? f.res + (int64_t)b0 * N : nullptr};
+    cudaError_t e = launch_q6_rows(x + (int64_t)b0 * xrow, w, y + (int64_t)b0 * N, K, N, row_bytes, nb, st,
+                                   f.swiglu_x, epi);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 cudaError_t gemv_q6_status(unsigned* out, bool clear) {
