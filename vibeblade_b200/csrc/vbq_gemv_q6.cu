@@ -144,6 +144,13 @@ __device__ __forceinline__ uint32_t lds_u8(uint32_t a) {
   asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v) : "r"(a));
   return v;
 }
+// atomic add on a shared word with acquire-release ordering at CTA scope; returns the old value
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], %2;"
+               : "=r"(old) : "r"(smem_u32(p)), "r"(v) : "memory");
+  return old;
+}
 // a * m + b on the FMA pipe (packing disjoint bit fields without the ALU pipe)
 __device__ __forceinline__ uint32_t mad_u32(uint32_t a, uint32_t m, uint32_t b) {
   uint32_t d;
@@ -477,14 +484,11 @@ gemv_q6_kernel(const __grid_constant__ ClassMaps maps, const float* __restrict__
       }
       __syncwarp();  // table and stage reads done
       // the last warp through slot u refills it with stage it + kStages: the warps' reads
-      // of the slot come before their count (release), the count before the refill
-      // (acquire), and the proxy fence orders them before the asynchronous copy
+      // of the slot come before their count (the __syncwarp above, then a release), the
+      // count before the refill (acquire), and the proxy fence orders them before the
+      // asynchronous copy
       unsigned last = 0u;
-      if (lane == 0) {
-        __threadfence_block();
-        last = atomicAdd(&bars.done[u], 1u) == (unsigned)(kConsumers - 1);
-        __threadfence_block();
-      }
+      if (lane == 0) last = atom_add_acq_rel(&bars.done[u], 1u) == (unsigned)(kConsumers - 1);
       if (__shfl_sync(0xffffffffu, last, 0)) {
         if (lane == 0) bars.done[u] = 0u;
         if (it + kStages < nst) {
