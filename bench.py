@@ -253,23 +253,26 @@ def bench_prefill(dev, steps: int) -> dict:
 def bench_lm_head(dev, steps: int) -> dict:
     """The lm_head GEMV at a Llama-3 vocabulary (4096 x 128256, batch 1; the reference's
     gemv_dequant_mt at cpp/src/fast_model.cpp:1022) in Q6_K -- the usual type of
-    output.weight in Q4_K_M files -- and Q4_K; two weight copies alternate (> L2)."""
+    output.weight in Q4_K_M files -- and Q4_K, plus Q6_K at batch 4; two weight copies
+    alternate (> L2)."""
     import torch
     import vibeblade_b200 as vb
     from vibeblade_b200.quantize import synthetic_weights
     K, N = 4096, 128256
     out = {"shape": f"{K}x{N}", "batch": 1}
     g = torch.Generator(device=dev).manual_seed(6)
-    x = torch.randn(1, K, generator=g, device=dev)
-    y = torch.empty(1, N, device=dev)
-    for t, name in ((14, "q6_k"), (12, "q4_k")):
+    for t, name, B in ((14, "q6_k", 1), (12, "q4_k", 1), (14, "q6_k_batch4", 4)):
+        x = torch.randn(B, K, generator=g, device=dev)
+        y = torch.empty(B, N, device=dev)
         ws = [synthetic_weights(K, N, t, seed=300 + i, device=dev) for i in range(2)]
         ms = _time_steps(lambda i: vb.gemv_dequant(x, ws[i % 2], y, K, N, t), 5 * steps, 4,
                          torch.cuda.current_stream(dev), 1)
-        nbytes = K * N * (210 if t == 14 else 144) // 256 + 4 * (K + N)
+        nbytes = K * N * (210 if t == 14 else 144) // 256 + 4 * B * (K + N)
         gbs = nbytes * 5 * steps / (ms * 1e-3) / 1e9
         out[name] = {"value": round(gbs, 1), "unit": "GB/s", "us_per_call": round(1e3 * ms / (5 * steps), 2),
                      "frac_of_hbm": round(gbs / peaks()["hbm_gbs"], 4)}
+        if B > 1:
+            out[name]["batch"] = B
         del ws
     return out
 
