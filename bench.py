@@ -329,11 +329,21 @@ def bench_tp(dev, rank: int, world: int, steps: int, prefill: bool = True) -> di
     dec = {"decode_b1_us_per_ffn": round(1e3 * dms / (5 * steps), 1),
            "decode_b16_us_per_ffn": round(1e3 * dms16 / (5 * steps), 1),
            "decode_b32_us_per_ffn": round(1e3 * dms32 / (5 * steps), 1)}
+    if world > 1:
+        # the same decode steps with the down GEMV writing into a buffer the peers map and
+        # the one-shot all-reduce over NVLink peer memory (vibeblade_b200.peer) instead
+        ffn.attach_peer(32, dev)
+        for b, xb in (("1", xd), ("16", xd16), ("32", xd32)):
+            pms = _time_steps(lambda _: ffn.decode(xb), 5 * steps, 5, stream, world)
+            dec[f"decode_b{b}_us_per_ffn_peer"] = round(1e3 * pms / (5 * steps), 1)
+        ffn.peer.close()
+        ffn.peer = None
     if not prefill:
         return {"metric": "70B FFN decode latency, batch 1 (Q8_0, TP over the job's GPUs)",
                 "value": dec["decode_b1_us_per_ffn"], "unit": "us", "higher_is_better": False,
                 "tp": world, "scaling": "strong", "steps": 5 * steps, **dec,
-                "collective": "torch.distributed all_reduce (NCCL) of the fp32 [B, 8192] decode partial sums"}
+                "collective": "torch.distributed all_reduce (NCCL) of the fp32 [B, 8192] decode partial sums; "
+                              "*_peer: the one-shot all-reduce over peer memory (vbq_peer_allreduce)"}
     x = torch.randn(M, H, generator=g, device=dev).to(torch.bfloat16)
     ms = _time_steps(lambda _: ffn.prefill(x), steps, 3, stream, world)
     # the same step without the collective (each rank's partial sum only): what the
@@ -348,7 +358,8 @@ def bench_tp(dev, rank: int, world: int, steps: int, prefill: bool = True) -> di
             "collective_exposed_ms": round((ms - ms_local) / steps, 4) if world > 1 else None, **dec,
             "collective": "torch.distributed all_reduce (NCCL) of the bf16 [M, 8192] prefill partial "
                           "sums (the FFN in two row halves: the first half's all-reduce overlapped "
-                          "with the second half's GEMMs) and of the fp32 [B, 8192] decode partial sums"}
+                          "with the second half's GEMMs) and of the fp32 [B, 8192] decode partial sums; "
+                          "decode *_peer: the one-shot all-reduce over peer memory (vbq_peer_allreduce)"}
 
 
 def _ref_libs():

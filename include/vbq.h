@@ -292,6 +292,40 @@ int vbq_device_status(int32_t* status, int32_t clear);
  */
 int vbq_debug_wait_probe(int64_t budget_cycles, int32_t arrive, void* stream);
 
+/*
+ * One-shot all-reduce of fp32 partial outputs over peer memory, for the row-split layers
+ * of tensor parallelism at decode (replaces the collective after the o and down GEMVs of a
+ * split layer; the reference runs those layers whole on one device,
+ * cpp/src/fast_model.cpp:813-824, :990-998).  One process per GPU; every rank calls it
+ * with the same epoch and n.
+ *   data[p]  (host array of `world` device pointers): rank p's partial of this call, n
+ *            floats, 16-byte aligned, readable from this device (CUDA IPC); data[rank] is
+ *            this rank's own, written by the work queued before on `stream`.
+ *   flags[p] (host array): rank p's flag array of 8 int32 (zero-filled once at set-up),
+ *            writable from this device; slot q holds the last epoch rank q published.
+ *   epoch:   1, 2, 3, ... per call; a rank's partials alternate between two buffers by
+ *            the epoch's parity (a buffer is rewritten only two calls later).
+ *   out:     n floats (16-byte aligned), the sum over p = 0 .. world - 1 in that order,
+ *            the same bits on every rank.
+ * The wait for the peers is bounded by timeout_cycles SM clock cycles (<= 0: about 1 s);
+ * a wait that gives up is reported by vbq_device_status as VBQ_ERR_TIMEOUT and `out` is
+ * then not the sum.  No multicast; world <= 8.
+ */
+int vbq_peer_allreduce(const float* const* data, int32_t* const* flags, int32_t world, int32_t rank,
+                       int32_t epoch, int64_t n, float* out, int64_t timeout_cycles, void* stream);
+
+/*
+ * CUDA IPC of a device buffer for vbq_peer_allreduce's set-up (no counterpart in the
+ * reference).  vbq_ipc_export writes the 64-byte handle of the allocation holding ptr and
+ * ptr's offset in it (the buffer may sit inside a caching allocator's block);
+ * vbq_ipc_import, in another process, maps that allocation for the current device (peer
+ * access enabled on first use) and returns the buffer's address there; vbq_ipc_close
+ * unmaps it (same ptr and offset).  None of them allocates device memory.
+ */
+int vbq_ipc_export(const void* ptr, void* handle64, int64_t* offset);
+int vbq_ipc_import(const void* handle64, int64_t offset, void** ptr);
+int vbq_ipc_close(void* ptr, int64_t offset);
+
 #ifdef __cplusplus
 }
 #endif

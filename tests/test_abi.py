@@ -130,3 +130,21 @@ def test_fused_entry_argument_errors_need_no_gpu(lib):
     assert b"flags" in lib.vbq_last_error()
     assert lib.vbq_gemv_ex(None, None, None, 16, 256, 2, 1, 0, None, None, None, 0, None) == _lib.VBQ_ERR_TYPE
     assert lib.vbq_gemm_ex(None, None, None, 4, 64, 300, 12, 0, None, None, None) == _lib.VBQ_ERR_SHAPE
+
+
+def test_peer_and_ipc_argument_errors_need_no_gpu(lib):
+    """vbq_peer_allreduce and the IPC helpers check their arguments before any CUDA call."""
+    from vibeblade_b200 import _lib
+    arr = (C.c_void_p * 2)(16, 32)
+    assert lib.vbq_peer_allreduce(arr, arr, 0, 0, 1, 8, 64, 0, None) == _lib.VBQ_ERR_SHAPE   # world
+    assert lib.vbq_peer_allreduce(arr, arr, 9, 0, 1, 8, 64, 0, None) == _lib.VBQ_ERR_SHAPE
+    assert lib.vbq_peer_allreduce(arr, arr, 2, 2, 1, 8, 64, 0, None) == _lib.VBQ_ERR_SHAPE   # rank
+    assert lib.vbq_peer_allreduce(arr, arr, 2, 0, 0, 8, 64, 0, None) == _lib.VBQ_ERR_SHAPE   # epoch
+    assert lib.vbq_peer_allreduce(arr, arr, 2, 0, 1, -1, 64, 0, None) == _lib.VBQ_ERR_SHAPE  # n
+    assert lib.vbq_peer_allreduce(None, arr, 2, 0, 1, 8, 64, 0, None) == _lib.VBQ_ERR_NULL
+    bad = (C.c_void_p * 2)(16, 36)  # 36 is not 16-byte aligned
+    assert lib.vbq_peer_allreduce(bad, arr, 2, 0, 1, 8, 64, 0, None) == _lib.VBQ_ERR_ALIGN
+    assert b"vbq_peer_allreduce" in lib.vbq_last_error()
+    assert lib.vbq_ipc_export(None, None, None) == _lib.VBQ_ERR_NULL
+    assert lib.vbq_ipc_import(None, 0, None) == _lib.VBQ_ERR_NULL
+    assert lib.vbq_ipc_close(None, 0) == _lib.VBQ_ERR_NULL

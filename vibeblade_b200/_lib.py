@@ -45,6 +45,12 @@ SIGNATURES = {
                               C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
                               C.c_void_p]),
     "vbq_debug_wait_probe": (C.c_int, [C.c_int64, C.c_int32, C.c_void_p]),
+    # data, flags (host arrays of device pointers), world, rank, epoch, n, out, timeout, stream
+    "vbq_peer_allreduce": (C.c_int, [C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.c_int32, C.c_int32,
+                                     C.c_int32, C.c_int64, C.c_void_p, C.c_int64, C.c_void_p]),
+    "vbq_ipc_export": (C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_int64)]),
+    "vbq_ipc_import": (C.c_int, [C.c_void_p, C.c_int64, C.POINTER(C.c_void_p)]),
+    "vbq_ipc_close": (C.c_int, [C.c_void_p, C.c_int64]),
     "vbq_gemm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int64,
                            C.c_int32, C.c_int32, C.c_void_p]),
     "vbq_gemv_static_scratch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64,

@@ -288,7 +288,7 @@ int vbq_gemm_ex(const void* a, const void* w, void* c, int64_t M, int64_t K, int
 
 int vbq_device_status(int32_t* status, int32_t clear) {
   if (!status) return fail(VBQ_ERR_NULL, "vbq_device_status: status is NULL");
-  unsigned g = 0, g2 = 0, g3 = 0, g4 = 0, g5 = 0, g6 = 0, g7 = 0;
+  unsigned g = 0, g2 = 0, g3 = 0, g4 = 0, g5 = 0, g6 = 0, g7 = 0, g8 = 0;
   cudaError_t e = vbq::gemv_status(&g, clear != 0);
   if (e == cudaSuccess) e = vbq::gemm_status(&g2, clear != 0);
   if (e == cudaSuccess) e = vbq::gemv_mma_status(&g3, clear != 0);
@@ -296,8 +296,9 @@ int vbq_device_status(int32_t* status, int32_t clear) {
   if (e == cudaSuccess) e = vbq::gemv_q8_status(&g5, clear != 0);
   if (e == cudaSuccess) e = vbq::gemv_half_status(&g6, clear != 0);
   if (e == cudaSuccess) e = vbq::gemv_q6_status(&g7, clear != 0);
+  if (e == cudaSuccess) e = vbq::peer_status(&g8, clear != 0);
   if (e != cudaSuccess) return cuda_fail(e, "vbq_device_status");
-  g |= g2 | g3 | g4 | g5 | g6 | g7;
+  g |= g2 | g3 | g4 | g5 | g6 | g7 | g8;
   *status = (int32_t)g;
   if (g & 1u) return fail(VBQ_ERR_TIMEOUT, "a bounded device-side wait gave up (a copy never completed)");
   return ok();
@@ -309,6 +310,48 @@ int vbq_debug_wait_probe(int64_t budget_cycles, int32_t arrive, void* stream) {
   if (arrive != 0 && arrive != 1) return fail(VBQ_ERR_SHAPE, "vbq_debug_wait_probe: arrive must be 0 or 1");
   cudaError_t e = vbq::launch_wait_probe((long long)budget_cycles, arrive, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "vbq_debug_wait_probe launch");
+  return ok();
+}
+
+int vbq_peer_allreduce(const float* const* data, int32_t* const* flags, int32_t world, int32_t rank,
+                       int32_t epoch, int64_t n, float* out, int64_t timeout_cycles, void* stream) {
+  if (world < 1 || world > 8) return fail(VBQ_ERR_SHAPE, "vbq_peer_allreduce: world must be in 1..8");
+  if (rank < 0 || rank >= world) return fail(VBQ_ERR_SHAPE, "vbq_peer_allreduce: rank out of range");
+  if (epoch < 1) return fail(VBQ_ERR_SHAPE, "vbq_peer_allreduce: epoch must be positive");
+  if (n < 0) return fail(VBQ_ERR_SHAPE, "vbq_peer_allreduce: negative n");
+  if (!data || !flags || (n > 0 && !out)) return fail(VBQ_ERR_NULL, "vbq_peer_allreduce: NULL pointer");
+  for (int32_t p = 0; p < world; ++p) {
+    if (!data[p] || !flags[p]) return fail(VBQ_ERR_NULL, "vbq_peer_allreduce: NULL peer pointer");
+    if (!aligned(data[p], 16) || !aligned(flags[p], 4))
+      return fail(VBQ_ERR_ALIGN, "vbq_peer_allreduce: peer data must be 16-byte aligned, flags 4-byte");
+  }
+  if (out && !aligned(out, 16)) return fail(VBQ_ERR_ALIGN, "vbq_peer_allreduce: out must be 16-byte aligned");
+  const long long budget = timeout_cycles > 0 ? (long long)timeout_cycles : 2000000000LL;
+  cudaError_t e = vbq::launch_peer_allreduce(data, reinterpret_cast<int* const*>(flags), world, rank, epoch, n,
+                                             out, budget, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "vbq_peer_allreduce launch");
+  return ok();
+}
+
+int vbq_ipc_export(const void* ptr, void* handle64, int64_t* offset) {
+  if (!ptr || !handle64 || !offset) return fail(VBQ_ERR_NULL, "vbq_ipc_export: NULL pointer");
+  cudaError_t e = vbq::ipc_export(ptr, handle64, offset);
+  if (e != cudaSuccess) return cuda_fail(e, "vbq_ipc_export");
+  return ok();
+}
+
+int vbq_ipc_import(const void* handle64, int64_t offset, void** ptr) {
+  if (!handle64 || !ptr) return fail(VBQ_ERR_NULL, "vbq_ipc_import: NULL pointer");
+  if (offset < 0) return fail(VBQ_ERR_SHAPE, "vbq_ipc_import: negative offset");
+  cudaError_t e = vbq::ipc_import(handle64, offset, ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "vbq_ipc_import");
+  return ok();
+}
+
+int vbq_ipc_close(void* ptr, int64_t offset) {
+  if (!ptr) return fail(VBQ_ERR_NULL, "vbq_ipc_close: NULL pointer");
+  cudaError_t e = vbq::ipc_close(ptr, offset);
+  if (e != cudaSuccess) return cuda_fail(e, "vbq_ipc_close");
   return ok();
 }
 

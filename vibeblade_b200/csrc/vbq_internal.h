@@ -145,6 +145,17 @@ cudaError_t gemv_mma_status(unsigned* out, bool clear);
 // One warp waiting on an mbarrier with the GEMV's bounded wait (vbq_debug_wait_probe).
 cudaError_t launch_wait_probe(long long budget_cycles, int arrive, cudaStream_t st);
 
+// One-shot all-reduce over peer memory (vbq_peer.cu): out = sum over p of data[p][0 .. n),
+// after publishing `epoch` to every peer's flags[rank] and waiting (bounded) for theirs.
+cudaError_t launch_peer_allreduce(const float* const* data, int* const* flags, int world, int rank,
+                                  int epoch, int64_t n, float* out, long long budget_cycles,
+                                  cudaStream_t st);
+cudaError_t peer_status(unsigned* out, bool clear);
+// CUDA IPC of a buffer that may sit inside a larger allocation (64-byte handle + offset).
+cudaError_t ipc_export(const void* ptr, void* handle_out, int64_t* offset_out);
+cudaError_t ipc_import(const void* handle, int64_t offset, void** ptr_out);
+cudaError_t ipc_close(void* ptr, int64_t offset);
+
 // Sticky device status bits of the GEMV kernels (kStatusTimeout = 1); synchronous.
 cudaError_t gemv_status(unsigned* out, bool clear);
 
