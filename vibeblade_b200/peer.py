@@ -37,14 +37,22 @@ class PeerAllReduce:
         # two data slots, then the flag array (int32 view of the last FLAG_INTS floats)
         self.buf = torch.zeros(2 * self.cap + FLAG_INTS, dtype=torch.float32, device=self.device)
         torch.cuda.synchronize(self.device)
+        # Every rank takes the same collective steps whatever fails, and all ranks raise
+        # together: a failure on one rank must not leave the others in a collective.
         handle = (C.c_char * 64)()
         off = C.c_int64()
+        info = None
         with torch.cuda.device(self.device):
-            _lib.check(self.lib.vbq_ipc_export(C.c_void_p(self.buf.data_ptr()), handle, C.byref(off)), self.lib)
+            if self.lib.vbq_ipc_export(C.c_void_p(self.buf.data_ptr()), handle, C.byref(off)) == _lib.VBQ_OK:
+                info = (bytes(handle), int(off.value))
         infos = [None] * self.world
-        dist.all_gather_object(infos, (bytes(handle), int(off.value)), group=group)
+        dist.all_gather_object(infos, info, group=group)
+        if any(i is None for i in infos):
+            raise RuntimeError("PeerAllReduce: CUDA IPC export failed on rank(s) "
+                               f"{[p for p, i in enumerate(infos) if i is None]}")
         self._imported = []  # (ptr, offset) of the peers' buffers mapped here
         bases = []
+        ok = True
         with torch.cuda.device(self.device):
             for p in range(self.world):
                 if p == self.rank:
@@ -52,9 +60,16 @@ class PeerAllReduce:
                     continue
                 hp = (C.c_char * 64).from_buffer_copy(infos[p][0])
                 ptr = C.c_void_p()
-                _lib.check(self.lib.vbq_ipc_import(hp, infos[p][1], C.byref(ptr)), self.lib)
+                if self.lib.vbq_ipc_import(hp, infos[p][1], C.byref(ptr)) != _lib.VBQ_OK:
+                    ok = False
+                    break
                 self._imported.append((ptr.value, infos[p][1]))
                 bases.append(ptr.value)
+        flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=self.device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+        if int(flag.item()) == 0:
+            self.close()
+            raise RuntimeError("PeerAllReduce: CUDA IPC import failed on some rank")
         self._bases = bases
         self._flags = (C.c_void_p * self.world)(*[b + 2 * self.cap * 4 for b in bases])
         self._data = [(C.c_void_p * self.world)(*[b + s * self.cap * 4 for b in bases]) for s in range(2)]
