@@ -333,11 +333,11 @@ def bench_tp(dev, rank: int, world: int, steps: int, prefill: bool = True) -> di
         # the same decode steps with the down GEMV writing into a buffer the peers map and
         # the one-shot all-reduce over NVLink peer memory (vibeblade_b200.peer) instead
         try:  # set-up fails on every rank together (PeerAllReduce), so all skip alike
-            ffn.attach_peer(32, dev)
+            ffn.attach_peer(16, dev)  # batches above 16 keep the collective (TPFFN.attach_peer)
         except RuntimeError as e:
             dec["decode_peer_error"] = str(e)[:200]
         if ffn.peer is not None:
-            for b, xb in (("1", xd), ("16", xd16), ("32", xd32)):
+            for b, xb in (("1", xd), ("16", xd16)):
                 pms = _time_steps(lambda _: ffn.decode(xb), 5 * steps, 5, stream, world)
                 dec[f"decode_b{b}_us_per_ffn_peer"] = round(1e3 * pms / (5 * steps), 1)
             ffn.peer.close()
