@@ -277,6 +277,35 @@ def bench_lm_head(dev, steps: int) -> dict:
     return out
 
 
+def bench_other_types(dev, steps: int) -> dict:
+    """The reference dispatcher's other block types (Q4_0, Q4_1, Q5_0, Q5_1, Q2_K, Q3_K,
+    Q5_K, Q8_K) through the generic GEMV kernel: config 2's 4096 x 14336 at batch 1,
+    synthetic weights (random codes, N(0, 1e-3) scales); enough copies alternate that they
+    never sit in L2 (>= 256 MB)."""
+    import torch
+    import vibeblade_b200 as vb
+    from vibeblade_b200 import formats as F
+    from vibeblade_b200.quantize import random_block_weights
+    K, N = 4096, 14336
+    out = {"shape": f"{K}x{N}", "batch": 1, "kernel": "vbq::gany::gemv_any_kernel (generic GEMV)"}
+    g = torch.Generator(device=dev).manual_seed(8)
+    x = torch.randn(1, K, generator=g, device=dev)
+    y = torch.empty(1, N, device=dev)
+    for t in F.OTHER_BLOCK_TYPES:
+        wbytes = K * F.row_bytes(t, N)
+        n_copies = max(2, -(-(256 << 20) // wbytes))
+        ws = [random_block_weights(K, N, t, seed=500 + i, device=dev) for i in range(n_copies)]
+        ms = _time_steps(lambda i: vb.gemv_dequant(x, ws[i % n_copies], y, K, N, t), 5 * steps, 4,
+                         torch.cuda.current_stream(dev), 1)
+        gbs = (wbytes + 4 * (K + N)) * 5 * steps / (ms * 1e-3) / 1e9
+        out[F.TYPE_NAMES[t].lower()] = {"value": round(gbs, 1), "unit": "GB/s",
+                                        "us_per_call": round(1e3 * ms / (5 * steps), 2),
+                                        "frac_of_hbm": round(gbs / peaks()["hbm_gbs"], 4)}
+        del ws
+    torch.cuda.empty_cache()
+    return out
+
+
 def bench_moe(dev, steps: int) -> dict:
     """MoE FFN, 8 experts top-2, hidden 4096, intermediate 14336, Q4_K,
     4096 tokens routed by N(0,1) logits (seed 3)."""
@@ -523,6 +552,8 @@ def run_only(args) -> None:
         res = bench_moe(dev, args.extras_steps)
     elif args.only == "lm_head":
         res = bench_lm_head(dev, args.extras_steps)
+    elif args.only == "other_types":
+        res = bench_other_types(dev, args.extras_steps)
     else:
         res = bench_tp(dev, rank, world, args.extras_steps)
     if world > 1:
@@ -881,6 +912,7 @@ def run_gpu(args) -> None:
             extras["prefill"] = _soft(bench_prefill, dev, args.extras_steps)
             extras["moe"] = _soft(bench_moe, dev, args.extras_steps)
             extras["lm_head"] = _soft(bench_lm_head, dev, args.extras_steps)
+            extras["other_types"] = _soft(bench_other_types, dev, args.extras_steps)
         extras["tp_ffn"] = bench_tp(dev, rank, world, args.extras_steps)
     else:  # config 5's decode side runs on the GEMV alone
         extras["tp_ffn_decode"] = bench_tp(dev, rank, world, args.extras_steps, prefill=False)
@@ -964,7 +996,7 @@ def main() -> None:
     ap.add_argument("--no-extras", action="store_true",
                     help="skip those; config 5 is then measured on its decode side only")
     ap.add_argument("--extras-steps", type=int, default=10)
-    ap.add_argument("--only", choices=["decode", "prefill", "moe", "lm_head", "tp"],
+    ap.add_argument("--only", choices=["decode", "prefill", "moe", "lm_head", "other_types", "tp"],
                     help="run just this measurement and print its JSON object")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -31,14 +31,25 @@
 extern "C" {
 #endif
 
-/* ggml type ids (cpp/include/ggml_types.h:12-13,17,21,23,26).  The quantized types are
- * the path's; the unquantized ones are read by vbq_dequantize and vbq_gemv (GGUF files keep
- * small tensors such as the MoE router, ffn_gate_inp, unquantized). */
+/* ggml type ids (cpp/include/ggml_types.h:11-27).  Q4_K, Q6_K and Q8_0 are the path's
+ * quantized types (every entry point); the unquantized ones are read by vbq_dequantize and
+ * vbq_gemv (GGUF files keep small tensors such as the MoE router, ffn_gate_inp,
+ * unquantized), and so are the reference dispatcher's other block types (Q4_0, Q4_1, Q5_0,
+ * Q5_1, Q2_K, Q3_K, Q5_K, Q8_K: cpp/src/dequant.cpp:412-422), each in the reference's own
+ * reading of its block.  Q8_1 (9) is not read, as in the reference. */
 #define VBQ_TYPE_F32 0
 #define VBQ_TYPE_F16 1
+#define VBQ_TYPE_Q4_0 2
+#define VBQ_TYPE_Q4_1 3
+#define VBQ_TYPE_Q5_0 6
+#define VBQ_TYPE_Q5_1 7
 #define VBQ_TYPE_Q8_0 8
+#define VBQ_TYPE_Q2_K 10
+#define VBQ_TYPE_Q3_K 11
 #define VBQ_TYPE_Q4_K 12
+#define VBQ_TYPE_Q5_K 13
 #define VBQ_TYPE_Q6_K 14
+#define VBQ_TYPE_Q8_K 15
 #define VBQ_TYPE_BF16 30
 
 /* element types of outputs / activations */
@@ -75,7 +86,11 @@ int vbq_row_bytes(int32_t type, int64_t n, int64_t* out_bytes);
  * `void dequantize_row(const void* row, float* out, int64_t n, ggml_type)`
  * (cpp/include/dequant.h:11); then n may be ragged (not a block multiple) and only n
  * values are written.  For rows > 1, n must be a multiple of the block size.
- * bf16 output rounds the fp32 dequantized value to nearest-even.
+ * bf16 output rounds the fp32 dequantized value to nearest-even.  Every type the
+ * reference's dispatcher takes is read, with its reading of each block (among them its
+ * Q2_K adding dmin without a sub-block min, Q3_K high bits from hmask[0..15] only, Q5_K
+ * fifth bits from 32 bytes further on per 64-value chunk, Q8_K's interleaved 33-byte
+ * sub-blocks: cpp/src/dequant.cpp:128-245, :317-354).
  */
 int vbq_dequantize(const void* w, void* out, int64_t rows, int64_t n, int32_t type,
                    int32_t out_dtype, void* stream);
@@ -97,9 +112,10 @@ int vbq_gemv_scratch_bytes(int64_t K, int64_t N, int32_t type, int32_t batch, si
  *     16 as consecutive launches over groups of up to 16 batch rows; any batch up to
  *     262140 on the generic kernel below, e.g. a prefill's tokens through the MoE router).
  * x is fp32 [batch, K], y fp32 [batch, N], both row-major.  N must be a multiple of
- * the block size (256 for Q4_K/Q6_K, 32 for Q8_0, 1 for F32/F16/BF16); widths that are
- * whole 256-column tiles of a quantized type run on the tiled kernels, the rest (the MoE
- * router's N = n_experts, unquantized weights) on a generic kernel without scratch.
+ * the block size (256 for the K-quants, 32 for Q4_0/Q4_1/Q5_0/Q5_1/Q8_0, 1 for
+ * F32/F16/BF16); widths that are whole 256-column tiles of Q4_K, Q6_K or Q8_0 run on the
+ * tiled kernels, the rest (the MoE router's N = n_experts, unquantized weights, the other
+ * block types) on a generic kernel without scratch.
  * W and y must be 16-byte aligned, x 4-byte aligned.  F16 weights are read through the
  * reference's f16_to_f32 (fp16 subnormals doubled), BF16 as the top half of an fp32.
  * scratch: caller-owned device memory of at least vbq_gemv_scratch_bytes(); it must be

@@ -19,8 +19,10 @@ _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _f64p = np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")
 _u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
 
-BLOCK_VALUES = {0: 1, 1: 1, 30: 1, 8: 32, 12: 256, 14: 256}
-BLOCK_BYTES = {0: 4, 1: 2, 30: 2, 8: 34, 12: 144, 14: 210}
+BLOCK_VALUES = {0: 1, 1: 1, 30: 1, 2: 32, 3: 32, 6: 32, 7: 32, 8: 32,
+                10: 256, 11: 256, 12: 256, 13: 256, 14: 256, 15: 256}
+BLOCK_BYTES = {0: 4, 1: 2, 30: 2, 2: 18, 3: 20, 6: 22, 7: 24, 8: 34,
+               10: 84, 11: 110, 12: 144, 13: 176, 14: 210, 15: 292}
 
 
 def row_bytes(qtype: int, n: int) -> int:

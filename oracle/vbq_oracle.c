@@ -19,15 +19,20 @@
 #include <math.h>
 
 /* ggml type ids: cpp/include/ggml_types.h:11-27 */
-enum { VBO_F32 = 0, VBO_F16 = 1, VBO_Q8_0 = 8, VBO_Q4_K = 12, VBO_Q6_K = 14, VBO_BF16 = 30 };
+enum {
+    VBO_F32 = 0, VBO_F16 = 1, VBO_Q4_0 = 2, VBO_Q4_1 = 3, VBO_Q5_0 = 6, VBO_Q5_1 = 7,
+    VBO_Q8_0 = 8, VBO_Q2_K = 10, VBO_Q3_K = 11, VBO_Q4_K = 12, VBO_Q5_K = 13, VBO_Q6_K = 14,
+    VBO_Q8_K = 15, VBO_BF16 = 30
+};
 
-/* Block geometry: cpp/include/ggml_types.h:31-71 (block sizes 32/256, byte sizes 34/144/210). */
+/* Block geometry: cpp/include/ggml_types.h:31-71 (values per block 1 / 32 / 256; bytes per
+ * block as the size table lists them, Q8_0 the 34-byte GGUF block, Q8_K 292). */
 int64_t vbo_block_values(int32_t type) {
     switch (type) {
         case VBO_F32: case VBO_F16: case VBO_BF16: return 1;
-        case VBO_Q8_0: return 32;
-        case VBO_Q4_K: return 256;
-        case VBO_Q6_K: return 256;
+        case VBO_Q4_0: case VBO_Q4_1: case VBO_Q5_0: case VBO_Q5_1: case VBO_Q8_0: return 32;
+        case VBO_Q2_K: case VBO_Q3_K: case VBO_Q4_K: case VBO_Q5_K: case VBO_Q6_K: case VBO_Q8_K:
+            return 256;
         default: return -1;
     }
 }
@@ -36,9 +41,17 @@ int64_t vbo_block_bytes(int32_t type) {
     switch (type) {
         case VBO_F32: return 4;
         case VBO_F16: case VBO_BF16: return 2;
+        case VBO_Q4_0: return 18;
+        case VBO_Q4_1: return 20;
+        case VBO_Q5_0: return 22;
+        case VBO_Q5_1: return 24;
         case VBO_Q8_0: return 34;
+        case VBO_Q2_K: return 84;
+        case VBO_Q3_K: return 110;
         case VBO_Q4_K: return 144;
+        case VBO_Q5_K: return 176;
         case VBO_Q6_K: return 210;
+        case VBO_Q8_K: return 292;
         default: return -1;
     }
 }
@@ -218,6 +231,153 @@ static void vbo_row_bf16(const uint8_t* row, float* out, int64_t n) {
     }
 }
 
+/* ---- the other block types of the reference's dispatcher (cpp/src/dequant.cpp:407-425) ----
+ * Each restates the reference's reading of its block, which is not always llama.cpp's:
+ * the index formulas below are the reference's loops solved for one value index.  fp16
+ * fields go through the reference's f16_to_f32 (subnormals doubled); every product and
+ * sum the reference writes as separate operations is rounded separately. */
+
+static int64_t rem_of(int64_t n, int64_t b, int64_t bv) {
+    int64_t r = n - b * bv;
+    return r > bv ? bv : r;
+}
+
+/* Q4_0, 18 B: d(f16) @0, qs[16] @2; value i = nibble (i&1) of qs[i>>1]; out = (q-8)*d
+ * (cpp/src/dequant.cpp:23-35). */
+void vbo_dequantize_row_q4_0(const uint8_t* row, float* out, int64_t n) {
+    for (int64_t b = 0; b * 32 < n; ++b) {
+        const uint8_t* blk = row + b * 18;
+        float d = vbo_f16_to_f32(rd16(blk));
+        for (int64_t i = 0; i < rem_of(n, b, 32); ++i) {
+            int q = (blk[2 + (i >> 1)] >> (4 * (i & 1))) & 15;
+            out[b * 32 + i] = (float)(q - 8) * d;
+        }
+    }
+}
+
+/* Q4_1, 20 B: d @0, m @2 (f16), qs[16] @4; out = d*q + m (cpp/src/dequant.cpp:40-53). */
+void vbo_dequantize_row_q4_1(const uint8_t* row, float* out, int64_t n) {
+    for (int64_t b = 0; b * 32 < n; ++b) {
+        const uint8_t* blk = row + b * 20;
+        float d = vbo_f16_to_f32(rd16(blk)), m = vbo_f16_to_f32(rd16(blk + 2));
+        for (int64_t i = 0; i < rem_of(n, b, 32); ++i) {
+            int q = (blk[4 + (i >> 1)] >> (4 * (i & 1))) & 15;
+            float p = d * (float)q;
+            out[b * 32 + i] = p + m;
+        }
+    }
+}
+
+/* Q5_0, 22 B: d @0, qh[4] @2 (bit i = fifth bit of value i), qs[16] @6;
+ * out = (q-16)*d (cpp/src/dequant.cpp:58-73). */
+void vbo_dequantize_row_q5_0(const uint8_t* row, float* out, int64_t n) {
+    for (int64_t b = 0; b * 32 < n; ++b) {
+        const uint8_t* blk = row + b * 22;
+        float d = vbo_f16_to_f32(rd16(blk));
+        for (int64_t i = 0; i < rem_of(n, b, 32); ++i) {
+            int lo = (blk[6 + (i >> 1)] >> (4 * (i & 1))) & 15;
+            int hi = (blk[2 + (i >> 3)] >> (i & 7)) & 1;
+            out[b * 32 + i] = (float)((lo | (hi << 4)) - 16) * d;
+        }
+    }
+}
+
+/* Q5_1, 24 B: d @0, m @2, qh[4] @4, qs[16] @8; out = d*q + m (cpp/src/dequant.cpp:78-93). */
+void vbo_dequantize_row_q5_1(const uint8_t* row, float* out, int64_t n) {
+    for (int64_t b = 0; b * 32 < n; ++b) {
+        const uint8_t* blk = row + b * 24;
+        float d = vbo_f16_to_f32(rd16(blk)), m = vbo_f16_to_f32(rd16(blk + 2));
+        for (int64_t i = 0; i < rem_of(n, b, 32); ++i) {
+            int lo = (blk[8 + (i >> 1)] >> (4 * (i & 1))) & 15;
+            int hi = (blk[4 + (i >> 3)] >> (i & 7)) & 1;
+            float p = d * (float)(lo | (hi << 4));
+            out[b * 32 + i] = p + m;
+        }
+    }
+}
+
+/* Q2_K, 84 B: scales[16] @0, qs[64] @16, d @80, dmin @82.  Value v: sub-block s = v>>4,
+ * l = v&15; code = bits 2(l&3).. of qs[4s + (l>>3)] (so values l and l+4 of a half share a
+ * code); out = (d*(scales[s]&15))*code + dmin -- the reference adds dmin itself, without
+ * a per-sub-block min (cpp/src/dequant.cpp:128-150). */
+void vbo_dequantize_row_q2_K(const uint8_t* row, float* out, int64_t n) {
+    for (int64_t b = 0; b * 256 < n; ++b) {
+        const uint8_t* blk = row + b * 84;
+        float d = vbo_f16_to_f32(rd16(blk + 80)), mn = vbo_f16_to_f32(rd16(blk + 82));
+        for (int64_t v = 0; v < rem_of(n, b, 256); ++v) {
+            int s = (int)(v >> 4), l = (int)(v & 15);
+            float dl = d * (float)(blk[s] & 15);
+            int q = (blk[16 + 4 * s + (l >> 3)] >> (2 * (l & 3))) & 3;
+            float p = dl * (float)q;
+            out[b * 256 + v] = p + mn;
+        }
+    }
+}
+
+/* Q3_K scale of sub-block j (get_scale_min_k3, cpp/src/dequant.cpp:155-166; its min is
+ * never used). */
+static int q3k_scale(int j, const uint8_t* s) {
+    if (j < 4) return s[j] & 63;
+    if (j < 8) return s[j + 4] & 63;
+    return (s[j - 4] >> 4) & 63;
+}
+
+/* Q3_K, 110 B: hmask[32] @0, qs[64] @32, scales[12] @96, d @108.  Value v: chunk c = v>>6,
+ * quarter t = (v>>4)&3, l = v&15; code = bits 2(l&3).. of qs[16c + 4t + (l>>3)]; high bit =
+ * bit (4c + 2t) of hmask[l], which is 0 once that shift reaches 8 (a byte shifted as an int);
+ * out = (d*scale(4c + t))*(code + 8*high) (cpp/src/dequant.cpp:168-218). */
+void vbo_dequantize_row_q3_K(const uint8_t* row, float* out, int64_t n) {
+    for (int64_t b = 0; b * 256 < n; ++b) {
+        const uint8_t* blk = row + b * 110;
+        float d = vbo_f16_to_f32(rd16(blk + 108));
+        for (int64_t v = 0; v < rem_of(n, b, 256); ++v) {
+            int c = (int)(v >> 6), t = (int)((v >> 4) & 3), l = (int)(v & 15);
+            float dt = d * (float)q3k_scale(4 * c + t, blk + 96);
+            int q = (blk[32 + 16 * c + 4 * t + (l >> 3)] >> (2 * (l & 3))) & 3;
+            int sh = 4 * c + 2 * t;
+            int h = sh < 8 ? (blk[l] >> sh) & 1 : 0;
+            out[b * 256 + v] = dt * (float)(q + 8 * h);
+        }
+    }
+}
+
+/* Q5_K, 176 B: d @0, dmin @2, scales[12] @4 (the Q4_K packing), qh[32] @16, qs[128] @48.
+ * The reference steps its qh pointer by 32 bytes per 64-value chunk like qs, so chunk c
+ * takes its fifth bits from bytes 16+32c.. (qs bytes from chunk 1 on) and always from bit
+ * 7 (first half) or bit 3 (second half).  Value v: c = v>>6, half = (v>>5)&1, l = v&31;
+ * out = (d*sc)*q - dmin*m with (sc, m) of sub-block 2c+half (cpp/src/dequant.cpp:307-354). */
+void vbo_dequantize_row_q5_K(const uint8_t* row, float* out, int64_t n) {
+    for (int64_t b = 0; b * 256 < n; ++b) {
+        const uint8_t* blk = row + b * 176;
+        float d = vbo_f16_to_f32(rd16(blk)), dmin = vbo_f16_to_f32(rd16(blk + 2));
+        for (int64_t v = 0; v < rem_of(n, b, 256); ++v) {
+            int c = (int)(v >> 6), half = (int)((v >> 5) & 1), l = (int)(v & 31);
+            int sc, mn;
+            q4k_scale_min(2 * c + half, blk + 4, &sc, &mn);
+            float d1 = d * (float)sc, m1 = dmin * (float)mn;
+            int qb = blk[48 + 32 * c + l], hb = blk[16 + 32 * c + l];
+            int q = half ? ((qb >> 4) | (((hb >> 3) & 1) << 4)) : ((qb & 15) | (((hb >> 7) & 1) << 4));
+            float p = d1 * (float)q;
+            out[b * 256 + v] = p - m1;
+        }
+    }
+}
+
+/* Q8_K, 292 B: d (float32) @0, then eight 33-byte sub-blocks at 4 + 33s: 32 int8 codes and
+ * an int8 scale; out = code * (d*scale) (cpp/src/dequant.cpp:226-245). */
+void vbo_dequantize_row_q8_K(const uint8_t* row, float* out, int64_t n) {
+    for (int64_t b = 0; b * 256 < n; ++b) {
+        const uint8_t* blk = row + b * 292;
+        float d;
+        memcpy(&d, blk, 4);
+        for (int64_t v = 0; v < rem_of(n, b, 256); ++v) {
+            const uint8_t* sub = blk + 4 + 33 * (v >> 5);
+            float ds = d * (float)(int8_t)sub[32];
+            out[b * 256 + v] = (float)(int8_t)sub[v & 31] * ds;
+        }
+    }
+}
+
 /* Dispatcher (cpp/src/dequant.cpp:407-425).  Returns 0, or -1 for an unsupported type
  * where the reference throws "Unsupported dequant type". */
 int vbo_dequantize_row(const void* row, float* out, int64_t n, int32_t type) {
@@ -228,6 +388,14 @@ int vbo_dequantize_row(const void* row, float* out, int64_t n, int32_t type) {
         case VBO_Q4_K: vbo_dequantize_row_q4_K((const uint8_t*)row, out, n); return 0;
         case VBO_Q6_K: vbo_dequantize_row_q6_K((const uint8_t*)row, out, n); return 0;
         case VBO_Q8_0: vbo_dequantize_row_q8_0((const uint8_t*)row, out, n); return 0;
+        case VBO_Q4_0: vbo_dequantize_row_q4_0((const uint8_t*)row, out, n); return 0;
+        case VBO_Q4_1: vbo_dequantize_row_q4_1((const uint8_t*)row, out, n); return 0;
+        case VBO_Q5_0: vbo_dequantize_row_q5_0((const uint8_t*)row, out, n); return 0;
+        case VBO_Q5_1: vbo_dequantize_row_q5_1((const uint8_t*)row, out, n); return 0;
+        case VBO_Q2_K: vbo_dequantize_row_q2_K((const uint8_t*)row, out, n); return 0;
+        case VBO_Q3_K: vbo_dequantize_row_q3_K((const uint8_t*)row, out, n); return 0;
+        case VBO_Q5_K: vbo_dequantize_row_q5_K((const uint8_t*)row, out, n); return 0;
+        case VBO_Q8_K: vbo_dequantize_row_q8_K((const uint8_t*)row, out, n); return 0;
         default: return -1;
     }
 }

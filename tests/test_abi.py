@@ -47,21 +47,34 @@ def test_row_bytes(lib):
     assert lib.vbq_row_bytes(12, 4096, C.byref(v)) == 0 and v.value == 16 * 144
     assert lib.vbq_row_bytes(14, 4096, C.byref(v)) == 0 and v.value == 16 * 210
     assert lib.vbq_row_bytes(8, 4096, C.byref(v)) == 0 and v.value == 128 * 34
-    assert lib.vbq_row_bytes(3, 4096, C.byref(v)) == 1
-    assert b"Unsupported dequant type: 3" in lib.vbq_last_error()
+    # the reference dispatcher's other block types (cpp/src/dequant.cpp:753-763)
+    for t, bv, bb in ((2, 32, 18), (3, 32, 20), (6, 32, 22), (7, 32, 24), (10, 256, 84),
+                      (11, 256, 110), (13, 256, 176), (15, 256, 292)):
+        assert lib.vbq_row_bytes(t, 4096, C.byref(v)) == 0 and v.value == 4096 // bv * bb, t
+    # Q8_1 (9) and unknown ids: the reference throws (cpp/src/dequant.cpp:423)
+    assert lib.vbq_row_bytes(9, 4096, C.byref(v)) == 1
+    assert b"Unsupported dequant type: 9" in lib.vbq_last_error()
+    assert lib.vbq_row_bytes(4, 4096, C.byref(v)) == 1
 
 
 def test_argument_errors_need_no_gpu(lib):
     from vibeblade_b200 import _lib
     # unsupported type: reference message (cpp/src/dequant.cpp:764)
-    assert lib.vbq_gemv(None, None, None, 16, 256, 2, 1, None, 0, None) == _lib.VBQ_ERR_TYPE
-    assert lib.vbq_last_error() == b"gemv_dequant: unsupported type 2"
+    assert lib.vbq_gemv(None, None, None, 16, 256, 9, 1, None, 0, None) == _lib.VBQ_ERR_TYPE
+    assert lib.vbq_last_error() == b"gemv_dequant: unsupported type 9"
     assert lib.vbq_gemv(None, None, None, 16, 256, 12, 33, None, 0, None) == _lib.VBQ_ERR_SHAPE
     assert lib.vbq_gemv(None, None, None, 16, 300, 12, 1, None, 0, None) == _lib.VBQ_ERR_SHAPE
     assert lib.vbq_gemv(None, None, None, 16, 256, 12, 1, None, 0, None) == _lib.VBQ_ERR_NULL
     assert lib.vbq_gemv(16, 16, 8, 16, 256, 12, 1, None, 0, None) == _lib.VBQ_ERR_ALIGN
     assert lib.vbq_dequantize(None, None, 2, 100, 12, 0, None) == _lib.VBQ_ERR_SHAPE
-    assert lib.vbq_dequantize(None, None, 1, 256, 13, 0, None) == _lib.VBQ_ERR_TYPE
+    assert lib.vbq_dequantize(None, None, 1, 256, 9, 0, None) == _lib.VBQ_ERR_TYPE
+    assert lib.vbq_dequantize(None, None, 2, 100, 2, 0, None) == _lib.VBQ_ERR_SHAPE  # Q4_0: 32s
+    assert lib.vbq_gemv(None, None, None, 16, 100, 13, 1, None, 0, None) == _lib.VBQ_ERR_SHAPE
+    assert lib.vbq_gemv(None, None, None, 16, 96, 6, 1, None, 0, None) == _lib.VBQ_ERR_NULL  # Q5_0 N=96 ok
+    # the other block types take the generic kernel: no scratch, any batch
+    v = C.c_size_t(7)
+    assert lib.vbq_gemv_scratch_bytes(4096, 14336, 13, 100, C.byref(v)) == 0 and v.value == 0
+    assert lib.vbq_gemm(None, None, None, 64, 256, 256, 13, 0, None) == _lib.VBQ_ERR_TYPE
     assert lib.vbq_dequantize(None, None, 1, 256, 12, 5, None) == _lib.VBQ_ERR_SHAPE
     assert lib.vbq_dequantize(0, 0, 0, 256, 12, 0, None) == _lib.VBQ_OK  # empty: no work
 
@@ -113,7 +126,7 @@ def test_python_face_rejects_host_tensors():
     with pytest.raises(RuntimeError, match="CUDA tensors"):
         vb.gemv_dequant(x, w, None, 4096, 4096, "Q4_K")
     with pytest.raises(RuntimeError, match="Unsupported dequant type"):
-        vb.gemv_dequant(x, w, None, 4096, 4096, 13)
+        vb.gemv_dequant(x, w, None, 4096, 4096, 9)
 
 
 def test_wait_probe_argument_errors_need_no_gpu(lib):
@@ -128,7 +141,7 @@ def test_fused_entry_argument_errors_need_no_gpu(lib):
     from vibeblade_b200 import _lib
     assert lib.vbq_gemv_ex(None, None, None, 16, 256, 12, 1, 4, None, None, None, 0, None) == _lib.VBQ_ERR_SHAPE
     assert b"flags" in lib.vbq_last_error()
-    assert lib.vbq_gemv_ex(None, None, None, 16, 256, 2, 1, 0, None, None, None, 0, None) == _lib.VBQ_ERR_TYPE
+    assert lib.vbq_gemv_ex(None, None, None, 16, 256, 9, 1, 0, None, None, None, 0, None) == _lib.VBQ_ERR_TYPE
     assert lib.vbq_gemm_ex(None, None, None, 4, 64, 300, 12, 0, None, None, None) == _lib.VBQ_ERR_SHAPE
 
 

@@ -29,19 +29,48 @@ int ok() {
   return VBQ_OK;
 }
 
-// the quantized weight types (tiled GEMV kernels, tensor-core GEMM, MoE)
+// the quantized weight types of the path (tiled GEMV kernels, tensor-core GEMM, MoE)
 bool quantized(int32_t t) { return t == VBQ_TYPE_Q4_K || t == VBQ_TYPE_Q6_K || t == VBQ_TYPE_Q8_0; }
-// every weight type the library reads (dequantize, GEMV): plus F32 / F16 / BF16
+// the reference dispatcher's other block types (cpp/src/dequant.cpp:412-422): dequantize
+// and the generic GEMV read them
+bool other_block_type(int32_t t) {
+  switch (t) {
+    case VBQ_TYPE_Q4_0: case VBQ_TYPE_Q4_1: case VBQ_TYPE_Q5_0: case VBQ_TYPE_Q5_1:
+    case VBQ_TYPE_Q2_K: case VBQ_TYPE_Q3_K: case VBQ_TYPE_Q5_K: case VBQ_TYPE_Q8_K:
+      return true;
+    default:
+      return false;
+  }
+}
+// every weight type the library reads (dequantize, GEMV): the reference's dequantize_row and
+// gemv_dequant take the same set (cpp/src/dequant.cpp:407-425, :748-765)
 bool supported(int32_t t) {
-  return quantized(t) || t == VBQ_TYPE_F32 || t == VBQ_TYPE_F16 || t == VBQ_TYPE_BF16;
+  return quantized(t) || other_block_type(t) || t == VBQ_TYPE_F32 || t == VBQ_TYPE_F16 ||
+         t == VBQ_TYPE_BF16;
 }
 
-int64_t block_values(int32_t t) { return t == VBQ_TYPE_Q8_0 ? 32 : (quantized(t) ? 256 : 1); }
+// values and bytes per block (cpp/include/ggml_types.h:31-71; Q8_0 the 34-byte GGUF block)
+int64_t block_values(int32_t t) {
+  switch (t) {
+    case VBQ_TYPE_F32: case VBQ_TYPE_F16: case VBQ_TYPE_BF16: return 1;
+    case VBQ_TYPE_Q4_0: case VBQ_TYPE_Q4_1: case VBQ_TYPE_Q5_0: case VBQ_TYPE_Q5_1:
+    case VBQ_TYPE_Q8_0: return 32;
+    default: return 256;  // Q2_K .. Q8_K
+  }
+}
 int64_t block_bytes(int32_t t) {
   switch (t) {
+    case VBQ_TYPE_Q4_0: return 18;
+    case VBQ_TYPE_Q4_1: return 20;
+    case VBQ_TYPE_Q5_0: return 22;
+    case VBQ_TYPE_Q5_1: return 24;
     case VBQ_TYPE_Q8_0: return 34;
+    case VBQ_TYPE_Q2_K: return 84;
+    case VBQ_TYPE_Q3_K: return 110;
     case VBQ_TYPE_Q4_K: return 144;
+    case VBQ_TYPE_Q5_K: return 176;
     case VBQ_TYPE_Q6_K: return 210;
+    case VBQ_TYPE_Q8_K: return 292;
     case VBQ_TYPE_F32: return 4;
     default: return 2;  // F16, BF16
   }

@@ -14,15 +14,33 @@ namespace vbq {
 
 constexpr int kF32 = 0;
 constexpr int kF16 = 1;
+constexpr int kQ4_0 = 2;
+constexpr int kQ4_1 = 3;
+constexpr int kQ5_0 = 6;
+constexpr int kQ5_1 = 7;
 constexpr int kQ8_0 = 8;
+constexpr int kQ2_K = 10;
+constexpr int kQ3_K = 11;
 constexpr int kQ4_K = 12;
+constexpr int kQ5_K = 13;
 constexpr int kQ6_K = 14;
+constexpr int kQ8_K = 15;
 constexpr int kBF16 = 30;
 
 template <int QT> struct Fmt;
 template <> struct Fmt<kQ4_K> { static constexpr int kValues = 256, kBytes = 144; };
 template <> struct Fmt<kQ6_K> { static constexpr int kValues = 256, kBytes = 210; };
 template <> struct Fmt<kQ8_0> { static constexpr int kValues = 32, kBytes = 34; };
+// the other block types of the reference's dispatcher (cpp/include/ggml_types.h:52-71,
+// :82-168), read by the dequant kernel and the generic GEMV only
+template <> struct Fmt<kQ4_0> { static constexpr int kValues = 32, kBytes = 18; };
+template <> struct Fmt<kQ4_1> { static constexpr int kValues = 32, kBytes = 20; };
+template <> struct Fmt<kQ5_0> { static constexpr int kValues = 32, kBytes = 22; };
+template <> struct Fmt<kQ5_1> { static constexpr int kValues = 32, kBytes = 24; };
+template <> struct Fmt<kQ2_K> { static constexpr int kValues = 256, kBytes = 84; };
+template <> struct Fmt<kQ3_K> { static constexpr int kValues = 256, kBytes = 110; };
+template <> struct Fmt<kQ5_K> { static constexpr int kValues = 256, kBytes = 176; };
+template <> struct Fmt<kQ8_K> { static constexpr int kValues = 256, kBytes = 292; };
 // unquantized weights (small GGUF tensors such as the MoE router): one value per "block"
 template <> struct Fmt<kF32> { static constexpr int kValues = 1, kBytes = 4; };
 template <> struct Fmt<kF16> { static constexpr int kValues = 1, kBytes = 2; };

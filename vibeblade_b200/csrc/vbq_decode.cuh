@@ -1,11 +1,12 @@
 // vbq_decode.cuh -- one lane's 8 consecutive values of a 256-value unit of a weight row.
 //
-// A unit is 256 consecutive values of one row: one Q4_K / Q6_K block, eight Q8_0 blocks,
+// A unit is 256 consecutive values of one row: one block of a 256-value type (Q2_K, Q3_K,
+// Q4_K, Q5_K, Q6_K, Q8_K), eight blocks of a 32-value type (Q4_0, Q4_1, Q5_0, Q5_1, Q8_0),
 // or 256 F32 / F16 / BF16 values; lane l produces values 8 l .. 8 l + 7.  Values are the
-// reference's dequantized fp32 values bit for bit (cpp/src/dequant.cpp:268-301, :359-402,
-// :407-411; the GGUF Q8_0 block of cpp/src/cuda_kernels.cu:718-735): every product and
-// difference the reference rounds separately is rounded separately here.  Used by the
-// dequant kernel and the generic GEMV.
+// reference's dequantized fp32 values bit for bit (cpp/src/dequant.cpp:23-93, :128-245,
+// :268-301, :317-402, :407-411; the GGUF Q8_0 block of cpp/src/cuda_kernels.cu:718-735):
+// every product and sum the reference rounds separately is rounded separately here.  Used
+// by the dequant kernel and the generic GEMV.
 #pragma once
 #include "vbq_common.cuh"
 
@@ -71,6 +72,148 @@ __device__ __forceinline__ void decode8<kQ8_0>(const uint8_t* __restrict__ unit,
     const int qv = (int)(int8_t)(uint8_t)(w >> (8 * (i & 3)));
     v[i] = __fmul_rn((float)qv, d);
   }
+}
+
+// ---- the other block types of the reference's dispatcher ----
+// Blocks sit at 2-byte-aligned offsets (every block size is even), so 16-bit fields are
+// read directly and 4-byte runs with ld_u32_a2.
+
+// Q4_0, 18 B (cpp/src/dequant.cpp:23-35): d @0, qs @2; value i of a block is nibble i&1 of
+// qs[i>>1], so the lane's 8 values (block lane/4, values 8(lane&3)..) are the 8 nibbles of
+// one 4-byte word, lowest first; out = (q - 8) * d.
+template <>
+__device__ __forceinline__ void decode8<kQ4_0>(const uint8_t* __restrict__ unit, int lane,
+                                               float v[8]) {
+  const uint8_t* blk = unit + 18 * (lane >> 2);
+  const float d = f16_ref(ld_u16(blk));
+  const uint32_t w = ld_u32_a2(blk + 2 + 4 * (lane & 3));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __fmul_rn((float)((int)((w >> (4 * i)) & 0xfu) - 8), d);
+}
+
+// Q4_1, 20 B (:40-53): d @0, m @2, qs @4; out = d * q + m.
+template <>
+__device__ __forceinline__ void decode8<kQ4_1>(const uint8_t* __restrict__ unit, int lane,
+                                               float v[8]) {
+  const uint8_t* blk = unit + 20 * (lane >> 2);
+  const float d = f16_ref(ld_u16(blk)), m = f16_ref(ld_u16(blk + 2));
+  const uint32_t w = ld_u32_a2(blk + 4 + 4 * (lane & 3));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __fadd_rn(__fmul_rn(d, (float)((w >> (4 * i)) & 0xfu)), m);
+}
+
+// Q5_0, 22 B (:58-73): d @0, qh @2 (bit i = fifth bit of value i), qs @6; out = (q - 16) * d.
+template <>
+__device__ __forceinline__ void decode8<kQ5_0>(const uint8_t* __restrict__ unit, int lane,
+                                               float v[8]) {
+  const uint8_t* blk = unit + 22 * (lane >> 2);
+  const float d = f16_ref(ld_u16(blk));
+  const uint32_t hb = ld_u32_a2(blk + 2) >> (8 * (lane & 3));
+  const uint32_t w = ld_u32_a2(blk + 6 + 4 * (lane & 3));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int q = (int)(((w >> (4 * i)) & 0xfu) | (((hb >> i) & 1u) << 4));
+    v[i] = __fmul_rn((float)(q - 16), d);
+  }
+}
+
+// Q5_1, 24 B (:78-93): d @0, m @2, qh @4, qs @8; out = d * q + m.
+template <>
+__device__ __forceinline__ void decode8<kQ5_1>(const uint8_t* __restrict__ unit, int lane,
+                                               float v[8]) {
+  const uint8_t* blk = unit + 24 * (lane >> 2);
+  const float d = f16_ref(ld_u16(blk)), m = f16_ref(ld_u16(blk + 2));
+  const uint32_t hb = ld_u32_a2(blk + 4) >> (8 * (lane & 3));
+  const uint32_t w = ld_u32_a2(blk + 8 + 4 * (lane & 3));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t q = ((w >> (4 * i)) & 0xfu) | (((hb >> i) & 1u) << 4);
+    v[i] = __fadd_rn(__fmul_rn(d, (float)q), m);
+  }
+}
+
+// Q2_K, 84 B (:128-150): scales[16] @0, qs[64] @16, d @80, dmin @82.  The lane's values
+// are half (lane&1) of sub-block lane/2; the reference reads value l of a sub-block from
+// bits 2(l&3) of qs[4s + l/8], so the lane's 8 codes come from one byte, each twice;
+// out = (d * (scale & 15)) * q + dmin (the reference adds dmin itself).
+template <>
+__device__ __forceinline__ void decode8<kQ2_K>(const uint8_t* __restrict__ blk, int lane,
+                                               float v[8]) {
+  const int s = lane >> 1;
+  const float d = f16_ref(ld_u16(blk + 80)), mn = f16_ref(ld_u16(blk + 82));
+  const float dl = __fmul_rn(d, (float)(blk[s] & 0xf));
+  const uint32_t q = blk[16 + 4 * s + (lane & 1)];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __fadd_rn(__fmul_rn(dl, (float)((q >> (2 * (i & 3))) & 3u)), mn);
+}
+
+// Q3_K scale of sub-block j (get_scale_min_k3, :155-166; its min is unused).
+__device__ __forceinline__ int q3k_scale(const uint8_t* __restrict__ sc, int j) {
+  if (j < 4) return sc[j] & 63;
+  if (j < 8) return sc[j + 4] & 63;
+  return (sc[j - 4] >> 4) & 63;
+}
+
+// Q3_K, 110 B (:168-218): hmask[32] @0, qs[64] @32, scales[12] @96, d @108.  The lane's
+// values: chunk c = lane/8 of 64, quarter t = (lane/2)&3, half (lane&1) of its 16; codes
+// from one byte, qs[16c + 4t + (lane&1)], each twice (bits 2(l&3)); the high bit of value l
+// is bit 4c + 2t of hmask[l], and 0 once that shift reaches 8 (the reference shifts a
+// byte); out = (d * scale(4c + t)) * (q + 8 h).
+template <>
+__device__ __forceinline__ void decode8<kQ3_K>(const uint8_t* __restrict__ blk, int lane,
+                                               float v[8]) {
+  const int c = lane >> 3, t = (lane >> 1) & 3, sh = 4 * c + 2 * t;
+  const float d = f16_ref(ld_u16(blk + 108));
+  const float dt = __fmul_rn(d, (float)q3k_scale(blk + 96, 4 * c + t));
+  const uint32_t q = blk[32 + 16 * c + 4 * t + (lane & 1)];
+  const uint8_t* hm = blk + 8 * (lane & 1);
+  const uint32_t h0 = ld_u32_a2(hm), h1 = ld_u32_a2(hm + 4);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t hbyte = byte_of(i < 4 ? h0 : h1, i & 3);
+    const uint32_t h = sh < 8 ? (hbyte >> sh) & 1u : 0u;
+    v[i] = __fmul_rn(dt, (float)(((q >> (2 * (i & 3))) & 3u) + 8u * h));
+  }
+}
+
+// Q5_K, 176 B (:307-354): d @0, dmin @2, scales[12] @4 (the Q4_K packing), qh[32] @16,
+// qs[128] @48.  The reference advances its qh pointer 32 bytes per 64-value chunk, as it
+// does qs, so chunk c reads its fifth bits from bytes 16 + 32c.. (qs bytes from chunk 1 on),
+// bit 7 for the chunk's first 32 values and bit 3 for the second.  The lane's values: chunk
+// c = lane/8, half (lane/4)&1, offset l0 = 8(lane&3); out = (d*sc)*q - dmin*m.
+template <>
+__device__ __forceinline__ void decode8<kQ5_K>(const uint8_t* __restrict__ blk, int lane,
+                                               float v[8]) {
+  const int c = lane >> 3, half = (lane >> 2) & 1, l0 = 8 * (lane & 3);
+  const float d = f16_ref(ld_u16(blk)), dmin = f16_ref(ld_u16(blk + 2));
+  const uint32_t s0 = ld_u32_a2(blk + 4), s1 = ld_u32_a2(blk + 8), s2 = ld_u32_a2(blk + 12);
+  int sc, mn;
+  q4k_scale_min(2 * c + half, s0, s1, s2, sc, mn);
+  const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
+  const uint8_t* qp = blk + 48 + 32 * c + l0;
+  const uint8_t* hp = blk + 16 + 32 * c + l0;
+  const uint32_t q0 = ld_u32_a2(qp), q1 = ld_u32_a2(qp + 4);
+  const uint32_t g0 = ld_u32_a2(hp), g1 = ld_u32_a2(hp + 4);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t qb = byte_of(i < 4 ? q0 : q1, i & 3), hb = byte_of(i < 4 ? g0 : g1, i & 3);
+    const uint32_t q = half ? ((qb >> 4) | (((hb >> 3) & 1u) << 4)) : ((qb & 0xfu) | (((hb >> 7) & 1u) << 4));
+    v[i] = __fsub_rn(__fmul_rn(d1, (float)q), m1);
+  }
+}
+
+// Q8_K, 292 B (:226-245): d (fp32) @0, then eight 33-byte sub-blocks at 4 + 33s, each 32
+// int8 codes and an int8 scale; out = q * (d * scale).  Sub-blocks start at odd offsets,
+// so the codes are read bytewise.
+template <>
+__device__ __forceinline__ void decode8<kQ8_K>(const uint8_t* __restrict__ blk, int lane,
+                                               float v[8]) {
+  const float d = __uint_as_float(ld_u16(blk) | (ld_u16(blk + 2) << 16));
+  const uint8_t* sub = blk + 4 + 33 * (lane >> 2);
+  const float ds = __fmul_rn(d, (float)(int)(int8_t)sub[32]);
+  const uint8_t* q = sub + 8 * (lane & 3);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __fmul_rn((float)(int)(int8_t)q[i], ds);
 }
 
 // F32 rows: the values as stored (memcpy in the reference's dequantize_row).

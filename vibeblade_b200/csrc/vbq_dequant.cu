@@ -1,14 +1,15 @@
 // vbq_dequant.cu -- k-quant block dequantization to fp32 / bf16 (sm_100a).
 //
-// Device form of the reference's dequantize_row_q4_K / _q6_K (cpp/src/dequant.cpp:268-301,
-// :359-402) and of the GGUF Q8_0 block (cpp/src/cuda_kernels.cu:718-735).  Values are
+// Device form of the reference's dequantize_row for every type its dispatcher takes
+// (cpp/src/dequant.cpp:407-425: the k-quants Q2_K..Q8_K, Q4_0 / Q4_1 / Q5_0 / Q5_1, F32 /
+// F16 / BF16) and of the GGUF Q8_0 block (cpp/src/cuda_kernels.cu:718-735).  Values are
 // bit-identical to the reference: every product and difference the reference rounds
 // separately is rounded separately here (__fmul_rn / __fsub_rn stop the compiler from
 // contracting them into an FMA).
 //
-// Work unit: 256 consecutive values of one row (one Q4_K/Q6_K block, eight Q8_0 blocks),
-// one warp per unit, 8 values per lane, so each warp writes 1 KB (fp32) or 512 B (bf16)
-// of contiguous output.  The kernel is HBM-bound on its writes.
+// Work unit: 256 consecutive values of one row (one block of a 256-value type, eight
+// blocks of a 32-value type), one warp per unit, 8 values per lane, so each warp writes
+// 1 KB (fp32) or 512 B (bf16) of contiguous output.  The kernel is HBM-bound on its writes.
 #include "vbq_common.cuh"
 #include "vbq_decode.cuh"
 #include "vbq_internal.h"
@@ -81,24 +82,25 @@ cudaError_t launch_dequant(int qtype, const void* w, void* out, int64_t rows, in
                            int64_t row_bytes, int out_dtype, cudaStream_t st) {
   const bool bf = out_dtype == 1;
   switch (qtype) {
-    case kQ4_K:
-      return bf ? launch_dequant_t<kQ4_K, __nv_bfloat16>(w, out, rows, n, row_bytes, st)
-                : launch_dequant_t<kQ4_K, float>(w, out, rows, n, row_bytes, st);
-    case kQ6_K:
-      return bf ? launch_dequant_t<kQ6_K, __nv_bfloat16>(w, out, rows, n, row_bytes, st)
-                : launch_dequant_t<kQ6_K, float>(w, out, rows, n, row_bytes, st);
-    case kQ8_0:
-      return bf ? launch_dequant_t<kQ8_0, __nv_bfloat16>(w, out, rows, n, row_bytes, st)
-                : launch_dequant_t<kQ8_0, float>(w, out, rows, n, row_bytes, st);
-    case kF32:
-      return bf ? launch_dequant_t<kF32, __nv_bfloat16>(w, out, rows, n, row_bytes, st)
-                : launch_dequant_t<kF32, float>(w, out, rows, n, row_bytes, st);
-    case kF16:
-      return bf ? launch_dequant_t<kF16, __nv_bfloat16>(w, out, rows, n, row_bytes, st)
-                : launch_dequant_t<kF16, float>(w, out, rows, n, row_bytes, st);
-    case kBF16:
-      return bf ? launch_dequant_t<kBF16, __nv_bfloat16>(w, out, rows, n, row_bytes, st)
-                : launch_dequant_t<kBF16, float>(w, out, rows, n, row_bytes, st);
+#define VBQ_DEQ_CASE(QT)                                                                  \
+  case QT:                                                                                \
+    return bf ? launch_dequant_t<QT, __nv_bfloat16>(w, out, rows, n, row_bytes, st)       \
+              : launch_dequant_t<QT, float>(w, out, rows, n, row_bytes, st);
+    VBQ_DEQ_CASE(kQ4_K)
+    VBQ_DEQ_CASE(kQ6_K)
+    VBQ_DEQ_CASE(kQ8_0)
+    VBQ_DEQ_CASE(kF32)
+    VBQ_DEQ_CASE(kF16)
+    VBQ_DEQ_CASE(kBF16)
+    VBQ_DEQ_CASE(kQ4_0)
+    VBQ_DEQ_CASE(kQ4_1)
+    VBQ_DEQ_CASE(kQ5_0)
+    VBQ_DEQ_CASE(kQ5_1)
+    VBQ_DEQ_CASE(kQ2_K)
+    VBQ_DEQ_CASE(kQ3_K)
+    VBQ_DEQ_CASE(kQ5_K)
+    VBQ_DEQ_CASE(kQ8_K)
+#undef VBQ_DEQ_CASE
     default:
       return cudaErrorInvalidValue;
   }

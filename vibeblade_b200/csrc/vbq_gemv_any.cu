@@ -1,6 +1,7 @@
-// vbq_gemv_any.cu -- the generic fused dequant-GEMV: any supported weight type (F32, F16,
-// BF16, Q8_0, Q4_K, Q6_K), any N that is a multiple of the type's block (1 / 32 / 256
-// values) and any batch (groups of 4 rows on the grid's z dimension).
+// vbq_gemv_any.cu -- the generic fused dequant-GEMV: any weight type the reference's
+// gemv_dequant takes (F32, F16, BF16, Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q2_K, Q3_K, Q4_K, Q5_K,
+// Q6_K, Q8_K), any N that is a multiple of the type's block (1 / 32 / 256 values) and any
+// batch (groups of 4 rows on the grid's z dimension).
 //
 //   y[b, n] = sum_k x[b, k] * deq(W)[k, n]  (+ bias[n]) (+ res[b, n])
 //
@@ -9,8 +10,9 @@
 // (cpp/src/dequant.cpp:739-780, every type its switch at :748-763 lists that this library
 // reads).  The tiled kernels cover N % 256 == 0 in the quantized types; this one takes what
 // they do not: the MoE router (cpp/src/fast_model.cpp:861: N = n_experts, usually an F32 or
-// F16 tensor in GGUF files), Q8_0 rows whose width is a multiple of 32 but not of 256, and
-// unquantized weights of any width.
+// F16 tensor in GGUF files), Q8_0 rows whose width is a multiple of 32 but not of 256,
+// unquantized weights of any width, and the block types outside the path's three (Q4_0 /
+// Q4_1 / Q5_0 / Q5_1 / Q2_K / Q3_K / Q5_K / Q8_K files).
 //
 // Decomposition: a CTA owns one 256-column segment of the output, a K-slice and a group of
 // up to 4 batch rows; its 8 warps take the slice's rows in turn (row k to warp k % 8), lane l
@@ -200,6 +202,14 @@ cudaError_t launch_gemv_any(int qtype, const float* x, const void* w, float* y, 
     case kQ8_0: return gany::launch_any_q<kQ8_0>(x, w, y, K, N, row_bytes, batch, st, f);
     case kQ4_K: return gany::launch_any_q<kQ4_K>(x, w, y, K, N, row_bytes, batch, st, f);
     case kQ6_K: return gany::launch_any_q<kQ6_K>(x, w, y, K, N, row_bytes, batch, st, f);
+    case kQ4_0: return gany::launch_any_q<kQ4_0>(x, w, y, K, N, row_bytes, batch, st, f);
+    case kQ4_1: return gany::launch_any_q<kQ4_1>(x, w, y, K, N, row_bytes, batch, st, f);
+    case kQ5_0: return gany::launch_any_q<kQ5_0>(x, w, y, K, N, row_bytes, batch, st, f);
+    case kQ5_1: return gany::launch_any_q<kQ5_1>(x, w, y, K, N, row_bytes, batch, st, f);
+    case kQ2_K: return gany::launch_any_q<kQ2_K>(x, w, y, K, N, row_bytes, batch, st, f);
+    case kQ3_K: return gany::launch_any_q<kQ3_K>(x, w, y, K, N, row_bytes, batch, st, f);
+    case kQ5_K: return gany::launch_any_q<kQ5_K>(x, w, y, K, N, row_bytes, batch, st, f);
+    case kQ8_K: return gany::launch_any_q<kQ8_K>(x, w, y, K, N, row_bytes, batch, st, f);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -10,25 +10,46 @@ from __future__ import annotations
 
 GGML_TYPE_F32 = 0
 GGML_TYPE_F16 = 1
+GGML_TYPE_Q4_0 = 2
+GGML_TYPE_Q4_1 = 3
+GGML_TYPE_Q5_0 = 6
+GGML_TYPE_Q5_1 = 7
 GGML_TYPE_Q8_0 = 8
+GGML_TYPE_Q2_K = 10
+GGML_TYPE_Q3_K = 11
 GGML_TYPE_Q4_K = 12
+GGML_TYPE_Q5_K = 13
 GGML_TYPE_Q6_K = 14
+GGML_TYPE_Q8_K = 15
 GGML_TYPE_BF16 = 30
 
 TYPE_NAMES = {GGML_TYPE_F32: "F32", GGML_TYPE_F16: "F16", GGML_TYPE_BF16: "BF16",
-              GGML_TYPE_Q8_0: "Q8_0", GGML_TYPE_Q4_K: "Q4_K", GGML_TYPE_Q6_K: "Q6_K"}
+              GGML_TYPE_Q4_0: "Q4_0", GGML_TYPE_Q4_1: "Q4_1", GGML_TYPE_Q5_0: "Q5_0",
+              GGML_TYPE_Q5_1: "Q5_1", GGML_TYPE_Q8_0: "Q8_0", GGML_TYPE_Q2_K: "Q2_K",
+              GGML_TYPE_Q3_K: "Q3_K", GGML_TYPE_Q4_K: "Q4_K", GGML_TYPE_Q5_K: "Q5_K",
+              GGML_TYPE_Q6_K: "Q6_K", GGML_TYPE_Q8_K: "Q8_K"}
 NAME_TO_TYPE = {v: k for k, v in TYPE_NAMES.items()}
 
 # values per block (cpp/include/ggml_types.h:31-50)
 BLOCK_VALUES = {GGML_TYPE_F32: 1, GGML_TYPE_F16: 1, GGML_TYPE_BF16: 1,
-                GGML_TYPE_Q8_0: 32, GGML_TYPE_Q4_K: 256, GGML_TYPE_Q6_K: 256}
+                GGML_TYPE_Q4_0: 32, GGML_TYPE_Q4_1: 32, GGML_TYPE_Q5_0: 32, GGML_TYPE_Q5_1: 32,
+                GGML_TYPE_Q8_0: 32, GGML_TYPE_Q2_K: 256, GGML_TYPE_Q3_K: 256,
+                GGML_TYPE_Q4_K: 256, GGML_TYPE_Q5_K: 256, GGML_TYPE_Q6_K: 256,
+                GGML_TYPE_Q8_K: 256}
 # bytes per block (cpp/include/ggml_types.h:52-71); Q8_0 is the 34-byte GGUF block
 BLOCK_BYTES = {GGML_TYPE_F32: 4, GGML_TYPE_F16: 2, GGML_TYPE_BF16: 2,
-               GGML_TYPE_Q8_0: 34, GGML_TYPE_Q4_K: 144, GGML_TYPE_Q6_K: 210}
-# the quantized types (the tensor-core GEMM, MoE and the tiled GEMV kernels take these;
-# F32 / F16 / BF16 weights -- small tensors such as the MoE router in GGUF files -- take
-# the generic GEMV)
+               GGML_TYPE_Q4_0: 18, GGML_TYPE_Q4_1: 20, GGML_TYPE_Q5_0: 22, GGML_TYPE_Q5_1: 24,
+               GGML_TYPE_Q8_0: 34, GGML_TYPE_Q2_K: 84, GGML_TYPE_Q3_K: 110,
+               GGML_TYPE_Q4_K: 144, GGML_TYPE_Q5_K: 176, GGML_TYPE_Q6_K: 210,
+               GGML_TYPE_Q8_K: 292}
+# the quantized types of the path (the tensor-core GEMM, MoE and the tiled GEMV kernels
+# take these; F32 / F16 / BF16 weights -- small tensors such as the MoE router in GGUF
+# files -- and the other block types take the generic GEMV)
 QUANTIZED = (GGML_TYPE_Q8_0, GGML_TYPE_Q4_K, GGML_TYPE_Q6_K)
+# the reference dispatcher's other block types (cpp/src/dequant.cpp:412-422): dequantize
+# and the generic GEMV read them, each in the reference's reading of its block
+OTHER_BLOCK_TYPES = (GGML_TYPE_Q4_0, GGML_TYPE_Q4_1, GGML_TYPE_Q5_0, GGML_TYPE_Q5_1,
+                     GGML_TYPE_Q2_K, GGML_TYPE_Q3_K, GGML_TYPE_Q5_K, GGML_TYPE_Q8_K)
 
 # byte offsets inside a block
 Q4K_D, Q4K_DMIN, Q4K_SCALES, Q4K_QS = 0, 2, 4, 16          # block_q4_K :118-124

@@ -143,3 +143,35 @@ def synthetic_weights(K: int, N: int, qtype, seed: int = 0, std: float = 0.02,
     g.manual_seed(seed)
     w = torch.randn(K, N, generator=g, device=dev, dtype=torch.float32) * std
     return quantize(w, qtype)
+
+
+# Scale fields of the block types this library reads but does not quantize to: (byte
+# offset, fp16 or fp32) per block (cpp/include/ggml_types.h:82-168).
+_SCALE_FIELDS = {
+    F.GGML_TYPE_Q4_0: [(0, torch.float16)], F.GGML_TYPE_Q4_1: [(0, torch.float16), (2, torch.float16)],
+    F.GGML_TYPE_Q5_0: [(0, torch.float16)], F.GGML_TYPE_Q5_1: [(0, torch.float16), (2, torch.float16)],
+    F.GGML_TYPE_Q2_K: [(80, torch.float16), (82, torch.float16)], F.GGML_TYPE_Q3_K: [(108, torch.float16)],
+    F.GGML_TYPE_Q5_K: [(0, torch.float16), (2, torch.float16)], F.GGML_TYPE_Q8_K: [(0, torch.float32)],
+}
+
+
+def random_block_weights(K: int, N: int, qtype, seed: int = 0, std: float = 1e-3,
+                         device: str | torch.device = "cpu") -> torch.Tensor:
+    """uint8 [K, row_bytes(qtype, N)] of random code bytes with every scale field drawn
+    N(0, std): synthetic weights for the block types without a quantizer here (Q4_0, Q4_1,
+    Q5_0, Q5_1, Q2_K, Q3_K, Q5_K, Q8_K).  Their dequantizers are functions of the bytes
+    alone, so such weights exercise the same arithmetic and the same bytes per value as a
+    file's."""
+    t = F.parse_type(qtype)
+    if t not in _SCALE_FIELDS:
+        raise ValueError(f"random_block_weights: type {t} has a quantizer (use synthetic_weights)")
+    bb, bv = F.BLOCK_BYTES[t], F.BLOCK_VALUES[t]
+    nb = N // bv
+    dev = torch.device(device)
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    w = torch.randint(0, 256, (K, nb, bb), generator=g, device=dev, dtype=torch.uint8)
+    for off, dt in _SCALE_FIELDS[t]:
+        vals = (torch.randn(K, nb, 1, generator=g, device=dev) * std).to(dt)
+        w[:, :, off:off + vals.element_size()] = vals.view(torch.uint8)
+    return w.reshape(K, nb * bb)

@@ -42,7 +42,9 @@ def check_split(kind: str, K: int, N: int, qtype, world: int) -> None:
         if N % world or (N // world) % SHARD_COLUMN_ALIGN or (N // world) % F.BLOCK_VALUES[t]:
             raise ValueError(f"column split: N={N} over {world} ranks must leave multiples of "
                              f"{SHARD_COLUMN_ALIGN} columns per rank")
-        if F.row_bytes(t, N // world) % 16:
+        # the tiled kernels and the GEMM read rows by TMA (16-byte strides); the generic
+        # GEMV, which takes every other block type, reads 2-byte-aligned rows
+        if t in F.QUANTIZED and F.row_bytes(t, N // world) % 16:
             raise ValueError("column split: shard rows must be a multiple of 16 bytes "
                              "(Q6_K: N / world % 2048 == 0)")
     elif kind == "row":
@@ -108,7 +110,16 @@ class TPLinear:
 
     def prefill(self, a: torch.Tensor, out_dtype=torch.float32,
                 out: torch.Tensor | None = None) -> torch.Tensor:
-        """a: bf16 [M, k_loc] -> [M, n_loc] (row split: a partial sum)."""
+        """a: bf16 [M, k_loc] -> [M, n_loc] (row split: a partial sum).  The tensor-core
+        GEMM takes Q4_K / Q6_K / Q8_0; the other types run as one generic GEMV over all M
+        rows (fp32 sums, as the reference's per-token loop computes them)."""
+        if self.t not in F.QUANTIZED:
+            y = gemv_dequant(a.float().contiguous(), self.w, None, self.k_loc, self.n_loc, self.t)
+            y = y.view(a.shape[0], self.n_loc).to(out_dtype)
+            if out is None:
+                return y
+            out.copy_(y)
+            return out
         return gemm_dequant(a, self.w, out, a.shape[0], self.k_loc, self.n_loc, self.t, out_dtype)
 
     def decode(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
