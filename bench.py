@@ -279,7 +279,7 @@ def bench_lm_head(dev, steps: int) -> dict:
 
 def bench_other_types(dev, steps: int) -> dict:
     """The reference dispatcher's other block types (Q4_0, Q4_1, Q5_0, Q5_1, Q2_K, Q3_K,
-    Q5_K, Q8_K) through the generic GEMV kernel: config 2's 4096 x 14336 at batch 1,
+    Q5_K, Q8_K) through their staged GEMV kernel: config 2's 4096 x 14336 at batch 1,
     synthetic weights (random codes, N(0, 1e-3) scales); enough copies alternate that they
     never sit in L2 (>= 256 MB)."""
     import torch
@@ -287,7 +287,8 @@ def bench_other_types(dev, steps: int) -> dict:
     from vibeblade_b200 import formats as F
     from vibeblade_b200.quantize import random_block_weights
     K, N = 4096, 14336
-    out = {"shape": f"{K}x{N}", "batch": 1, "kernel": "vbq::gany::gemv_any_kernel (generic GEMV)"}
+    out = {"shape": f"{K}x{N}", "batch": 1,
+           "kernel": "vbq::gstage::gemv_stage_kernel (per-warp cp.async rings, fp32x2 CUDA-core dot)"}
     g = torch.Generator(device=dev).manual_seed(8)
     x = torch.randn(1, K, generator=g, device=dev)
     y = torch.empty(1, N, device=dev)

@@ -67,6 +67,20 @@ __device__ __forceinline__ float f16_ieee(uint32_t h) {
 
 __device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xffu; }
 
+// (float)u for 0 <= u < 2^23, exactly, without an integer-to-float conversion: u in the
+// mantissa of 2^23, then 2^23 subtracted (both steps exact).  The conversion unit runs at a
+// fraction of the FP32 rate, the OR and FADD at the full rate.
+__device__ __forceinline__ float u2f(uint32_t u) {
+  return __fsub_rn(__uint_as_float(0x4b000000u | u), 8388608.0f);
+}
+// (float)((int)u - OFF) the same way, for 0 <= u < 2^23 and 0 <= OFF < 2^23.
+template <int OFF>
+__device__ __forceinline__ float u2f_minus(uint32_t u) {
+  return __fsub_rn(__uint_as_float(0x4b000000u | u), 8388608.0f + (float)OFF);
+}
+// (float)(int8_t)b for the byte b (the low 8 bits of b).
+__device__ __forceinline__ float s8f(uint32_t b) { return u2f_minus<128>((b & 0xffu) ^ 0x80u); }
+
 // nan -> 0, +-inf -> +-65504, then clip to +-65504 (vibeblade/moe.py:472-473)
 __device__ __forceinline__ float sanitize(float v) {
   if (v != v) return 0.0f;

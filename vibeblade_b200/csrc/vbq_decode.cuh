@@ -76,7 +76,8 @@ __device__ __forceinline__ void decode8<kQ8_0>(const uint8_t* __restrict__ unit,
 
 // ---- the other block types of the reference's dispatcher ----
 // Blocks sit at 2-byte-aligned offsets (every block size is even), so 16-bit fields are
-// read directly and 4-byte runs with ld_u32_a2.
+// read directly and 4-byte runs with ld_u32_a2.  Small integers become floats through
+// u2f / s8f (exact, at the FP32 rate).
 
 // Q4_0, 18 B (cpp/src/dequant.cpp:23-35): d @0, qs @2; value i of a block is nibble i&1 of
 // qs[i>>1], so the lane's 8 values (block lane/4, values 8(lane&3)..) are the 8 nibbles of
@@ -88,7 +89,7 @@ __device__ __forceinline__ void decode8<kQ4_0>(const uint8_t* __restrict__ unit,
   const float d = f16_ref(ld_u16(blk));
   const uint32_t w = ld_u32_a2(blk + 2 + 4 * (lane & 3));
 #pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = __fmul_rn((float)((int)((w >> (4 * i)) & 0xfu) - 8), d);
+  for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(u2f_minus<8>((w >> (4 * i)) & 0xfu), d);
 }
 
 // Q4_1, 20 B (:40-53): d @0, m @2, qs @4; out = d * q + m.
@@ -99,7 +100,7 @@ __device__ __forceinline__ void decode8<kQ4_1>(const uint8_t* __restrict__ unit,
   const float d = f16_ref(ld_u16(blk)), m = f16_ref(ld_u16(blk + 2));
   const uint32_t w = ld_u32_a2(blk + 4 + 4 * (lane & 3));
 #pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = __fadd_rn(__fmul_rn(d, (float)((w >> (4 * i)) & 0xfu)), m);
+  for (int i = 0; i < 8; ++i) v[i] = __fadd_rn(__fmul_rn(d, u2f((w >> (4 * i)) & 0xfu)), m);
 }
 
 // Q5_0, 22 B (:58-73): d @0, qh @2 (bit i = fifth bit of value i), qs @6; out = (q - 16) * d.
@@ -112,8 +113,8 @@ __device__ __forceinline__ void decode8<kQ5_0>(const uint8_t* __restrict__ unit,
   const uint32_t w = ld_u32_a2(blk + 6 + 4 * (lane & 3));
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const int q = (int)(((w >> (4 * i)) & 0xfu) | (((hb >> i) & 1u) << 4));
-    v[i] = __fmul_rn((float)(q - 16), d);
+    const uint32_t q = ((w >> (4 * i)) & 0xfu) | (((hb >> i) & 1u) << 4);
+    v[i] = __fmul_rn(u2f_minus<16>(q), d);
   }
 }
 
@@ -128,7 +129,7 @@ __device__ __forceinline__ void decode8<kQ5_1>(const uint8_t* __restrict__ unit,
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const uint32_t q = ((w >> (4 * i)) & 0xfu) | (((hb >> i) & 1u) << 4);
-    v[i] = __fadd_rn(__fmul_rn(d, (float)q), m);
+    v[i] = __fadd_rn(__fmul_rn(d, u2f(q)), m);
   }
 }
 
@@ -141,10 +142,10 @@ __device__ __forceinline__ void decode8<kQ2_K>(const uint8_t* __restrict__ blk, 
                                                float v[8]) {
   const int s = lane >> 1;
   const float d = f16_ref(ld_u16(blk + 80)), mn = f16_ref(ld_u16(blk + 82));
-  const float dl = __fmul_rn(d, (float)(blk[s] & 0xf));
+  const float dl = __fmul_rn(d, u2f(blk[s] & 0xfu));
   const uint32_t q = blk[16 + 4 * s + (lane & 1)];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = __fadd_rn(__fmul_rn(dl, (float)((q >> (2 * (i & 3))) & 3u)), mn);
+  for (int i = 0; i < 8; ++i) v[i] = __fadd_rn(__fmul_rn(dl, u2f((q >> (2 * (i & 3))) & 3u)), mn);
 }
 
 // Q3_K scale of sub-block j (get_scale_min_k3, :155-166; its min is unused).
@@ -164,7 +165,7 @@ __device__ __forceinline__ void decode8<kQ3_K>(const uint8_t* __restrict__ blk, 
                                                float v[8]) {
   const int c = lane >> 3, t = (lane >> 1) & 3, sh = 4 * c + 2 * t;
   const float d = f16_ref(ld_u16(blk + 108));
-  const float dt = __fmul_rn(d, (float)q3k_scale(blk + 96, 4 * c + t));
+  const float dt = __fmul_rn(d, u2f((uint32_t)q3k_scale(blk + 96, 4 * c + t)));
   const uint32_t q = blk[32 + 16 * c + 4 * t + (lane & 1)];
   const uint8_t* hm = blk + 8 * (lane & 1);
   const uint32_t h0 = ld_u32_a2(hm), h1 = ld_u32_a2(hm + 4);
@@ -172,7 +173,7 @@ __device__ __forceinline__ void decode8<kQ3_K>(const uint8_t* __restrict__ blk, 
   for (int i = 0; i < 8; ++i) {
     const uint32_t hbyte = byte_of(i < 4 ? h0 : h1, i & 3);
     const uint32_t h = sh < 8 ? (hbyte >> sh) & 1u : 0u;
-    v[i] = __fmul_rn(dt, (float)(((q >> (2 * (i & 3))) & 3u) + 8u * h));
+    v[i] = __fmul_rn(dt, u2f(((q >> (2 * (i & 3))) & 3u) + 8u * h));
   }
 }
 
@@ -189,7 +190,7 @@ __device__ __forceinline__ void decode8<kQ5_K>(const uint8_t* __restrict__ blk, 
   const uint32_t s0 = ld_u32_a2(blk + 4), s1 = ld_u32_a2(blk + 8), s2 = ld_u32_a2(blk + 12);
   int sc, mn;
   q4k_scale_min(2 * c + half, s0, s1, s2, sc, mn);
-  const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
+  const float d1 = __fmul_rn(d, u2f((uint32_t)sc)), m1 = __fmul_rn(dmin, u2f((uint32_t)mn));
   const uint8_t* qp = blk + 48 + 32 * c + l0;
   const uint8_t* hp = blk + 16 + 32 * c + l0;
   const uint32_t q0 = ld_u32_a2(qp), q1 = ld_u32_a2(qp + 4);
@@ -198,7 +199,7 @@ __device__ __forceinline__ void decode8<kQ5_K>(const uint8_t* __restrict__ blk, 
   for (int i = 0; i < 8; ++i) {
     const uint32_t qb = byte_of(i < 4 ? q0 : q1, i & 3), hb = byte_of(i < 4 ? g0 : g1, i & 3);
     const uint32_t q = half ? ((qb >> 4) | (((hb >> 3) & 1u) << 4)) : ((qb & 0xfu) | (((hb >> 7) & 1u) << 4));
-    v[i] = __fsub_rn(__fmul_rn(d1, (float)q), m1);
+    v[i] = __fsub_rn(__fmul_rn(d1, u2f(q)), m1);
   }
 }
 
@@ -210,10 +211,10 @@ __device__ __forceinline__ void decode8<kQ8_K>(const uint8_t* __restrict__ blk, 
                                                float v[8]) {
   const float d = __uint_as_float(ld_u16(blk) | (ld_u16(blk + 2) << 16));
   const uint8_t* sub = blk + 4 + 33 * (lane >> 2);
-  const float ds = __fmul_rn(d, (float)(int)(int8_t)sub[32]);
+  const float ds = __fmul_rn(d, s8f(sub[32]));
   const uint8_t* q = sub + 8 * (lane & 3);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = __fmul_rn((float)(int)(int8_t)q[i], ds);
+  for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(s8f(q[i]), ds);
 }
 
 // F32 rows: the values as stored (memcpy in the reference's dequantize_row).

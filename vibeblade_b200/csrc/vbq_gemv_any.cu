@@ -195,6 +195,10 @@ cudaError_t launch_gemv_any(int qtype, const float* x, const void* w, float* y, 
                             const GemvFuse& f) {
   if (batch < 1 || K < 1 || N < 1 || K > INT32_MAX || N > INT32_MAX) return cudaErrorInvalidValue;
   if ((batch + gany::kMaxBatch - 1) / gany::kMaxBatch > 65535) return cudaErrorInvalidValue;
+  if (gemv_stage_takes(qtype, K, N, row_bytes, w)) {
+    const cudaError_t e = launch_gemv_stage(qtype, x, w, y, K, N, row_bytes, batch, st, f);
+    if (e != cudaErrorNotSupported) return e;  // else: a K-slice too long for its shared memory
+  }
   switch (qtype) {
     case kF32: return gany::launch_any_q<kF32>(x, w, y, K, N, row_bytes, batch, st, f);
     case kF16: return gany::launch_any_q<kF16>(x, w, y, K, N, row_bytes, batch, st, f);

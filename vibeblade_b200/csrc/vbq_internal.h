@@ -22,6 +22,20 @@ struct DeviceOnce {
   }
 };
 
+// A per-device int a launcher computes once (resident CTAs per SM, say): set before the
+// launcher's DeviceOnce mark, read after its done() check, so a reader that sees the mark
+// sees the value.  Devices past 63 read 1.
+struct DeviceSlots {
+  std::atomic<int> v[64] = {};
+  void set(int dev, int x) {
+    if (dev < 64) v[dev].store(x, std::memory_order_release);
+  }
+  int get(int dev) const {
+    const int x = dev < 64 ? v[dev].load(std::memory_order_acquire) : 1;
+    return x > 0 ? x : 1;
+  }
+};
+
 cudaError_t launch_dequant(int qtype, const void* w, void* out, int64_t rows, int64_t n,
                            int64_t row_bytes, int out_dtype, cudaStream_t st);
 
@@ -54,12 +68,20 @@ cudaError_t launch_gemv(int qtype, const float* x, const void* w, float* y, int6
                         int64_t N, int64_t row_bytes, int batch, const GemvPlan& plan,
                         void* scratch, cudaStream_t st, const GemvFuse& f = GemvFuse{});
 
-// Generic GEMV (vbq_gemv_any.cu): any type (F32, F16, BF16, Q8_0, Q4_K, Q6_K), any N that
-// is a multiple of the block, any batch (groups of 4 rows on the grid), optional bias [N]
-// and residual [batch, N] added to the output; no scratch.
+// Generic GEMV (vbq_gemv_any.cu): any type the library reads, any N that is a multiple of
+// the block, any batch (groups of 4 rows on the grid), optional bias [N] and residual
+// [batch, N] added to the output; no scratch.  The reference dispatcher's other block types
+// (Q4_0 .. Q8_K) go to the staged kernel (vbq_gemv_stage.cu) when it takes the shape.
 cudaError_t launch_gemv_any(int qtype, const float* x, const void* w, float* y, int64_t K,
                             int64_t N, int64_t row_bytes, int batch, cudaStream_t st,
                             const GemvFuse& f = GemvFuse{});
+
+// Staged GEMV for Q4_0, Q4_1, Q5_0, Q5_1, Q2_K, Q3_K, Q5_K, Q8_K (vbq_gemv_stage.cu): takes
+// N a multiple of its column unit (256, or 512 for Q3_K), 4-byte-aligned rows, a 16-byte
+// aligned w and K * row_bytes a multiple of 16.
+bool gemv_stage_takes(int qtype, int64_t K, int64_t N, int64_t row_bytes, const void* w);
+cudaError_t launch_gemv_stage(int qtype, const float* x, const void* w, float* y, int64_t K, int64_t N,
+                              int64_t row_bytes, int batch, cudaStream_t st, const GemvFuse& f);
 
 // Tensor-core (integer mma.sync) Q4_K GEMV, batch 1..16, when gemv_mma_fits(); the K-splits
 // of a tile form one thread-block cluster and add up in the leader's shared memory.
