@@ -167,3 +167,33 @@ def test_tp_linear_emulated(cuda):
     assert float((part - full).abs().max() / full.abs().max()) <= 1e-5
     pre = sum(r.prefill(a[:, i * K // 2:(i + 1) * K // 2]) for i, r in enumerate(rows))
     assert float((pre - full_a).abs().max() / full_a.abs().max()) <= 1e-5
+
+
+def test_gguf_dequant_row(cuda, oracle, tmp_path):
+    """GGUFFile.dequant_row (the reference's VibeBladeFast.dequant_row debug binding,
+    cpp/src/bindings.cpp:407-436) on every type it takes: one row, a prefix of a row, and a
+    count running on into the next row, bit-exact against the oracle's dequantize_row of
+    the same bytes."""
+    import gguf_files as G
+    from vibeblade_b200.gguf import GGUFFile
+    from vibeblade_b200.quantize import synthetic_weights
+    rng = np.random.default_rng(21)
+    K, N = 3, 512
+    ws = {F.GGML_TYPE_Q4_0: random_blocks(F.GGML_TYPE_Q4_0, K, N, rng),
+          F.GGML_TYPE_Q5_0: random_blocks(F.GGML_TYPE_Q5_0, K, N, rng),
+          F.GGML_TYPE_Q5_K: random_blocks(F.GGML_TYPE_Q5_K, K, N, rng),
+          F.GGML_TYPE_F32: rng.normal(0, 1, (K, N)).astype(np.float32).view(np.uint8),
+          F.GGML_TYPE_F16: rng.normal(0, 1, (K, N)).astype(np.float16).view(np.uint8)}
+    for t in (F.GGML_TYPE_Q4_K, F.GGML_TYPE_Q6_K, F.GGML_TYPE_Q8_0):
+        ws[t] = synthetic_weights(K, N, t, seed=t).numpy()
+    path = G.write(tmp_path / "r.gguf", [],
+                   [G.weight_tensor(F.TYPE_NAMES[t], w, K, N, t) for t, w in ws.items()])
+    with GGUFFile(path) as f:
+        for t, w in ws.items():
+            flat = np.ascontiguousarray(w).view(np.uint8).reshape(-1)
+            rb = F.row_bytes(t, N)
+            for row, n in ((1, 0), (2, 100), (0, 2 * N)):
+                got = f.dequant_row(F.TYPE_NAMES[t], row, n, device=cuda)
+                nn = n if n > 0 else N
+                want = oracle.dequantize_row(flat[row * rb:], nn, t)
+                assert got.shape == (nn,) and bits_equal(got, want), (t, row, n)

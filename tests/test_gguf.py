@@ -201,3 +201,22 @@ def test_tensor_data_keeps_the_file_alive(tmp_path):
     p = G.write(tmp_path / "a.gguf", [], [G.weight_tensor("w", w, 4, 256, F.GGML_TYPE_Q4_K)])
     a = GGUFFile(p).tensor_data("w")  # the file object goes away; the array keeps it
     assert np.array_equal(a, w.reshape(-1))
+
+
+def test_dequant_row_errors_need_no_gpu(tmp_path):
+    """VibeBladeFast.dequant_row's errors (cpp/src/bindings.cpp:407-436) come before any
+    device work: an unknown tensor, a type outside its switch, and (here, where the
+    reference would read past the tensor) a row beyond the tensor."""
+    w = _weights(F.GGML_TYPE_Q4_K, 4, 256, 9)
+    q2 = np.zeros((2, 84), np.uint8)  # Q2_K: read by dequantize, not by dequant_row
+    p = G.write(tmp_path / "d.gguf", [], [G.weight_tensor("w", w, 4, 256, F.GGML_TYPE_Q4_K),
+                                          G.weight_tensor("q2", q2, 2, 256, F.GGML_TYPE_Q2_K)])
+    with GGUFFile(p) as f:
+        with pytest.raises(RuntimeError, match="Tensor not found: nope"):
+            f.dequant_row("nope")
+        with pytest.raises(RuntimeError, match="Unsupported type for dequant_row"):
+            f.dequant_row("q2")
+        with pytest.raises(RuntimeError, match="runs past"):
+            f.dequant_row("w", 4)
+        with pytest.raises(RuntimeError, match="runs past"):
+            f.dequant_row("w", 3, 512)

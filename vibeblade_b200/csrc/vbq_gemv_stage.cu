@@ -11,9 +11,9 @@
 // Decomposition: a CTA owns C 256-column units of the output (C = 2 for Q3_K, whose
 // 110-byte unit is not a whole number of 4-byte words; 1 otherwise), a K-slice and a group
 // of up to 4 batch rows.  Each of its 8 warps streams a contiguous share of the slice's rows
-// through a ring of its own in shared memory (kRing stages of kWRows rows), with 16-byte
+// through a ring of its own in shared memory (3-8 stages of 8 rows), with 16-byte
 // cp.async of the granules that cover each row's chunk, so the loop has no CTA-wide
-// barrier; the first kRing - 1 stages are issued before the dependency wait on the
+// barrier; all but one of the ring's stages are issued before the dependency wait on the
 // previous grid (weights do not depend on it).  After that wait the slice's activations
 // (B x kslice fp32) are loaded into shared memory once, so no row waits on a global load.
 // Lane l takes values 8 l .. 8 l + 7 of each unit of a row from shared memory and adds
@@ -40,8 +40,7 @@ namespace gstage {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = 32 * kWarps;
-constexpr int kRing = 8;        // stages of a warp's ring
-constexpr int kWRows = 4;       // rows per stage
+constexpr int kWRows = 8;       // rows per stage of a warp's ring
 constexpr int kMaxBatch = 4;    // batch rows per CTA
 constexpr int kMaxSplit = 8;    // portable cluster size
 
@@ -54,6 +53,11 @@ template <int QT> struct Cfg {
   static constexpr int kGran = (kChunk + 12 + 15) / 16;
   static constexpr int kPitch = 16 * kGran;                     // a row's place in a stage
   static constexpr int kStage = kWRows * kPitch;
+  // stages per warp ring: about 80 KB of rings per CTA, 3 to 8 stages (measured on B200 at
+  // 4096 x 14336, batch 1: 8 rows a stage and ~64-80 KB beat 4 rows and 41-78 KB, and
+  // larger rings cost Q8_K its second CTA per SM)
+  static constexpr int kRingRaw = 81920 / (kWarps * kStage);
+  static constexpr int kRing = kRingRaw < 3 ? 3 : (kRingRaw > 8 ? 8 : kRingRaw);
   static constexpr int kWarpRing = kRing * kStage;              // one warp's ring
   static constexpr int kRingBytes = kWarps * kWarpRing;
   // after the loop the same memory holds [warp][b][C * 256] sums and the CTA's [b][C * 256]
@@ -225,17 +229,21 @@ template <> struct Dot<kQ3_K> {
   template <int B>
   __device__ __forceinline__ static void row(const uint8_t* blk, int lane, const float (&x)[B],
                                              float2 (&acc)[B][4], float (&)[B], const uint2*) {
-    const int c = lane >> 3, t = (lane >> 1) & 3, sh = 4 * c + 2 * t;
+    const int c = lane >> 3, t = (lane >> 1) & 3, sh = 4 * c + 2 * t, j = 4 * c + t;
     const float d = f16_ref(s_u16(blk + 108));
-    const float dt = __fmul_rn(d, u2f((uint32_t)q3k_scale(blk + 96, 4 * c + t)));
+    // get_scale_min_k3's scale of sub-block j without a branch (lanes hold different j):
+    // byte j (j < 4), j + 4 (j < 8) or j - 4 (its high nibble) of the 12 scale bytes
+    const int sidx = j < 4 ? j : (j < 8 ? j + 4 : j - 4);
+    const uint32_t sb = blk[96 + sidx];
+    const uint32_t scale = j < 8 ? (sb & 63u) : (sb >> 4);
+    const float dt = __fmul_rn(d, u2f(scale));
     const uint32_t q = blk[32 + 16 * c + 4 * t + (lane & 1)];
     const uint32_t qrep = (q & 3u) | ((q & 0x0cu) << 6) | ((q & 0x30u) << 12) | ((q & 0xc0u) << 18);
     const uint8_t* hm = blk + 8 * (lane & 1);
-    uint32_t m0 = 0, m1 = 0;
-    if (sh < 8) {
-      m0 = ((ld_u32_a2(hm) >> sh) & 0x01010101u) << 3;
-      m1 = ((ld_u32_a2(hm + 4) >> sh) & 0x01010101u) << 3;
-    }
+    // high bits: bit sh of each hmask byte, none once sh reaches 8 (masked, not branched)
+    const uint32_t keep = sh < 8 ? 0x01010101u : 0u;
+    const uint32_t m0 = ((ld_u32_a2(hm) >> (sh & 7)) & keep) << 3;
+    const uint32_t m1 = ((ld_u32_a2(hm + 4) >> (sh & 7)) & keep) << 3;
     float2 f[4];
     pairs_from_bytes(qrep + m0, qrep + m1, -k2p23, f);
     float s[B];
@@ -254,8 +262,8 @@ template <> struct Dot<kQ5_K> {
     const int c = lane >> 3, half = (lane >> 2) & 1, l0 = 8 * (lane & 3);
     const uint32_t dd = s_u32(blk);
     const float d = f16_ref(dd & 0xffffu), dmin = f16_ref(dd >> 16);
-    int sc, mn;
-    q4k_scale_min(2 * c + half, s_u32(blk + 4), s_u32(blk + 8), s_u32(blk + 12), sc, mn);
+    int sc, mn;  // sub-block 2c + half differs across the warp: the branch-free unpacking
+    Q4kScaleRecipe(2 * c + half).apply(s_u32(blk + 4), s_u32(blk + 8), s_u32(blk + 12), sc, mn);
     const float d1 = __fmul_rn(d, u2f((uint32_t)sc)), m1 = __fmul_rn(dmin, u2f((uint32_t)mn));
     const uint8_t* qp = blk + 48 + 32 * c + l0;
     const uint8_t* hp = blk + 16 + 32 * c + l0;
@@ -351,7 +359,7 @@ gemv_stage_kernel(const float* __restrict__ x, const uint8_t* __restrict__ w, fl
 
   // prologue: the first kRing - 1 stages (weights only) before the dependency wait
 #pragma unroll 1
-  for (int s = 0; s < kRing - 1; ++s) {
+  for (int s = 0; s < C::kRing - 1; ++s) {
     if (s < nst) {
       const int r0 = wr0 + s * kWRows;
       issue_rows<QT>(ring + s * C::kStage, w, RB, col0, r0, min(kWRows, wr1 - r0), lane);
@@ -387,17 +395,17 @@ gemv_stage_kernel(const float* __restrict__ x, const uint8_t* __restrict__ w, fl
   // the warp's own ring: no CTA-wide barrier in the loop
 #pragma unroll 1
   for (int s = 0; s < nst; ++s) {
-    cp_async_wait<kRing - 2>();
+    cp_async_wait<C::kRing - 2>();
     __syncwarp();  // stage s has landed for every lane; stage s - 1 is consumed
     {
-      const int sn = s + kRing - 1;  // refill the slot of stage s - 1
+      const int sn = s + C::kRing - 1;  // refill the slot of stage s - 1
       if (sn < nst) {
         const int r0 = wr0 + sn * kWRows;
-        issue_rows<QT>(ring + (sn % kRing) * C::kStage, w, RB, col0, r0, min(kWRows, wr1 - r0), lane);
+        issue_rows<QT>(ring + (sn % C::kRing) * C::kStage, w, RB, col0, r0, min(kWRows, wr1 - r0), lane);
       }
       cp_async_commit();
     }
-    const uint8_t* stage = ring + (s % kRing) * C::kStage;
+    const uint8_t* stage = ring + (s % C::kRing) * C::kStage;
     const int kb = wr0 + s * kWRows;  // the stage's first row
     if (kb + kWRows <= wr1) {
       // a full stage: no per-row test, so the rows' shared-memory reads overlap

@@ -183,6 +183,40 @@ class GGUFFile:
             K *= d
         return K, info.dims[0], info.type
 
+    # the types the reference's dequant_row binding sizes rows for (cpp/src/bindings.cpp:
+    # 416-425), anything else raising "Unsupported type for dequant_row"
+    _DEQUANT_ROW_TYPES = (F.GGML_TYPE_F32, F.GGML_TYPE_F16, F.GGML_TYPE_Q4_0, F.GGML_TYPE_Q5_0,
+                          F.GGML_TYPE_Q8_0, F.GGML_TYPE_Q4_K, F.GGML_TYPE_Q5_K, F.GGML_TYPE_Q6_K)
+
+    def dequant_row(self, tensor_name: str, row_idx: int = 0, n_elements: int = 0,
+                    device=None) -> np.ndarray:
+        """``VibeBladeFast.dequant_row(tensor_name, row_idx=0, n_elements=0)``
+        (cpp/src/bindings.cpp:407-436): row `row_idx` of a tensor (rows of dims[0] values),
+        dequantized on the device, as fp32 numpy.  n_elements <= 0 means the whole row; a
+        larger count runs on into the following rows, as there.  The same errors as the
+        reference: "Tensor not found: <name>", "Unsupported type for dequant_row" (it takes
+        F32, F16, Q4_0, Q5_0, Q8_0, Q4_K, Q5_K, Q6_K).  Unlike the reference, which reads
+        whatever lies there, a row or count reaching past the tensor's bytes raises.  Q8_0
+        rows decode the GGUF block (fp16 scale), not the reference CPU reader's fp32 one."""
+        info = self.tensor_info(tensor_name)
+        if info is None:
+            raise RuntimeError(f"Tensor not found: {tensor_name}")
+        t = info.type
+        if t not in self._DEQUANT_ROW_TYPES:
+            raise RuntimeError("Unsupported type for dequant_row")
+        ne0 = info.dims[0]
+        rb = F.row_bytes(t, ne0)
+        n = int(n_elements) if n_elements > 0 else int(ne0)
+        start, nbytes = int(row_idx) * rb, F.tensor_nbytes(t, n)
+        data = self.tensor_data(tensor_name)
+        if row_idx < 0 or start + nbytes > data.size:
+            raise RuntimeError(f"dequant_row: row {row_idx} x {n} values of '{tensor_name}' runs past "
+                               f"its {data.size} bytes")
+        from .dequant import dequantize_row
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        row = torch.from_numpy(np.array(data[start:start + nbytes])).to(dev)
+        return dequantize_row(row, None, n, t).cpu().numpy()
+
     # -- metadata (the reference's defaults when a key is missing) --
     def meta_count(self, key: str, kind: int) -> int | None:
         """Length of `key`'s value of `kind` (META_*; 1 for a scalar), or None without one."""
