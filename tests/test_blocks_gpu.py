@@ -197,3 +197,28 @@ def test_gguf_dequant_row(cuda, oracle, tmp_path):
                 nn = n if n > 0 else N
                 want = oracle.dequantize_row(flat[row * rb:], nn, t)
                 assert got.shape == (nn,) and bits_equal(got, want), (t, row, n)
+
+
+@pytest.mark.parametrize("qtype", [F.GGML_TYPE_Q5_K, F.GGML_TYPE_Q4_0])
+def test_gemv_swiglu_input(cuda, qtype):
+    """The fused SwiGLU input (x = silu(gate) * up of a packed [B, 2K] buffer) gives the
+    same bits as a SwiGLU pass followed by the plain GEMV."""
+    from vibeblade_b200 import tp
+    K, N, batch = 512, 1024, 5
+    rng = np.random.default_rng(qtype + 3)
+    wd = torch.from_numpy(random_blocks(qtype, K, N, rng)).to(cuda)
+    gu = torch.from_numpy(rng.normal(0, 2, (batch, 2 * K)).astype(np.float32)).to(cuda)
+    fused = vb.gemv_fused(gu, wd, None, K, N, qtype, swiglu_input=True)
+    plain = vb.gemv_dequant(tp.swiglu_rows(gu, K), wd, None, K, N, qtype)
+    assert torch.equal(fused, plain)
+
+
+def test_gemv_long_rows_fall_back(cuda, oracle):
+    """A K-slice whose activations overflow the staged kernel's shared memory (very long
+    rows at batch 4) runs on the generic kernel instead, with the same bar."""
+    K, N, batch, t = 120000, 256, 4, F.GGML_TYPE_Q4_1
+    rng = np.random.default_rng(8)
+    w = random_blocks(t, K, N, rng, std=1e-3)
+    x = rng.normal(0, 1, (batch, K)).astype(np.float32)
+    y = vb.gemv_dequant(torch.from_numpy(x).to(cuda), torch.from_numpy(w).to(cuda), None, K, N, t)
+    assert max_rel(y.cpu().numpy(), oracle.gemv_dequant(x, w, K, N, t)) <= 1e-3
