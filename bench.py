@@ -288,7 +288,9 @@ def bench_other_types(dev, steps: int) -> dict:
     from vibeblade_b200.quantize import random_block_weights
     K, N = 4096, 14336
     out = {"shape": f"{K}x{N}", "batch": 1,
-           "kernel": "vbq::gstage::gemv_stage_kernel (per-warp cp.async rings, fp32x2 CUDA-core dot)"}
+           "kernel": ("vbq::gstage::gemv_stage_kernel (per-warp cp.async rings, fp32x2 CUDA-core dot); "
+                      "Q5_K: vbq::gmma::gemv_mma_kernel<1, false, true> (the Q4_K u8 x s8 tensor-core "
+                      "kernel with the fifth bits merged into its A fragments)")}
     g = torch.Generator(device=dev).manual_seed(8)
     x = torch.randn(1, K, generator=g, device=dev)
     y = torch.empty(1, N, device=dev)

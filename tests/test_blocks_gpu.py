@@ -222,3 +222,49 @@ def test_gemv_long_rows_fall_back(cuda, oracle):
     x = rng.normal(0, 1, (batch, K)).astype(np.float32)
     y = vb.gemv_dequant(torch.from_numpy(x).to(cuda), torch.from_numpy(w).to(cuda), None, K, N, t)
     assert max_rel(y.cpu().numpy(), oracle.gemv_dequant(x, w, K, N, t)) <= 1e-3
+
+
+def _outlier_rows(rng, batch, K, frac=0.01, lo=100.0, hi=1000.0):
+    """N(0, 1) activations with `frac` of each row's channels scaled 100-1000x (random sign)
+    and one at the last row of the first 32-row slice, like real hidden states."""
+    x = rng.normal(0, 1, (batch, K)).astype(np.float32)
+    n = max(1, int(frac * K))
+    for b in range(batch):
+        idx = rng.choice(K, n, replace=False)
+        x[b, idx] *= (rng.uniform(lo, hi, n) * rng.choice([-1.0, 1.0], n)).astype(np.float32)
+        x[b, 31] = np.float32(hi)
+    return x
+
+
+def _columns_ok(y, ref, what):
+    """1e-3 of each row's largest output, and 1e-3 relative on every output >= 1e-2 of it."""
+    y, ref = np.asarray(y, np.float64), np.asarray(ref, np.float64)
+    mx = np.abs(ref).max(axis=1, keepdims=True)
+    err = np.abs(y - ref)
+    assert (err / mx).max() <= 1e-3, f"{what}: max-norm {(err / mx).max():.3g}"
+    big = np.abs(ref) >= 1e-2 * mx
+    assert (err[big] / np.abs(ref[big])).max() <= 1e-3, f"{what}: per-column"
+
+
+@pytest.mark.parametrize("K,N", [(4096, 14336), (14336, 4096)])
+@pytest.mark.parametrize("batch", [1, 2, 4, 16])
+def test_q5k_tensor_core_gemv(cuda, oracle, K, N, batch):
+    """Q5_K at decode batches runs on the Q4_K kernel's integer tensor-core form (fifth bits
+    merged into the A fragments, codes 0..31 in u8): outlier activations, per-column bar,
+    against the fp64 product of the bit-exact device dequantization and the reference's
+    sequential fp32 sums; the device status stays clean and repeats are bit-identical."""
+    t = F.GGML_TYPE_Q5_K
+    rng = np.random.default_rng(K + batch)
+    wh = random_blocks(t, K, N, rng, std=2e-4)
+    w = torch.from_numpy(wh).to(cuda)
+    x = _outlier_rows(rng, batch, K)
+    xd = torch.from_numpy(x).to(cuda)
+    y = vb.gemv_dequant(xd, w, None, K, N, t)
+    assert torch.equal(y, vb.gemv_dequant(xd, w, None, K, N, t))
+    assert vb.device_status() == 0
+    deq = vb.dequantize(w, K, N, t).double()
+    ref64 = (xd.double() @ deq).cpu().numpy()
+    del deq
+    _columns_ok(y.cpu().numpy(), ref64, "fp64")
+    if batch <= 4:
+        _columns_ok(y.cpu().numpy(), oracle.gemv_dequant(x, wh, K, N, t), "oracle")

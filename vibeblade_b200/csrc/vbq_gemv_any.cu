@@ -195,6 +195,12 @@ cudaError_t launch_gemv_any(int qtype, const float* x, const void* w, float* y, 
                             const GemvFuse& f) {
   if (batch < 1 || K < 1 || N < 1 || K > INT32_MAX || N > INT32_MAX) return cudaErrorInvalidValue;
   if ((batch + gany::kMaxBatch - 1) / gany::kMaxBatch > 65535) return cudaErrorInvalidValue;
+  // Q5_K decode batches on the integer tensor cores (the Q4_K kernel's Q5_K form)
+  if (qtype == kQ5_K && batch <= 16 && gemv_mma_fits(K, N, batch) && row_bytes % 16 == 0 &&
+      (reinterpret_cast<uintptr_t>(w) & 15u) == 0) {
+    const cudaError_t e = launch_gemv_mma_q5k(x, w, y, K, N, row_bytes, batch, st, f);
+    if (e != cudaErrorNotSupported) return e;
+  }
   if (gemv_stage_takes(qtype, K, N, row_bytes, w)) {
     const cudaError_t e = launch_gemv_stage(qtype, x, w, y, K, N, row_bytes, batch, st, f);
     if (e != cudaErrorNotSupported) return e;  // else: a K-slice too long for its shared memory

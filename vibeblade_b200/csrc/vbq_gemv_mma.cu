@@ -1,4 +1,5 @@
-// vbq_gemv_mma.cu -- Q4_K dequant-GEMV on the integer tensor cores (decode, batch 1..4).
+// vbq_gemv_mma.cu -- Q4_K dequant-GEMV on the integer tensor cores (decode, batch 1..4), and
+// its Q5_K form (176-byte rows, fifth bits merged into the A fragments; see Geo / Q5).
 //
 //   y[b, n] = sum_k x[b, k] * deq(W)[k, n],  deq(W)[k, n] = dl[k, s] * q[k, n] - ml[k, s]
 //
@@ -60,9 +61,16 @@ namespace gmma {
 constexpr int kConsumers = 8;
 constexpr int kThreads = 32 * (kConsumers + 1);
 constexpr int kRows = 16 * kConsumers;   // rows per stage
-constexpr int kPitch = 144;              // one Q4_K block per row
-constexpr int kStageBytes = kRows * kPitch;  // 18432
 constexpr int kStages = 4;  // a power of two (slot = stage & (kStages - 1))
+// Row geometry of a stage: one Q4_K block (144 B, codes at byte 16) or, with Q5, one Q5_K
+// block (176 B: d, dmin and the 12 scale bytes as in Q4_K, the 32 fifth-bit bytes at 16,
+// codes at 48) per row.
+template <bool Q5> struct Geo {
+  static constexpr int kPitch = Q5 ? 176 : 144;
+  static constexpr int kQs = Q5 ? 48 : 16;
+  static constexpr int kStageBytes = kRows * kPitch;  // 18432 / 22528
+  static constexpr int kTblOff = kStages * kStageBytes;
+};
 // B table per warp and column set: [4 local sub-blocks][8 columns][32 rows] s8, each
 // column's rows ordered so that lane (g, t)'s two fragment words (k = 4t.., 16 + 4t..) are
 // adjacent (one 8-byte load at byte 8t of column g; conflict-free per half warp).  Sub-block
@@ -77,34 +85,34 @@ struct Bars {
   uint64_t red;  // the cluster leader's: the other splits' partial sums have landed
   int abort;
 };
-constexpr int kTblOff = kStages * kStageBytes;
 constexpr int kRedOff = 0;  // the per-warp outputs reuse the stage ring afterwards
-static_assert(kRedBytes <= kStages * kStageBytes, "reduction buffer inside the ring");
-template <int NSET> struct Lay {
-  static constexpr int kBarOff = kTblOff + kConsumers * NSET * kTblBytes;
+static_assert(kRedBytes <= kStages * Geo<false>::kStageBytes, "reduction buffer inside the ring");
+template <int NSET, bool Q5 = false> struct Lay {
+  static constexpr int kBarOff = Geo<Q5>::kTblOff + kConsumers * NSET * kTblBytes;
   // the leader's receive slots: splits 1 .. S-1, batch x 256 fp32 each (sized at launch)
   static constexpr int kRecvOff = kBarOff + 128;
   static constexpr int kSmem = kRecvOff + 128;  // + alignment slack; plus the slots
 };
 constexpr int kMaxSplit = 16;  // cluster size limit (non-portable above 8)
 
-template <int BATCH, bool SWIGLU>
+template <int BATCH, bool SWIGLU, bool Q5 = false>
 __global__ void __launch_bounds__(kThreads, BATCH <= 2 ? 2 : 1)
 gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restrict__ x,
                 float* y, int K, int N, int batch, Epi epi) {
+  using G = Geo<Q5>;
   constexpr int NSET = BATCH <= 2 ? 1 : 2;  // B column sets: two batch rows per set
   constexpr int kDownEvery = BATCH <= 2 ? 1 : 2;  // stages between shrink tests (a power of two)
   extern __shared__ uint8_t smem_raw[];
   // 128-byte aligned: TMA destinations and ldmatrix rows
   uint8_t* smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
-  using L = Lay<NSET>;
+  using L = Lay<NSET, Q5>;
   Bars& bars = *reinterpret_cast<Bars*>(smem + L::kBarOff);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y, S = gridDim.y;
   // CTA `split` takes the 128-row stages split, split + S, split + 2S, ... of the matrix
   const int tot_st = (K + kRows - 1) / kRows;
   const int nst = split < tot_st ? (tot_st - split + S - 1) / S : 0;
-  auto stage = [&](int s) { return smem + s * kStageBytes; };
+  auto stage = [&](int s) { return smem + s * G::kStageBytes; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -153,8 +161,8 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
           break;
         }
         const uint32_t fb = smem_u32(&bars.full[s]);
-        mbar_arrive_expect_tx(fb, kStageBytes);
-        tma_load_2d(smem_u32(stage(s)), &tmap_w, tile * (kPitch / 2), (split + S * it) * kRows, fb);
+        mbar_arrive_expect_tx(fb, G::kStageBytes);
+        tma_load_2d(smem_u32(stage(s)), &tmap_w, tile * (G::kPitch / 2), (split + S * it) * kRows, fb);
       }
       // every issued stage lands before the CTA may exit
       for (int j = (it > kStages ? it - kStages : 0); j < it; ++j)
@@ -176,7 +184,7 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
       // are adjacent; rows 2 rp, 2 rp + 1 are one 16-bit slot
       const int kap0 = 8 * ((rp & 7) >> 1) + 4 * (rp >> 3) + 2 * (rp & 1);
       const int g = lane >> 2, t = lane & 3;  // MMA fragment role
-      uint8_t* tbl = smem + kTblOff + warp * NSET * kTblBytes;
+      uint8_t* tbl = smem + G::kTblOff + warp * NSET * kTblBytes;
       for (int i = lane; i < NSET * kTblBytes / 4; i += 32) reinterpret_cast<uint32_t*>(tbl)[i] = 0u;
       __syncwarp();
       for (int i = lane; i < NSET * 4 * 2 * 8; i += 32) {  // all-ones columns 3 and 7
@@ -192,7 +200,7 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
       const uint32_t sel_lo = 0x7440u | (uint32_t)(2 * gl), sel_hi = sel_lo + 1u;  // sub-block byte
       const int row0 = rw + 2 * rp;  // stage row of this lane's first row
       // ldmatrix: lane L gives row rw + L (matrix L >> 3, row L & 7) of the warp's qs bytes
-      const uint32_t lm_lane = smem_u32(smem) + (uint32_t)((rw + lane) * kPitch + 16 + 64 * GP);
+      const uint32_t lm_lane = smem_u32(smem) + (uint32_t)((rw + lane) * G::kPitch + G::kQs + 64 * GP);
       asm volatile("griddepcontrol.wait;" ::: "memory");
 
       int acc[NSET][4][2][4];  // [set][chunk][low / high nibbles][fragment]
@@ -234,7 +242,8 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
               // the pair's halves: lane t even keeps row g, lane t odd row g + 8
               const float mine = odd ? p1 : p0, other = odd ? p0 : p1;
               const float sum = mine + __shfl_xor_sync(0xffffffffu, other, 1);
-              const float f = h ? sb * 0.0625f : sb;  // high nibbles entered as 16 q
+              // Q4_K high nibbles are entered as 16 q; Q5_K codes always as q
+              const float f = (h && !Q5) ? sb * 0.0625f : sb;
               fac[z][c][h] = fmaf(sum, f, fac[z][c][h]);
               a[0] = a[1] = a[2] = a[3] = 0;
             }
@@ -275,11 +284,11 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
             if (lane == 0) give_up();
             break;
           }
-          const uint8_t* st = smem + u * kStageBytes;
+          const uint8_t* st = smem + u * G::kStageBytes;
           // ---- scales of the lane's two rows (get_scale_min_k4, cpp/src/dequant.cpp:258-266,
           // four sub-blocks per word) ----
-          const uint4 h0 = *reinterpret_cast<const uint4*>(st + row0 * kPitch);
-          const uint4 h1 = *reinterpret_cast<const uint4*>(st + (row0 + 1) * kPitch);
+          const uint4 h0 = *reinterpret_cast<const uint4*>(st + row0 * G::kPitch);
+          const uint4 h1 = *reinterpret_cast<const uint4*>(st + (row0 + 1) * G::kPitch);
           uint32_t s0, s1, m0, m1;
           if constexpr (GP == 0) {  // sub-blocks 0-3: 6-bit fields of scale bytes 0-3 / 4-7
             s0 = h0.y & 0x3f3f3f3fu;
@@ -374,18 +383,39 @@ gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restr
             }
           __syncwarp();
           // ---- 4 chunks of 16 byte columns x 32 rows: low- and high-nibble MMAs per set ----
-          const uint32_t lm = lm_lane + (uint32_t)(u * kStageBytes);
+          const uint32_t lm = lm_lane + (uint32_t)(u * G::kStageBytes);
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            uint32_t a0, a1, a2, a3;  // A rows m = g / g + 8: byte columns g / g + 8
-            ldmatrix_a8_trans(lm + 16 * c, a0, a1, a2, a3);
+            uint32_t a[4];  // A rows m = g / g + 8: byte columns g / g + 8
+            ldmatrix_a8_trans(lm + 16 * c, a[0], a[1], a[2], a[3]);
+            uint32_t lo[4], hi[4];
+            if constexpr (Q5) {
+              // Q5_K (cpp/src/dequant.cpp:317-354): the fifth bits of code byte l' sit in byte
+              // 16 + l' of the block (the reference steps its qh pointer 32 bytes a chunk),
+              // 32 bytes before the code byte: the same ldmatrix 32 bytes lower puts them in
+              // the same fragment places; bit 7 belongs to the low nibble's value, bit 3 to
+              // the high nibble's.  Both codes enter as q (0..31).
+              uint32_t hb[4];
+              ldmatrix_a8_trans(lm + 16 * c - 32, hb[0], hb[1], hb[2], hb[3]);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                lo[i] = (a[i] & 0x0f0f0f0fu) | ((hb[i] >> 3) & 0x10101010u);
+                hi[i] = ((a[i] >> 4) & 0x0f0f0f0fu) | ((hb[i] << 1) & 0x10101010u);
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                lo[i] = a[i] & 0x0f0f0f0fu;
+                hi[i] = a[i] & 0xf0f0f0f0u;
+              }
+            }
 #pragma unroll
             for (int z = 0; z < NSET; ++z) {
               const uint8_t* tz = tfrag + z * kTblBytes + (2 * (c >> 1)) * kSbStride;
               const uint2 bl = *reinterpret_cast<const uint2*>(tz);
               const uint2 bh = *reinterpret_cast<const uint2*>(tz + kSbStride);
-              mma_u8s8(acc[z][c][0], a0 & 0x0f0f0f0fu, a1 & 0x0f0f0f0fu, a2 & 0x0f0f0f0fu, a3 & 0x0f0f0f0fu, bl.x, bl.y);
-              mma_u8s8(acc[z][c][1], a0 & 0xf0f0f0f0u, a1 & 0xf0f0f0f0u, a2 & 0xf0f0f0f0u, a3 & 0xf0f0f0f0u, bh.x, bh.y);
+              mma_u8s8(acc[z][c][0], lo[0], lo[1], lo[2], lo[3], bl.x, bl.y);
+              mma_u8s8(acc[z][c][1], hi[0], hi[1], hi[2], hi[3], bh.x, bh.y);
             }
           }
           __syncwarp();  // table and stage reads done
@@ -508,7 +538,7 @@ static EncodeTiledFnG encode_fn_g() {
 // tile's cluster at once with 25 % to spare (cudaOccupancyMaxActiveClusters, cached per
 // shape).  Measured on B200 (us per launch, batch 1): 4096 x 14336 S = 4: 11.6, S = 5
 // (56 clusters in 56-59 places): 16.3; 4096 x 6144 S = 8: 8.3, S = 12: 11.7.
-template <int BATCH, bool SW>
+template <int BATCH, bool SW, bool Q5>
 static int choose_splits(int64_t K, int64_t N, int batch, int smem_base) {
   using namespace gmma;
   const int tiles = (int)(N / 256);
@@ -547,7 +577,7 @@ static int choose_splits(int64_t K, int64_t N, int batch, int smem_base) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int active = 0;
-    if (cudaOccupancyMaxActiveClusters(&active, gmma::gemv_mma_kernel<BATCH, SW>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&active, gmma::gemv_mma_kernel<BATCH, SW, Q5>, &cfg) != cudaSuccess) {
       cudaGetLastError();
       active = 0;
     }
@@ -560,17 +590,17 @@ static int choose_splits(int64_t K, int64_t N, int batch, int smem_base) {
   return S;
 }
 
-template <int BATCH, bool SWIGLU>
+template <int BATCH, bool SWIGLU, bool Q5 = false>
 static cudaError_t launch_t(const float* x, const void* w, float* y, int64_t K, int64_t N,
                             int64_t RB, int batch, cudaStream_t st, Epi epi) {
   using namespace gmma;
   auto enc = encode_fn_g();
   if (!enc) return cudaErrorNotSupported;
   CUtensorMap mw;
-  if (!weight_map(reinterpret_cast<EncodeTiledFn>(enc), w, K, RB, kPitch, kRows, &mw))
+  if (!weight_map(reinterpret_cast<EncodeTiledFn>(enc), w, K, RB, Geo<Q5>::kPitch, kRows, &mw))
     return cudaErrorInvalidValue;
-  auto kern = gemv_mma_kernel<BATCH, SWIGLU>;
-  constexpr int kBase = Lay<(BATCH <= 2 ? 1 : 2)>::kSmem;
+  auto kern = gemv_mma_kernel<BATCH, SWIGLU, Q5>;
+  constexpr int kBase = Lay<(BATCH <= 2 ? 1 : 2), Q5>::kSmem;
   static DeviceOnce configured;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -582,7 +612,7 @@ static cudaError_t launch_t(const float* x, const void* w, float* y, int64_t K, 
     if (e != cudaSuccess) return e;
     configured.mark(dev);
   }
-  const int S = choose_splits<BATCH, SWIGLU>(K, N, batch, kBase);
+  const int S = choose_splits<BATCH, SWIGLU, Q5>(K, N, batch, kBase);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(N / 256), (unsigned)S, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -614,12 +644,12 @@ bool gemv_mma_fits(int64_t K, int64_t N, int batch) {
 // launches over groups of 4 batch rows (each streams the weights again).  Measured on
 // B200, 4096 x 14336: batch 8 grouped 33.2 us / wide 31.3 us / fp16 28.7 us; batch 16
 // grouped 64.5 us / wide 51.9 us / fp16 40.4 us.
-template <bool SW>
+template <bool SW, bool Q5 = false>
 static cudaError_t launch_group(const float* x, const void* w, float* y, int64_t K, int64_t N,
                                 int64_t row_bytes, int nb, cudaStream_t st, Epi epi) {
-  return nb == 1   ? launch_t<1, SW>(x, w, y, K, N, row_bytes, nb, st, epi)
-         : nb == 2 ? launch_t<2, SW>(x, w, y, K, N, row_bytes, nb, st, epi)
-                   : launch_t<4, SW>(x, w, y, K, N, row_bytes, nb, st, epi);
+  return nb == 1   ? launch_t<1, SW, Q5>(x, w, y, K, N, row_bytes, nb, st, epi)
+         : nb == 2 ? launch_t<2, SW, Q5>(x, w, y, K, N, row_bytes, nb, st, epi)
+                   : launch_t<4, SW, Q5>(x, w, y, K, N, row_bytes, nb, st, epi);
 }
 
 cudaError_t launch_gemv_mma_q4k(const float* x, const void* w, float* y, int64_t K, int64_t N,
@@ -637,6 +667,25 @@ cudaError_t launch_gemv_mma_q4k(const float* x, const void* w, float* y, int64_t
     const Epi epi{f.bias, f.res ? f.res + (int64_t)b0 * N : nullptr};
     cudaError_t e = f.swiglu_x ? launch_group<true>(xg, w, yg, K, N, row_bytes, nb, st, epi)
                                : launch_group<false>(xg, w, yg, K, N, row_bytes, nb, st, epi);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+// Q5_K on the same kernel (batch 1..16, as groups of up to 4 batch rows): the Q4_K
+// kernel with 176-byte rows and the fifth bits merged into its A fragments.  Rows of 176
+// bytes are always whole 16-byte granules, so every width of whole 256-column tiles fits.
+cudaError_t launch_gemv_mma_q5k(const float* x, const void* w, float* y, int64_t K, int64_t N,
+                                int64_t row_bytes, int batch, cudaStream_t st, const GemvFuse& f) {
+  if (!gemv_mma_fits(K, N, batch) || row_bytes % 16 != 0) return cudaErrorNotSupported;
+  const int64_t xrow = f.swiglu_x ? 2 * K : K;
+  for (int b0 = 0; b0 < batch; b0 += 4) {
+    const int nb = batch - b0 < 4 ? batch - b0 : 4;
+    const float* xg = x + (int64_t)b0 * xrow;
+    float* yg = y + (int64_t)b0 * N;
+    const Epi epi{f.bias, f.res ? f.res + (int64_t)b0 * N : nullptr};
+    cudaError_t e = f.swiglu_x ? launch_group<true, true>(xg, w, yg, K, N, row_bytes, nb, st, epi)
+                               : launch_group<false, true>(xg, w, yg, K, N, row_bytes, nb, st, epi);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;

@@ -76,6 +76,11 @@ cudaError_t launch_gemv_any(int qtype, const float* x, const void* w, float* y, 
                             int64_t N, int64_t row_bytes, int batch, cudaStream_t st,
                             const GemvFuse& f = GemvFuse{});
 
+// Q5_K on the Q4_K integer tensor-core kernel (vbq_gemv_mma.cu), batch 1..16 as groups of 4,
+// when gemv_mma_fits() and the rows are whole 16-byte granules.
+cudaError_t launch_gemv_mma_q5k(const float* x, const void* w, float* y, int64_t K, int64_t N,
+                                int64_t row_bytes, int batch, cudaStream_t st, const GemvFuse& f);
+
 // Staged GEMV for Q4_0, Q4_1, Q5_0, Q5_1, Q2_K, Q3_K, Q5_K, Q8_K (vbq_gemv_stage.cu): takes
 // N a multiple of its column unit (256, or 512 for Q3_K), 4-byte-aligned rows, a 16-byte
 // aligned w and K * row_bytes a multiple of 16.
