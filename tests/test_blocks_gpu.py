@@ -246,15 +246,18 @@ def _columns_ok(y, ref, what):
     assert (err[big] / np.abs(ref[big])).max() <= 1e-3, f"{what}: per-column"
 
 
+@pytest.mark.parametrize("t", [F.GGML_TYPE_Q5_K, F.GGML_TYPE_Q4_0, F.GGML_TYPE_Q4_1, F.GGML_TYPE_Q5_0,
+                               F.GGML_TYPE_Q5_1])
 @pytest.mark.parametrize("K,N", [(4096, 14336), (14336, 4096)])
 @pytest.mark.parametrize("batch", [1, 2, 4, 16])
-def test_q5k_tensor_core_gemv(cuda, oracle, K, N, batch):
-    """Q5_K at decode batches runs on the Q4_K kernel's integer tensor-core form (fifth bits
-    merged into the A fragments, codes 0..31 in u8): outlier activations, per-column bar,
-    against the fp64 product of the bit-exact device dequantization and the reference's
-    sequential fp32 sums; the device status stays clean and repeats are bit-identical."""
-    t = F.GGML_TYPE_Q5_K
-    rng = np.random.default_rng(K + batch)
+def test_tensor_core_gemv_outliers(cuda, oracle, t, K, N, batch):
+    """Decode batches of these types run on the integer tensor cores: Q5_K on the Q4_K
+    kernel's form (fifth bits merged into the A fragments, codes 0..31 in u8), Q4_0 / Q4_1 /
+    Q5_0 / Q5_1 on the Q8_0 kernel's (nibbles as u8 codes, fifth bits from qh, the -8 / -16
+    offsets and the + m terms summed apart).  Outlier activations, per-column bar, against
+    the fp64 product of the bit-exact device dequantization and the reference's sequential
+    fp32 sums; the device status stays clean and repeats are bit-identical."""
+    rng = np.random.default_rng(K + batch + t)
     wh = random_blocks(t, K, N, rng, std=2e-4)
     w = torch.from_numpy(wh).to(cuda)
     x = _outlier_rows(rng, batch, K)

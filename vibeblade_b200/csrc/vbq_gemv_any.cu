@@ -195,6 +195,13 @@ cudaError_t launch_gemv_any(int qtype, const float* x, const void* w, float* y, 
                             const GemvFuse& f) {
   if (batch < 1 || K < 1 || N < 1 || K > INT32_MAX || N > INT32_MAX) return cudaErrorInvalidValue;
   if ((batch + gany::kMaxBatch - 1) / gany::kMaxBatch > 65535) return cudaErrorInvalidValue;
+  // Q4_0 / Q4_1 / Q5_0 / Q5_1 decode batches on the integer tensor cores (the Q8_0 kernel's
+  // 4- and 5-bit forms)
+  if ((qtype == kQ4_0 || qtype == kQ4_1 || qtype == kQ5_0 || qtype == kQ5_1) && batch <= 16 &&
+      gemv_q8_fits(K, N, batch) && row_bytes % 16 == 0 && (reinterpret_cast<uintptr_t>(w) & 15u) == 0) {
+    const cudaError_t e = launch_gemv_q4x_mma(qtype, x, w, y, K, N, row_bytes, batch, st, f);
+    if (e != cudaErrorNotSupported) return e;
+  }
   // Q5_K decode batches on the integer tensor cores (the Q4_K kernel's Q5_K form)
   if (qtype == kQ5_K && batch <= 16 && gemv_mma_fits(K, N, batch) && row_bytes % 16 == 0 &&
       (reinterpret_cast<uintptr_t>(w) & 15u) == 0) {

@@ -76,6 +76,11 @@ cudaError_t launch_gemv_any(int qtype, const float* x, const void* w, float* y, 
                             int64_t N, int64_t row_bytes, int batch, cudaStream_t st,
                             const GemvFuse& f = GemvFuse{});
 
+// Q4_0 / Q4_1 / Q5_0 / Q5_1 on the Q8_0 integer tensor-core kernel (vbq_gemv_q8.cu), batch
+// 1..16 as groups of 4, when gemv_q8_fits() and the rows are whole 16-byte granules.
+cudaError_t launch_gemv_q4x_mma(int qtype, const float* x, const void* w, float* y, int64_t K, int64_t N,
+                                int64_t row_bytes, int batch, cudaStream_t st, const GemvFuse& f);
+
 // Q5_K on the Q4_K integer tensor-core kernel (vbq_gemv_mma.cu), batch 1..16 as groups of 4,
 // when gemv_mma_fits() and the rows are whole 16-byte granules.
 cudaError_t launch_gemv_mma_q5k(const float* x, const void* w, float* y, int64_t K, int64_t N,
