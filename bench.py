@@ -290,7 +290,9 @@ def bench_other_types(dev, steps: int) -> dict:
     out = {"shape": f"{K}x{N}", "batch": 1,
            "kernel": ("vbq::gstage::gemv_stage_kernel (per-warp cp.async rings, fp32x2 CUDA-core dot); "
                       "Q5_K: vbq::gmma::gemv_mma_kernel<1, false, true> (the Q4_K u8 x s8 tensor-core "
-                      "kernel with the fifth bits merged into its A fragments)")}
+                      "kernel with the fifth bits merged into its A fragments); Q4_0 / Q4_1 / Q5_0 / "
+                      "Q5_1: vbq::gq8::gemv_q8_kernel<1, false, F> (the Q8_0 tensor-core kernel, "
+                      "nibbles as u8 codes)")}
     g = torch.Generator(device=dev).manual_seed(8)
     x = torch.randn(1, K, generator=g, device=dev)
     y = torch.empty(1, N, device=dev)
