@@ -508,11 +508,32 @@ static int choose_splits_q8(int64_t K, int64_t N, int batch, int smem_base) {
   using namespace gq8;
   const int tiles = (int)(N / 256);
   const int64_t tot_st = (K + kRows - 1) / kRows;
-  int S = tiles > 0 ? 2 * sm_count() / tiles : 1;
+  // resident CTAs per SM: two for Q8_0 (272-byte rows); the 4- and 5-bit forms' smaller
+  // stages fit three where their registers allow (queried once per device)
+  int per_sm = 2;
+  if constexpr (F != kQ8_0) {
+    static DeviceOnce queried;
+    static DeviceSlots slots_per_sm;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) {
+      if (!queried.done(dev)) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q8_kernel<BATCH, SW, F>, kThreads,
+                                                          smem_base + 8 * 1024) != cudaSuccess) {
+          cudaGetLastError();
+          n = 2;
+        }
+        slots_per_sm.set(dev, n < 2 ? 2 : (n > 3 ? 3 : n));
+        queried.mark(dev);
+      }
+      per_sm = slots_per_sm.get(dev);
+    }
+  }
+  int S = tiles > 0 ? per_sm * sm_count() / tiles : 1;
   if (S > 16) S = 16;
   if (S > tot_st) S = (int)tot_st;
   if (S < 1) S = 1;
-  const int cap = 112 * 1024;  // two CTAs per SM
+  const int cap = per_sm >= 3 ? 72 * 1024 : 112 * 1024;  // per_sm CTAs per SM
   if (gemv_split_override()) {
     S = gemv_split_override() > 16 ? 16 : gemv_split_override();
     if (S > tot_st) S = (int)tot_st;
