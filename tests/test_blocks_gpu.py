@@ -215,8 +215,9 @@ def test_gemv_swiglu_input(cuda, qtype):
 
 def test_gemv_long_rows_fall_back(cuda, oracle):
     """A K-slice whose activations overflow the staged kernel's shared memory (very long
-    rows at batch 4) runs on the generic kernel instead, with the same bar."""
-    K, N, batch, t = 120000, 256, 4, F.GGML_TYPE_Q4_1
+    rows at batch 4, a type the tensor-core kernels do not take) runs on the generic
+    kernel instead, with the same bar."""
+    K, N, batch, t = 120000, 256, 4, F.GGML_TYPE_Q2_K
     rng = np.random.default_rng(8)
     w = random_blocks(t, K, N, rng, std=1e-3)
     x = rng.normal(0, 1, (batch, K)).astype(np.float32)
