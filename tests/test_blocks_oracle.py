@@ -7,6 +7,7 @@ from __future__ import annotations
 
 import numpy as np
 import pytest
+import torch
 
 from block_fill import BLOCK_BYTES, BLOCK_VALUES, TYPES, edge_blocks, random_blocks
 from conftest import bits_equal, load_golden
@@ -65,3 +66,17 @@ def test_block_tables_agree():
     for t in TYPES:
         assert F.BLOCK_VALUES[t] == BLOCK_VALUES[t] and F.BLOCK_BYTES[t] == BLOCK_BYTES[t]
         assert F.parse_type(F.TYPE_NAMES[t]) == t
+
+
+def test_random_block_weights(oracle):
+    """The library's synthetic weights for the types without a quantizer (the bench's
+    `other_types` object): the reference's block sizes, finite values of the chosen scale,
+    and a refusal for the types that have a quantizer."""
+    from vibeblade_b200.quantize import random_block_weights
+    for t in TYPES:
+        w = random_block_weights(8, 512, t, seed=1, std=1e-3)
+        assert w.dtype == torch.uint8 and tuple(w.shape) == (8, F.row_bytes(t, 512))
+        v = oracle.dequantize(w.numpy(), 8, 512, t)
+        assert np.isfinite(v).all() and 0 < np.abs(v).max() < 100  # Q8_K: d * int8 scale * int8 code
+    with pytest.raises(ValueError):
+        random_block_weights(8, 512, F.GGML_TYPE_Q4_K)

@@ -79,6 +79,26 @@ def test_split_rules():
         tp.check_split("row", 100, 256, F.GGML_TYPE_Q4_K, 8)
     with pytest.raises(ValueError):  # Q6_K shard rows must stay 16-byte multiples
         tp.check_split("column", 64, 2048, F.GGML_TYPE_Q6_K, 2)
+    # the types only the generic / staged GEMV read take 2-byte-aligned shard rows: a Q3_K
+    # shard of 256 columns is 110 bytes a row, a Q8_K one 292
+    tp.check_split("column", 64, 2048, F.GGML_TYPE_Q3_K, 8)
+    tp.check_split("column", 64, 512, F.GGML_TYPE_Q8_K, 2)
+    with pytest.raises(ValueError):  # whole 256-column tiles still
+        tp.check_split("column", 64, 512, F.GGML_TYPE_Q4_0, 4)
+
+
+def test_column_shards_of_the_other_block_types(oracle):
+    """Column shards of the dispatcher's other block types are the same bytes as the
+    columns of the whole matrix (block-aligned byte ranges of every row)."""
+    from block_fill import TYPES, random_blocks
+    rng = np.random.default_rng(5)
+    K, N, world = 6, 1024, 2
+    for t in TYPES:
+        w = torch.from_numpy(random_blocks(t, K, N, rng))
+        full = oracle.dequantize(w.numpy(), K, N, t)
+        parts = [oracle.dequantize(tp.shard(w, K, N, t, "column", r, world).numpy(), K, N // world, t)
+                 for r in range(world)]
+        np.testing.assert_array_equal(np.concatenate(parts, axis=1).view(np.uint32), full.view(np.uint32))
 
 
 def _silu(x):
