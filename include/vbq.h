@@ -114,8 +114,9 @@ int vbq_gemv_scratch_bytes(int64_t K, int64_t N, int32_t type, int32_t batch, si
  * x is fp32 [batch, K], y fp32 [batch, N], both row-major.  N must be a multiple of
  * the block size (256 for the K-quants, 32 for Q4_0/Q4_1/Q5_0/Q5_1/Q8_0, 1 for
  * F32/F16/BF16); widths that are whole 256-column tiles of Q4_K, Q6_K or Q8_0 run on the
- * tiled kernels, the rest (the MoE router's N = n_experts, unquantized weights, the other
- * block types) on a generic kernel without scratch.
+ * tiled kernels, as do batches up to 16 of Q4_0 / Q4_1 / Q5_0 / Q5_1 / Q5_K (no scratch);
+ * the rest (the MoE router's N = n_experts, unquantized weights, the other block types) on
+ * generic and staged kernels without scratch.
  * W and y must be 16-byte aligned, x 4-byte aligned.  F16 weights are read through the
  * reference's f16_to_f32 (fp16 subnormals doubled), BF16 as the top half of an fp32.
  * scratch: caller-owned device memory of at least vbq_gemv_scratch_bytes(); it must be
